@@ -1,0 +1,203 @@
+/* C ABI of libsiglip2_b200.so: the SigLIP-2 NaFlex vision-tower forward on
+ * B200 (sm_100a).
+ *
+ * Conventions
+ *  - Every pointer argument named *_dev is device memory owned by the caller
+ *    (the library never allocates on the forward path).  Host arrays are
+ *    named *_host.
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ *    stream).  All work is enqueued on it; nothing synchronises unless the
+ *    function says so.
+ *  - Every function returns a siglip2_status; on failure
+ *    siglip2_last_error() (thread-local) describes the cause.  Arguments are
+ *    validated on the host before any launch; kernels never trap.
+ *  - Row-major 2-D tensors, leading dimensions in elements.  Element type of
+ *    the activation/weight tensors is `dtype` (SIGLIP2_BF16 or SIGLIP2_F16 on
+ *    the tensor-core path, SIGLIP2_F32 on the fp32 path); biases and the
+ *    LayerNorm-folding vectors are always float32.
+ *
+ * Reference interfaces replaced (tohskai/SigLIP-2):
+ *  siglip2_forward / siglip2_forward_padded
+ *       -> Siglip2SequenceVisionTransformer.forward       model.py:260-292
+ *          Siglip2SequenceVisionTransformerOptimized.forward
+ *                                                          optimized_siglip2/model_optimized.py:356-388
+ *          (+ transformers Siglip2VisionTransformer.forward head/padded entry)
+ *  siglip2_gemm      -> nn.Linear projections               model.py:59-62,138-141,184-185
+ *                       fused Linear+GELU                   optimized_siglip2/ops/MLP.py:233-304
+ *                       LayerNorm feeding a Linear           model.py:211,219 / ops/layer_norm.py:364-547
+ *  siglip2_layernorm -> nn.LayerNorm (post_layernorm)       model.py:256-258,286
+ *  siglip2_posemb    -> Siglip2SequenceEmbeddings pos-emb resize loop  model.py:90-119
+ *  siglip2_fmha_varlen -> flex_attention + document block mask         model.py:156-163
+ *  siglip2_map_head  -> transformers Siglip2MultiheadAttentionPoolingHead.forward
+ *                       (modeling_siglip2.py:670-719; not in the reference)
+ */
+#ifndef SIGLIP2_B200_H
+#define SIGLIP2_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  SIGLIP2_OK = 0,
+  SIGLIP2_ERR_ARG = -1,
+  SIGLIP2_ERR_ALIGN = -2,
+  SIGLIP2_ERR_SHAPE = -3,
+  SIGLIP2_ERR_CUDA = -4,
+  SIGLIP2_ERR_TIMEOUT = -5,
+  SIGLIP2_ERR_UNSUPPORTED = -6
+} siglip2_status;
+
+typedef enum { SIGLIP2_F32 = 0, SIGLIP2_BF16 = 1, SIGLIP2_F16 = 2 } siglip2_dtype;
+
+typedef enum {
+  SIGLIP2_EPI_BIAS = 0,       /* out = A.B^T + bias                                   */
+  SIGLIP2_EPI_BIAS_RES = 1,   /* out = A.B^T + bias + res            (res may == out) */
+  SIGLIP2_EPI_LN = 2,         /* out = rstd(A)*(A.B^T - mu(A)*c1) + c2   (LayerNorm of A folded) */
+  SIGLIP2_EPI_LN_GELU = 3,    /* out = gelu_tanh(rstd(A)*(A.B^T - mu(A)*c1) + c2)      */
+  SIGLIP2_EPI_BIAS_GELU = 4   /* out = gelu_tanh(A.B^T + bias)                        */
+} siglip2_epilogue;
+
+/* Library version (major*10000 + minor*100 + patch). */
+int siglip2_version(void);
+
+/* Thread-local description of the last failure. */
+const char* siglip2_last_error(void);
+
+/* Synchronises the current device and returns SIGLIP2_ERR_TIMEOUT if a kernel
+ * gave up on a bounded wait since the last reset (the failing site id is in
+ * siglip2_last_error()).  reset != 0 clears the flag. */
+int siglip2_check_device(int reset);
+
+/* out[M,N] = epilogue(A[M,K] . B[N,K]^T).
+ * Tensor-core path (dtype BF16/F16): K, lda, ldb, ldo, ldr multiples of 8;
+ * N multiple of 8; base pointers 16-byte aligned.  For the LN epilogues
+ * mu/rstd are the LayerNorm statistics of each row of A over its K columns
+ * (eps applied), c1/c2 the folded column vectors [N]. */
+int siglip2_gemm(int dtype, int epilogue, const void* a_dev, int lda, const void* b_dev, int ldb, void* out_dev,
+                 int ldo, int M, int N, int K, const float* bias_dev, const void* res_dev, int ldr,
+                 const float* c1_dev, const float* c2_dev, float eps, void* stream);
+
+/* LayerNorm over the last dimension (fp32 statistics, biased variance).
+ * Packed mode (cu_seqlens_dev == NULL): y[r] = LN(x[r]) for r < rows.
+ * Padded mode: rows = B * max_patches destination rows; destination (b, i)
+ * is LN(x[cu[b] + i]) when i < cu[b+1] - cu[b], else zeros.
+ * Replaces nn.LayerNorm (post_layernorm, model.py:256-258,286). */
+int siglip2_layernorm(int dtype, const void* x_dev, void* y_dev, const float* gamma_dev, const float* beta_dev,
+                      int rows, int D, float eps, const int* cu_seqlens_dev, int max_patches, void* stream);
+
+/* tok_img[t] = image index of packed token t (cu_seqlens_dev has B+1 entries). */
+int siglip2_token_image(const int* cu_seqlens_dev, int B, int N, int* tok_img_dev, void* stream);
+
+/* Position embeddings for the packed sequence: out[t] = antialiased bilinear
+ * resize of the grid x grid table (float32 [grid*grid, D], row-major h, w)
+ * to image (h, w) = hw_dev[2b], hw_dev[2b+1], evaluated at token t's (y, x).
+ * Replaces the per-image F.interpolate loop, model.py:90-116. */
+int siglip2_posemb(int dtype, const float* table_dev, int grid, int D, const int* tok_img_dev, const int* hw_dev,
+                   const int* cu_seqlens_dev, int N, void* out_dev, void* stream);
+
+/* Per-image attention over the packed sequence.  qkv_dev: [N, 3*heads*HDP]
+ * with HDP = siglip2_padded_head_dim(head_dim); column (w*heads + h)*HDP + d
+ * holds q (w=0), k (w=1), v (w=2) of head h, dim d, and columns
+ * d >= head_dim must be zero.  tiles_dev: n_tiles (image, query_tile) int32
+ * pairs covering ceil(L_b / 128) query tiles of every image.  out_dev:
+ * [N, ldo] receives softmax(q k^T / sqrt(head_dim)) v per head at columns
+ * h*head_dim ...  Replaces flex_attention with the document mask,
+ * model.py:156-163. */
+int siglip2_fmha_varlen(int dtype, const void* qkv_dev, int N, const int* cu_seqlens_dev, const int* tiles_dev,
+                        int n_tiles, int heads, int head_dim, void* out_dev, int ldo, void* stream);
+
+/* Head dimension as stored in the QKV buffer (64 -> 64, 72 -> 80, 96 -> 96). */
+int siglip2_padded_head_dim(int head_dim);
+
+/* ------------------------------------------------------------------------
+ * Whole-tower forward
+ * ------------------------------------------------------------------------ */
+
+/* Model hyper-parameters (Siglip2VisionConfig, model.py:39-49). */
+typedef struct {
+  int hidden;         /* D */
+  int intermediate;   /* I */
+  int layers;
+  int heads;          /* H; head_dim = D / H */
+  int head_dim;
+  int patch_dim;      /* num_channels * patch_size^2 */
+  int pos_grid;       /* sqrt(num_patches) */
+  float eps;          /* layer_norm_eps */
+  int dtype;          /* siglip2_dtype of weights and activations */
+  int has_head;       /* attention-pooling head present */
+} siglip2_config;
+
+/* Device pointers of one encoder layer, pre-packed by the host layer:
+ *  qkv_w  [3*H*HDP, D]: rows (w*H + h)*HDP + d = (W_w * ln1.gamma)[h*hd + d]
+ *         for d < head_dim, zero rows for the padding d >= head_dim;
+ *  qkv_c1 = row sums of qkv_w, qkv_c2 = b + W . ln1.beta (zero in padding);
+ *  fc1_w = W1 * ln2.gamma, fc1_c1 / fc1_c2 likewise;
+ *  out_w / fc2_w as in the reference, biases float32. */
+typedef struct {
+  const void* qkv_w;
+  const float* qkv_c1;
+  const float* qkv_c2;
+  const void* out_w;
+  const float* out_b;
+  const void* fc1_w;
+  const float* fc1_c1;
+  const float* fc1_c2;
+  const void* fc2_w;
+  const float* fc2_b;
+} siglip2_layer_weights;
+
+typedef struct {
+  const void* patch_w;                  /* [D, patch_dim] */
+  const float* patch_b;                 /* [D] */
+  const float* pos_table;               /* [pos_grid^2, D] float32 */
+  const siglip2_layer_weights* layers;  /* HOST array of `layers` entries */
+  const float* post_ln_w;
+  const float* post_ln_b;
+  /* attention-pooling head (has_head) */
+  const float* head_u;        /* [H, D] float32: W_k,h^T q_h * log2(e)/sqrt(hd), q = W_q probe + b_q */
+  const void* head_v_w;       /* [D, D] = in_proj_weight[2D:3D] */
+  const float* head_v_b;      /* [D] */
+  const void* head_o_w;       /* [D, D] out_proj */
+  const float* head_o_b;
+  const void* head_fc1_w;     /* [I, D] * head.layernorm.gamma */
+  const float* head_fc1_c1;
+  const float* head_fc1_c2;
+  const void* head_fc2_w;     /* [D, I] */
+  const float* head_fc2_b;
+} siglip2_weights;
+
+/* Number of int32 entries of the metadata array for `batch` images with
+ * grids hw_host[2b], hw_host[2b+1]; also returns the packed token count and
+ * the number of 128-row attention tiles.  Returns <0 on invalid grids. */
+int siglip2_metadata_size(const int32_t* hw_host, int batch, int* n_tokens, int* n_tiles);
+
+/* Fill the metadata array (host memory, siglip2_metadata_size() entries):
+ * cu_seqlens[B+1] | hw[2B] | zero pad to an even offset | tiles[2*n_tiles]
+ * (longest images first; the tile list is read as 8-byte pairs).  The
+ * caller copies it to device memory (meta_dev) for siglip2_forward. */
+int siglip2_metadata(const int32_t* hw_host, int batch, int32_t* meta_host, size_t capacity);
+
+/* Workspace bytes siglip2_forward needs for this configuration. */
+size_t siglip2_workspace_size(const siglip2_config* cfg, int batch, int n_tokens);
+
+/* The forward pass.
+ *  patches_dev: packed [N, patch_dim] (max_patches == 0, the reference's
+ *     forward((seq_patches, token_grids))) or padded [B, max_patches,
+ *     patch_dim] whose first h*w rows per image are valid (HF-style entry);
+ *  hw_host: [2B] grids; meta_dev: device copy of siglip2_metadata();
+ *  last_hidden_dev: packed [N, D] or padded [B, max_patches, D] (padded rows
+ *     written as zeros); pooled_dev: [B, D] or NULL (needs has_head).
+ * Enqueues only this library's kernels on `stream`; no allocation, no sync. */
+int siglip2_forward(const siglip2_config* cfg, const siglip2_weights* w, const void* patches_dev, int batch,
+                    int max_patches, const int32_t* hw_host, const int32_t* meta_dev, void* last_hidden_dev,
+                    void* pooled_dev, void* workspace_dev, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SIGLIP2_B200_H */

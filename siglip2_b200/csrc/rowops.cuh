@@ -1,0 +1,220 @@
+// Bandwidth-bound row kernels: the stand-alone LayerNorm (post_layernorm,
+// whose output is last_hidden_state) and the per-image antialiased resize of
+// the learned position grid.  Both move 16 bytes per thread per access
+// (8 x bf16/f16, 4 x f32) and reduce with warp shuffles.
+#pragma once
+
+#include "ptx.cuh"
+
+namespace sg {
+
+template <typename T>
+struct Vec16 {
+  static constexpr int N = 16 / sizeof(T);
+};
+
+template <typename T>
+__device__ __forceinline__ void load_vec(const T* p, float* f) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  if constexpr (sizeof(T) == 4) {
+    f[0] = __uint_as_float(u.x);
+    f[1] = __uint_as_float(u.y);
+    f[2] = __uint_as_float(u.z);
+    f[3] = __uint_as_float(u.w);
+  } else {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 t = Pack2<T>::unpack(w[i]);
+      f[2 * i] = t.x;
+      f[2 * i + 1] = t.y;
+    }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void store_vec(T* p, const float* f) {
+  uint4 u;
+  if constexpr (sizeof(T) == 4) {
+    u.x = __float_as_uint(f[0]);
+    u.y = __float_as_uint(f[1]);
+    u.z = __float_as_uint(f[2]);
+    u.w = __float_as_uint(f[3]);
+  } else {
+    u.x = Pack2<T>::pack(f[0], f[1]);
+    u.y = Pack2<T>::pack(f[2], f[3]);
+    u.z = Pack2<T>::pack(f[4], f[5]);
+    u.w = Pack2<T>::pack(f[6], f[7]);
+  }
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// ---------------------------------------------------------------------------
+// LayerNorm, one warp per row, two-pass (mean, then centred variance) from
+// registers; D <= 32 * 8 * MAXV elements.
+//
+// Packed mode (cu == nullptr): rows = N, y[r] = LN(x[r]).
+// Padded mode: rows = B * P destination rows; destination (b, i) takes source
+// row cu[b] + i when i < cu[b+1] - cu[b] and is zero otherwise.
+// ---------------------------------------------------------------------------
+template <typename T, int MAXV>
+__global__ void __launch_bounds__(256) layernorm_kernel(const T* __restrict__ x, T* __restrict__ y,
+                                                        const float* __restrict__ gamma,
+                                                        const float* __restrict__ beta, int rows, int D, float eps,
+                                                        const int* __restrict__ cu, int P) {
+  constexpr int V = Vec16<T>::N;
+  const int warps_per_block = blockDim.x >> 5;
+  const int row = blockIdx.x * warps_per_block + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int nvec = D / V;
+  int src = row;
+  if (cu != nullptr) {
+    const int b = row / P, i = row - (row / P) * P;
+    const int L = cu[b + 1] - cu[b];
+    if (i >= L) {
+      float z[V];
+#pragma unroll
+      for (int k = 0; k < V; ++k) z[k] = 0.f;
+      for (int v = lane; v < nvec; v += 32) store_vec(y + static_cast<size_t>(row) * D + v * V, z);
+      return;
+    }
+    src = cu[b] + i;
+  }
+  const T* xr = x + static_cast<size_t>(src) * D;
+  float f[MAXV][V];
+  float s = 0.f;
+#pragma unroll
+  for (int c = 0; c < MAXV; ++c) {
+    const int v = lane + c * 32;
+    if (v < nvec) {
+      load_vec(xr + v * V, f[c]);
+#pragma unroll
+      for (int k = 0; k < V; ++k) s += f[c][k];
+    }
+  }
+  const float mean = warp_sum(s) / static_cast<float>(D);
+  float q = 0.f;
+#pragma unroll
+  for (int c = 0; c < MAXV; ++c) {
+    const int v = lane + c * 32;
+    if (v < nvec) {
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        const float d = f[c][k] - mean;
+        q = fmaf(d, d, q);
+      }
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(q) / static_cast<float>(D) + eps);
+  T* yr = y + static_cast<size_t>(row) * D;
+#pragma unroll
+  for (int c = 0; c < MAXV; ++c) {
+    const int v = lane + c * 32;
+    if (v < nvec) {
+      float o[V];
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        const int col = v * V + k;
+        o[k] = (f[c][k] - mean) * rstd * __ldg(gamma + col) + __ldg(beta + col);
+      }
+      store_vec(yr + v * V, o);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Antialiased bilinear resize of the G x G position grid to each image's
+// (h, w), written row-major (h outer, w inner) into the packed token order.
+//
+// One axis of F.interpolate(bilinear, align_corners=False, antialias=True):
+//   scale = G / n; support = max(scale, 1); centre c = scale (i + 0.5);
+//   taps j in [max(int(c - support + 0.5), 0), min(int(c + support + 0.5), G))
+//   weight tri((j - c + 0.5) / max(scale, 1)), tri(t) = max(0, 1 - |t|),
+//   normalised to sum 1.
+// ---------------------------------------------------------------------------
+struct AxisTaps {
+  int lo, hi;
+  float center, inv, norm;
+};
+
+__device__ __forceinline__ AxisTaps axis_taps(int i, int n, int G) {
+  AxisTaps a;
+  const float scale = static_cast<float>(G) / static_cast<float>(n);
+  const float support = scale >= 1.f ? scale : 1.f;
+  a.inv = scale >= 1.f ? 1.f / scale : 1.f;
+  a.center = scale * (static_cast<float>(i) + 0.5f);
+  a.lo = max(static_cast<int>(a.center - support + 0.5f), 0);
+  a.hi = min(static_cast<int>(a.center + support + 0.5f), G);
+  float tot = 0.f;
+  for (int j = a.lo; j < a.hi; ++j) tot += fmaxf(0.f, 1.f - fabsf((static_cast<float>(j) - a.center + 0.5f) * a.inv));
+  a.norm = tot > 0.f ? 1.f / tot : 0.f;
+  return a;
+}
+
+__device__ __forceinline__ float axis_w(const AxisTaps& a, int j) {
+  return fmaxf(0.f, 1.f - fabsf((static_cast<float>(j) - a.center + 0.5f) * a.inv)) * a.norm;
+}
+
+// grid: (ceil(N / tokens_per_block)), block: (D / 8 threads per token) x tokens
+// tok_img[t] = image of token t; hw[2b], hw[2b+1] = (h, w); cu = row starts.
+template <typename T>
+__global__ void posemb_kernel(const float* __restrict__ table, int G, int D, const int* __restrict__ tok_img,
+                              const int* __restrict__ hw, const int* __restrict__ cu, int N, T* __restrict__ out) {
+  const int vec_per_tok = D / 8;
+  const int t = blockIdx.x * blockDim.y + threadIdx.y;
+  const int v = threadIdx.x;
+  if (t >= N || v >= vec_per_tok) return;
+  const int b = tok_img[t];
+  const int h = hw[2 * b], w = hw[2 * b + 1];
+  const int i = t - cu[b];
+  const int yy = i / w, xx = i - (i / w) * w;
+  const AxisTaps ay = axis_taps(yy, h, G);
+  const AxisTaps ax = axis_taps(xx, w, G);
+  float acc[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+  for (int a = ay.lo; a < ay.hi; ++a) {
+    const float wa = axis_w(ay, a);
+    for (int c = ax.lo; c < ax.hi; ++c) {
+      const float wgt = wa * axis_w(ax, c);
+      const float4* src = reinterpret_cast<const float4*>(table + (static_cast<size_t>(a) * G + c) * D + v * 8);
+      const float4 p0 = __ldg(src), p1 = __ldg(src + 1);
+      acc[0] = fmaf(wgt, p0.x, acc[0]);
+      acc[1] = fmaf(wgt, p0.y, acc[1]);
+      acc[2] = fmaf(wgt, p0.z, acc[2]);
+      acc[3] = fmaf(wgt, p0.w, acc[3]);
+      acc[4] = fmaf(wgt, p1.x, acc[4]);
+      acc[5] = fmaf(wgt, p1.y, acc[5]);
+      acc[6] = fmaf(wgt, p1.z, acc[6]);
+      acc[7] = fmaf(wgt, p1.w, acc[7]);
+    }
+  }
+  T* o = out + static_cast<size_t>(t) * D + v * 8;
+  if constexpr (sizeof(T) == 4) {
+    store_vec(o, acc);
+    store_vec(o + 4, acc + 4);
+  } else {
+    store_vec(o, acc);
+  }
+}
+
+// token -> image index from row starts (one thread per token, binary search)
+__global__ void token_image_kernel(const int* __restrict__ cu, int B, int N, int* __restrict__ tok_img) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= N) return;
+  int lo = 0, hi = B;  // find b with cu[b] <= t < cu[b+1]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (cu[mid] <= t) lo = mid; else hi = mid;
+  }
+  tok_img[t] = lo;
+}
+
+}  // namespace sg

@@ -1,0 +1,464 @@
+// C-ABI entry points of libsiglip2_b200.so (see include/siglip2_b200.h).
+// One translation unit: every kernel header is included here and compiled
+// for sm_100a only.
+#include <algorithm>
+#include <type_traits>
+#include <vector>
+
+#include "host_common.cuh"
+#include "gemm.cuh"
+#include "rowops.cuh"
+#include "fmha.cuh"
+#include "forward.cuh"
+
+using namespace sg;
+
+namespace {
+
+template <typename T, int BN, int EPI>
+int launch_gemm_tc(const void* a, int lda, const void* b, int ldb, const GemmParams& p, cudaStream_t stream) {
+  CUtensorMap ta, tb;
+  SG_TRY(make_tmap_2d(&ta, a, 2, p.M, p.K, lda, kGemmBM, kGemmBK));
+  SG_TRY(make_tmap_2d(&tb, b, 2, p.N, p.K, ldb, BN, kGemmBK));
+  constexpr bool kLN = (EPI == kEpiLn || EPI == kEpiLnGelu);
+  constexpr int threads = GemmThreads<kLN>::kThreads;
+  constexpr int smem = GemmCfg<BN>::kSmemBytes;
+  auto kern = gemm_tc_kernel<T, BN, EPI>;
+  static bool attr_done = false;  // per instantiation
+  if (!attr_done) {
+    SG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr_done = true;
+  }
+  const int tiles = ((p.M + kGemmBM - 1) / kGemmBM) * ((p.N + BN - 1) / BN);
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  kern<<<grid, threads, smem, stream>>>(ta, tb, p);
+  SG_LAUNCH_CHECK();
+  return SIGLIP2_OK;
+}
+
+template <typename T, int BN>
+int dispatch_epi(int epi, const void* a, int lda, const void* b, int ldb, const GemmParams& p, cudaStream_t s) {
+  switch (epi) {
+    case kEpiBias: return launch_gemm_tc<T, BN, kEpiBias>(a, lda, b, ldb, p, s);
+    case kEpiBiasRes: return launch_gemm_tc<T, BN, kEpiBiasRes>(a, lda, b, ldb, p, s);
+    case kEpiLn: return launch_gemm_tc<T, BN, kEpiLn>(a, lda, b, ldb, p, s);
+    case kEpiLnGelu: return launch_gemm_tc<T, BN, kEpiLnGelu>(a, lda, b, ldb, p, s);
+    case kEpiBiasGelu: return launch_gemm_tc<T, BN, kEpiBiasGelu>(a, lda, b, ldb, p, s);
+    default: return set_error(SIGLIP2_ERR_ARG, "unknown epilogue %d", epi);
+  }
+}
+
+// Tile width: 192 when it divides N exactly (1152, 768, 1536 ...), else 256.
+template <typename T>
+int dispatch_bn(int epi, const void* a, int lda, const void* b, int ldb, const GemmParams& p, cudaStream_t s) {
+  if (p.N % 192 == 0 && p.N % 256 != 0) return dispatch_epi<T, 192>(epi, a, lda, b, ldb, p, s);
+  return dispatch_epi<T, 256>(epi, a, lda, b, ldb, p, s);
+}
+
+}  // namespace
+
+int sg_gemm_impl(int dtype, int epi, const void* a, int lda, const void* b, int ldb, void* out, int ldo, int M, int N,
+                 int K, const float* bias, const void* res, int ldr, const float* c1, const float* c2, float eps,
+                 cudaStream_t stream) {
+  SG_CHECK_ARG(M >= 0 && N > 0 && K > 0, "bad GEMM shape M=%d N=%d K=%d", M, N, K);
+  if (M == 0) return SIGLIP2_OK;
+  SG_CHECK_ARG(a && b && out, "null operand");
+  SG_CHECK_ARG(epi >= 0 && epi <= 4, "unknown epilogue %d", epi);
+  const bool ln = (epi == kEpiLn || epi == kEpiLnGelu);
+  SG_CHECK_ARG(!ln || (c1 && c2), "LN epilogue needs c1 and c2");
+  SG_CHECK_ARG(ln || bias, "bias epilogue needs bias");
+  SG_CHECK_ARG(epi != kEpiBiasRes || res, "residual epilogue needs res");
+  SG_CHECK_ARG(!ln || K % kGemmBK == 0, "LN-folded GEMM needs K %% 64 == 0 (K=%d)", K);
+  if (dtype != SIGLIP2_BF16 && dtype != SIGLIP2_F16)
+    return set_error(SIGLIP2_ERR_UNSUPPORTED, "tensor-core GEMM supports bf16/f16 only (dtype=%d)", dtype);
+  if (N % 8 || K % 8 || lda % 8 || ldb % 8 || ldo % 8 || (epi == kEpiBiasRes && ldr % 8))
+    return set_error(SIGLIP2_ERR_ALIGN, "N, K and leading dimensions must be multiples of 8");
+  if (lda < K || ldb < K || ldo < N || (epi == kEpiBiasRes && ldr < N))
+    return set_error(SIGLIP2_ERR_SHAPE, "leading dimension smaller than the row");
+  if (!aligned16(out) || (res && !aligned16(res)))
+    return set_error(SIGLIP2_ERR_ALIGN, "output/residual must be 16-byte aligned");
+  GemmParams p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.out = out;
+  p.ldo = ldo;
+  p.bias = bias;
+  p.res = res;
+  p.ldr = ldr;
+  p.c1 = c1;
+  p.c2 = c2;
+  p.eps = eps;
+  if (dtype == SIGLIP2_BF16) return dispatch_bn<__nv_bfloat16>(epi, a, lda, b, ldb, p, stream);
+  return dispatch_bn<__half>(epi, a, lda, b, ldb, p, stream);
+}
+
+
+// ---------------------------------------------------------------------------
+// LayerNorm
+// ---------------------------------------------------------------------------
+template <typename T>
+int launch_layernorm(const void* x, void* y, const float* g, const float* b, int rows, int D, float eps, const int* cu,
+                     int P, cudaStream_t s) {
+  constexpr int V = Vec16<T>::N;
+  SG_CHECK_ARG(D % V == 0, "LayerNorm width %d must be a multiple of %d", D, V);
+  const int nvec = D / V;
+  const int threads = 256, rows_per_block = threads / 32;
+  const int grid = (rows + rows_per_block - 1) / rows_per_block;
+  if (rows == 0) return SIGLIP2_OK;
+  if (nvec <= 32 * 2)
+    layernorm_kernel<T, 2><<<grid, threads, 0, s>>>(static_cast<const T*>(x), static_cast<T*>(y), g, b, rows, D, eps, cu, P);
+  else if (nvec <= 32 * 4)
+    layernorm_kernel<T, 4><<<grid, threads, 0, s>>>(static_cast<const T*>(x), static_cast<T*>(y), g, b, rows, D, eps, cu, P);
+  else if (nvec <= 32 * 8)
+    layernorm_kernel<T, 8><<<grid, threads, 0, s>>>(static_cast<const T*>(x), static_cast<T*>(y), g, b, rows, D, eps, cu, P);
+  else if (nvec <= 32 * 12)
+    layernorm_kernel<T, 12><<<grid, threads, 0, s>>>(static_cast<const T*>(x), static_cast<T*>(y), g, b, rows, D, eps, cu, P);
+  else
+    return set_error(SIGLIP2_ERR_UNSUPPORTED, "LayerNorm width %d too large", D);
+  SG_LAUNCH_CHECK();
+  return SIGLIP2_OK;
+}
+
+int sg_layernorm_impl(int dtype, const void* x, void* y, const float* g, const float* b, int rows, int D, float eps,
+                      const int* cu, int P, cudaStream_t s) {
+  SG_CHECK_ARG(x && y && g && b && rows >= 0 && D > 0, "bad LayerNorm arguments");
+  SG_CHECK_ARG(cu == nullptr || P > 0, "padded LayerNorm needs P > 0");
+  if (!aligned16(x) || !aligned16(y)) return set_error(SIGLIP2_ERR_ALIGN, "LayerNorm tensors must be 16-byte aligned");
+  switch (dtype) {
+    case SIGLIP2_BF16: return launch_layernorm<__nv_bfloat16>(x, y, g, b, rows, D, eps, cu, P, s);
+    case SIGLIP2_F16: return launch_layernorm<__half>(x, y, g, b, rows, D, eps, cu, P, s);
+    case SIGLIP2_F32: return launch_layernorm<float>(x, y, g, b, rows, D, eps, cu, P, s);
+    default: return set_error(SIGLIP2_ERR_ARG, "unknown dtype %d", dtype);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// position-embedding resize into packed token order
+// ---------------------------------------------------------------------------
+int sg_posemb_impl(int dtype, const float* table, int G, int D, const int* tok_img, const int* hw, const int* cu, int N,
+                   void* out, cudaStream_t s) {
+  SG_CHECK_ARG(table && tok_img && hw && cu && out && G > 0 && D > 0 && N >= 0, "bad posemb arguments");
+  SG_CHECK_ARG(D % 8 == 0 && D / 8 <= 1024, "posemb width %d must be a multiple of 8 and <= 8192", D);
+  if (N == 0) return SIGLIP2_OK;
+  const int vpt = D / 8;
+  const int tpb = vpt >= 256 ? 1 : 256 / vpt;
+  dim3 block(vpt, tpb), grid((N + tpb - 1) / tpb);
+  switch (dtype) {
+    case SIGLIP2_BF16: posemb_kernel<__nv_bfloat16><<<grid, block, 0, s>>>(table, G, D, tok_img, hw, cu, N, static_cast<__nv_bfloat16*>(out)); break;
+    case SIGLIP2_F16: posemb_kernel<__half><<<grid, block, 0, s>>>(table, G, D, tok_img, hw, cu, N, static_cast<__half*>(out)); break;
+    case SIGLIP2_F32: posemb_kernel<float><<<grid, block, 0, s>>>(table, G, D, tok_img, hw, cu, N, static_cast<float*>(out)); break;
+    default: return set_error(SIGLIP2_ERR_ARG, "unknown dtype %d", dtype);
+  }
+  SG_LAUNCH_CHECK();
+  return SIGLIP2_OK;
+}
+
+int sg_token_image_impl(const int* cu, int B, int N, int* tok_img, cudaStream_t s) {
+  if (N == 0) return SIGLIP2_OK;
+  token_image_kernel<<<(N + 255) / 256, 256, 0, s>>>(cu, B, N, tok_img);
+  SG_LAUNCH_CHECK();
+  return SIGLIP2_OK;
+}
+
+// ---------------------------------------------------------------------------
+// varlen attention
+// ---------------------------------------------------------------------------
+template <typename T, int HDP>
+int launch_fmha(const void* qkv, int N, const int* cu, const int2* tiles, int n_tiles, int H, int hd, void* out, int ldo,
+                cudaStream_t s) {
+  CUtensorMap ta, tr;
+  const int ldq = 3 * H * HDP;
+  SG_TRY(make_tmap_2d(&ta, qkv, 2, N, ldq, ldq, 128, 64));
+  if (HDP > 64) SG_TRY(make_tmap_2d(&tr, qkv, 2, N, ldq, ldq, 128, HDP - 64));
+  else tr = ta;
+  FmhaParams p;
+  p.cu = cu;
+  p.tiles = tiles;
+  p.heads = H;
+  p.head_dim = hd;
+  p.out = out;
+  p.ld_out = ldo;
+  p.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(hd));
+  auto kern = fmha_varlen_kernel<T, HDP>;
+  constexpr int smem = FmhaCfg<HDP>::kSmem;
+  static bool attr_done = false;
+  if (!attr_done) {
+    SG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr_done = true;
+  }
+  dim3 grid(n_tiles, H);
+  kern<<<grid, 192, smem, s>>>(ta, tr, p);
+  SG_LAUNCH_CHECK();
+  return SIGLIP2_OK;
+}
+
+template <typename T>
+int dispatch_fmha(const void* qkv, int N, const int* cu, const int2* tiles, int n_tiles, int H, int hd, void* out,
+                  int ldo, cudaStream_t s) {
+  switch (hd) {
+    case 64: return launch_fmha<T, 64>(qkv, N, cu, tiles, n_tiles, H, hd, out, ldo, s);
+    case 72: return launch_fmha<T, 80>(qkv, N, cu, tiles, n_tiles, H, hd, out, ldo, s);
+    case 80: return launch_fmha<T, 80>(qkv, N, cu, tiles, n_tiles, H, hd, out, ldo, s);
+    case 96: return launch_fmha<T, 96>(qkv, N, cu, tiles, n_tiles, H, hd, out, ldo, s);
+    default: return set_error(SIGLIP2_ERR_UNSUPPORTED, "head_dim %d not supported (64, 72, 80, 96)", hd);
+  }
+}
+
+
+int sg_fmha_impl(int dtype, const void* qkv, int N, const int* cu, const int* tiles, int n_tiles, int H, int hd,
+                 void* out, int ldo, cudaStream_t s) {
+  SG_CHECK_ARG(qkv && cu && tiles && out && N >= 0 && n_tiles >= 0 && H > 0 && hd > 0, "bad attention arguments");
+  SG_CHECK_ARG(hd % 8 == 0 && ldo % 8 == 0 && ldo >= H * hd, "head_dim and ldo must be multiples of 8");
+  if (N == 0 || n_tiles == 0) return SIGLIP2_OK;
+  if (H > 65535) return set_error(SIGLIP2_ERR_UNSUPPORTED, "too many heads");
+  if (!aligned16(out)) return set_error(SIGLIP2_ERR_ALIGN, "attention output must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(tiles) & 7u)
+    return set_error(SIGLIP2_ERR_ALIGN, "attention tile list must be 8-byte aligned (read as int32 pairs)");
+  const int2* t2 = reinterpret_cast<const int2*>(tiles);
+  if (dtype == SIGLIP2_BF16) return dispatch_fmha<__nv_bfloat16>(qkv, N, cu, t2, n_tiles, H, hd, out, ldo, s);
+  if (dtype == SIGLIP2_F16) return dispatch_fmha<__half>(qkv, N, cu, t2, n_tiles, H, hd, out, ldo, s);
+  return set_error(SIGLIP2_ERR_UNSUPPORTED, "tensor-core attention supports bf16/f16 only");
+}
+
+// ---------------------------------------------------------------------------
+// head + forward
+// ---------------------------------------------------------------------------
+int sg_head_pool_impl(int dtype, const void* x, int D, int H, const int* cu, int B, int pad_P, const float* u,
+                      float* scores, void* pooled, cudaStream_t s) {
+  SG_CHECK_ARG(H % 4 == 0 && H <= 16 && D % 8 == 0, "head pooling needs H %% 4 == 0, H <= 16, D %% 8 == 0");
+  const int threads = (D / 8) * (H / 4);
+  SG_CHECK_ARG(threads <= 1024, "head pooling: D=%d H=%d needs too many threads", D, H);
+  const int smem = (H * D + 2 * H) * 4;
+  int nt = threads < 128 ? 128 : (threads + 31) / 32 * 32;
+  switch (dtype) {
+    case SIGLIP2_BF16: {
+      auto k = head_pool_kernel<__nv_bfloat16>;
+      SG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      k<<<B, nt, smem, s>>>(static_cast<const __nv_bfloat16*>(x), D, H, cu, pad_P, u, scores, static_cast<__nv_bfloat16*>(pooled));
+      break;
+    }
+    case SIGLIP2_F16: {
+      auto k = head_pool_kernel<__half>;
+      SG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      k<<<B, nt, smem, s>>>(static_cast<const __half*>(x), D, H, cu, pad_P, u, scores, static_cast<__half*>(pooled));
+      break;
+    }
+    case SIGLIP2_F32: {
+      auto k = head_pool_kernel<float>;
+      SG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      k<<<B, nt, smem, s>>>(static_cast<const float*>(x), D, H, cu, pad_P, u, scores, static_cast<float*>(pooled));
+      break;
+    }
+    default: return set_error(SIGLIP2_ERR_ARG, "unknown dtype %d", dtype);
+  }
+  SG_LAUNCH_CHECK();
+  return SIGLIP2_OK;
+}
+
+template <typename T>
+int launch_select(const void* Y, int H, int hd, int D, int B, void* out, cudaStream_t s) {
+  const int n = B * (D / 8);
+  head_select_kernel<T><<<(n + 255) / 256, 256, 0, s>>>(static_cast<const T*>(Y), H, hd, D, B, static_cast<T*>(out));
+  SG_LAUNCH_CHECK();
+  return SIGLIP2_OK;
+}
+
+template <typename T>
+int launch_gather(const void* padded, int C, int P, const int* cu, const int* tok, int N, void* packed, cudaStream_t s) {
+  const size_t n = static_cast<size_t>(N) * (C / (16 / sizeof(T)));
+  if (n == 0) return SIGLIP2_OK;
+  gather_rows_kernel<T><<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(static_cast<const T*>(padded), C, P, cu, tok, N,
+                                                                       static_cast<T*>(packed));
+  SG_LAUNCH_CHECK();
+  return SIGLIP2_OK;
+}
+
+int validate_config(const siglip2_config* c) {
+  SG_CHECK_ARG(c != nullptr, "null config");
+  SG_CHECK_ARG(c->hidden > 0 && c->intermediate > 0 && c->layers >= 0 && c->heads > 0 && c->patch_dim > 0 &&
+                   c->pos_grid > 0,
+               "non-positive config field");
+  SG_CHECK_ARG(c->head_dim * c->heads == c->hidden, "head_dim * heads != hidden");
+  if (c->dtype != SIGLIP2_BF16 && c->dtype != SIGLIP2_F16)
+    return set_error(SIGLIP2_ERR_UNSUPPORTED, "forward supports bf16/f16 on the tensor-core path (dtype %d)", c->dtype);
+  if (c->hidden % 64 || c->intermediate % 8 || c->patch_dim % 8)
+    return set_error(SIGLIP2_ERR_UNSUPPORTED, "hidden must be a multiple of 64, intermediate/patch_dim of 8");
+  if (c->head_dim != 64 && c->head_dim != 72 && c->head_dim != 80 && c->head_dim != 96)
+    return set_error(SIGLIP2_ERR_UNSUPPORTED, "head_dim %d not supported (64, 72, 80, 96)", c->head_dim);
+  return SIGLIP2_OK;
+}
+
+int sg_forward_impl(const siglip2_config* c, const siglip2_weights* w, const void* patches, int B, int P,
+                    const int32_t* hw_host, const int32_t* meta, void* last_hidden, void* pooled, void* ws,
+                    size_t ws_bytes, cudaStream_t s) {
+  SG_TRY(validate_config(c));
+  SG_CHECK_ARG(w && patches && hw_host && meta && last_hidden && ws && B > 0 && P >= 0, "null forward argument");
+  SG_CHECK_ARG(!pooled || c->has_head, "pooled output requested but the model has no head");
+  int N = 0, T = 0;
+  SG_TRY(meta_counts(hw_host, B, &N, &T));
+  for (int b = 0; b < B && P > 0; ++b)
+    if (hw_host[2 * b] * hw_host[2 * b + 1] > P)
+      return set_error(SIGLIP2_ERR_SHAPE, "image %d: h*w = %d exceeds max_patches %d", b,
+                       hw_host[2 * b] * hw_host[2 * b + 1], P);
+  const size_t need = forward_workspace(c, B, N, nullptr, nullptr);
+  if (ws_bytes < need) return set_error(SIGLIP2_ERR_ARG, "workspace too small: %zu < %zu bytes", ws_bytes, need);
+  if (!aligned16(patches) || !aligned16(last_hidden) || (pooled && !aligned16(pooled)) || !aligned16(ws) ||
+      (reinterpret_cast<uintptr_t>(meta) & 7u))
+    return set_error(SIGLIP2_ERR_ALIGN, "forward buffers must be 16-byte aligned");
+  FwdBuffers f;
+  forward_workspace(c, B, N, &f, static_cast<uint8_t*>(ws));
+  const int* cu = meta;
+  const int* hw = meta + B + 1;
+  const int* tiles = meta + meta_tiles_offset(B);
+  const int dt = c->dtype;
+  const int D = c->hidden, I = c->intermediate, H = c->heads, hd = c->head_dim;
+  const int hdp = padded_head_dim(hd);
+  const int nqkv = 3 * H * hdp;
+
+  // embeddings: x = pos(hw) ; x = patches Wp^T + bp + x
+  SG_TRY(sg_token_image_impl(cu, B, N, f.tok_img, s));
+  SG_TRY(sg_posemb_impl(dt, w->pos_table, c->pos_grid, D, f.tok_img, hw, cu, N, f.x, s));
+  const void* prow = patches;
+  if (P > 0) {
+    if (dt == SIGLIP2_BF16) SG_TRY(launch_gather<__nv_bfloat16>(patches, c->patch_dim, P, cu, f.tok_img, N, f.hmid, s));
+    else SG_TRY(launch_gather<__half>(patches, c->patch_dim, P, cu, f.tok_img, N, f.hmid, s));
+    prow = f.hmid;
+  }
+  SG_TRY(sg_gemm_impl(dt, kEpiBiasRes, prow, c->patch_dim, w->patch_w, c->patch_dim, f.x, D, N, D, c->patch_dim,
+                      w->patch_b, f.x, D, nullptr, nullptr, 0.f, s));
+  for (int l = 0; l < c->layers; ++l) {
+    const siglip2_layer_weights& lw = w->layers[l];
+    SG_TRY(sg_gemm_impl(dt, kEpiLn, f.x, D, lw.qkv_w, D, f.qkv, nqkv, N, nqkv, D, nullptr, nullptr, 0, lw.qkv_c1,
+                        lw.qkv_c2, c->eps, s));
+    SG_TRY(sg_fmha_impl(dt, f.qkv, N, cu, tiles, T, H, hd, f.attn, D, s));
+    SG_TRY(sg_gemm_impl(dt, kEpiBiasRes, f.attn, D, lw.out_w, D, f.x, D, N, D, D, lw.out_b, f.x, D, nullptr, nullptr,
+                        0.f, s));
+    SG_TRY(sg_gemm_impl(dt, kEpiLnGelu, f.x, D, lw.fc1_w, D, f.hmid, I, N, I, D, nullptr, nullptr, 0, lw.fc1_c1,
+                        lw.fc1_c2, c->eps, s));
+    SG_TRY(sg_gemm_impl(dt, kEpiBiasRes, f.hmid, I, lw.fc2_w, I, f.x, D, N, D, I, lw.fc2_b, f.x, D, nullptr, nullptr,
+                        0.f, s));
+  }
+  // post-LayerNorm -> last_hidden_state (packed or padded with zero rows)
+  SG_TRY(sg_layernorm_impl(dt, f.x, last_hidden, w->post_ln_w, w->post_ln_b, P > 0 ? B * P : N, D, c->eps,
+                           P > 0 ? cu : nullptr, P, s));
+  if (pooled) {
+    SG_TRY(sg_head_pool_impl(dt, last_hidden, D, H, cu, B, P, w->head_u, f.scores, f.hpool, s));
+    SG_TRY(sg_gemm_impl(dt, kEpiBias, f.hpool, D, w->head_v_w, D, f.hY, D, B * H, D, D, w->head_v_b, nullptr, 0,
+                        nullptr, nullptr, 0.f, s));
+    if (dt == SIGLIP2_BF16) SG_TRY(launch_select<__nv_bfloat16>(f.hY, H, hd, D, B, f.hattn, s));
+    else SG_TRY(launch_select<__half>(f.hY, H, hd, D, B, f.hattn, s));
+    SG_TRY(sg_gemm_impl(dt, kEpiBias, f.hattn, D, w->head_o_w, D, f.ha, D, B, D, D, w->head_o_b, nullptr, 0, nullptr,
+                        nullptr, 0.f, s));
+    SG_TRY(sg_gemm_impl(dt, kEpiLnGelu, f.ha, D, w->head_fc1_w, D, f.hmid2, I, B, I, D, nullptr, nullptr, 0,
+                        w->head_fc1_c1, w->head_fc1_c2, c->eps, s));
+    SG_TRY(sg_gemm_impl(dt, kEpiBiasRes, f.hmid2, I, w->head_fc2_w, I, pooled, D, B, D, I, w->head_fc2_b, f.ha, D,
+                        nullptr, nullptr, 0.f, s));
+  }
+  return SIGLIP2_OK;
+}
+
+extern "C" {
+
+int siglip2_version(void) { return 100; }
+
+const char* siglip2_last_error(void) { return t_last_error; }
+
+int siglip2_check_device(int reset) {
+  SG_CUDA(cudaDeviceSynchronize());
+  int flag = 0;
+  SG_CUDA(cudaMemcpyFromSymbol(&flag, g_device_error, sizeof(int)));
+  if (reset && flag) {
+    const int zero = 0;
+    SG_CUDA(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)));
+  }
+  if (flag) return set_error(SIGLIP2_ERR_TIMEOUT, "a kernel gave up on a bounded wait (site %d)", flag);
+  return SIGLIP2_OK;
+}
+
+int siglip2_gemm(int dtype, int epilogue, const void* a_dev, int lda, const void* b_dev, int ldb, void* out_dev,
+                 int ldo, int M, int N, int K, const float* bias_dev, const void* res_dev, int ldr,
+                 const float* c1_dev, const float* c2_dev, float eps, void* stream) {
+  return sg_gemm_impl(dtype, epilogue, a_dev, lda, b_dev, ldb, out_dev, ldo, M, N, K, bias_dev, res_dev, ldr, c1_dev,
+                      c2_dev, eps, static_cast<cudaStream_t>(stream));
+}
+
+int siglip2_layernorm(int dtype, const void* x_dev, void* y_dev, const float* gamma_dev, const float* beta_dev,
+                      int rows, int D, float eps, const int* cu_seqlens_dev, int max_patches, void* stream) {
+  return sg_layernorm_impl(dtype, x_dev, y_dev, gamma_dev, beta_dev, rows, D, eps, cu_seqlens_dev, max_patches,
+                           static_cast<cudaStream_t>(stream));
+}
+
+int siglip2_token_image(const int* cu_seqlens_dev, int B, int N, int* tok_img_dev, void* stream) {
+  SG_CHECK_ARG(cu_seqlens_dev && tok_img_dev && B > 0 && N >= 0, "bad token_image arguments");
+  return sg_token_image_impl(cu_seqlens_dev, B, N, tok_img_dev, static_cast<cudaStream_t>(stream));
+}
+
+int siglip2_posemb(int dtype, const float* table_dev, int grid, int D, const int* tok_img_dev, const int* hw_dev,
+                   const int* cu_seqlens_dev, int N, void* out_dev, void* stream) {
+  return sg_posemb_impl(dtype, table_dev, grid, D, tok_img_dev, hw_dev, cu_seqlens_dev, N, out_dev,
+                        static_cast<cudaStream_t>(stream));
+}
+
+int siglip2_fmha_varlen(int dtype, const void* qkv_dev, int N, const int* cu_seqlens_dev, const int* tiles_dev,
+                        int n_tiles, int heads, int head_dim, void* out_dev, int ldo, void* stream) {
+  return sg_fmha_impl(dtype, qkv_dev, N, cu_seqlens_dev, tiles_dev, n_tiles, heads, head_dim, out_dev, ldo,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int siglip2_padded_head_dim(int head_dim) { return padded_head_dim(head_dim); }
+
+int siglip2_metadata_size(const int32_t* hw_host, int batch, int* n_tokens, int* n_tiles) {
+  SG_CHECK_ARG(hw_host && batch > 0, "bad metadata arguments");
+  int N = 0, T = 0;
+  SG_TRY(meta_counts(hw_host, batch, &N, &T));
+  if (n_tokens) *n_tokens = N;
+  if (n_tiles) *n_tiles = T;
+  return static_cast<int>(meta_entries(batch, T));
+}
+
+int siglip2_metadata(const int32_t* hw_host, int batch, int32_t* meta_host, size_t capacity) {
+  SG_CHECK_ARG(hw_host && meta_host && batch > 0, "bad metadata arguments");
+  int N = 0, T = 0;
+  SG_TRY(meta_counts(hw_host, batch, &N, &T));
+  const size_t need = meta_entries(batch, T);
+  SG_CHECK_ARG(capacity >= need, "metadata capacity %zu < %zu", capacity, need);
+  for (size_t i = 0; i < need; ++i) meta_host[i] = 0;
+  int32_t* cu = meta_host;
+  int32_t* hw = meta_host + batch + 1;
+  int32_t* tiles = meta_host + meta_tiles_offset(batch);
+  cu[0] = 0;
+  for (int b = 0; b < batch; ++b) {
+    cu[b + 1] = cu[b] + hw_host[2 * b] * hw_host[2 * b + 1];
+    hw[2 * b] = hw_host[2 * b];
+    hw[2 * b + 1] = hw_host[2 * b + 1];
+  }
+  // attention tiles, longest images first (their CTAs start first: shorter tail)
+  std::vector<int> order(batch);
+  for (int b = 0; b < batch; ++b) order[b] = b;
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return cu[a + 1] - cu[a] > cu[b + 1] - cu[b]; });
+  int k = 0;
+  for (int b : order) {
+    const int nq = (cu[b + 1] - cu[b] + 127) / 128;
+    for (int q = 0; q < nq; ++q) {
+      tiles[2 * k] = b;
+      tiles[2 * k + 1] = q;
+      ++k;
+    }
+  }
+  return SIGLIP2_OK;
+}
+
+size_t siglip2_workspace_size(const siglip2_config* cfg, int batch, int n_tokens) {
+  if (!cfg || batch <= 0 || n_tokens < 0) return 0;
+  return forward_workspace(cfg, batch, n_tokens, nullptr, nullptr);
+}
+
+int siglip2_forward(const siglip2_config* cfg, const siglip2_weights* w, const void* patches_dev, int batch,
+                    int max_patches, const int32_t* hw_host, const int32_t* meta_dev, void* last_hidden_dev,
+                    void* pooled_dev, void* workspace_dev, size_t workspace_bytes, void* stream) {
+  return sg_forward_impl(cfg, w, patches_dev, batch, max_patches, hw_host, meta_dev, last_hidden_dev, pooled_dev,
+                         workspace_dev, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

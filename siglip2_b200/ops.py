@@ -1,0 +1,115 @@
+"""Torch-facing wrappers over the C ABI (device pointers + current stream).
+
+Each wrapper validates dtype/device/contiguity, allocates outputs with the
+caching allocator and calls the library; nothing here computes on the CPU.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib as L
+
+_DT = {torch.float32: L.DTYPE_F32, torch.bfloat16: L.DTYPE_BF16, torch.float16: L.DTYPE_F16}
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DT[dt]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {dt}") from None
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("siglip2_b200 kernels take CUDA tensors only")
+
+
+def gemm(a: torch.Tensor, w: torch.Tensor, epilogue: int, bias=None, res=None, c1=None, c2=None,
+         eps: float = 1e-6, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``out = epilogue(a @ w.T)`` on the tensor cores (``siglip2_gemm``)."""
+    _need_cuda(a, w, bias, res, c1, c2, out)
+    assert a.dim() == 2 and w.dim() == 2 and a.shape[1] == w.shape[1]
+    assert a.stride(1) == 1 and w.stride(1) == 1
+    M, K = a.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=a.dtype, device=a.device)
+    L.call("siglip2_gemm", dtype_code(a.dtype), epilogue, a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0),
+           out.data_ptr(), out.stride(0), M, N, K, _ptr(bias), _ptr(res), res.stride(0) if res is not None else 0,
+           _ptr(c1), _ptr(c2), float(eps), _stream(a.device))
+    return out
+
+
+def fold_layernorm(w: torch.Tensor, b: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, dtype):
+    """LayerNorm(gamma, beta) followed by Linear(w, b) as a GEMM on the raw
+    input: returns ``(w*gamma in dtype, c1, c2)`` with ``c1 = rowsum(w*gamma)``
+    (of the rounded matrix) and ``c2 = b + w @ beta`` (fp32)."""
+    wf = w.float()
+    wg = (wf * gamma.float()[None, :]).to(dtype)
+    c1 = wg.float().sum(1)
+    c2 = (b.float() if b is not None else torch.zeros(w.shape[0], device=w.device)) + wf @ beta.float()
+    return wg.contiguous(), c1.contiguous(), c2.contiguous()
+
+
+def layernorm(x: torch.Tensor, gamma, beta, eps: float, cu_seqlens=None, batch: int = 0, max_patches: int = 0):
+    """Packed ``LN(x)`` or, with ``cu_seqlens``, the padded ``[B*P, D]`` scatter."""
+    _need_cuda(x, gamma, beta)
+    D = x.shape[-1]
+    if cu_seqlens is None:
+        rows = x.numel() // D
+        y = torch.empty_like(x)
+    else:
+        rows = batch * max_patches
+        y = torch.empty((batch, max_patches, D), dtype=x.dtype, device=x.device)
+    L.call("siglip2_layernorm", dtype_code(x.dtype), x.data_ptr(), y.data_ptr(), gamma.data_ptr(), beta.data_ptr(),
+           rows, D, float(eps), _ptr(cu_seqlens), max_patches, _stream(x.device))
+    return y
+
+
+def token_image(cu_seqlens: torch.Tensor, n_tokens: int) -> torch.Tensor:
+    out = torch.empty(n_tokens, dtype=torch.int32, device=cu_seqlens.device)
+    L.call("siglip2_token_image", cu_seqlens.data_ptr(), cu_seqlens.numel() - 1, n_tokens, out.data_ptr(),
+           _stream(cu_seqlens.device))
+    return out
+
+
+def posemb(table_f32: torch.Tensor, hw: torch.Tensor, cu_seqlens: torch.Tensor, tok_img: torch.Tensor, n_tokens: int,
+           dtype) -> torch.Tensor:
+    G = int(round(table_f32.shape[0] ** 0.5))
+    D = table_f32.shape[1]
+    out = torch.empty((n_tokens, D), dtype=dtype, device=table_f32.device)
+    L.call("siglip2_posemb", dtype_code(dtype), table_f32.data_ptr(), G, D, tok_img.data_ptr(), hw.data_ptr(),
+           cu_seqlens.data_ptr(), n_tokens, out.data_ptr(), _stream(table_f32.device))
+    return out
+
+
+def padded_head_dim(head_dim: int) -> int:
+    return int(L.load().siglip2_padded_head_dim(head_dim))
+
+
+def attention_tiles(lens) -> torch.Tensor:
+    """(image, query-tile) int32 pairs for every 128-row query tile, longest
+    images first (better tail behaviour)."""
+    order = sorted(range(len(lens)), key=lambda b: -int(lens[b]))
+    t = [(b, q) for b in order for q in range((int(lens[b]) + 127) // 128)]
+    return torch.tensor(t, dtype=torch.int32).reshape(-1, 2)
+
+
+def fmha_varlen(qkv: torch.Tensor, cu_seqlens: torch.Tensor, tiles: torch.Tensor, heads: int, head_dim: int,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    _need_cuda(qkv, cu_seqlens, tiles)
+    N = qkv.shape[0]
+    if out is None:
+        out = torch.empty((N, heads * head_dim), dtype=qkv.dtype, device=qkv.device)
+    L.call("siglip2_fmha_varlen", dtype_code(qkv.dtype), qkv.data_ptr(), N, cu_seqlens.data_ptr(), tiles.data_ptr(),
+           tiles.shape[0], heads, head_dim, out.data_ptr(), out.stride(0), _stream(qkv.device))
+    return out

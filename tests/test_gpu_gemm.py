@@ -1,0 +1,86 @@
+"""tcgen05 GEMM entry point (``siglip2_gemm``) against torch fp32 math on the
+same bf16/f16 inputs, for every fused epilogue and the ragged shapes of the
+tower (N=4304, K=4304, M not a multiple of 128)."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+from siglip2_b200 import _lib as L  # noqa: E402
+from siglip2_b200 import ops  # noqa: E402
+
+
+def _gelu(x):
+    return F.gelu(x, approximate="tanh")
+
+
+def _close(out, ref, tol=1.5e-2):
+    out = out.float()
+    scale = ref.abs().max().item() + 1e-6
+    err = (out - ref).abs().max().item()
+    cos = F.cosine_similarity(out.flatten(), ref.flatten(), dim=0).item()
+    assert err / scale < tol and cos > 0.9999, (err, scale, cos)
+
+
+SHAPES = [(300, 1152, 1152), (1000, 4304, 1152), (777, 1152, 4304), (128, 256, 64), (4097, 3840, 1152),
+          (64, 768, 768), (1, 2304, 768)]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M,N,K", SHAPES)
+@pytest.mark.parametrize("epi", [L.EPI_BIAS, L.EPI_BIAS_RES, L.EPI_BIAS_GELU])
+def test_gemm_bias_epilogues(dtype, M, N, K, epi):
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N)
+    a = torch.randn(M, K, device="cuda", generator=g).to(dtype)
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.03).to(dtype)
+    bias = torch.randn(N, device="cuda", generator=g) * 0.1
+    res = torch.randn(M, N, device="cuda", generator=g).to(dtype) if epi == L.EPI_BIAS_RES else None
+    out = ops.gemm(a, w, epi, bias=bias, res=res)
+    ref = a.float() @ w.float().T + bias
+    if epi == L.EPI_BIAS_RES:
+        ref = ref + res.float()
+    if epi == L.EPI_BIAS_GELU:
+        ref = _gelu(ref)
+    torch.cuda.synchronize()
+    _close(out, ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M,N,K", [(300, 3840, 1152), (1000, 4304, 1152), (513, 2304, 768), (200, 1536, 1536)])
+@pytest.mark.parametrize("gelu", [False, True])
+def test_gemm_layernorm_folded(dtype, M, N, K, gelu):
+    g = torch.Generator(device="cuda").manual_seed(N + K)
+    # residual-stream-like rows: non-zero mean, varied scale
+    x = (torch.randn(M, K, device="cuda", generator=g) * (1 + 3 * torch.rand(M, 1, device="cuda", generator=g))
+         + torch.randn(M, 1, device="cuda", generator=g) * 2).to(dtype)
+    w = torch.randn(N, K, device="cuda", generator=g) * 0.03
+    b = torch.randn(N, device="cuda", generator=g) * 0.1
+    gamma = 1 + 0.2 * torch.randn(K, device="cuda", generator=g)
+    beta = 0.1 * torch.randn(K, device="cuda", generator=g)
+    wg, c1, c2 = ops.fold_layernorm(w, b, gamma, beta, dtype)
+    out = ops.gemm(x, wg, L.EPI_LN_GELU if gelu else L.EPI_LN, c1=c1, c2=c2, eps=1e-6)
+    ref = F.layer_norm(x.float(), (K,), gamma, beta, 1e-6) @ w.T + b
+    if gelu:
+        ref = _gelu(ref)
+    torch.cuda.synchronize()
+    _close(out, ref, tol=2e-2)
+
+
+def test_gemm_inplace_residual():
+    a = torch.randn(333, 1152, device="cuda").bfloat16()
+    w = (torch.randn(1152, 1152, device="cuda") * 0.03).bfloat16()
+    bias = torch.randn(1152, device="cuda") * 0.1
+    x = torch.randn(333, 1152, device="cuda").bfloat16()
+    ref = a.float() @ w.float().T + bias + x.float()
+    ops.gemm(a, w, L.EPI_BIAS_RES, bias=bias, res=x, out=x)
+    torch.cuda.synchronize()
+    _close(x, ref)
+
+
+def test_gemm_rejects_bad_args():
+    a = torch.randn(16, 100, device="cuda").bfloat16()  # K=100 is not a multiple of 8
+    w = torch.randn(64, 100, device="cuda").bfloat16()
+    with pytest.raises(L.Siglip2Error):
+        ops.gemm(a, w, L.EPI_BIAS, bias=torch.zeros(64, device="cuda"))
+    L.check(L.load().siglip2_check_device(1))

@@ -1,0 +1,100 @@
+"""Varlen attention, LayerNorm and position-embedding kernels against torch
+fp32 math on the same inputs (GPU)."""
+import math
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+from oracle import siglip2_oracle as O  # noqa: E402
+from siglip2_b200 import ops  # noqa: E402
+
+
+def _cu(lens):
+    return torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32, device="cuda")
+
+
+def _pack_qkv(q, k, v, H, hd, hdp):
+    N = q.shape[0]
+    buf = torch.zeros(N, 3, H, hdp, dtype=q.dtype, device=q.device)
+    for w, t in enumerate((q, k, v)):
+        buf[:, w, :, :hd] = t.view(N, H, hd)
+    return buf.view(N, 3 * H * hdp)
+
+
+def _ref_attn(q, k, v, lens, H, hd):
+    out = torch.empty_like(q, dtype=torch.float32)
+    s = 0
+    for L in lens:
+        sl = slice(s, s + L)
+        qh = q[sl].float().view(L, H, hd).transpose(0, 1)
+        kh = k[sl].float().view(L, H, hd).transpose(0, 1)
+        vh = v[sl].float().view(L, H, hd).transpose(0, 1)
+        p = torch.softmax(qh @ kh.transpose(1, 2) / math.sqrt(hd), -1)
+        out[sl] = (p @ vh).transpose(0, 1).reshape(L, H * hd)
+        s += L
+    return out
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("H,hd", [(16, 72), (12, 64), (16, 96), (2, 72)])
+@pytest.mark.parametrize("lens", [[1, 7, 129, 300, 1024, 128, 256, 65], [576], [900, 3, 1000]])
+def test_fmha_varlen(dtype, H, hd, lens):
+    g = torch.Generator(device="cuda").manual_seed(sum(lens) + hd)
+    N = sum(lens)
+    q, k, v = (torch.randn(N, H * hd, device="cuda", generator=g).to(dtype) for _ in range(3))
+    hdp = ops.padded_head_dim(hd)
+    qkv = _pack_qkv(q, k, v, H, hd, hdp)
+    cu = _cu(lens)
+    tiles = ops.attention_tiles(lens).cuda()
+    out = ops.fmha_varlen(qkv, cu, tiles, H, hd)
+    ref = _ref_attn(q, k, v, lens, H, hd)
+    torch.cuda.synchronize()
+    err = (out.float() - ref).abs().max().item()
+    assert err < 2e-2, err
+    cos = F.cosine_similarity(out.float().flatten(), ref.flatten(), dim=0).item()
+    assert cos > 0.9999
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("D", [768, 1152, 1536, 1024])
+def test_layernorm_packed_and_padded(dtype, D):
+    lens = [5, 300, 17, 256]
+    N, P = sum(lens), 320
+    x = (torch.randn(N, D, device="cuda") * 3 + 1).to(dtype)
+    gamma = 1 + 0.1 * torch.randn(D, device="cuda")
+    beta = 0.1 * torch.randn(D, device="cuda")
+    ref = F.layer_norm(x.float(), (D,), gamma, beta, 1e-6)
+    y = ops.layernorm(x, gamma, beta, 1e-6)
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    assert (y.float() - ref).abs().max().item() < tol
+    yp = ops.layernorm(x, gamma, beta, 1e-6, cu_seqlens=_cu(lens), batch=len(lens), max_patches=P)
+    s = 0
+    for b, L in enumerate(lens):
+        assert (yp[b, :L].float() - ref[s:s + L]).abs().max().item() < tol
+        assert not yp[b, L:].any()
+        s += L
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_posemb_matches_interpolate(dtype):
+    D = 1152
+    table = torch.randn(256, D, device="cuda") * 0.02
+    grids = [(18, 18), (24, 31), (11, 37), (8, 128), (1, 1), (3, 5), (16, 16), (40, 25)]
+    lens = [h * w for h, w in grids]
+    N = sum(lens)
+    cu = _cu(lens)
+    hw = torch.tensor(grids, dtype=torch.int32, device="cuda").flatten()
+    tok = ops.token_image(cu, N)
+    out = ops.posemb(table, hw, cu, tok, N, dtype)
+    grid = table.view(16, 16, D).permute(2, 0, 1)[None]
+    refs = [F.interpolate(grid, size=(h, w), mode="bilinear", align_corners=False, antialias=True)[0]
+            .reshape(D, h * w).T for h, w in grids]
+    ref = torch.cat(refs, 0)
+    torch.cuda.synchronize()
+    tol = 1e-6 if dtype == torch.float32 else 2e-3
+    assert (out.float() - ref).abs().max().item() < tol
+    assert (tok.cpu().numpy() == np.repeat(np.arange(len(lens)), lens)).all()
