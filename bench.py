@@ -1,0 +1,359 @@
+"""Throughput of the SigLIP-2 NaFlex vision-tower forward on B200.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl ours|reference] [--workload cfg2]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one process per GPU)
+
+Workload (default): So400m/16 NaFlex tower, bf16, 64 images per GPU at
+max_patches 1024 with seeded (h, w) (area U[256, 1024], aspect log-U[1/4, 4]),
+pixels U[-1, 1], random-init weights (trunc-normal std 0.02), MAP head.  A step
+is one forward of the 64 images through the HF-style public API
+``model(pixel_values, attention_mask, spatial_shapes)`` followed (N > 1) by the
+NCCL all-gather of the pooled embeddings.
+
+``value``: images/s over all ranks with inputs already in HBM.  ``e2e``: the
+same with pixel_values in pinned host memory (H2D inside every step) and the
+pooled embeddings read back to the host.  ``roofline``: the dominant kernel
+(the fc1 GEMM with LayerNorm + GELU epilogue) timed alone with CUDA events
+against the measured dense-bf16 peak.  ``cpu_baseline``: the numpy oracle
+(fp32) of the same workload on the host cores, a bounded sample of images.
+
+``--impl reference`` times the reference algorithm's CPU implementation
+(the numpy restatement of model.py + the transformers head; the reference
+itself is Python that cannot be shipped here) on the host cores, on the same
+workload and metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from siglip2_b200 import workloads as W  # noqa: E402
+
+METRIC = "images/sec/GPU So400m-NaFlex bf16 @1024 patches; % of dense BF16 TC peak"
+UNIT = "images/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="cfg2", choices=sorted(W.WORKLOADS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="bounded CPU-baseline sample length")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 1590.0, 6650.0, "fallback"
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    REASONS = {
+        "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80, "sw_power_cap": 0x4,
+    }
+
+    def __init__(self, index: int):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for name, bit in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.1)
+
+    def __enter__(self):
+        if self.nv is not None:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self.nv is not None:
+            self.t.join()
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# --------------------------------------------------------------------------- workload
+def build_inputs(wl, rank: int):
+    shapes = W.sample_spatial_shapes(wl.sampler, wl.batch, wl.max_patches, seed=1337 + rank)
+    cfg_probe = W.PRESETS[wl.preset]
+    pv, mask = W.make_pixels(shapes, wl.max_patches, 3 * 16 * 16, seed=1337 + rank, dtype=wl.dtype)
+    return shapes, pv, mask
+
+
+def build_model(wl, device):
+    from siglip2_b200 import Siglip2SequenceVisionTransformer, Siglip2VisionConfig
+    cfg = W.preset_config(wl.preset, config_cls=Siglip2VisionConfig)
+    sd = W.init_state_dict(cfg, seed=1337, with_head=True)
+    m = Siglip2SequenceVisionTransformer(cfg)
+    m.load_state_dict(sd)
+    return cfg, m.to(device=device, dtype=wl.dtype).eval()
+
+
+def flops_forward(cfg, shapes) -> float:
+    from oracle.siglip2_oracle import flops_per_image  # FLOP model only (formula), not the oracle path
+    return sum(flops_per_image(cfg, int(h) * int(w)) for h, w in shapes.tolist())
+
+
+# --------------------------------------------------------------------------- CPU side
+def cpu_sample(wl, seconds: float):
+    """The numpy oracle (fp32) over as many of the workload's images as fit in
+    `seconds` (at least one).  Returns (images/s, cores, sample description)."""
+    from oracle import siglip2_oracle as O
+    cores = os.cpu_count() or 1
+    try:
+        from threadpoolctl import threadpool_limits
+        limiter = threadpool_limits(limits=cores)
+    except Exception:
+        limiter = None
+    cfg = W.preset_config(wl.preset, config_cls=O.OracleConfig)
+    sd = {k: v.float().numpy() for k, v in W.init_state_dict(cfg, seed=1337, with_head=True).items()}
+    shapes, pv, mask = build_inputs(wl, 0)
+    pv = pv.float().numpy()
+    done, t0 = 0, time.perf_counter()
+    while done < wl.batch:
+        b = done
+        L = int(shapes[b, 0] * shapes[b, 1])
+        O.forward_padded(sd, cfg, pv[b:b + 1, :L], mask[b:b + 1, :L].numpy(), shapes[b:b + 1].numpy(), dt=np.float32)
+        done += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = time.perf_counter() - t0
+    if limiter is not None:
+        limiter.unregister() if hasattr(limiter, "unregister") else None
+    return done / dt, cores, f"{done} of the {wl.batch} images of rank 0's batch, numpy fp32, {cores} threads, {dt:.1f} s"
+
+
+def run_reference_arm(args, wl, rank, world):
+    if rank != 0:
+        return
+    from oracle import siglip2_oracle as O
+    cores = os.cpu_count() or 1
+    cfg = W.preset_config(wl.preset, config_cls=O.OracleConfig)
+    sd = {k: v.float().numpy() for k, v in W.init_state_dict(cfg, seed=1337, with_head=True).items()}
+    shapes, pv, mask = build_inputs(wl, 0)
+    pv = pv.float().numpy()
+    per_step = 1  # one image of the batch per step keeps K + W steps within minutes
+
+    def step(i):
+        b = i % wl.batch
+        L = int(shapes[b, 0] * shapes[b, 1])
+        O.forward_padded(sd, cfg, pv[b:b + 1, :L], mask[b:b + 1, :L].numpy(), shapes[b:b + 1].numpy(), dt=np.float32)
+
+    for i in range(args.warmup):
+        step(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        step(args.warmup + i)
+    dt = time.perf_counter() - t0
+    val = per_step * args.steps / dt
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": wl.name, "images_per_step": per_step, "max_patches": wl.max_patches},
+        "cpu_baseline": {"value": val, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"{per_step} image per step of rank 0's {wl.batch}-image batch (numpy fp32 "
+                                   f"restatement of model.py + transformers head)"},
+        "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# --------------------------------------------------------------------------- GPU arm
+def main():
+    args = parse()
+    wl = W.WORKLOADS[args.workload]
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference_arm(args, wl, rank, world)
+        return
+    assert args.warmup >= 3, "at least 3 warm-up steps"
+    import datetime
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    from siglip2_b200 import _lib as L
+    from siglip2_b200 import ops
+
+    cfg, model = build_model(wl, dev)
+    shapes, pv_cpu, mask_cpu = build_inputs(wl, rank)
+    shapes_cpu = shapes.to(torch.int64)
+    pv = pv_cpu.to(dev)
+    mask = mask_cpu.to(dev)
+    pv_pinned = pv_cpu.pin_memory()
+    mask_pinned = mask_cpu.pin_memory()
+    B, D = wl.batch, cfg.hidden_size
+    gathered = torch.empty((world * B, D), dtype=wl.dtype, device=dev) if world > 1 else None
+
+    def step(pixels, msk):
+        out = model(pixels, msk, shapes_cpu)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, out.pooler_output)
+        return out
+
+    def sync_all():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    # ---- device-resident throughput
+    for _ in range(args.warmup):
+        step(pv, mask)
+    sync_all()
+    lib = L.load()
+    n0 = lib.siglip2_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        sync_all()
+        e0.record()
+        for _ in range(args.steps):
+            step(pv, mask)
+        e1.record()
+        sync_all()
+    launches = (lib.siglip2_launch_count() - n0)
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    images = world * B * args.steps
+    value = images / (ms / 1e3)
+    peak_tf, peak_hbm, peak_kind = peaks()
+    fl = flops_forward(cfg, shapes)
+    tflops = fl / (ms_step / 1e3) / 1e12
+
+    # ---- end-to-end through the public API from pinned host memory
+    h2d = pv_pinned.numel() * pv_pinned.element_size() + mask_pinned.numel() * mask_pinned.element_size()
+    d2h = B * D * torch.tensor([], dtype=wl.dtype).element_size()
+    host_out = torch.empty((B, D), dtype=wl.dtype, pin_memory=True)
+    for _ in range(2):
+        o = step(pv_pinned.to(dev, non_blocking=True), mask_pinned.to(dev, non_blocking=True))
+        host_out.copy_(o.pooler_output, non_blocking=True)
+    sync_all()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record()
+    for _ in range(args.steps):
+        o = step(pv_pinned.to(dev, non_blocking=True), mask_pinned.to(dev, non_blocking=True))
+        host_out.copy_(o.pooler_output, non_blocking=True)
+    e3.record()
+    sync_all()
+    ms_e2e = e2.elapsed_time(e3)
+    if world > 1:
+        t = torch.tensor([ms_e2e], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_e2e = float(t.item())
+    e2e_value = images / (ms_e2e / 1e3)
+
+    # ---- dominant kernel alone: fc1 GEMM (LN-folded, GELU) on this batch's token count
+    roofline = None
+    if rank == 0:
+        N = int((shapes[:, 0] * shapes[:, 1]).sum())
+        I = cfg.intermediate_size
+        a = torch.randn(N, D, device=dev).to(wl.dtype)
+        w = (torch.randn(I, D, device=dev) * 0.02).to(wl.dtype)
+        c1 = torch.randn(I, device=dev)
+        c2 = torch.randn(I, device=dev)
+        out = torch.empty(N, I, device=dev, dtype=wl.dtype)
+        for _ in range(3):
+            ops.gemm(a, w, L.EPI_LN_GELU, c1=c1, c2=c2, out=out)
+        torch.cuda.synchronize(dev)
+        reps = 20
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(reps):
+            ops.gemm(a, w, L.EPI_LN_GELU, c1=c1, c2=c2, out=out)
+        s1.record()
+        torch.cuda.synchronize(dev)
+        kms = s0.elapsed_time(s1) / reps
+        kfl = 2.0 * N * I * D
+        ach = kfl / (kms / 1e3) / 1e12
+        traffic = None
+        try:
+            with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+                tr = json.load(f)["gemm_fc1_ln_gelu"]
+                traffic = tr["bytes_per_token"] * N
+        except Exception:
+            pass
+        roofline = {"bound": "tensor", "kernel": f"gemm_tc_kernel<bf16,256,LnGelu> M={N} N={I} K={D}",
+                    "achieved": round(ach, 1), "peak": peak_tf, "unit": "TFLOP/s",
+                    "frac": round(ach / peak_tf, 4), "peak_kind": f"{peak_kind} bf16_tflops (burst)",
+                    "ms_per_launch": round(kms, 4), "traffic": traffic}
+        del a, w, out
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, cores, sample = cpu_sample(wl, args.cpu_seconds)
+        cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16" if wl.dtype == torch.bfloat16 else str(wl.dtype).split(".")[-1],
+            "data": "synthetic (seeded NaFlex grids, U[-1,1] pixels, trunc-normal weights)",
+            "config": {"workload": wl.name, "images_per_gpu": B, "max_patches": wl.max_patches,
+                       "valid_tokens_per_gpu": int((shapes[:, 0] * shapes[:, 1]).sum()),
+                       "padding_frac": round(1 - float((shapes[:, 0] * shapes[:, 1]).sum()) / (B * wl.max_patches), 4),
+                       "parallelism": f"dp{world} (images sharded, NCCL all-gather of pooled embeddings)",
+                       "l2": "working set (inputs 100 MB + weights 0.86 GB per step) larger than L2"},
+            "tflops_algorithmic": round(tflops, 1), "pct_of_peak": round(100 * tflops / peak_tf, 2),
+            "peak": {"bf16_tflops": peak_tf, "kind": peak_kind},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": int(launches),
+            "roofline": roofline, "cpu_baseline": cpu, "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -67,6 +67,9 @@ int siglip2_version(void);
 /* Thread-local description of the last failure. */
 const char* siglip2_last_error(void);
 
+/* Number of kernel launches this library has enqueued since it was loaded. */
+unsigned long long siglip2_launch_count(void);
+
 /* Synchronises the current device and returns SIGLIP2_ERR_TIMEOUT if a kernel
  * gave up on a bounded wait since the last reset (the failing site id is in
  * siglip2_last_error()).  reset != 0 clears the flag. */

@@ -39,18 +39,16 @@ enum GemmEpilogue : int {
 
 struct GemmParams {
   int M, N, K;
-  void* out;             // [M, ldo] (element type T)
-  int ldo;               // elements
   const float* bias;     // [N] (kEpiBias*, kEpiBiasRes)
-  const void* res;       // [M, ldr] element type T (kEpiBiasRes); may alias out
-  int ldr;
   const float* c1;       // [N] (kEpiLn*)
   const float* c2;       // [N] (kEpiLn*)
   float eps;             // LayerNorm epsilon (kEpiLn*)
 };
 
 constexpr int kGemmBM = 128;
-constexpr int kGemmBK = 64;  // 64 x 2B = one 128-byte swizzle row
+constexpr int kGemmBK = 64;     // 64 x 2B = one 128-byte swizzle row
+constexpr int kEpiCols = 32;    // epilogue chunk: 32 columns = one 64B-swizzled staging row
+constexpr int kEpiWarps = 4;
 
 template <int BN>
 struct GemmCfg {
@@ -60,8 +58,11 @@ struct GemmCfg {
   static constexpr int kStages = (200 * 1024) / kStageBytes;  // 4 for BN=256, 5 for BN=192
   static constexpr int kTmemCols = 512;                        // 2 accumulators, 256-column slots
   static constexpr int kAccStride = 256;
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 1024 /*barriers+stats*/ +
-                                    2 * 2 * kGemmBM * 4;
+  static constexpr int kStaging = kEpiWarps * 2 * 32 * kEpiCols * 2;  // 2 x [32 rows][32 cols] per warp
+  static constexpr int kOffStaging = kStages * kStageBytes;
+  static constexpr int kOffBars = kOffStaging + kStaging;
+  static constexpr int kOffStats = kOffBars + 1024;
+  static constexpr int kSmemBytes = kOffStats + 2 * 2 * kGemmBM * 4 + 1024 /*alignment slack*/;
 };
 
 template <bool LN>
@@ -70,13 +71,38 @@ struct GemmThreads {
   static constexpr int kThreads = kWarps * 32;
 };
 
+// keeps the compiler from using tcgen05.ld destination registers before the
+// tcgen05.wait::ld that makes them valid
+#define SG_REG_FENCE_32(r)                                                                               \
+  asm volatile(""                                                                                        \
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),       \
+                 "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),   \
+                 "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]),             \
+                 "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]),             \
+                 "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31]))
+
+__device__ __forceinline__ void load_param32(const float* __restrict__ p, int col0, int N, float* v) {
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (col0 + 4 * q < N) f = __ldg(reinterpret_cast<const float4*>(p + col0) + q);  // N % 8 == 0
+    v[4 * q] = f.x;
+    v[4 * q + 1] = f.y;
+    v[4 * q + 2] = f.z;
+    v[4 * q + 3] = f.w;
+  }
+}
+
 template <typename T, int BN, int EPI>
 __global__ void __launch_bounds__(GemmThreads<(EPI == kEpiLn || EPI == kEpiLnGelu)>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
                    const GemmParams p) {
   constexpr bool kLN = (EPI == kEpiLn || EPI == kEpiLnGelu);
+  constexpr bool kRes = (EPI == kEpiBiasRes);
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::kStages;
+  constexpr int NCH = BN / kEpiCols;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kIdesc = make_idesc(kGemmBM, BN, kBF16, false, false);
 
@@ -84,7 +110,8 @@ __global__ void __launch_bounds__(GemmThreads<(EPI == kEpiLn || EPI == kEpiLnGel
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smA = smem;
   uint8_t* smB = smem + STAGES * Cfg::kStageA;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::kStageBytes);
+  uint8_t* staging = smem + Cfg::kOffStaging;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBars);
   uint64_t* full = bars;                 // [STAGES]
   uint64_t* empty = bars + STAGES;       // [STAGES]
   uint64_t* tfull = bars + 2 * STAGES;   // [2]
@@ -92,10 +119,11 @@ __global__ void __launch_bounds__(GemmThreads<(EPI == kEpiLn || EPI == kEpiLnGel
   uint64_t* sfull = tempty + 2;          // [2]
   uint64_t* sempty = sfull + 2;          // [2]
   uint64_t* mdone = sempty + 2;          // [1] all issued MMAs complete (teardown)
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mdone + 1);
+  uint64_t* resbar = mdone + 1;          // [kEpiWarps][2] residual chunk landed in staging
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(resbar + 2 * kEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  float* st_mean = reinterpret_cast<float*>(smem + STAGES * Cfg::kStageBytes + 1024);  // [2][128]
-  float* st_rstd = st_mean + 2 * kGemmBM;                                               // [2][128]
+  float* st_mean = reinterpret_cast<float*>(smem + Cfg::kOffStats);  // [2][128]
+  float* st_rstd = st_mean + 2 * kGemmBM;                              // [2][128]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -111,17 +139,20 @@ __global__ void __launch_bounds__(GemmThreads<(EPI == kEpiLn || EPI == kEpiLnGel
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);
+      mbar_init(&tempty[b], kEpiWarps);
       mbar_init(&sfull[b], kGemmBM);
-      mbar_init(&sempty[b], 4);
+      mbar_init(&sempty[b], kEpiWarps);
     }
     mbar_init(mdone, 1);
+    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&resbar[i], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmO);
+    if (kRes) tma_prefetch_desc(&tmR);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, Cfg::kTmemCols);
@@ -158,7 +189,7 @@ __global__ void __launch_bounds__(GemmThreads<(EPI == kEpiLn || EPI == kEpiLnGel
           }
         }
       }
-      // Tail: make sure no TMA write is still in flight into this CTA's shared
+      // Tail: no TMA write may still be in flight into this CTA's shared
       // memory when it exits (wait until the consumers released every stage,
       // which implies the loads landed).
       for (int i = 0; i < STAGES && i < issued; ++i) {
@@ -216,10 +247,18 @@ __global__ void __launch_bounds__(GemmThreads<(EPI == kEpiLn || EPI == kEpiLnGel
       umma_commit(mdone);
       mbar_wait(mdone, 0, 113);
     }
-  } else if (warp < 6) {
+  } else if (warp < 2 + kEpiWarps) {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    // Warp (warp & 3) may only touch TMEM lanes 32*(warp&3) .. +31: it owns
+    // those 32 rows of the tile, 32 columns per chunk.  Each chunk goes
+    // TMEM -> registers -> fused math -> 64B-swizzled staging -> TMA store
+    // (the residual, if any, arrives in the same staging buffer by TMA).
+    const int ew = warp - 2;
+    const int q = warp & 3;
     const int row_in_tile = q * 32 + lane;
+    uint8_t* stg = staging + ew * (2 * 32 * kEpiCols * 2);
+    uint64_t* rbar = resbar + 2 * ew;
+    uint32_t rph0 = 0, rph1 = 0;
     int t = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
       const int buf = t & 1;
@@ -242,70 +281,103 @@ __global__ void __launch_bounds__(GemmThreads<(EPI == kEpiLn || EPI == kEpiLnGel
         __syncwarp();
         if (lane == 0) mbar_arrive(&sempty[buf]);
       }
-      const int row = m0 + row_in_tile;
-      const bool row_ok = row < p.M;
-      T* out_row = reinterpret_cast<T*>(p.out) + static_cast<size_t>(row) * p.ldo;
-      const T* res_row = nullptr;
-      if constexpr (EPI == kEpiBiasRes) res_row = reinterpret_cast<const T*>(p.res) + static_cast<size_t>(row) * p.ldr;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        const uint32_t taddr = tmem_base + buf * Cfg::kAccStride + c * 32 + (static_cast<uint32_t>(q * 32) << 16);
-        SG_TMEM_LD_32(taddr, r);
-        tmem_ld_wait();
-        const int col0 = n0 + c * 32;
-        if (col0 >= p.N) continue;
-        float v[32];
+      const int row0 = m0 + q * 32;
+      const uint32_t tbase = tmem_base + buf * Cfg::kAccStride + (static_cast<uint32_t>(q * 32) << 16);
+      uint32_t ra[32], rb[32];
+      SG_TMEM_LD_32(tbase, ra);
+      tmem_ld_wait();
+      SG_REG_FENCE_32(ra);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        if constexpr (EPI == kEpiLn || EPI == kEpiLnGelu) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int col = min(col0 + j, p.N - 1);
-            v[j] = rstd * (v[j] - mu * __ldg(p.c1 + col)) + __ldg(p.c2 + col);
-            if constexpr (EPI == kEpiLnGelu) v[j] = gelu_tanh(v[j]);
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int col = min(col0 + j, p.N - 1);
-            v[j] += __ldg(p.bias + col);
-            if constexpr (EPI == kEpiBiasGelu) v[j] = gelu_tanh(v[j]);
+      for (int c = 0; c < NCH; ++c) {
+        uint32_t* cur = (c & 1) ? rb : ra;
+        uint32_t* nxt = (c & 1) ? ra : rb;
+        if (c + 1 < NCH) SG_TMEM_LD_32(tbase + (c + 1) * kEpiCols, nxt);
+        const int col0 = n0 + c * kEpiCols;
+        const int sb = c & 1;  // staging buffer
+        uint8_t* sbuf = stg + sb * (32 * kEpiCols * 2);
+        // the store issued from this buffer two chunks ago must have read it
+        if (lane == 0) tma_store_wait_read<1>();
+        __syncwarp();
+        if constexpr (kRes) {
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&rbar[sb], 32 * kEpiCols * 2);
+            tma_load_2d(sbuf, &tmR, &rbar[sb], col0, row0);
           }
         }
-        if (row_ok) {
+        float v[32];
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const int col = col0 + g * 8;
-            if (col < p.N) {  // N is a multiple of 8: a 16-byte group is all in or all out
-              if constexpr (EPI == kEpiBiasRes) {
-                const uint4 rv = *reinterpret_cast<const uint4*>(res_row + col);
-                const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(cur[j]);
+        if (col0 < p.N) {
+          if constexpr (kLN) {
+            float a[32], b[32];
+            load_param32(p.c1, col0, p.N, a);
+            load_param32(p.c2, col0, p.N, b);
 #pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                  const float2 f = Pack2<T>::unpack(rw[h]);
-                  v[g * 8 + 2 * h] += f.x;
-                  v[g * 8 + 2 * h + 1] += f.y;
-                }
-              }
-              uint4 o;
-              o.x = Pack2<T>::pack(v[g * 8 + 0], v[g * 8 + 1]);
-              o.y = Pack2<T>::pack(v[g * 8 + 2], v[g * 8 + 3]);
-              o.z = Pack2<T>::pack(v[g * 8 + 4], v[g * 8 + 5]);
-              o.w = Pack2<T>::pack(v[g * 8 + 6], v[g * 8 + 7]);
-              *reinterpret_cast<uint4*>(out_row + col) = o;
+            for (int j = 0; j < 32; ++j) {
+              v[j] = fmaf(rstd, fmaf(-mu, a[j], v[j]), b[j]);
+              if constexpr (EPI == kEpiLnGelu) v[j] = gelu_tanh(v[j]);
+            }
+          } else {
+            float a[32];
+            load_param32(p.bias, col0, p.N, a);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              v[j] += a[j];
+              if constexpr (EPI == kEpiBiasGelu) v[j] = gelu_tanh(v[j]);
             }
           }
         }
+        // 64B-swizzled staging: 16B chunk g of row r lives at chunk g ^ ((r >> 1) & 3)
+        const int sw = (lane >> 1) & 3;
+        uint8_t* srow = sbuf + lane * (kEpiCols * 2);
+        if constexpr (kRes) {
+          const uint32_t ph = sb ? rph1 : rph0;
+          if (!mbar_wait(&rbar[sb], ph, 123)) *abort_flag = 1;
+          if (sb) rph1 ^= 1; else rph0 ^= 1;
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const uint4 rv = *reinterpret_cast<const uint4*>(srow + ((g ^ sw) << 4));
+            const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              const float2 f = Pack2<T>::unpack(rw[h]);
+              v[g * 8 + 2 * h] += f.x;
+              v[g * 8 + 2 * h + 1] += f.y;
+            }
+          }
+        }
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          uint4 o;
+          o.x = Pack2<T>::pack(v[g * 8 + 0], v[g * 8 + 1]);
+          o.y = Pack2<T>::pack(v[g * 8 + 2], v[g * 8 + 3]);
+          o.z = Pack2<T>::pack(v[g * 8 + 4], v[g * 8 + 5]);
+          o.w = Pack2<T>::pack(v[g * 8 + 6], v[g * 8 + 7]);
+          *reinterpret_cast<uint4*>(srow + ((g ^ sw) << 4)) = o;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && col0 < p.N && row0 < p.M) {
+          tma_store_2d(&tmO, sbuf, col0, row0);
+        }
+        if (lane == 0) tma_store_commit();
+        if (c + 1 < NCH) {
+          tmem_ld_wait();
+          SG_REG_FENCE_32(nxt);
+        } else {
+          // accumulator fully read: hand the TMEM buffer back to the MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[buf]);
+        }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[buf]);
     }
+    if (lane == 0) tma_store_wait_all<0>();
+    __syncwarp();
   } else {
     // ------------------------------------------------------------ LayerNorm row statistics
     if constexpr (kLN) {
-      const int r = threadIdx.x - 6 * 32;  // 0..127: row within the tile
+      const int r = threadIdx.x - (2 + kEpiWarps) * 32;  // 0..127: row within the tile
       int stage = 0;
       uint32_t phase = 0;
       int t = 0;
@@ -327,9 +399,10 @@ __global__ void __launch_bounds__(GemmThreads<(EPI == kEpiLn || EPI == kEpiLnGel
           const uint8_t* rowp = smA + stage * Cfg::kStageA + r * 128;
 #pragma unroll
           for (int ch = 0; ch < 8; ++ch) {
-            // the 128B swizzle only permutes 16B chunks within the row, and the
-            // sum does not care about their order
-            const uint4 u = *reinterpret_cast<const uint4*>(rowp + ch * 16);
+            // the 128B swizzle permutes the 16B chunks of a row; the sum does
+            // not care about order, and reading chunk ch ^ (r & 7) puts the 8
+            // rows of each 8-lane phase on 8 different bank groups
+            const uint4 u = *reinterpret_cast<const uint4*>(rowp + ((ch ^ (r & 7)) << 4));
             const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
             for (int h = 0; h < 4; ++h) {

@@ -8,6 +8,7 @@
 #include <stdint.h>
 #include <stdio.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "../../include/siglip2_b200.h"
@@ -39,6 +40,7 @@ inline int set_error(int code, const char* fmt, ...) {
 
 #define SG_LAUNCH_CHECK()                                                                          \
   do {                                                                                             \
+    ::sg::launch_counter().fetch_add(1, std::memory_order_relaxed);                                \
     cudaError_t e_ = cudaGetLastError();                                                           \
     if (e_ != cudaSuccess)                                                                         \
       return ::sg::set_error(SIGLIP2_ERR_CUDA, "kernel launch failed: %s (%s:%d)", cudaGetErrorString(e_), \
@@ -50,6 +52,12 @@ inline int set_error(int code, const char* fmt, ...) {
     int rc_ = (expr);          \
     if (rc_ != SIGLIP2_OK) return rc_; \
   } while (0)
+
+// Kernel launches issued by this library since load (host-side count).
+inline std::atomic<unsigned long long>& launch_counter() {
+  static std::atomic<unsigned long long> n{0};
+  return n;
+}
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

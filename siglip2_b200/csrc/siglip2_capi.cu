@@ -15,11 +15,25 @@ using namespace sg;
 
 namespace {
 
+struct GemmIO {
+  const void* a;
+  int lda;
+  const void* b;
+  int ldb;
+  void* out;
+  int ldo;
+  const void* res;
+  int ldr;
+};
+
 template <typename T, int BN, int EPI>
-int launch_gemm_tc(const void* a, int lda, const void* b, int ldb, const GemmParams& p, cudaStream_t stream) {
-  CUtensorMap ta, tb;
-  SG_TRY(make_tmap_2d(&ta, a, 2, p.M, p.K, lda, kGemmBM, kGemmBK));
-  SG_TRY(make_tmap_2d(&tb, b, 2, p.N, p.K, ldb, BN, kGemmBK));
+int launch_gemm_tc(const GemmIO& io, const GemmParams& p, cudaStream_t stream) {
+  CUtensorMap ta, tb, to, tr;
+  SG_TRY(make_tmap_2d(&ta, io.a, 2, p.M, p.K, io.lda, kGemmBM, kGemmBK));
+  SG_TRY(make_tmap_2d(&tb, io.b, 2, p.N, p.K, io.ldb, BN, kGemmBK));
+  SG_TRY(make_tmap_2d(&to, io.out, 2, p.M, p.N, io.ldo, 32, kEpiCols));
+  if (EPI == kEpiBiasRes) SG_TRY(make_tmap_2d(&tr, io.res, 2, p.M, p.N, io.ldr, 32, kEpiCols));
+  else tr = to;
   constexpr bool kLN = (EPI == kEpiLn || EPI == kEpiLnGelu);
   constexpr int threads = GemmThreads<kLN>::kThreads;
   constexpr int smem = GemmCfg<BN>::kSmemBytes;
@@ -31,28 +45,28 @@ int launch_gemm_tc(const void* a, int lda, const void* b, int ldb, const GemmPar
   }
   const int tiles = ((p.M + kGemmBM - 1) / kGemmBM) * ((p.N + BN - 1) / BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kern<<<grid, threads, smem, stream>>>(ta, tb, p);
+  kern<<<grid, threads, smem, stream>>>(ta, tb, to, tr, p);
   SG_LAUNCH_CHECK();
   return SIGLIP2_OK;
 }
 
 template <typename T, int BN>
-int dispatch_epi(int epi, const void* a, int lda, const void* b, int ldb, const GemmParams& p, cudaStream_t s) {
+int dispatch_epi(int epi, const GemmIO& io, const GemmParams& p, cudaStream_t s) {
   switch (epi) {
-    case kEpiBias: return launch_gemm_tc<T, BN, kEpiBias>(a, lda, b, ldb, p, s);
-    case kEpiBiasRes: return launch_gemm_tc<T, BN, kEpiBiasRes>(a, lda, b, ldb, p, s);
-    case kEpiLn: return launch_gemm_tc<T, BN, kEpiLn>(a, lda, b, ldb, p, s);
-    case kEpiLnGelu: return launch_gemm_tc<T, BN, kEpiLnGelu>(a, lda, b, ldb, p, s);
-    case kEpiBiasGelu: return launch_gemm_tc<T, BN, kEpiBiasGelu>(a, lda, b, ldb, p, s);
+    case kEpiBias: return launch_gemm_tc<T, BN, kEpiBias>(io, p, s);
+    case kEpiBiasRes: return launch_gemm_tc<T, BN, kEpiBiasRes>(io, p, s);
+    case kEpiLn: return launch_gemm_tc<T, BN, kEpiLn>(io, p, s);
+    case kEpiLnGelu: return launch_gemm_tc<T, BN, kEpiLnGelu>(io, p, s);
+    case kEpiBiasGelu: return launch_gemm_tc<T, BN, kEpiBiasGelu>(io, p, s);
     default: return set_error(SIGLIP2_ERR_ARG, "unknown epilogue %d", epi);
   }
 }
 
 // Tile width: 192 when it divides N exactly (1152, 768, 1536 ...), else 256.
 template <typename T>
-int dispatch_bn(int epi, const void* a, int lda, const void* b, int ldb, const GemmParams& p, cudaStream_t s) {
-  if (p.N % 192 == 0 && p.N % 256 != 0) return dispatch_epi<T, 192>(epi, a, lda, b, ldb, p, s);
-  return dispatch_epi<T, 256>(epi, a, lda, b, ldb, p, s);
+int dispatch_bn(int epi, const GemmIO& io, const GemmParams& p, cudaStream_t s) {
+  if (p.N % 192 == 0 && p.N % 256 != 0) return dispatch_epi<T, 192>(epi, io, p, s);
+  return dispatch_epi<T, 256>(epi, io, p, s);
 }
 
 }  // namespace
@@ -77,20 +91,19 @@ int sg_gemm_impl(int dtype, int epi, const void* a, int lda, const void* b, int 
     return set_error(SIGLIP2_ERR_SHAPE, "leading dimension smaller than the row");
   if (!aligned16(out) || (res && !aligned16(res)))
     return set_error(SIGLIP2_ERR_ALIGN, "output/residual must be 16-byte aligned");
+  if ((c1 && !aligned16(c1)) || (c2 && !aligned16(c2)) || (bias && !aligned16(bias)))
+    return set_error(SIGLIP2_ERR_ALIGN, "bias / c1 / c2 vectors must be 16-byte aligned");
   GemmParams p;
   p.M = M;
   p.N = N;
   p.K = K;
-  p.out = out;
-  p.ldo = ldo;
   p.bias = bias;
-  p.res = res;
-  p.ldr = ldr;
   p.c1 = c1;
   p.c2 = c2;
   p.eps = eps;
-  if (dtype == SIGLIP2_BF16) return dispatch_bn<__nv_bfloat16>(epi, a, lda, b, ldb, p, stream);
-  return dispatch_bn<__half>(epi, a, lda, b, ldb, p, stream);
+  GemmIO io{a, lda, b, ldb, out, ldo, res, ldr};
+  if (dtype == SIGLIP2_BF16) return dispatch_bn<__nv_bfloat16>(epi, io, p, stream);
+  return dispatch_bn<__half>(epi, io, p, stream);
 }
 
 
@@ -363,6 +376,8 @@ extern "C" {
 int siglip2_version(void) { return 100; }
 
 const char* siglip2_last_error(void) { return t_last_error; }
+
+unsigned long long siglip2_launch_count(void) { return launch_counter().load(); }
 
 int siglip2_check_device(int reset) {
   SG_CUDA(cudaDeviceSynchronize());

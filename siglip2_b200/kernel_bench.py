@@ -1,0 +1,118 @@
+"""Per-kernel timing driver at the tower's shapes (CUDA events), also the
+command the ncu summaries under ``profiles/`` were captured with.
+
+    python -m siglip2_b200.kernel_bench gemm --epi ln_gelu --m 39178 --n 4304 --k 1152
+    python -m siglip2_b200.kernel_bench fmha --preset so400m --images 64 --max-patches 1024
+    python -m siglip2_b200.kernel_bench layer --preset so400m --images 64 --max-patches 1024
+
+Prints one JSON line per measurement: milliseconds per launch and the
+algorithmic TFLOP/s (dense contractions only).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+
+import torch
+
+from . import _lib as L
+from . import ops
+from . import workloads as W
+
+EPIS = {"bias": L.EPI_BIAS, "bias_res": L.EPI_BIAS_RES, "ln": L.EPI_LN, "ln_gelu": L.EPI_LN_GELU,
+        "bias_gelu": L.EPI_BIAS_GELU}
+
+
+def _time(fn, reps: int, warmup: int = 3) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / reps
+
+
+def bench_gemm(m, n, k, epi, reps, dtype=torch.bfloat16, warmup=3):
+    a = torch.randn(m, k, device="cuda").to(dtype)
+    w = (torch.randn(n, k, device="cuda") * 0.02).to(dtype)
+    vec = torch.randn(n, device="cuda") * 0.1
+    res = torch.randn(m, n, device="cuda").to(dtype) if EPIS[epi] == L.EPI_BIAS_RES else None
+    out = torch.empty(m, n, device="cuda", dtype=dtype)
+    ms = _time(lambda: ops.gemm(a, w, EPIS[epi], bias=vec, res=res, c1=vec, c2=vec, out=out), reps, warmup)
+    return {"kernel": "gemm", "epi": epi, "M": m, "N": n, "K": k, "ms": ms, "tflops": 2 * m * n * k / ms / 1e9}
+
+
+def _shapes(preset, images, max_patches, seed=1337):
+    return W.sample_spatial_shapes("area_aspect" if max_patches > 256 else "full", images, max_patches, seed)
+
+
+def bench_fmha(preset, images, max_patches, reps, dtype=torch.bfloat16, warmup=3):
+    D, _, _, H = W.PRESETS[preset]
+    hd = D // H
+    shapes = _shapes(preset, images, max_patches)
+    lens = (shapes[:, 0] * shapes[:, 1]).tolist()
+    N = sum(lens)
+    hdp = ops.padded_head_dim(hd)
+    qkv = torch.randn(N, 3, H, hdp, device="cuda").to(dtype)
+    qkv[..., hd:] = 0
+    qkv = qkv.view(N, -1)
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0).tolist()), dtype=torch.int32, device="cuda")
+    tiles = ops.attention_tiles(lens).cuda()
+    out = torch.empty(N, D, device="cuda", dtype=dtype)
+    ms = _time(lambda: ops.fmha_varlen(qkv, cu, tiles, H, hd, out=out), reps, warmup)
+    fl = sum(4 * L_ * L_ * D for L_ in lens)
+    return {"kernel": "fmha", "preset": preset, "images": images, "tokens": N, "ms": ms, "tflops": fl / ms / 1e9}
+
+
+def bench_layer(preset, images, max_patches, reps):
+    D, I, _, H = W.PRESETS[preset]
+    hdp = ops.padded_head_dim(D // H)
+    N = int((lambda s: (s[:, 0] * s[:, 1]).sum())(_shapes(preset, images, max_patches)))
+    out = []
+    for name, n, k, epi in (("qkv", 3 * H * hdp, D, "ln"), ("out", D, D, "bias_res"), ("fc1", I, D, "ln_gelu"),
+                            ("fc2", D, I, "bias_res")):
+        r = bench_gemm(N, n, k, epi, reps)
+        r["name"] = name
+        out.append(r)
+    out.append(bench_fmha(preset, images, max_patches, reps))
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    g = sub.add_parser("gemm")
+    g.add_argument("--m", type=int, default=39178)
+    g.add_argument("--n", type=int, default=4304)
+    g.add_argument("--k", type=int, default=1152)
+    g.add_argument("--epi", default="ln_gelu", choices=sorted(EPIS))
+    g.add_argument("--reps", type=int, default=20)
+    g.add_argument("--warmup", type=int, default=3)
+    f = sub.add_parser("fmha")
+    f.add_argument("--preset", default="so400m")
+    f.add_argument("--images", type=int, default=64)
+    f.add_argument("--max-patches", type=int, default=1024)
+    f.add_argument("--reps", type=int, default=20)
+    f.add_argument("--warmup", type=int, default=3)
+    y = sub.add_parser("layer")
+    y.add_argument("--preset", default="so400m")
+    y.add_argument("--images", type=int, default=64)
+    y.add_argument("--max-patches", type=int, default=1024)
+    y.add_argument("--reps", type=int, default=20)
+    a = ap.parse_args()
+    if a.cmd == "gemm":
+        print(json.dumps(bench_gemm(a.m, a.n, a.k, a.epi, a.reps, warmup=a.warmup)))
+    elif a.cmd == "fmha":
+        print(json.dumps(bench_fmha(a.preset, a.images, a.max_patches, a.reps, warmup=a.warmup)))
+    else:
+        for r in bench_layer(a.preset, a.images, a.max_patches, a.reps):
+            print(json.dumps(r))
+
+
+if __name__ == "__main__":
+    main()

@@ -344,9 +344,15 @@ class Siglip2SequenceVisionTransformer(nn.Module):
         B, P = pixel_values.shape[:2]
         lens = hw[:, 0].astype(np.int64) * hw[:, 1]
         if attention_mask is not None:
-            m = attention_mask.detach().to("cpu")
-            if m.shape != (B, P) or not torch.equal(m.sum(1).to(torch.int64), torch.from_numpy(lens)):
-                raise ValueError("attention_mask must mark exactly the first h*w rows of every image")
+            # spatial_shapes defines the valid rows; the mask must agree.  Its
+            # contents are checked when it is on the host (checking a device
+            # mask would synchronise the stream on every call).
+            if tuple(attention_mask.shape) != (B, P):
+                raise ValueError(f"attention_mask must be [B, P] = [{B}, {P}]")
+            if not attention_mask.is_cuda:
+                m = attention_mask.detach()
+                if not torch.equal(m.sum(1).to(torch.int64), torch.from_numpy(lens)):
+                    raise ValueError("attention_mask must mark exactly the first h*w rows of every image")
         last, pooled = tower_forward(pk, pixel_values, hw, P, self.head is not None)
         return Siglip2Output(last, pooled)
 
