@@ -116,6 +116,18 @@ int siglip2_fmha_varlen(int dtype, const void* qkv_dev, int N, const int* cu_seq
 /* Head dimension as stored in the QKV buffer (64 -> 64, 72 -> 80, 96 -> 96). */
 int siglip2_padded_head_dim(int head_dim);
 
+/* Attention pooling of the MAP head, first half: for every image b and head h
+ *   p_jh = softmax_j(x_j . u_h)   over the image's rows j,
+ *   pooled[b, h, :] = sum_j p_jh x_j            ([B, heads, D], dtype)
+ * x_dev rows of image b are cu[b] + j (max_patches == 0) or b*max_patches + j.
+ * u_dev [heads, D] float32 = W_k,h^T q_h * log2(e) / sqrt(head_dim) (scores
+ * are base-2).  scores_dev: caller scratch of N_tokens * heads floats.
+ * Replaces the probe attention of transformers
+ * Siglip2MultiheadAttentionPoolingHead (modeling_siglip2.py:670-719); the
+ * value/out projections and MLP follow as siglip2_gemm calls. */
+int siglip2_head_pool(int dtype, const void* x_dev, int D, int heads, const int* cu_seqlens_dev, int B,
+                      int max_patches, const float* u_dev, float* scores_dev, void* pooled_dev, void* stream);
+
 /* ------------------------------------------------------------------------
  * Whole-tower forward
  * ------------------------------------------------------------------------ */

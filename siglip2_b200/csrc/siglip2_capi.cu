@@ -371,6 +371,7 @@ int sg_forward_impl(const siglip2_config* c, const siglip2_weights* w, const voi
   return SIGLIP2_OK;
 }
 
+
 extern "C" {
 
 int siglip2_version(void) { return 100; }
@@ -422,6 +423,16 @@ int siglip2_fmha_varlen(int dtype, const void* qkv_dev, int N, const int* cu_seq
 }
 
 int siglip2_padded_head_dim(int head_dim) { return padded_head_dim(head_dim); }
+
+int siglip2_head_pool(int dtype, const void* x_dev, int D, int heads, const int* cu_seqlens_dev, int B,
+                      int max_patches, const float* u_dev, float* scores_dev, void* pooled_dev, void* stream) {
+  SG_CHECK_ARG(x_dev && cu_seqlens_dev && u_dev && scores_dev && pooled_dev && B > 0 && max_patches >= 0,
+               "bad head_pool arguments");
+  if (!aligned16(x_dev) || !aligned16(pooled_dev))
+    return set_error(SIGLIP2_ERR_ALIGN, "head_pool tensors must be 16-byte aligned");
+  return sg_head_pool_impl(dtype, x_dev, D, heads, cu_seqlens_dev, B, max_patches, u_dev, scores_dev, pooled_dev,
+                           static_cast<cudaStream_t>(stream));
+}
 
 int siglip2_metadata_size(const int32_t* hw_host, int batch, int* n_tokens, int* n_tiles) {
   SG_CHECK_ARG(hw_host && batch > 0, "bad metadata arguments");

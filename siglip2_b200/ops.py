@@ -113,3 +113,17 @@ def fmha_varlen(qkv: torch.Tensor, cu_seqlens: torch.Tensor, tiles: torch.Tensor
     L.call("siglip2_fmha_varlen", dtype_code(qkv.dtype), qkv.data_ptr(), N, cu_seqlens.data_ptr(), tiles.data_ptr(),
            tiles.shape[0], heads, head_dim, out.data_ptr(), out.stride(0), _stream(qkv.device))
     return out
+
+
+def head_pool(x: torch.Tensor, u: torch.Tensor, cu_seqlens: torch.Tensor, n_tokens: int, max_patches: int = 0,
+              scores: torch.Tensor | None = None) -> torch.Tensor:
+    """``pooled[b, h] = sum_j softmax_j(x_j . u_h) x_j`` (``siglip2_head_pool``)."""
+    _need_cuda(x, u, cu_seqlens)
+    H, D = u.shape
+    B = cu_seqlens.numel() - 1
+    if scores is None:
+        scores = torch.empty(n_tokens * H, dtype=torch.float32, device=x.device)
+    pooled = torch.empty((B, H, D), dtype=x.dtype, device=x.device)
+    L.call("siglip2_head_pool", dtype_code(x.dtype), x.data_ptr(), D, H, cu_seqlens.data_ptr(), B, max_patches,
+           u.data_ptr(), scores.data_ptr(), pooled.data_ptr(), _stream(x.device))
+    return pooled

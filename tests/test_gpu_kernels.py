@@ -98,3 +98,28 @@ def test_posemb_matches_interpolate(dtype):
     tol = 1e-6 if dtype == torch.float32 else 2e-3
     assert (out.float() - ref).abs().max().item() < tol
     assert (tok.cpu().numpy() == np.repeat(np.arange(len(lens)), lens)).all()
+
+
+def _ref_pool(x, u, lens):
+    out, s = [], 0
+    for L_ in lens:
+        xs = x[s:s + L_].float()
+        p = torch.softmax((xs @ u.T) * math.log(2.0), dim=0)  # u is in base-2 units
+        out.append(p.T @ xs)
+        s += L_
+    return torch.stack(out)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("D,H", [(1152, 16), (768, 12), (1536, 16)])
+def test_head_pool(dtype, D, H):
+    lens = [1, 37, 300, 1024, 128]
+    N = sum(lens)
+    g = torch.Generator(device="cuda").manual_seed(D + H)
+    x = torch.randn(N, D, device="cuda", generator=g).to(dtype)
+    u = torch.randn(H, D, device="cuda", generator=g) * 0.05
+    pooled = ops.head_pool(x, u, _cu(lens), N)
+    ref = _ref_pool(x, u, lens)
+    torch.cuda.synchronize()
+    tol = 1e-4 if dtype == torch.float32 else 2e-2
+    assert (pooled.float() - ref).abs().max().item() < tol
