@@ -128,6 +128,24 @@ int siglip2_padded_head_dim(int head_dim);
 int siglip2_head_pool(int dtype, const void* x_dev, int D, int heads, const int* cu_seqlens_dev, int B,
                       int max_patches, const float* u_dev, float* scores_dev, void* pooled_dev, void* stream);
 
+/* siglip2_head_pool for callers that cannot allocate device memory when they
+ * call in (a serving process that plans one fixed memory arena at start-up
+ * and forbids allocation afterwards; a C/FFI host without a caching
+ * allocator, where a cudaMalloc per call would synchronise the device).  No
+ * counterpart in the reference.  Same inputs and result as
+ * siglip2_head_pool, but the score scratch is a fixed 4 MiB device array
+ * inside the library (1,048,576 floats, reserved on every GPU that loads the
+ * library until exit): n_tokens * heads above that is rejected with
+ * SIGLIP2_ERR_SHAPE.  n_tokens must equal cu_seqlens[B].  Nothing is
+ * allocated (no cudaMalloc/cudaFree).  The first call on each device looks up
+ * the array's device address once (cudaGetSymbolAddress) with that device
+ * current; make that first call before any stream capture.  All calls share
+ * the one array, so calls that overlap on the GPU (other streams, other host
+ * threads) race: serialise them.  The scratch is fully rewritten by every
+ * call before it is read, so leftover contents never leak into a result. */
+int siglip2_head_pool_noalloc(int dtype, const void* x_dev, int D, int heads, const int* cu_seqlens_dev, int B,
+                              int max_patches, int n_tokens, const float* u_dev, void* pooled_dev, void* stream);
+
 /* ------------------------------------------------------------------------
  * Whole-tower forward
  * ------------------------------------------------------------------------ */

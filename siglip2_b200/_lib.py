@@ -28,6 +28,8 @@ SIGNATURES = {
     "siglip2_fmha_varlen": (_c_int, [_c_int, _vp, _c_int, _vp, _vp, _c_int, _c_int, _c_int, _vp, _c_int, _vp]),
     "siglip2_padded_head_dim": (_c_int, [_c_int]),
     "siglip2_head_pool": (_c_int, [_c_int, _vp, _c_int, _c_int, _vp, _c_int, _c_int, _vp, _vp, _vp, _vp]),
+    "siglip2_head_pool_noalloc": (_c_int, [_c_int, _vp, _c_int, _c_int, _vp, _c_int, _c_int, _c_int, _vp, _vp,
+                                           _vp]),
     "siglip2_metadata_size": (_c_int, [_vp, _c_int, _vp, _vp]),
     "siglip2_metadata": (_c_int, [_vp, _c_int, _vp, ctypes.c_size_t]),
     "siglip2_workspace_size": (ctypes.c_size_t, [_vp, _c_int, _c_int]),

@@ -371,6 +371,43 @@ int sg_forward_impl(const siglip2_config* c, const siglip2_weights* w, const voi
   return SIGLIP2_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Head pooling with no allocation at all.
+//
+// Some callers cannot allocate device memory when they call in: inference
+// servers that carve one fixed arena at start-up and forbid any allocation
+// afterwards, and plain C / FFI hosts that have no caching allocator, where a
+// cudaMalloc per call would synchronise the device and stall other streams.
+// For them the per-token score scratch of the pooling kernel lives in this
+// fixed device array instead of caller memory.  It is reserved on every GPU
+// that loads the library and held until the process exits.
+// ---------------------------------------------------------------------------
+constexpr size_t kNoAllocScoreCapacity = size_t(1) << 20;  // floats: 4 MiB, e.g. 65,536 tokens x 16 heads
+static __device__ __align__(256) float g_noalloc_scores[kNoAllocScoreCapacity];
+
+namespace {
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of g_noalloc_scores on the current device.  In host code the
+// array's name is only a host-side stand-in, so the address is looked up once
+// per device (with that device current) and cached.
+int noalloc_scores_ptr(float** out) {
+  int dev = 0;
+  SG_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return set_error(SIGLIP2_ERR_UNSUPPORTED, "device ordinal %d beyond %d", dev, kNoAllocMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    SG_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scores));
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return SIGLIP2_OK;
+}
+}  // namespace
 
 extern "C" {
 
@@ -423,6 +460,23 @@ int siglip2_fmha_varlen(int dtype, const void* qkv_dev, int N, const int* cu_seq
 }
 
 int siglip2_padded_head_dim(int head_dim) { return padded_head_dim(head_dim); }
+
+int siglip2_head_pool_noalloc(int dtype, const void* x_dev, int D, int heads, const int* cu_seqlens_dev, int B,
+                              int max_patches, int n_tokens, const float* u_dev, void* pooled_dev, void* stream) {
+  SG_CHECK_ARG(x_dev && cu_seqlens_dev && u_dev && pooled_dev && B > 0 && max_patches >= 0 && n_tokens >= 0 &&
+                   heads > 0,
+               "bad head_pool_noalloc arguments");
+  if (static_cast<size_t>(n_tokens) * static_cast<size_t>(heads) > kNoAllocScoreCapacity)
+    return set_error(SIGLIP2_ERR_SHAPE,
+                     "head_pool_noalloc: %d tokens x %d heads needs %zu score floats, the fixed scratch holds %zu",
+                     n_tokens, heads, static_cast<size_t>(n_tokens) * heads, kNoAllocScoreCapacity);
+  if (!aligned16(x_dev) || !aligned16(pooled_dev))
+    return set_error(SIGLIP2_ERR_ALIGN, "head_pool tensors must be 16-byte aligned");
+  float* scores = nullptr;
+  SG_TRY(noalloc_scores_ptr(&scores));
+  return sg_head_pool_impl(dtype, x_dev, D, heads, cu_seqlens_dev, B, max_patches, u_dev, scores, pooled_dev,
+                           static_cast<cudaStream_t>(stream));
+}
 
 int siglip2_head_pool(int dtype, const void* x_dev, int D, int heads, const int* cu_seqlens_dev, int B,
                       int max_patches, const float* u_dev, float* scores_dev, void* pooled_dev, void* stream) {
