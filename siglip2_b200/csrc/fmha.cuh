@@ -9,15 +9,20 @@
 // (head_dim 64 | 72 | 96), split into a 64-wide slab (128B swizzle) plus an
 // R = HDP-64 wide slab (32B / 64B swizzle).
 //
-// One CTA per (128-query tile of one image, head):
-//   warp 0     TMA: Q once, then K/V tiles of 128 keys into a 3-stage ring
-//   warp 1     TMEM owner + MMA issuer:  S_j = Q K_j^T  (128x128, fp32 in TMEM,
-//              double-buffered), then O += P_{j-1} V_{j-1}  (128xHDP in TMEM)
+// One CTA per (128-query tile of one image, head); two CTAs share an SM
+// (256 TMEM columns and <= 96 KB of shared memory each), so one CTA's MMAs run
+// while the other's softmax warps work.
+//   warp 0     TMA: Q once, K tiles of 128 keys into a 2-deep ring, V tiles
+//   warp 1     TMEM owner + MMA issuer:
+//                S_j = Q K_j^T          128x128 fp32 in TMEM columns [0,128)
+//                O  += P_j V_j          P_j (bf16/f16) read from TMEM columns
+//                                       [0,64) where the softmax wrote it over
+//                                       S_j; O (128 x HDP fp32) in [128, 128+HDP)
 //   warps 2-5  softmax: each thread owns one query row (its TMEM lane):
-//              masks keys past the image end, online max with lazy rescale
+//              keys past the image end masked, online max with lazy rescale
 //              (O is rescaled in TMEM only when the running max grows by more
-//              than 2^8), P = exp2(S*scale*log2e - m) in bf16/f16 written to a
-//              128B-swizzled shared tile, final O / l stored to out[N, H*hd].
+//              than 2^8), P = exp2(S*scale*log2e - m) packed in pairs into
+//              TMEM, final O / l stored to out[N, H*hd].
 #pragma once
 
 #include "ptx.cuh"
@@ -44,42 +49,42 @@ template <int HDP>
 struct FmhaCfg {
   static constexpr int R = HDP - 64;                 // remainder slab width (0, 16, 32)
   static constexpr int kSlabA = 128 * 64 * 2;        // 16 KB
-  static constexpr int kSlabR = 128 * (R > 0 ? R : 16) * 2;
+  static constexpr int kSlabR = 128 * R * 2;
   static constexpr int kSlabRAl = (kSlabR + 1023) / 1024 * 1024;
   static constexpr int kTile = kSlabA + kSlabRAl;    // one 128 x HDP operand
-  static constexpr int kStages = 3;
+  static constexpr int kKStages = 2;
   static constexpr int kQ = 0;
   static constexpr int kK = kTile;
-  static constexpr int kV = kK + kStages * kTile;
-  static constexpr int kP = kV + kStages * kTile;
-  static constexpr int kBar = kP + 2 * kSlabA;       // P: 128 x 128 as two 64-wide slabs
+  static constexpr int kV = kK + kKStages * kTile;
+  static constexpr int kBar = kV + kTile;
   static constexpr int kSmem = kBar + 256 + 1024;
-  static constexpr int kTileBytes = kSlabA + (R > 0 ? 128 * R * 2 : 0);  // TMA bytes per operand
+  static constexpr int kTileBytes = kSlabA + kSlabR;  // TMA bytes per operand tile
+  static constexpr uint32_t kTmemCols = 256;
+  static constexpr uint32_t kColO = 128;
 };
 
 template <typename T, int HDP>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(192, 2)
     fmha_varlen_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmR,
                        const FmhaParams p) {
   using C = FmhaCfg<HDP>;
   constexpr int R = C::R;
-  constexpr int ST = C::kStages;
+  constexpr int KS = C::kKStages;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kIdescS = make_idesc(128, 128, kBF16, false, false);
   constexpr uint32_t kIdescO64 = make_idesc(128, 64, kBF16, false, true);
   constexpr uint32_t kIdescOR = make_idesc(128, R > 0 ? R : 16, kBF16, false, true);
-  constexpr uint32_t kTmemCols = 512;
-  constexpr uint32_t kColO = 256;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBar);
   uint64_t* q_full = bars;            // 1
-  uint64_t* kv_full = bars + 1;       // ST
-  uint64_t* kv_empty = kv_full + ST;  // ST
-  uint64_t* s_full = kv_empty + ST;   // 2
-  uint64_t* s_free = s_full + 2;      // 2
-  uint64_t* p_full = s_free + 2;      // 1
+  uint64_t* k_full = bars + 1;        // KS
+  uint64_t* k_empty = k_full + KS;    // KS
+  uint64_t* v_full = k_empty + KS;    // 1
+  uint64_t* v_empty = v_full + 1;     // 1
+  uint64_t* s_full = v_empty + 1;     // 1
+  uint64_t* p_full = s_full + 1;      // 1
   uint64_t* pv_done = p_full + 1;     // 1
   uint64_t* mdone = pv_done + 1;      // 1
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mdone + 1);
@@ -99,14 +104,13 @@ __global__ void __launch_bounds__(192, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < ST; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+    for (int s = 0; s < KS; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&s_full[b], 1);
-      mbar_init(&s_free[b], 128);
-    }
+    mbar_init(v_full, 1);
+    mbar_init(v_empty, 1);
+    mbar_init(s_full, 1);
     mbar_init(p_full, 128);
     mbar_init(pv_done, 1);
     mbar_init(mdone, 1);
@@ -114,7 +118,7 @@ __global__ void __launch_bounds__(192, 1)
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, kTmemCols);
+    tmem_alloc(tmem_holder, C::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -130,30 +134,34 @@ __global__ void __launch_bounds__(192, 1)
       mbar_arrive_expect_tx(q_full, C::kTileBytes);
       tma_load_2d(smem + C::kQ, &tmA, q_full, colQ, q_row0);
       if (R > 0) tma_load_2d(smem + C::kQ + C::kSlabA, &tmR, q_full, colQ + 64, q_row0);
-      int issued = 0;
+      int k_issued = 0, v_issued = 0;
       for (int j = 0; j < n_kv; ++j) {
-        const int st = j % ST;
-        const uint32_t ph = (j / ST) & 1;
-        if (*abort_flag || !mbar_wait(&kv_empty[st], ph ^ 1, 201)) {
+        const int ks = j % KS;
+        const int kv_row = img_row0 + j * 128;
+        if (*abort_flag || !mbar_wait(&k_empty[ks], ((j / KS) & 1) ^ 1, 201)) {
           *abort_flag = 1;
           break;
         }
-        uint8_t* kb = smem + C::kK + st * C::kTile;
-        uint8_t* vb = smem + C::kV + st * C::kTile;
-        const int kv_row = img_row0 + j * 128;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * C::kTileBytes);
-        tma_load_2d(kb, &tmA, &kv_full[st], colK, kv_row);
-        tma_load_2d(vb, &tmA, &kv_full[st], colV, kv_row);
-        if (R > 0) {
-          tma_load_2d(kb + C::kSlabA, &tmR, &kv_full[st], colK + 64, kv_row);
-          tma_load_2d(vb + C::kSlabA, &tmR, &kv_full[st], colV + 64, kv_row);
+        uint8_t* kb = smem + C::kK + ks * C::kTile;
+        mbar_arrive_expect_tx(&k_full[ks], C::kTileBytes);
+        tma_load_2d(kb, &tmA, &k_full[ks], colK, kv_row);
+        if (R > 0) tma_load_2d(kb + C::kSlabA, &tmR, &k_full[ks], colK + 64, kv_row);
+        ++k_issued;
+        if (*abort_flag || !mbar_wait(v_empty, (j & 1) ^ 1, 202)) {
+          *abort_flag = 1;
+          break;
         }
-        ++issued;
+        uint8_t* vb = smem + C::kV;
+        mbar_arrive_expect_tx(v_full, C::kTileBytes);
+        tma_load_2d(vb, &tmA, v_full, colV, kv_row);
+        if (R > 0) tma_load_2d(vb + C::kSlabA, &tmR, v_full, colV + 64, kv_row);
+        ++v_issued;
       }
       // no TMA write may still be in flight when the CTA exits
-      mbar_wait(q_full, 0, 202);
-      for (int j = (issued > ST ? issued - ST : 0); j < issued; ++j)
-        mbar_wait(&kv_full[j % ST], (j / ST) & 1, 203);
+      mbar_wait(q_full, 0, 203);
+      for (int j = (k_issued > KS ? k_issued - KS : 0); j < k_issued; ++j)
+        mbar_wait(&k_full[j % KS], (j / KS) & 1, 204);
+      if (v_issued > 0) mbar_wait(v_full, (v_issued - 1) & 1, 205);
     }
   } else if (warp == 1) {
     // --------------------------------------------------------------- MMA
@@ -161,56 +169,41 @@ __global__ void __launch_bounds__(192, 1)
       bool ok = mbar_wait(q_full, 0, 211);
       const uint32_t qa = smem_u32(smem + C::kQ);
       const uint32_t qr = qa + C::kSlabA;
-      auto issue_pv = [&](int jj) {
-        const int st = jj % ST;
-        const uint32_t va = smem_u32(smem + C::kV + st * C::kTile);
-        const uint32_t vr = va + C::kSlabA;
-        const uint32_t pa = smem_u32(smem + C::kP);
-#pragma unroll
-        for (int s = 0; s < 8; ++s) {  // 16 keys per MMA
-          const uint64_t adesc = kmajor_desc(pa + (s >> 2) * C::kSlabA + (s & 3) * 32, 128);
-          const uint32_t acc = (jj > 0 || s > 0) ? 1u : 0u;
-          umma_ss(tmem + kColO, adesc, mnmajor_desc(va + s * 16 * 128, 128, 0), kIdescO64, acc);
-          if constexpr (R > 0) umma_ss(tmem + kColO + 64, adesc, mnmajor_desc(vr + s * 16 * R * 2, R * 2, 0),
-                                       kIdescOR, acc);
-        }
-        umma_commit(pv_done);
-        umma_commit(&kv_empty[st]);
-      };
+      const uint32_t va = smem_u32(smem + C::kV);
+      const uint32_t vr = va + C::kSlabA;
       for (int j = 0; j < n_kv && ok; ++j) {
-        const int st = j % ST;
-        const int sb = j & 1;
-        if (*abort_flag || !mbar_wait(&kv_full[st], (j / ST) & 1, 212) ||
-            !mbar_wait(&s_free[sb], ((j >> 1) & 1) ^ 1, 213)) {
+        const int ks = j % KS;
+        // S/P columns are reused: PV_{j-1} must have consumed P_{j-1}
+        if (*abort_flag || !mbar_wait(&k_full[ks], (j / KS) & 1, 212) ||
+            (j > 0 && !mbar_wait(pv_done, (j - 1) & 1, 213))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t ka = smem_u32(smem + C::kK + st * C::kTile);
+        const uint32_t ka = smem_u32(smem + C::kK + ks * C::kTile);
         const uint32_t kr = ka + C::kSlabA;
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          umma_ss(tmem + sb * 128, kmajor_desc(qa + k * 32, 128), kmajor_desc(ka + k * 32, 128), kIdescS, k > 0);
+          umma_ss(tmem, kmajor_desc(qa + k * 32, 128), kmajor_desc(ka + k * 32, 128), kIdescS, k > 0);
 #pragma unroll
         for (int k = 0; k < R / 16; ++k)
-          umma_ss(tmem + sb * 128, kmajor_desc(qr + k * 32, R * 2), kmajor_desc(kr + k * 32, R * 2), kIdescS, 1);
-        umma_commit(&s_full[sb]);
-        if (j > 0) {
-          if (!mbar_wait(p_full, (j - 1) & 1, 214)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          issue_pv(j - 1);
-        }
-      }
-      if (ok && n_kv > 0) {
-        if (mbar_wait(p_full, (n_kv - 1) & 1, 215)) {
-          tc_fence_after();
-          issue_pv(n_kv - 1);
-        } else {
+          umma_ss(tmem, kmajor_desc(qr + k * 32, R * 2), kmajor_desc(kr + k * 32, R * 2), kIdescS, 1);
+        umma_commit(s_full);
+        umma_commit(&k_empty[ks]);
+        if (!mbar_wait(p_full, j & 1, 214) || !mbar_wait(v_full, j & 1, 215)) {
           ok = false;
+          break;
         }
+        tc_fence_after();
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {  // 16 keys per MMA; P columns [8s, 8s+8)
+          const uint32_t acc = (j > 0 || s > 0) ? 1u : 0u;
+          umma_ts(tmem + C::kColO, tmem + s * 8, mnmajor_desc(va + s * 16 * 128, 128, 0), kIdescO64, acc);
+          if constexpr (R > 0)
+            umma_ts(tmem + C::kColO + 64, tmem + s * 8, mnmajor_desc(vr + s * 16 * R * 2, R * 2, 0), kIdescOR, acc);
+        }
+        umma_commit(pv_done);
+        umma_commit(v_empty);
       }
       if (!ok) *abort_flag = 1;
       umma_commit(mdone);
@@ -218,39 +211,48 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // --------------------------------------------------------------- softmax + epilogue
-    const int q = warp & 3;  // TMEM lane quarter of this warp
+    const int q = warp & 3;       // TMEM lane quarter of this warp
     const int r = q * 32 + lane;  // query row within the tile
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
-    uint8_t* P = smem + C::kP;
-    float m_use = -INFINITY, l = 0.f;
+    const float sc = p.scale_log2;
+    float m_use = 0.f, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      const int sb = j & 1;
-      if (*abort_flag || !mbar_wait(&s_full[sb], (j >> 1) & 1, 221)) {
+      if (*abort_flag || !mbar_wait(s_full, j & 1, 221)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float s[128];
-      {
-        uint32_t u[32];
+      const int valid = L - j * 128;  // keys of this image in the tile (>= 1)
+      // pass 1: row max of S_j (32 columns at a time)
+      // 8 independent partial maxima (no long dependency chain); keys past
+      // the image end are masked only in the image's last, partial tile
+      float mx[8];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          SG_TMEM_LD_32(tmem + sb * 128 + c * 32 + lane_off, u);
-          tmem_ld_wait();
+      for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
+      const bool full_tile = valid >= 128;
+#pragma unroll 1
+      for (int c = 0; c < 4; c += 2) {
+        uint32_t u[32], u2[32];
+        SG_TMEM_LD_32(tmem + c * 32 + lane_off, u);
+        SG_TMEM_LD_32(tmem + (c + 1) * 32 + lane_off, u2);
+        tmem_ld_wait();
+        if (full_tile) {
 #pragma unroll
-          for (int k = 0; k < 32; ++k) s[c * 32 + k] = __uint_as_float(u[k]);
+          for (int k = 0; k < 32; ++k) {
+            mx[k & 7] = fmaxf(mx[k & 7], __uint_as_float(u[k]));
+            mx[k & 7] = fmaxf(mx[k & 7], __uint_as_float(u2[k]));
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < 32; ++k) {
+            if (c * 32 + k < valid) mx[k & 7] = fmaxf(mx[k & 7], __uint_as_float(u[k]));
+            if ((c + 1) * 32 + k < valid) mx[k & 7] = fmaxf(mx[k & 7], __uint_as_float(u2[k]));
+          }
         }
       }
-      tc_fence_before();
-      mbar_arrive(&s_free[sb]);
-      const int valid = L - j * 128;  // keys of this image in the tile (>= 1)
-      float mt = -INFINITY;
-#pragma unroll
-      for (int k = 0; k < 128; ++k) {
-        s[k] = k < valid ? s[k] * p.scale_log2 : -INFINITY;
-        mt = fmaxf(mt, s[k]);
-      }
+      float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      mt *= sc;
       float alpha = 1.f;
       if (j == 0) {
         m_use = mt;
@@ -258,45 +260,55 @@ __global__ void __launch_bounds__(192, 1)
         alpha = ex2_approx(m_use - mt);
         m_use = mt;
       }
-      float rs = 0.f;
+      // O is stable here: S_j was issued only after PV_{j-1} completed
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        uint32_t u[16];
 #pragma unroll
-      for (int k = 0; k < 128; ++k) {
-        s[k] = ex2_approx(s[k] - m_use);
-        rs += s[k];
-      }
-      l = l * alpha + rs;
-      if (j > 0) {
-        // PV_{j-1} must be done: O is about to be rescaled and P overwritten
-        if (!mbar_wait(pv_done, (j - 1) & 1, 222)) {
-          ok = false;
-          break;
+        for (int c = 0; c < HDP / 16; ++c) {
+          SG_TMEM_LD_16(tmem + C::kColO + c * 16 + lane_off, u);
+          tmem_ld_wait();
+#pragma unroll
+          for (int k = 0; k < 16; ++k) u[k] = __float_as_uint(__uint_as_float(u[k]) * alpha);
+          SG_TMEM_ST_16(tmem + C::kColO + c * 16 + lane_off, u);
         }
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
-          uint32_t u[16];
+      }
+      // pass 2: P = exp2(S*scale - m) written over S_j: P column 16c+k holds
+      // keys 32c+2k (low half) and 32c+2k+1; chunk c only overwrites columns
+      // of chunks already read
+      float ps[8];
 #pragma unroll
-          for (int c = 0; c < HDP / 16; ++c) {
-            SG_TMEM_LD_16(tmem + kColO + c * 16 + lane_off, u);
-            tmem_ld_wait();
+      for (int i = 0; i < 8; ++i) ps[i] = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t u[32];
+        SG_TMEM_LD_32(tmem + c * 32 + lane_off, u);
+        tmem_ld_wait();
+        uint32_t w[16];
+        if (full_tile) {
 #pragma unroll
-            for (int k = 0; k < 16; ++k) u[k] = __float_as_uint(__uint_as_float(u[k]) * alpha);
-            SG_TMEM_ST_16(tmem + kColO + c * 16 + lane_off, u);
+          for (int k = 0; k < 16; ++k) {
+            const float p0 = ex2_approx(fmaf(__uint_as_float(u[2 * k]), sc, -m_use));
+            const float p1 = ex2_approx(fmaf(__uint_as_float(u[2 * k + 1]), sc, -m_use));
+            ps[k & 7] += p0 + p1;
+            w[k] = Pack2<T>::pack(p0, p1);
           }
-          tmem_st_wait();
-        }
-      }
-      // P row r -> two 64-key slabs, 128B swizzle (16B chunk c ^ (r & 7))
+        } else {
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        uint4 v;
-        v.x = Pack2<T>::pack(s[c * 8 + 0], s[c * 8 + 1]);
-        v.y = Pack2<T>::pack(s[c * 8 + 2], s[c * 8 + 3]);
-        v.z = Pack2<T>::pack(s[c * 8 + 4], s[c * 8 + 5]);
-        v.w = Pack2<T>::pack(s[c * 8 + 6], s[c * 8 + 7]);
-        const int slab = c >> 3, cc = c & 7;
-        *reinterpret_cast<uint4*>(P + slab * C::kSlabA + r * 128 + ((cc ^ (r & 7)) << 4)) = v;
+          for (int k = 0; k < 16; ++k) {
+            const int k0 = c * 32 + 2 * k;
+            const float x0 = k0 < valid ? __uint_as_float(u[2 * k]) : -INFINITY;
+            const float x1 = k0 + 1 < valid ? __uint_as_float(u[2 * k + 1]) : -INFINITY;
+            const float p0 = ex2_approx(fmaf(x0, sc, -m_use));
+            const float p1 = ex2_approx(fmaf(x1, sc, -m_use));
+            ps[k & 7] += p0 + p1;
+            w[k] = Pack2<T>::pack(p0, p1);
+          }
+        }
+        SG_TMEM_ST_16(tmem + c * 16 + lane_off, w);
       }
-      fence_proxy_async_smem();
+      const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+      l = l * alpha + rs;
+      tmem_st_wait();
       tc_fence_before();
       mbar_arrive(p_full);
     }
@@ -309,7 +321,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
       for (int c = 0; c < HDP / 16; ++c) {
         uint32_t u[16];
-        SG_TMEM_LD_16(tmem + kColO + c * 16 + lane_off, u);
+        SG_TMEM_LD_16(tmem + C::kColO + c * 16 + lane_off, u);
         tmem_ld_wait();
         if (row_ok) {
 #pragma unroll
@@ -334,7 +346,7 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+  if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
 }
 
 }  // namespace sg

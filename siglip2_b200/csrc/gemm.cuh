@@ -388,7 +388,8 @@ __global__ void __launch_bounds__(GemmThreads<(EPI == kEpiLn || EPI == kEpiLnGel
           *abort_flag = 1;
           break;
         }
-        float shift = 0.f, s1 = 0.f, s2 = 0.f;
+        // 4 independent (sum, sum of squares) pairs: no long FMA dependency chain
+        float shift = 0.f, s1v[4] = {0.f, 0.f, 0.f, 0.f}, s2v[4] = {0.f, 0.f, 0.f, 0.f};
         bool ok = true;
         for (int kb = 0; kb < nk; ++kb) {
           if (*abort_flag || !mbar_wait(&full[stage], phase, 132)) {
@@ -409,9 +410,9 @@ __global__ void __launch_bounds__(GemmThreads<(EPI == kEpiLn || EPI == kEpiLnGel
               const float2 f = Pack2<T>::unpack(w4[h]);
               if (kb == 0 && ch == 0 && h == 0) shift = f.x;
               const float a = f.x - shift, b = f.y - shift;
-              s1 += a + b;
-              s2 = fmaf(a, a, s2);
-              s2 = fmaf(b, b, s2);
+              s1v[h] += a + b;
+              s2v[h] = fmaf(a, a, s2v[h]);
+              s2v[h] = fmaf(b, b, s2v[h]);
             }
           }
           __syncwarp();
@@ -423,8 +424,8 @@ __global__ void __launch_bounds__(GemmThreads<(EPI == kEpiLn || EPI == kEpiLnGel
         }
         if (!ok) break;
         const float inv_k = 1.0f / static_cast<float>(p.K);
-        const float m1 = s1 * inv_k;
-        const float var = fmaxf(s2 * inv_k - m1 * m1, 0.f);
+        const float m1 = ((s1v[0] + s1v[1]) + (s1v[2] + s1v[3])) * inv_k;
+        const float var = fmaxf(((s2v[0] + s2v[1]) + (s2v[2] + s2v[3])) * inv_k - m1 * m1, 0.f);
         st_mean[buf * kGemmBM + r] = shift + m1;
         st_rstd[buf * kGemmBM + r] = rsqrtf(var + p.eps);
         mbar_arrive(&sfull[buf]);
