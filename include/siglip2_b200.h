@@ -70,6 +70,12 @@ const char* siglip2_last_error(void);
 /* Number of kernel launches this library has enqueued since it was loaded. */
 unsigned long long siglip2_launch_count(void);
 
+/* GEMM kernel selection for every later siglip2_gemm / siglip2_forward call of
+ * the process: 0 = automatic (default), 1 = one SM per 128 x BN tile,
+ * 2 = CTA pairs on two SMs per 256 x BN tile (tcgen05 cta_group::2). */
+int siglip2_set_gemm_variant(int variant);
+int siglip2_get_gemm_variant(void);
+
 /* Synchronises the current device and returns SIGLIP2_ERR_TIMEOUT if a kernel
  * gave up on a bounded wait since the last reset (the failing site id is in
  * siglip2_last_error()).  reset != 0 clears the flag. */

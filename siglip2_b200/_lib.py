@@ -20,6 +20,8 @@ SIGNATURES = {
     "siglip2_last_error": (ctypes.c_char_p, []),
     "siglip2_check_device": (_c_int, [_c_int]),
     "siglip2_launch_count": (ctypes.c_ulonglong, []),
+    "siglip2_set_gemm_variant": (_c_int, [_c_int]),
+    "siglip2_get_gemm_variant": (_c_int, []),
     "siglip2_gemm": (_c_int, [_c_int, _c_int, _vp, _c_int, _vp, _c_int, _vp, _c_int, _c_int, _c_int, _c_int,
                               _vp, _vp, _c_int, _vp, _vp, _c_float, _vp]),
     "siglip2_layernorm": (_c_int, [_c_int, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_float, _vp, _c_int, _vp]),

@@ -50,12 +50,18 @@ constexpr int kGemmBK = 64;     // 64 x 2B = one 128-byte swizzle row
 constexpr int kEpiCols = 32;    // epilogue chunk: 32 columns = one 64B-swizzled staging row
 constexpr int kEpiWarps = 4;
 
-template <int BN>
+// SUB = 64-wide K slabs per pipeline stage (1 or 2).  More K per stage means
+// fewer MMA-complete -> refill round trips per FLOP; measured on B200 the
+// round trip, not the stage count, limits the mainloop.
+template <int BN, int SUB = 1>
 struct GemmCfg {
-  static constexpr int kStageA = kGemmBM * kGemmBK * 2;
-  static constexpr int kStageB = BN * kGemmBK * 2;
+  static constexpr int kSub = SUB;
+  static constexpr int kSlabA = kGemmBM * kGemmBK * 2;
+  static constexpr int kSlabB = BN * kGemmBK * 2;
+  static constexpr int kStageA = kSlabA * SUB;
+  static constexpr int kStageB = kSlabB * SUB;
   static constexpr int kStageBytes = kStageA + kStageB;
-  static constexpr int kStages = (200 * 1024) / kStageBytes;  // 4 for BN=256, 5 for BN=192
+  static constexpr int kStages = (200 * 1024) / kStageBytes;  // BN=256: 4 (SUB 1) / 2 (SUB 2)
   static constexpr int kTmemCols = 512;                        // 2 accumulators, 256-column slots
   static constexpr int kAccStride = 256;
   static constexpr int kStaging = kEpiWarps * 2 * 32 * kEpiCols * 2;  // 2 x [32 rows][32 cols] per warp
@@ -93,16 +99,220 @@ __device__ __forceinline__ void load_param32(const float* __restrict__ p, int co
   }
 }
 
-template <typename T, int BN, int EPI>
+
+// Epilogue of one CTA (4 warps, warp & 3 = TMEM lane quarter = 32 rows each):
+// TMEM -> registers -> fused math -> 64B-swizzled staging -> TMA store, 32
+// columns per chunk, the residual (if any) arriving in the staging buffer by
+// TMA.  `row_base` is the first output row of this CTA's 128-row tile half;
+// `tempty_addr` is the shared::cluster address of the barrier that hands the
+// accumulator back to the MMA issuer.
+template <typename T, int BN, int EPI, bool kCluster>
+__device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtensorMap* tmO, const CUtensorMap* tmR,
+                                              uint32_t tmem_base, uint32_t acc_stride, uint8_t* staging,
+                                              uint64_t* resbar, uint64_t* tfull, uint32_t tempty_addr0,
+                                              uint32_t tempty_addr1, uint64_t* sfull, uint64_t* sempty,
+                                              const float* st_mean, const float* st_rstd, volatile int* abort_flag,
+                                              int warp, int lane, int first_tile, int tile_step, int num_tiles,
+                                              int n_tiles, int rows_per_tile, int row_offset) {
+  constexpr bool kLN = (EPI == kEpiLn || EPI == kEpiLnGelu);
+  constexpr bool kRes = (EPI == kEpiBiasRes);
+  constexpr int NCH = BN / kEpiCols;
+  const int ew = warp - 2;
+  const int q = warp & 3;
+  const int row_in_tile = q * 32 + lane;
+  uint8_t* stg = staging + ew * (2 * 32 * kEpiCols * 2);
+  uint64_t* rbar = resbar + 2 * ew;
+  uint32_t rph0 = 0, rph1 = 0;
+  int t = 0;
+  for (int tile = first_tile; tile < num_tiles; tile += tile_step, ++t) {
+    const int buf = t & 1;
+    const uint32_t tph = (t >> 1) & 1;
+    const int m0 = (tile / n_tiles) * rows_per_tile + row_offset;
+    const int n0 = (tile % n_tiles) * BN;
+    if (*abort_flag || !mbar_wait<kCluster>(&tfull[buf], tph, 121)) {
+      *abort_flag = 1;
+      break;
+    }
+    tc_fence_after();
+    float mu = 0.f, rstd = 1.f;
+    if constexpr (kLN) {
+      if (!mbar_wait(&sfull[buf], tph, 122)) {
+        *abort_flag = 1;
+        break;
+      }
+      mu = st_mean[buf * kGemmBM + row_in_tile];
+      rstd = st_rstd[buf * kGemmBM + row_in_tile];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sempty[buf]);
+    }
+    const int row0 = m0 + q * 32;
+    const uint32_t tbase = tmem_base + buf * acc_stride + (static_cast<uint32_t>(q * 32) << 16);
+    uint32_t ra[32], rb[32];
+    SG_TMEM_LD_32(tbase, ra);
+    tmem_ld_wait();
+    SG_REG_FENCE_32(ra);
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      uint32_t* cur = (c & 1) ? rb : ra;
+      uint32_t* nxt = (c & 1) ? ra : rb;
+      if (c + 1 < NCH) SG_TMEM_LD_32(tbase + (c + 1) * kEpiCols, nxt);
+      const int col0 = n0 + c * kEpiCols;
+      const int sb = c & 1;  // staging buffer
+      uint8_t* sbuf = stg + sb * (32 * kEpiCols * 2);
+      // the store issued from this buffer two chunks ago must have read it
+      if (lane == 0) tma_store_wait_read<1>();
+      __syncwarp();
+      if constexpr (kRes) {
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&rbar[sb], 32 * kEpiCols * 2);
+          tma_load_2d(sbuf, tmR, &rbar[sb], col0, row0);
+        }
+      }
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(cur[j]);
+      if (col0 < p.N) {
+        if constexpr (kLN) {
+          float a[32], b[32];
+          load_param32(p.c1, col0, p.N, a);
+          load_param32(p.c2, col0, p.N, b);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            v[j] = fmaf(rstd, fmaf(-mu, a[j], v[j]), b[j]);
+            if constexpr (EPI == kEpiLnGelu) v[j] = gelu_tanh(v[j]);
+          }
+        } else {
+          float a[32];
+          load_param32(p.bias, col0, p.N, a);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            v[j] += a[j];
+            if constexpr (EPI == kEpiBiasGelu) v[j] = gelu_tanh(v[j]);
+          }
+        }
+      }
+      // 64B-swizzled staging: 16B chunk g of row r lives at chunk g ^ ((r >> 1) & 3)
+      const int sw = (lane >> 1) & 3;
+      uint8_t* srow = sbuf + lane * (kEpiCols * 2);
+      if constexpr (kRes) {
+        const uint32_t ph = sb ? rph1 : rph0;
+        if (!mbar_wait(&rbar[sb], ph, 123)) *abort_flag = 1;
+        if (sb) rph1 ^= 1; else rph0 ^= 1;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const uint4 rv = *reinterpret_cast<const uint4*>(srow + ((g ^ sw) << 4));
+          const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const float2 f = Pack2<T>::unpack(rw[h]);
+            v[g * 8 + 2 * h] += f.x;
+            v[g * 8 + 2 * h + 1] += f.y;
+          }
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        uint4 o;
+        o.x = Pack2<T>::pack(v[g * 8 + 0], v[g * 8 + 1]);
+        o.y = Pack2<T>::pack(v[g * 8 + 2], v[g * 8 + 3]);
+        o.z = Pack2<T>::pack(v[g * 8 + 4], v[g * 8 + 5]);
+        o.w = Pack2<T>::pack(v[g * 8 + 6], v[g * 8 + 7]);
+        *reinterpret_cast<uint4*>(srow + ((g ^ sw) << 4)) = o;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && col0 < p.N && row0 < p.M) {
+        tma_store_2d(tmO, sbuf, col0, row0);
+      }
+      if (lane == 0) tma_store_commit();
+      if (c + 1 < NCH) {
+        tmem_ld_wait();
+        SG_REG_FENCE_32(nxt);
+      } else {
+        // accumulator fully read: hand the TMEM buffer back to the MMA issuer
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(buf ? tempty_addr1 : tempty_addr0);
+      }
+    }
+  }
+  if (lane == 0) tma_store_wait_all<0>();
+  __syncwarp();
+}
+
+// LayerNorm row statistics of the A tiles (warps 6-9; thread r = row r of
+// this CTA's 128-row A half).  `ready[s]` signals that stage s has landed.
+template <typename T, int STAGES, int SUB, bool kCluster>
+__device__ __forceinline__ void gemm_row_stats(const GemmParams& p, const uint8_t* smA, int stage_a_bytes,
+                                               uint64_t* ready, uint64_t* empty, uint64_t* sfull, uint64_t* sempty,
+                                               float* st_mean, float* st_rstd, volatile int* abort_flag, int r,
+                                               int lane, int first_tile, int tile_step, int num_tiles, int nk) {
+  int stage = 0;
+  uint32_t phase = 0;
+  int t = 0;
+  for (int tile = first_tile; tile < num_tiles; tile += tile_step, ++t) {
+    const int buf = t & 1;
+    const uint32_t tph = (t >> 1) & 1;
+    if (*abort_flag || !mbar_wait(&sempty[buf], tph ^ 1, 131)) {
+      *abort_flag = 1;
+      break;
+    }
+    // 4 independent (sum, sum of squares) pairs: no long FMA dependency chain
+    float shift = 0.f, s1v[4] = {0.f, 0.f, 0.f, 0.f}, s2v[4] = {0.f, 0.f, 0.f, 0.f};
+    bool ok = true;
+    for (int kb = 0; kb < nk; ++kb) {
+      if (*abort_flag || !mbar_wait<kCluster>(&ready[stage], phase, 132)) {
+        ok = false;
+        *abort_flag = 1;
+        break;
+      }
+#pragma unroll
+      for (int sub = 0; sub < SUB; ++sub) {
+      const uint8_t* rowp = smA + stage * stage_a_bytes + sub * (kGemmBM * 128) + r * 128;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        // the 128B swizzle permutes the 16B chunks of a row; the sum does
+        // not care about order, and reading chunk ch ^ (r & 7) puts the 8
+        // rows of each 8-lane phase on 8 different bank groups
+        const uint4 u = *reinterpret_cast<const uint4*>(rowp + ((ch ^ (r & 7)) << 4));
+        const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float2 f = Pack2<T>::unpack(w4[h]);
+          if (kb == 0 && sub == 0 && ch == 0 && h == 0) shift = f.x;
+          const float a = f.x - shift, b = f.y - shift;
+          s1v[h] += a + b;
+          s2v[h] = fmaf(a, a, s2v[h]);
+          s2v[h] = fmaf(b, b, s2v[h]);
+        }
+      }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[stage]);
+      if (++stage == STAGES) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+    if (!ok) break;
+    const float inv_k = 1.0f / static_cast<float>(p.K);
+    const float m1 = ((s1v[0] + s1v[1]) + (s1v[2] + s1v[3])) * inv_k;
+    const float var = fmaxf(((s2v[0] + s2v[1]) + (s2v[2] + s2v[3])) * inv_k - m1 * m1, 0.f);
+    st_mean[buf * kGemmBM + r] = shift + m1;
+    st_rstd[buf * kGemmBM + r] = rsqrtf(var + p.eps);
+    mbar_arrive(&sfull[buf]);
+  }
+}
+
+template <typename T, int BN, int EPI, int SUB>
 __global__ void __launch_bounds__(GemmThreads<(EPI == kEpiLn || EPI == kEpiLnGelu)>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
                    const GemmParams p) {
   constexpr bool kLN = (EPI == kEpiLn || EPI == kEpiLnGelu);
   constexpr bool kRes = (EPI == kEpiBiasRes);
-  using Cfg = GemmCfg<BN>;
+  using Cfg = GemmCfg<BN, SUB>;
   constexpr int STAGES = Cfg::kStages;
-  constexpr int NCH = BN / kEpiCols;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kIdesc = make_idesc(kGemmBM, BN, kBF16, false, false);
 
@@ -130,7 +340,7 @@ __global__ void __launch_bounds__(GemmThreads<(EPI == kEpiLn || EPI == kEpiLnGel
   const int m_tiles = (p.M + kGemmBM - 1) / kGemmBM;
   const int n_tiles = (p.N + BN - 1) / BN;
   const int num_tiles = m_tiles * n_tiles;
-  const int nk = (p.K + kGemmBK - 1) / kGemmBK;
+  const int nk = (p.K + kGemmBK * SUB - 1) / (kGemmBK * SUB);  // pipeline stages per tile
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -180,8 +390,12 @@ __global__ void __launch_bounds__(GemmThreads<(EPI == kEpiLn || EPI == kEpiLnGel
             break;
           }
           mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
-          tma_load_2d(smA + stage * Cfg::kStageA, &tmA, &full[stage], kb * kGemmBK, m0);
-          tma_load_2d(smB + stage * Cfg::kStageB, &tmB, &full[stage], kb * kGemmBK, n0);
+#pragma unroll
+          for (int sub = 0; sub < SUB; ++sub) {
+            const int kx = (kb * SUB + sub) * kGemmBK;
+            tma_load_2d(smA + stage * Cfg::kStageA + sub * Cfg::kSlabA, &tmA, &full[stage], kx, m0);
+            tma_load_2d(smB + stage * Cfg::kStageB + sub * Cfg::kSlabB, &tmB, &full[stage], kx, n0);
+          }
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -229,9 +443,12 @@ __global__ void __launch_bounds__(GemmThreads<(EPI == kEpiLn || EPI == kEpiLnGel
           const uint32_t a_base = smem_u32(smA + stage * Cfg::kStageA);
           const uint32_t b_base = smem_u32(smB + stage * Cfg::kStageB);
 #pragma unroll
-          for (int k = 0; k < kGemmBK / 16; ++k) {
-            umma_ss(d_tmem, kmajor_desc(a_base + k * 32, 128), kmajor_desc(b_base + k * 32, 128), kIdesc,
-                    (kb | k) != 0);
+          for (int sub = 0; sub < SUB; ++sub) {
+#pragma unroll
+            for (int k = 0; k < kGemmBK / 16; ++k) {
+              umma_ss(d_tmem, kmajor_desc(a_base + sub * Cfg::kSlabA + k * 32, 128),
+                      kmajor_desc(b_base + sub * Cfg::kSlabB + k * 32, 128), kIdesc, (kb | sub | k) != 0);
+            }
           }
           umma_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -253,183 +470,16 @@ __global__ void __launch_bounds__(GemmThreads<(EPI == kEpiLn || EPI == kEpiLnGel
     // those 32 rows of the tile, 32 columns per chunk.  Each chunk goes
     // TMEM -> registers -> fused math -> 64B-swizzled staging -> TMA store
     // (the residual, if any, arrives in the same staging buffer by TMA).
-    const int ew = warp - 2;
-    const int q = warp & 3;
-    const int row_in_tile = q * 32 + lane;
-    uint8_t* stg = staging + ew * (2 * 32 * kEpiCols * 2);
-    uint64_t* rbar = resbar + 2 * ew;
-    uint32_t rph0 = 0, rph1 = 0;
-    int t = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
-      const int buf = t & 1;
-      const uint32_t tph = (t >> 1) & 1;
-      const int m0 = (tile / n_tiles) * kGemmBM;
-      const int n0 = (tile % n_tiles) * BN;
-      if (*abort_flag || !mbar_wait(&tfull[buf], tph, 121)) {
-        *abort_flag = 1;
-        break;
-      }
-      tc_fence_after();
-      float mu = 0.f, rstd = 1.f;
-      if constexpr (kLN) {
-        if (!mbar_wait(&sfull[buf], tph, 122)) {
-          *abort_flag = 1;
-          break;
-        }
-        mu = st_mean[buf * kGemmBM + row_in_tile];
-        rstd = st_rstd[buf * kGemmBM + row_in_tile];
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sempty[buf]);
-      }
-      const int row0 = m0 + q * 32;
-      const uint32_t tbase = tmem_base + buf * Cfg::kAccStride + (static_cast<uint32_t>(q * 32) << 16);
-      uint32_t ra[32], rb[32];
-      SG_TMEM_LD_32(tbase, ra);
-      tmem_ld_wait();
-      SG_REG_FENCE_32(ra);
-#pragma unroll
-      for (int c = 0; c < NCH; ++c) {
-        uint32_t* cur = (c & 1) ? rb : ra;
-        uint32_t* nxt = (c & 1) ? ra : rb;
-        if (c + 1 < NCH) SG_TMEM_LD_32(tbase + (c + 1) * kEpiCols, nxt);
-        const int col0 = n0 + c * kEpiCols;
-        const int sb = c & 1;  // staging buffer
-        uint8_t* sbuf = stg + sb * (32 * kEpiCols * 2);
-        // the store issued from this buffer two chunks ago must have read it
-        if (lane == 0) tma_store_wait_read<1>();
-        __syncwarp();
-        if constexpr (kRes) {
-          if (lane == 0) {
-            mbar_arrive_expect_tx(&rbar[sb], 32 * kEpiCols * 2);
-            tma_load_2d(sbuf, &tmR, &rbar[sb], col0, row0);
-          }
-        }
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(cur[j]);
-        if (col0 < p.N) {
-          if constexpr (kLN) {
-            float a[32], b[32];
-            load_param32(p.c1, col0, p.N, a);
-            load_param32(p.c2, col0, p.N, b);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              v[j] = fmaf(rstd, fmaf(-mu, a[j], v[j]), b[j]);
-              if constexpr (EPI == kEpiLnGelu) v[j] = gelu_tanh(v[j]);
-            }
-          } else {
-            float a[32];
-            load_param32(p.bias, col0, p.N, a);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              v[j] += a[j];
-              if constexpr (EPI == kEpiBiasGelu) v[j] = gelu_tanh(v[j]);
-            }
-          }
-        }
-        // 64B-swizzled staging: 16B chunk g of row r lives at chunk g ^ ((r >> 1) & 3)
-        const int sw = (lane >> 1) & 3;
-        uint8_t* srow = sbuf + lane * (kEpiCols * 2);
-        if constexpr (kRes) {
-          const uint32_t ph = sb ? rph1 : rph0;
-          if (!mbar_wait(&rbar[sb], ph, 123)) *abort_flag = 1;
-          if (sb) rph1 ^= 1; else rph0 ^= 1;
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const uint4 rv = *reinterpret_cast<const uint4*>(srow + ((g ^ sw) << 4));
-            const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
-#pragma unroll
-            for (int h = 0; h < 4; ++h) {
-              const float2 f = Pack2<T>::unpack(rw[h]);
-              v[g * 8 + 2 * h] += f.x;
-              v[g * 8 + 2 * h + 1] += f.y;
-            }
-          }
-        }
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          uint4 o;
-          o.x = Pack2<T>::pack(v[g * 8 + 0], v[g * 8 + 1]);
-          o.y = Pack2<T>::pack(v[g * 8 + 2], v[g * 8 + 3]);
-          o.z = Pack2<T>::pack(v[g * 8 + 4], v[g * 8 + 5]);
-          o.w = Pack2<T>::pack(v[g * 8 + 6], v[g * 8 + 7]);
-          *reinterpret_cast<uint4*>(srow + ((g ^ sw) << 4)) = o;
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0 && col0 < p.N && row0 < p.M) {
-          tma_store_2d(&tmO, sbuf, col0, row0);
-        }
-        if (lane == 0) tma_store_commit();
-        if (c + 1 < NCH) {
-          tmem_ld_wait();
-          SG_REG_FENCE_32(nxt);
-        } else {
-          // accumulator fully read: hand the TMEM buffer back to the MMA warp
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[buf]);
-        }
-      }
-    }
-    if (lane == 0) tma_store_wait_all<0>();
-    __syncwarp();
+    const uint32_t te0 = mapa_shared(smem_u32(&tempty[0]), 0), te1 = mapa_shared(smem_u32(&tempty[1]), 0);
+    gemm_epilogue<T, BN, EPI, false>(p, &tmO, &tmR, tmem_base, Cfg::kAccStride, staging, resbar, tfull, te0, te1,
+                                     sfull, sempty, st_mean, st_rstd, abort_flag, warp, lane, blockIdx.x, gridDim.x,
+                                     num_tiles, n_tiles, kGemmBM, 0);
   } else {
     // ------------------------------------------------------------ LayerNorm row statistics
     if constexpr (kLN) {
-      const int r = threadIdx.x - (2 + kEpiWarps) * 32;  // 0..127: row within the tile
-      int stage = 0;
-      uint32_t phase = 0;
-      int t = 0;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
-        const int buf = t & 1;
-        const uint32_t tph = (t >> 1) & 1;
-        if (*abort_flag || !mbar_wait(&sempty[buf], tph ^ 1, 131)) {
-          *abort_flag = 1;
-          break;
-        }
-        // 4 independent (sum, sum of squares) pairs: no long FMA dependency chain
-        float shift = 0.f, s1v[4] = {0.f, 0.f, 0.f, 0.f}, s2v[4] = {0.f, 0.f, 0.f, 0.f};
-        bool ok = true;
-        for (int kb = 0; kb < nk; ++kb) {
-          if (*abort_flag || !mbar_wait(&full[stage], phase, 132)) {
-            ok = false;
-            *abort_flag = 1;
-            break;
-          }
-          const uint8_t* rowp = smA + stage * Cfg::kStageA + r * 128;
-#pragma unroll
-          for (int ch = 0; ch < 8; ++ch) {
-            // the 128B swizzle permutes the 16B chunks of a row; the sum does
-            // not care about order, and reading chunk ch ^ (r & 7) puts the 8
-            // rows of each 8-lane phase on 8 different bank groups
-            const uint4 u = *reinterpret_cast<const uint4*>(rowp + ((ch ^ (r & 7)) << 4));
-            const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-            for (int h = 0; h < 4; ++h) {
-              const float2 f = Pack2<T>::unpack(w4[h]);
-              if (kb == 0 && ch == 0 && h == 0) shift = f.x;
-              const float a = f.x - shift, b = f.y - shift;
-              s1v[h] += a + b;
-              s2v[h] = fmaf(a, a, s2v[h]);
-              s2v[h] = fmaf(b, b, s2v[h]);
-            }
-          }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&empty[stage]);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
-          }
-        }
-        if (!ok) break;
-        const float inv_k = 1.0f / static_cast<float>(p.K);
-        const float m1 = ((s1v[0] + s1v[1]) + (s1v[2] + s1v[3])) * inv_k;
-        const float var = fmaxf(((s2v[0] + s2v[1]) + (s2v[2] + s2v[3])) * inv_k - m1 * m1, 0.f);
-        st_mean[buf * kGemmBM + r] = shift + m1;
-        st_rstd[buf * kGemmBM + r] = rsqrtf(var + p.eps);
-        mbar_arrive(&sfull[buf]);
-      }
+      gemm_row_stats<T, STAGES, SUB, false>(p, smA, Cfg::kStageA, full, empty, sfull, sempty, st_mean, st_rstd,
+                                       abort_flag, threadIdx.x - (2 + kEpiWarps) * 32, lane, blockIdx.x, gridDim.x,
+                                       num_tiles, nk);
     }
   }
 
@@ -438,6 +488,225 @@ __global__ void __launch_bounds__(GemmThreads<(EPI == kEpiLn || EPI == kEpiLnGel
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, Cfg::kTmemCols);
+}
+
+
+// ============================================================================
+// 2-SM variant: a CTA pair (cluster of 2) computes a 256 x BN tile with
+// tcgen05.mma.cta_group::2.  Each CTA's smem holds its 128 rows of A and its
+// BN/2 rows of B for every stage (same offsets in both CTAs); both CTAs load
+// their own halves with plain TMA copies whose completion bytes go to the
+// leader's (rank 0) full barrier.  The leader alone issues the MMAs and
+// multicast-commits the stage-free and accumulator-ready barriers to both
+// CTAs; each CTA drains its own 128 rows of the accumulator from its own TMEM
+// and reports back to the leader's accumulator-free barrier.  Per SM this
+// halves the B operand's shared-memory footprint and traffic.
+// ============================================================================
+template <int BN, int SUB = 1>
+struct Gemm2Cfg {
+  static constexpr int kSub = SUB;
+  static constexpr int kSlabA = kGemmBM * kGemmBK * 2;          // this CTA's 128 rows of A
+  static constexpr int kSlabB = (BN / 2) * kGemmBK * 2;         // this CTA's half of B
+  static constexpr int kStageA = kSlabA * SUB;
+  static constexpr int kStageB = kSlabB * SUB;
+  static constexpr int kStageBytes = kStageA + kStageB;
+  static constexpr int kStages = (196 * 1024) / kStageBytes;    // BN=256: 6 (SUB 1) / 3 (SUB 2)
+  static constexpr int kTmemCols = 512;
+  static constexpr int kAccStride = 256;
+  static constexpr int kStaging = kEpiWarps * 2 * 32 * kEpiCols * 2;
+  static constexpr int kOffStaging = kStages * kStageBytes;
+  static constexpr int kOffBars = kOffStaging + kStaging;
+  static constexpr int kOffStats = kOffBars + 1024;
+  static constexpr int kSmemBytes = kOffStats + 2 * 2 * kGemmBM * 4 + 1024;
+};
+
+template <typename T, int BN, int EPI, int SUB>
+__global__ void __launch_bounds__(GemmThreads<(EPI == kEpiLn || EPI == kEpiLnGelu)>::kThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
+                    const GemmParams p) {
+  constexpr bool kLN = (EPI == kEpiLn || EPI == kEpiLnGelu);
+  constexpr bool kRes = (EPI == kEpiBiasRes);
+  using Cfg = Gemm2Cfg<BN, SUB>;
+  constexpr int STAGES = Cfg::kStages;
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t kIdesc = make_idesc(2 * kGemmBM, BN, kBF16, false, false);
+  constexpr int kTileRows = 2 * kGemmBM;
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smA = smem;
+  uint8_t* smB = smem + STAGES * Cfg::kStageA;
+  uint8_t* staging = smem + Cfg::kOffStaging;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBars);
+  uint64_t* full = bars;                 // [STAGES] leader: both CTAs' halves landed
+  uint64_t* empty = bars + STAGES;       // [STAGES] both: stage free (MMA commit + stats warps)
+  uint64_t* aready = empty + STAGES;     // [STAGES] both: stage landed (forwarded for the stats warps)
+  uint64_t* tfull = aready + STAGES;     // [2] both: accumulator ready
+  uint64_t* tempty = tfull + 2;          // [2] leader: accumulator drained by both CTAs
+  uint64_t* sfull = tempty + 2;          // [2]
+  uint64_t* sempty = sfull + 2;          // [2]
+  uint64_t* mdone = sempty + 2;          // [1]
+  uint64_t* resbar = mdone + 1;          // [kEpiWarps][2]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(resbar + 2 * kEpiWarps);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  float* st_mean = reinterpret_cast<float*>(smem + Cfg::kOffStats);
+  float* st_rstd = st_mean + 2 * kGemmBM;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+  const int m_tiles = (p.M + kTileRows - 1) / kTileRows;
+  const int n_tiles = (p.N + BN - 1) / BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int nk = (p.K + kGemmBK * SUB - 1) / (kGemmBK * SUB);  // pipeline stages per tile
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kLN ? 5 : 1);
+      mbar_init(&aready[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 2 * kEpiWarps);
+      mbar_init(&sfull[b], kGemmBM);
+      mbar_init(&sempty[b], kEpiWarps);
+    }
+    mbar_init(mdone, 1);
+    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&resbar[i], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmO);
+    if (kRes) tma_prefetch_desc(&tmR);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_holder, Cfg::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers initialised before any remote signal
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
+        const int m0 = (tile / n_tiles) * kTileRows + static_cast<int>(rank) * kGemmBM;
+        const int n0 = (tile % n_tiles) * BN + static_cast<int>(rank) * (BN / 2);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (*abort_flag || !mbar_wait<true>(&empty[stage], phase ^ 1, 141)) {
+            ok = false;
+            *abort_flag = 1;
+            break;
+          }
+          const uint32_t fbar = mapa_shared(smem_u32(&full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::kStageBytes);
+#pragma unroll
+          for (int sub = 0; sub < SUB; ++sub) {
+            const int kx = (kb * SUB + sub) * kGemmBK;
+            tma_load_2d_pair(smA + stage * Cfg::kStageA + sub * Cfg::kSlabA, &tmA, fbar, kx, m0);
+            tma_load_2d_pair(smB + stage * Cfg::kStageB + sub * Cfg::kSlabB, &tmB, fbar, kx, n0);
+          }
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Tail: every stage released again means every load landed and was consumed.
+      for (int i = 0; i < STAGES && i < issued; ++i) {
+        mbar_wait<true>(&empty[stage], phase ^ 1, 142);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (lane == 0 && leader) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int t = 0;
+      bool ok = true;
+      const uint32_t peer_aready0 = mapa_shared(smem_u32(&aready[0]), 1);
+      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs, ++t) {
+        const int buf = t & 1;
+        const uint32_t tph = (t >> 1) & 1;
+        if (*abort_flag || !mbar_wait<true>(&tempty[buf], tph ^ 1, 151)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * Cfg::kAccStride;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (*abort_flag || !mbar_wait<true>(&full[stage], phase, 152)) {
+            ok = false;
+            *abort_flag = 1;
+            break;
+          }
+          if constexpr (kLN) {
+            // tell both CTAs' statistics warps that their A half landed
+            mbar_arrive(&aready[stage]);
+            mbar_arrive_cluster(peer_aready0 + stage * 8);
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smA + stage * Cfg::kStageA);
+          const uint32_t b_base = smem_u32(smB + stage * Cfg::kStageB);
+#pragma unroll
+          for (int sub = 0; sub < SUB; ++sub) {
+#pragma unroll
+            for (int k = 0; k < kGemmBK / 16; ++k) {
+              umma_ss_pair(d_tmem, kmajor_desc(a_base + sub * Cfg::kSlabA + k * 32, 128),
+                           kmajor_desc(b_base + sub * Cfg::kSlabB + k * 32, 128), kIdesc, (kb | sub | k) != 0);
+            }
+          }
+          umma_commit_pair_mc(&empty[stage], 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair_mc(&tfull[buf], 0x3);
+      }
+      umma_commit_pair(mdone);
+      mbar_wait<true>(mdone, 0, 153);
+    }
+  } else if (warp < 2 + kEpiWarps) {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const uint32_t te0 = mapa_shared(smem_u32(&tempty[0]), 0), te1 = mapa_shared(smem_u32(&tempty[1]), 0);
+    gemm_epilogue<T, BN, EPI, true>(p, &tmO, &tmR, tmem_base, Cfg::kAccStride, staging, resbar, tfull, te0, te1,
+                                    sfull, sempty, st_mean, st_rstd, abort_flag, warp, lane, pair, num_pairs,
+                                    num_tiles, n_tiles, kTileRows, static_cast<int>(rank) * kGemmBM);
+  } else {
+    // ------------------------------------------------------------ LayerNorm row statistics (both CTAs)
+    if constexpr (kLN) {
+      gemm_row_stats<T, STAGES, SUB, true>(p, smA, Cfg::kStageA, aready, empty, sfull, sempty, st_mean, st_rstd,
+                                      abort_flag, threadIdx.x - (2 + kEpiWarps) * 32, lane, pair, num_pairs,
+                                      num_tiles, nk);
+    }
+  }
+
+  // ---------------------------------------------------------------- teardown
+  tc_fence_before();
+  cluster_sync();  // no remote arrive or TMA completion may target an exited CTA
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
 }
 
 }  // namespace sg

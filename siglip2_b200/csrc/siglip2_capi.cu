@@ -26,7 +26,7 @@ struct GemmIO {
   int ldr;
 };
 
-template <typename T, int BN, int EPI>
+template <typename T, int BN, int EPI, int SUB>
 int launch_gemm_tc(const GemmIO& io, const GemmParams& p, cudaStream_t stream) {
   CUtensorMap ta, tb, to, tr;
   SG_TRY(make_tmap_2d(&ta, io.a, 2, p.M, p.K, io.lda, kGemmBM, kGemmBK));
@@ -36,8 +36,8 @@ int launch_gemm_tc(const GemmIO& io, const GemmParams& p, cudaStream_t stream) {
   else tr = to;
   constexpr bool kLN = (EPI == kEpiLn || EPI == kEpiLnGelu);
   constexpr int threads = GemmThreads<kLN>::kThreads;
-  constexpr int smem = GemmCfg<BN>::kSmemBytes;
-  auto kern = gemm_tc_kernel<T, BN, EPI>;
+  constexpr int smem = GemmCfg<BN, SUB>::kSmemBytes;
+  auto kern = gemm_tc_kernel<T, BN, EPI, SUB>;
   static bool attr_done = false;  // per instantiation
   if (!attr_done) {
     SG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
@@ -50,14 +50,67 @@ int launch_gemm_tc(const GemmIO& io, const GemmParams& p, cudaStream_t stream) {
   return SIGLIP2_OK;
 }
 
+// 2-SM variant: clusters of 2 CTAs, one pair per 2 SMs, 256 x BN tiles.
+template <typename T, int BN, int EPI, int SUB>
+int launch_gemm_tc2(const GemmIO& io, const GemmParams& p, cudaStream_t stream) {
+  CUtensorMap ta, tb, to, tr;
+  SG_TRY(make_tmap_2d(&ta, io.a, 2, p.M, p.K, io.lda, kGemmBM, kGemmBK));
+  SG_TRY(make_tmap_2d(&tb, io.b, 2, p.N, p.K, io.ldb, BN / 2, kGemmBK));
+  SG_TRY(make_tmap_2d(&to, io.out, 2, p.M, p.N, io.ldo, 32, kEpiCols));
+  if (EPI == kEpiBiasRes) SG_TRY(make_tmap_2d(&tr, io.res, 2, p.M, p.N, io.ldr, 32, kEpiCols));
+  else tr = to;
+  constexpr bool kLN = (EPI == kEpiLn || EPI == kEpiLnGelu);
+  constexpr int threads = GemmThreads<kLN>::kThreads;
+  constexpr int smem = Gemm2Cfg<BN, SUB>::kSmemBytes;
+  auto kern = gemm_tc2_kernel<T, BN, EPI, SUB>;
+  static bool attr_done = false;  // per instantiation
+  if (!attr_done) {
+    SG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr_done = true;
+  }
+  const int tiles = ((p.M + 2 * kGemmBM - 1) / (2 * kGemmBM)) * ((p.N + BN - 1) / BN);
+  const int pairs = std::min(tiles, sm_count() / 2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  SG_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, to, tr, p));
+  SG_LAUNCH_CHECK();
+  return SIGLIP2_OK;
+}
+
+// GEMM kernel selection: 0 = automatic, 1 = one SM per tile, 2 = SM pairs.
+std::atomic<int> g_gemm_variant{0};
+
+// Automatic choice (measured on B200 at the tower's shapes, K = 128 per stage
+// in both): LayerNorm-folded GEMMs on one SM per tile (their statistics warps
+// read the A stage locally), the others on SM pairs.
+template <typename T, int BN, int EPI>
+int launch_gemm_any(const GemmIO& io, const GemmParams& p, cudaStream_t s) {
+  constexpr bool kLN = (EPI == kEpiLn || EPI == kEpiLnGelu);
+  int v = g_gemm_variant.load();
+  if (v == 0) v = kLN ? 1 : 2;
+  if (v == 2) return launch_gemm_tc2<T, BN, EPI, 2>(io, p, s);
+  if (BN == 256) return launch_gemm_tc<T, BN, EPI, 2>(io, p, s);
+  return launch_gemm_tc<T, BN, EPI, 1>(io, p, s);  // BN=192 keeps 5 stages of K=64
+}
+
 template <typename T, int BN>
 int dispatch_epi(int epi, const GemmIO& io, const GemmParams& p, cudaStream_t s) {
   switch (epi) {
-    case kEpiBias: return launch_gemm_tc<T, BN, kEpiBias>(io, p, s);
-    case kEpiBiasRes: return launch_gemm_tc<T, BN, kEpiBiasRes>(io, p, s);
-    case kEpiLn: return launch_gemm_tc<T, BN, kEpiLn>(io, p, s);
-    case kEpiLnGelu: return launch_gemm_tc<T, BN, kEpiLnGelu>(io, p, s);
-    case kEpiBiasGelu: return launch_gemm_tc<T, BN, kEpiBiasGelu>(io, p, s);
+    case kEpiBias: return launch_gemm_any<T, BN, kEpiBias>(io, p, s);
+    case kEpiBiasRes: return launch_gemm_any<T, BN, kEpiBiasRes>(io, p, s);
+    case kEpiLn: return launch_gemm_any<T, BN, kEpiLn>(io, p, s);
+    case kEpiLnGelu: return launch_gemm_any<T, BN, kEpiLnGelu>(io, p, s);
+    case kEpiBiasGelu: return launch_gemm_any<T, BN, kEpiBiasGelu>(io, p, s);
     default: return set_error(SIGLIP2_ERR_ARG, "unknown epilogue %d", epi);
   }
 }
@@ -416,6 +469,14 @@ int siglip2_version(void) { return 100; }
 const char* siglip2_last_error(void) { return t_last_error; }
 
 unsigned long long siglip2_launch_count(void) { return launch_counter().load(); }
+
+int siglip2_set_gemm_variant(int variant) {
+  SG_CHECK_ARG(variant >= 0 && variant <= 2, "GEMM variant must be 0 (auto), 1 (1-SM) or 2 (SM pairs)");
+  g_gemm_variant.store(variant);
+  return SIGLIP2_OK;
+}
+
+int siglip2_get_gemm_variant(void) { return g_gemm_variant.load(); }
 
 int siglip2_check_device(int reset) {
   SG_CUDA(cudaDeviceSynchronize());

@@ -104,7 +104,10 @@ def main():
     y.add_argument("--images", type=int, default=64)
     y.add_argument("--max-patches", type=int, default=1024)
     y.add_argument("--reps", type=int, default=20)
+    for sp in (g, f, y):
+        sp.add_argument("--variant", type=int, default=0, help="GEMM kernel: 0 auto, 1 one SM, 2 SM pairs")
     a = ap.parse_args()
+    L.check(L.load().siglip2_set_gemm_variant(a.variant))
     if a.cmd == "gemm":
         print(json.dumps(bench_gemm(a.m, a.n, a.k, a.epi, a.reps, warmup=a.warmup)))
     elif a.cmd == "fmha":

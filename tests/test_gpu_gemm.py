@@ -11,6 +11,17 @@ from siglip2_b200 import _lib as L  # noqa: E402
 from siglip2_b200 import ops  # noqa: E402
 
 
+@pytest.fixture(params=[1, 2], ids=["1sm", "2sm"], autouse=True)
+def gemm_variant(request):
+    """Every GEMM test runs on both kernels: one SM per 128-row tile and
+    CTA pairs (tcgen05 cta_group::2) per 256-row tile."""
+    lib = L.load()
+    old = lib.siglip2_get_gemm_variant()
+    L.check(lib.siglip2_set_gemm_variant(request.param))
+    yield request.param
+    L.check(lib.siglip2_set_gemm_variant(old))
+
+
 def _gelu(x):
     return F.gelu(x, approximate="tanh")
 
