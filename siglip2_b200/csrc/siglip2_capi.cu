@@ -290,6 +290,40 @@ int sg_fmha_impl(int dtype, const void* qkv, int N, const int* cu, const int* ti
 // ---------------------------------------------------------------------------
 // head + forward
 // ---------------------------------------------------------------------------
+template <typename T>
+int launch_head_pool_parallel(const void* x, int D, int H, const int* cu, int B, int pad_P, const int* tok_img, int N,
+                              const float* u, float* scores, void* pooled, cudaStream_t s) {
+  const int smem = H * D * 4;
+  auto ks = head_scores_kernel<T>;
+  SG_CUDA(cudaFuncSetAttribute(ks, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int warps = 16;
+  int blocks = (N + warps - 1) / warps;
+  blocks = std::min(blocks, 4 * sm_count());
+  if (N > 0) {
+    ks<<<blocks, warps * 32, smem, s>>>(static_cast<const T*>(x), D, H, cu, B, pad_P, tok_img, N, u, scores);
+    SG_LAUNCH_CHECK();
+  }
+  dim3 grid(B, (D + 63) / 64);
+  head_pool_rows_kernel<T><<<grid, 256, 0, s>>>(static_cast<const T*>(x), D, H, cu, pad_P, scores,
+                                                static_cast<T*>(pooled));
+  SG_LAUNCH_CHECK();
+  return SIGLIP2_OK;
+}
+
+// Parallel pooling (scores over all tokens, then per (image, 64 columns)).
+// tok_img (token -> image) is needed only when the hidden state is padded.
+int sg_head_pool_parallel(int dtype, const void* x, int D, int H, const int* cu, int B, int pad_P, const int* tok_img,
+                          int N, const float* u, float* scores, void* pooled, cudaStream_t s) {
+  SG_CHECK_ARG(H <= 16 && D % 8 == 0, "head pooling needs H <= 16 and D %% 8 == 0");
+  SG_CHECK_ARG(pad_P == 0 || tok_img != nullptr, "padded head pooling needs the token -> image map");
+  switch (dtype) {
+    case SIGLIP2_BF16: return launch_head_pool_parallel<__nv_bfloat16>(x, D, H, cu, B, pad_P, tok_img, N, u, scores, pooled, s);
+    case SIGLIP2_F16: return launch_head_pool_parallel<__half>(x, D, H, cu, B, pad_P, tok_img, N, u, scores, pooled, s);
+    case SIGLIP2_F32: return launch_head_pool_parallel<float>(x, D, H, cu, B, pad_P, tok_img, N, u, scores, pooled, s);
+    default: return set_error(SIGLIP2_ERR_ARG, "unknown dtype %d", dtype);
+  }
+}
+
 int sg_head_pool_impl(int dtype, const void* x, int D, int H, const int* cu, int B, int pad_P, const float* u,
                       float* scores, void* pooled, cudaStream_t s) {
   SG_CHECK_ARG(H % 4 == 0 && H <= 16 && D % 8 == 0, "head pooling needs H %% 4 == 0, H <= 16, D %% 8 == 0");
@@ -409,7 +443,7 @@ int sg_forward_impl(const siglip2_config* c, const siglip2_weights* w, const voi
   SG_TRY(sg_layernorm_impl(dt, f.x, last_hidden, w->post_ln_w, w->post_ln_b, P > 0 ? B * P : N, D, c->eps,
                            P > 0 ? cu : nullptr, P, s));
   if (pooled) {
-    SG_TRY(sg_head_pool_impl(dt, last_hidden, D, H, cu, B, P, w->head_u, f.scores, f.hpool, s));
+    SG_TRY(sg_head_pool_parallel(dt, last_hidden, D, H, cu, B, P, f.tok_img, N, w->head_u, f.scores, f.hpool, s));
     SG_TRY(sg_gemm_impl(dt, kEpiBias, f.hpool, D, w->head_v_w, D, f.hY, D, B * H, D, D, w->head_v_b, nullptr, 0,
                         nullptr, nullptr, 0.f, s));
     if (dt == SIGLIP2_BF16) SG_TRY(launch_select<__nv_bfloat16>(f.hY, H, hd, D, B, f.hattn, s));
