@@ -10,19 +10,18 @@
 // R = HDP-64 wide slab (32B / 64B swizzle).
 //
 // One CTA per (128-query tile of one image, head); two CTAs share an SM
-// (256 TMEM columns and <= 96 KB of shared memory each), so one CTA's MMAs run
-// while the other's softmax warps work.
-//   warp 0     TMA: Q once, K tiles of 128 keys into a 2-deep ring, V tiles
-//   warp 1     TMEM owner + MMA issuer:
-//                S_j = Q K_j^T          128x128 fp32 in TMEM columns [0,128)
-//                O  += P_j V_j          P_j (bf16/f16) read from TMEM columns
-//                                       [0,64) where the softmax wrote it over
-//                                       S_j; O (128 x HDP fp32) in [128, 128+HDP)
+// (256 TMEM columns and <= 96 KB of shared memory each).  Keys come in tiles
+// of KT = 96.  TMEM columns: S [0, 96) fp32, P [96, 144) (bf16/f16 pairs),
+// O [144, 144 + HDP) fp32.  Because P has its own columns, S_{j+1} = Q K_{j+1}^T
+// runs on the tensor cores while the softmax warps turn S_j into P_j.
+//   warp 0     TMA: Q once, K and V tiles into 2-deep rings
+//   warp 1     TMEM owner + MMA issuer: S_j as soon as the softmax has read
+//              S_{j-1}; then O += P_{j-1} V_{j-1} (P read from TMEM)
 //   warps 2-5  softmax: each thread owns one query row (its TMEM lane):
-//              keys past the image end masked, online max with lazy rescale
-//              (O is rescaled in TMEM only when the running max grows by more
-//              than 2^8), P = exp2(S*scale*log2e - m) packed in pairs into
-//              TMEM, final O / l stored to out[N, H*hd].
+//              loads S_j into registers and frees it, masks keys past the
+//              image end, online max with lazy rescale (O is rescaled in TMEM
+//              only when the running max grows by more than 2^8), writes
+//              P = exp2(S*scale*log2e - m) packed in pairs, final O / l.
 #pragma once
 
 #include "ptx.cuh"
@@ -47,46 +46,54 @@ __device__ __forceinline__ float ex2_approx(float x) {
 
 template <int HDP>
 struct FmhaCfg {
-  static constexpr int R = HDP - 64;                 // remainder slab width (0, 16, 32)
-  static constexpr int kSlabA = 128 * 64 * 2;        // 16 KB
-  static constexpr int kSlabR = 128 * R * 2;
-  static constexpr int kSlabRAl = (kSlabR + 1023) / 1024 * 1024;
-  static constexpr int kTile = kSlabA + kSlabRAl;    // one 128 x HDP operand
-  static constexpr int kKStages = 2;
+  static constexpr int R = HDP - 64;                  // remainder slab width (0, 16, 32)
+  static constexpr int KT = 96;                       // keys per tile
+  static constexpr int kQSlabA = 128 * 64 * 2;        // Q: 128 rows
+  static constexpr int kQSlabR = 128 * R * 2;
+  static constexpr int kQTile = kQSlabA + (kQSlabR + 1023) / 1024 * 1024;
+  static constexpr int kKSlabA = KT * 64 * 2;         // K / V: 96 rows (12 KB, a multiple of 1 KB)
+  static constexpr int kKSlabR = KT * R * 2;
+  static constexpr int kKTile = kKSlabA + (kKSlabR + 1023) / 1024 * 1024;
+  static constexpr int kStages = 2;
   static constexpr int kQ = 0;
-  static constexpr int kK = kTile;
-  static constexpr int kV = kK + kKStages * kTile;
-  static constexpr int kBar = kV + kTile;
+  static constexpr int kK = kQTile;
+  static constexpr int kV = kK + kStages * kKTile;
+  static constexpr int kBar = kV + kStages * kKTile;
   static constexpr int kSmem = kBar + 256 + 1024;
-  static constexpr int kTileBytes = kSlabA + kSlabR;  // TMA bytes per operand tile
+  static constexpr int kQBytes = kQSlabA + kQSlabR;   // TMA bytes
+  static constexpr int kKBytes = kKSlabA + kKSlabR;
   static constexpr uint32_t kTmemCols = 256;
-  static constexpr uint32_t kColO = 128;
+  static constexpr uint32_t kColP = KT;               // 48 columns of packed pairs
+  static constexpr uint32_t kColO = KT + KT / 2;      // 144
 };
 
 template <typename T, int HDP>
 __global__ void __launch_bounds__(192, 2)
-    fmha_varlen_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmR,
+    fmha_varlen_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmQR,
+                       const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmKR,
                        const FmhaParams p) {
   using C = FmhaCfg<HDP>;
   constexpr int R = C::R;
-  constexpr int KS = C::kKStages;
+  constexpr int KT = C::KT;
+  constexpr int ST = C::kStages;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr uint32_t kIdescS = make_idesc(128, 128, kBF16, false, false);
+  constexpr uint32_t kIdescS = make_idesc(128, KT, kBF16, false, false);
   constexpr uint32_t kIdescO64 = make_idesc(128, 64, kBF16, false, true);
   constexpr uint32_t kIdescOR = make_idesc(128, R > 0 ? R : 16, kBF16, false, true);
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBar);
-  uint64_t* q_full = bars;            // 1
-  uint64_t* k_full = bars + 1;        // KS
-  uint64_t* k_empty = k_full + KS;    // KS
-  uint64_t* v_full = k_empty + KS;    // 1
-  uint64_t* v_empty = v_full + 1;     // 1
-  uint64_t* s_full = v_empty + 1;     // 1
-  uint64_t* p_full = s_full + 1;      // 1
-  uint64_t* pv_done = p_full + 1;     // 1
-  uint64_t* mdone = pv_done + 1;      // 1
+  uint64_t* q_full = bars;           // 1
+  uint64_t* k_full = bars + 1;       // ST
+  uint64_t* k_empty = k_full + ST;   // ST
+  uint64_t* v_full = k_empty + ST;   // ST
+  uint64_t* v_empty = v_full + ST;   // ST
+  uint64_t* s_full = v_empty + ST;   // 1: S_j computed
+  uint64_t* s_free = s_full + 1;     // 1: S_j read by the softmax (128 arrivals)
+  uint64_t* p_full = s_free + 1;     // 1: P_j written, O rescaled (128 arrivals)
+  uint64_t* pv_done = p_full + 1;    // 1: O += P_j V_j complete
+  uint64_t* mdone = pv_done + 1;     // 1
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mdone + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -97,20 +104,21 @@ __global__ void __launch_bounds__(192, 2)
   const int img_row0 = __ldg(p.cu + tile.x);
   const int L = __ldg(p.cu + tile.x + 1) - img_row0;
   const int q_row0 = img_row0 + tile.y * 128;
-  const int n_kv = (L + 127) / 128;
+  const int n_kv = (L + KT - 1) / KT;
   const int colQ = head * HDP;
   const int colK = (p.heads + head) * HDP;
   const int colV = (2 * p.heads + head) * HDP;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < KS; ++s) {
+    for (int s = 0; s < ST; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
-    mbar_init(v_full, 1);
-    mbar_init(v_empty, 1);
     mbar_init(s_full, 1);
+    mbar_init(s_free, 128);
     mbar_init(p_full, 128);
     mbar_init(pv_done, 1);
     mbar_init(mdone, 1);
@@ -129,59 +137,80 @@ __global__ void __launch_bounds__(192, 2)
   if (warp == 0) {
     // --------------------------------------------------------------- TMA
     if (lane == 0) {
-      tma_prefetch_desc(&tmA);
-      if (R > 0) tma_prefetch_desc(&tmR);
-      mbar_arrive_expect_tx(q_full, C::kTileBytes);
-      tma_load_2d(smem + C::kQ, &tmA, q_full, colQ, q_row0);
-      if (R > 0) tma_load_2d(smem + C::kQ + C::kSlabA, &tmR, q_full, colQ + 64, q_row0);
-      int k_issued = 0, v_issued = 0;
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      if (R > 0) {
+        tma_prefetch_desc(&tmQR);
+        tma_prefetch_desc(&tmKR);
+      }
+      mbar_arrive_expect_tx(q_full, C::kQBytes);
+      tma_load_2d(smem + C::kQ, &tmQ, q_full, colQ, q_row0);
+      if (R > 0) tma_load_2d(smem + C::kQ + C::kQSlabA, &tmQR, q_full, colQ + 64, q_row0);
+      int issued = 0;
       for (int j = 0; j < n_kv; ++j) {
-        const int ks = j % KS;
-        const int kv_row = img_row0 + j * 128;
-        if (*abort_flag || !mbar_wait(&k_empty[ks], ((j / KS) & 1) ^ 1, 201)) {
+        const int st = j % ST;
+        const uint32_t eph = ((j / ST) & 1) ^ 1;
+        const int kv_row = img_row0 + j * KT;
+        if (*abort_flag || !mbar_wait(&k_empty[st], eph, 201)) {
           *abort_flag = 1;
           break;
         }
-        uint8_t* kb = smem + C::kK + ks * C::kTile;
-        mbar_arrive_expect_tx(&k_full[ks], C::kTileBytes);
-        tma_load_2d(kb, &tmA, &k_full[ks], colK, kv_row);
-        if (R > 0) tma_load_2d(kb + C::kSlabA, &tmR, &k_full[ks], colK + 64, kv_row);
-        ++k_issued;
-        if (*abort_flag || !mbar_wait(v_empty, (j & 1) ^ 1, 202)) {
+        uint8_t* kb = smem + C::kK + st * C::kKTile;
+        mbar_arrive_expect_tx(&k_full[st], C::kKBytes);
+        tma_load_2d(kb, &tmK, &k_full[st], colK, kv_row);
+        if (R > 0) tma_load_2d(kb + C::kKSlabA, &tmKR, &k_full[st], colK + 64, kv_row);
+        if (*abort_flag || !mbar_wait(&v_empty[st], eph, 202)) {
           *abort_flag = 1;
           break;
         }
-        uint8_t* vb = smem + C::kV;
-        mbar_arrive_expect_tx(v_full, C::kTileBytes);
-        tma_load_2d(vb, &tmA, v_full, colV, kv_row);
-        if (R > 0) tma_load_2d(vb + C::kSlabA, &tmR, v_full, colV + 64, kv_row);
-        ++v_issued;
+        uint8_t* vb = smem + C::kV + st * C::kKTile;
+        mbar_arrive_expect_tx(&v_full[st], C::kKBytes);
+        tma_load_2d(vb, &tmK, &v_full[st], colV, kv_row);
+        if (R > 0) tma_load_2d(vb + C::kKSlabA, &tmKR, &v_full[st], colV + 64, kv_row);
+        ++issued;
       }
       // no TMA write may still be in flight when the CTA exits
       mbar_wait(q_full, 0, 203);
-      for (int j = (k_issued > KS ? k_issued - KS : 0); j < k_issued; ++j)
-        mbar_wait(&k_full[j % KS], (j / KS) & 1, 204);
-      if (v_issued > 0) mbar_wait(v_full, (v_issued - 1) & 1, 205);
+      for (int j = (issued > ST ? issued - ST : 0); j < issued; ++j) {
+        mbar_wait(&k_full[j % ST], (j / ST) & 1, 204);
+        mbar_wait(&v_full[j % ST], (j / ST) & 1, 205);
+      }
     }
   } else if (warp == 1) {
     // --------------------------------------------------------------- MMA
     if (lane == 0) {
       bool ok = mbar_wait(q_full, 0, 211);
       const uint32_t qa = smem_u32(smem + C::kQ);
-      const uint32_t qr = qa + C::kSlabA;
-      const uint32_t va = smem_u32(smem + C::kV);
-      const uint32_t vr = va + C::kSlabA;
+      const uint32_t qr = qa + C::kQSlabA;
+      auto issue_pv = [&](int jj) -> bool {
+        const int st = jj % ST;
+        if (!mbar_wait(p_full, jj & 1, 214) || !mbar_wait(&v_full[st], (jj / ST) & 1, 215)) return false;
+        tc_fence_after();
+        const uint32_t va = smem_u32(smem + C::kV + st * C::kKTile);
+        const uint32_t vr = va + C::kKSlabA;
+#pragma unroll
+        for (int s = 0; s < KT / 16; ++s) {  // 16 keys per MMA; P columns [kColP + 8s, +8)
+          const uint32_t acc = (jj > 0 || s > 0) ? 1u : 0u;
+          umma_ts(tmem + C::kColO, tmem + C::kColP + s * 8, mnmajor_desc(va + s * 16 * 128, 128, 0), kIdescO64, acc);
+          if constexpr (R > 0)
+            umma_ts(tmem + C::kColO + 64, tmem + C::kColP + s * 8, mnmajor_desc(vr + s * 16 * R * 2, R * 2, 0),
+                    kIdescOR, acc);
+        }
+        umma_commit(pv_done);
+        umma_commit(&v_empty[st]);
+        return true;
+      };
       for (int j = 0; j < n_kv && ok; ++j) {
-        const int ks = j % KS;
-        // S/P columns are reused: PV_{j-1} must have consumed P_{j-1}
-        if (*abort_flag || !mbar_wait(&k_full[ks], (j / KS) & 1, 212) ||
-            (j > 0 && !mbar_wait(pv_done, (j - 1) & 1, 213))) {
+        const int st = j % ST;
+        // S_j overwrites S_{j-1}: the softmax must have read it
+        if (*abort_flag || !mbar_wait(&k_full[st], (j / ST) & 1, 212) ||
+            (j > 0 && !mbar_wait(s_free, (j - 1) & 1, 213))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t ka = smem_u32(smem + C::kK + ks * C::kTile);
-        const uint32_t kr = ka + C::kSlabA;
+        const uint32_t ka = smem_u32(smem + C::kK + st * C::kKTile);
+        const uint32_t kr = ka + C::kKSlabA;
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           umma_ss(tmem, kmajor_desc(qa + k * 32, 128), kmajor_desc(ka + k * 32, 128), kIdescS, k > 0);
@@ -189,22 +218,10 @@ __global__ void __launch_bounds__(192, 2)
         for (int k = 0; k < R / 16; ++k)
           umma_ss(tmem, kmajor_desc(qr + k * 32, R * 2), kmajor_desc(kr + k * 32, R * 2), kIdescS, 1);
         umma_commit(s_full);
-        umma_commit(&k_empty[ks]);
-        if (!mbar_wait(p_full, j & 1, 214) || !mbar_wait(v_full, j & 1, 215)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-#pragma unroll
-        for (int s = 0; s < 8; ++s) {  // 16 keys per MMA; P columns [8s, 8s+8)
-          const uint32_t acc = (j > 0 || s > 0) ? 1u : 0u;
-          umma_ts(tmem + C::kColO, tmem + s * 8, mnmajor_desc(va + s * 16 * 128, 128, 0), kIdescO64, acc);
-          if constexpr (R > 0)
-            umma_ts(tmem + C::kColO + 64, tmem + s * 8, mnmajor_desc(vr + s * 16 * R * 2, R * 2, 0), kIdescOR, acc);
-        }
-        umma_commit(pv_done);
-        umma_commit(v_empty);
+        umma_commit(&k_empty[st]);
+        if (j > 0 && !issue_pv(j - 1)) ok = false;
       }
+      if (ok && n_kv > 0 && !issue_pv(n_kv - 1)) ok = false;
       if (!ok) *abort_flag = 1;
       umma_commit(mdone);
       mbar_wait(mdone, 0, 216);
@@ -223,34 +240,33 @@ __global__ void __launch_bounds__(192, 2)
         break;
       }
       tc_fence_after();
-      const int valid = L - j * 128;  // keys of this image in the tile (>= 1)
-      // pass 1: row max of S_j (32 columns at a time)
-      // 8 independent partial maxima (no long dependency chain); keys past
-      // the image end are masked only in the image's last, partial tile
-      float mx[8];
+      float s[KT];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
-      const bool full_tile = valid >= 128;
-#pragma unroll 1
-      for (int c = 0; c < 4; c += 2) {
-        uint32_t u[32], u2[32];
-        SG_TMEM_LD_32(tmem + c * 32 + lane_off, u);
-        SG_TMEM_LD_32(tmem + (c + 1) * 32 + lane_off, u2);
+      for (int c = 0; c < KT / 16; c += 2) {
+        uint32_t u[16], u2[16];
+        SG_TMEM_LD_16(tmem + c * 16 + lane_off, u);
+        SG_TMEM_LD_16(tmem + (c + 1) * 16 + lane_off, u2);
         tmem_ld_wait();
-        if (full_tile) {
 #pragma unroll
-          for (int k = 0; k < 32; ++k) {
-            mx[k & 7] = fmaxf(mx[k & 7], __uint_as_float(u[k]));
-            mx[k & 7] = fmaxf(mx[k & 7], __uint_as_float(u2[k]));
-          }
-        } else {
-#pragma unroll
-          for (int k = 0; k < 32; ++k) {
-            if (c * 32 + k < valid) mx[k & 7] = fmaxf(mx[k & 7], __uint_as_float(u[k]));
-            if ((c + 1) * 32 + k < valid) mx[k & 7] = fmaxf(mx[k & 7], __uint_as_float(u2[k]));
-          }
+        for (int k = 0; k < 16; ++k) {
+          s[c * 16 + k] = __uint_as_float(u[k]);
+          s[(c + 1) * 16 + k] = __uint_as_float(u2[k]);
         }
       }
+      // S_j is in registers: let the MMA warp compute S_{j+1}
+      tc_fence_before();
+      mbar_arrive(s_free);
+      const int valid = L - j * KT;  // keys of this image in the tile (>= 1)
+      if (valid < KT) {
+#pragma unroll
+        for (int k = 0; k < KT; ++k)
+          if (k >= valid) s[k] = -INFINITY;
+      }
+      float mx[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx[i] = s[i];
+#pragma unroll
+      for (int k = 8; k < KT; ++k) mx[k & 7] = fmaxf(mx[k & 7], s[k]);
       float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
       mt *= sc;
       float alpha = 1.f;
@@ -260,54 +276,39 @@ __global__ void __launch_bounds__(192, 2)
         alpha = ex2_approx(m_use - mt);
         m_use = mt;
       }
-      // O is stable here: S_j was issued only after PV_{j-1} completed
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-        uint32_t u[16];
-#pragma unroll
-        for (int c = 0; c < HDP / 16; ++c) {
-          SG_TMEM_LD_16(tmem + C::kColO + c * 16 + lane_off, u);
-          tmem_ld_wait();
-#pragma unroll
-          for (int k = 0; k < 16; ++k) u[k] = __float_as_uint(__uint_as_float(u[k]) * alpha);
-          SG_TMEM_ST_16(tmem + C::kColO + c * 16 + lane_off, u);
-        }
-      }
-      // pass 2: P = exp2(S*scale - m) written over S_j: P column 16c+k holds
-      // keys 32c+2k (low half) and 32c+2k+1; chunk c only overwrites columns
-      // of chunks already read
       float ps[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) ps[i] = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t u[32];
-        SG_TMEM_LD_32(tmem + c * 32 + lane_off, u);
-        tmem_ld_wait();
-        uint32_t w[16];
-        if (full_tile) {
+      uint32_t w[KT / 2];
 #pragma unroll
-          for (int k = 0; k < 16; ++k) {
-            const float p0 = ex2_approx(fmaf(__uint_as_float(u[2 * k]), sc, -m_use));
-            const float p1 = ex2_approx(fmaf(__uint_as_float(u[2 * k + 1]), sc, -m_use));
-            ps[k & 7] += p0 + p1;
-            w[k] = Pack2<T>::pack(p0, p1);
-          }
-        } else {
+      for (int k = 0; k < KT / 2; ++k) {
+        const float p0 = ex2_approx(fmaf(s[2 * k], sc, -m_use));
+        const float p1 = ex2_approx(fmaf(s[2 * k + 1], sc, -m_use));
+        ps[k & 7] += p0 + p1;
+        w[k] = Pack2<T>::pack(p0, p1);
+      }
+      l = l * alpha + (((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7])));
+      if (j > 0) {
+        // PV_{j-1} must be done: P's columns are rewritten and O may be rescaled
+        if (!mbar_wait(pv_done, (j - 1) & 1, 222)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+          uint32_t u[16];
 #pragma unroll
-          for (int k = 0; k < 16; ++k) {
-            const int k0 = c * 32 + 2 * k;
-            const float x0 = k0 < valid ? __uint_as_float(u[2 * k]) : -INFINITY;
-            const float x1 = k0 + 1 < valid ? __uint_as_float(u[2 * k + 1]) : -INFINITY;
-            const float p0 = ex2_approx(fmaf(x0, sc, -m_use));
-            const float p1 = ex2_approx(fmaf(x1, sc, -m_use));
-            ps[k & 7] += p0 + p1;
-            w[k] = Pack2<T>::pack(p0, p1);
+          for (int c = 0; c < HDP / 16; ++c) {
+            SG_TMEM_LD_16(tmem + C::kColO + c * 16 + lane_off, u);
+            tmem_ld_wait();
+#pragma unroll
+            for (int k = 0; k < 16; ++k) u[k] = __float_as_uint(__uint_as_float(u[k]) * alpha);
+            SG_TMEM_ST_16(tmem + C::kColO + c * 16 + lane_off, u);
           }
         }
-        SG_TMEM_ST_16(tmem + c * 16 + lane_off, w);
       }
-      const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
-      l = l * alpha + rs;
+#pragma unroll
+      for (int c = 0; c < KT / 16; ++c) SG_TMEM_ST_8(tmem + C::kColP + c * 8 + lane_off, (w + c * 8));
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(p_full);

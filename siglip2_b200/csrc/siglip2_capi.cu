@@ -233,11 +233,18 @@ int sg_token_image_impl(const int* cu, int B, int N, int* tok_img, cudaStream_t 
 template <typename T, int HDP>
 int launch_fmha(const void* qkv, int N, const int* cu, const int2* tiles, int n_tiles, int H, int hd, void* out, int ldo,
                 cudaStream_t s) {
-  CUtensorMap ta, tr;
+  using C = FmhaCfg<HDP>;
+  CUtensorMap tq, tqr, tk, tkr;
   const int ldq = 3 * H * HDP;
-  SG_TRY(make_tmap_2d(&ta, qkv, 2, N, ldq, ldq, 128, 64));
-  if (HDP > 64) SG_TRY(make_tmap_2d(&tr, qkv, 2, N, ldq, ldq, 128, HDP - 64));
-  else tr = ta;
+  SG_TRY(make_tmap_2d(&tq, qkv, 2, N, ldq, ldq, 128, 64));
+  SG_TRY(make_tmap_2d(&tk, qkv, 2, N, ldq, ldq, C::KT, 64));
+  if (HDP > 64) {
+    SG_TRY(make_tmap_2d(&tqr, qkv, 2, N, ldq, ldq, 128, HDP - 64));
+    SG_TRY(make_tmap_2d(&tkr, qkv, 2, N, ldq, ldq, C::KT, HDP - 64));
+  } else {
+    tqr = tq;
+    tkr = tk;
+  }
   FmhaParams p;
   p.cu = cu;
   p.tiles = tiles;
@@ -254,7 +261,7 @@ int launch_fmha(const void* qkv, int N, const int* cu, const int2* tiles, int n_
     attr_done = true;
   }
   dim3 grid(n_tiles, H);
-  kern<<<grid, 192, smem, s>>>(ta, tr, p);
+  kern<<<grid, 192, smem, s>>>(tq, tqr, tk, tkr, p);
   SG_LAUNCH_CHECK();
   return SIGLIP2_OK;
 }
