@@ -58,7 +58,14 @@ typedef enum {
   SIGLIP2_EPI_BIAS_RES = 1,   /* out = A.B^T + bias + res            (res may == out) */
   SIGLIP2_EPI_LN = 2,         /* out = rstd(A)*(A.B^T - mu(A)*c1) + c2   (LayerNorm of A folded) */
   SIGLIP2_EPI_LN_GELU = 3,    /* out = gelu_tanh(rstd(A)*(A.B^T - mu(A)*c1) + c2)      */
-  SIGLIP2_EPI_BIAS_GELU = 4   /* out = gelu_tanh(A.B^T + bias)                        */
+  SIGLIP2_EPI_BIAS_GELU = 4,  /* out = gelu_tanh(A.B^T + bias)                        */
+  /* siglip2_gemm_rowsums only: LayerNorm statistics come from, or go to,
+   * per-row (sum, sum of squares) float pairs of the residual stream */
+  SIGLIP2_EPI_LN_ROWSUMS = 5,      /* as SIGLIP2_EPI_LN, mu/rstd from rs_in[M] over K columns */
+  SIGLIP2_EPI_LN_ROWSUMS_GELU = 6, /* as SIGLIP2_EPI_LN_GELU, likewise                        */
+  SIGLIP2_EPI_BIAS_RES_ROWSUMS = 7 /* as SIGLIP2_EPI_BIAS_RES, and rs_acc[row] += (sum, sum of
+                                      squares) of the row's rounded outputs; rows of rs_zero
+                                      are set to zero (optional)                              */
 } siglip2_epilogue;
 
 /* Library version (major*10000 + minor*100 + patch). */
@@ -89,6 +96,18 @@ int siglip2_check_device(int reset);
 int siglip2_gemm(int dtype, int epilogue, const void* a_dev, int lda, const void* b_dev, int ldb, void* out_dev,
                  int ldo, int M, int N, int K, const float* bias_dev, const void* res_dev, int ldr,
                  const float* c1_dev, const float* c2_dev, float eps, void* stream);
+
+/* siglip2_gemm with row-sum LayerNorm plumbing: the GEMM that writes the
+ * residual stream (SIGLIP2_EPI_BIAS_RES_ROWSUMS) accumulates each row's sum
+ * and sum of squares into rs_acc (float pairs, zero beforehand), and the
+ * LayerNorm-folded GEMM that reads it (SIGLIP2_EPI_LN_ROWSUMS[_GELU]) takes
+ * mu = sum/K and rstd = 1/sqrt(sumsq/K - mu^2 + eps) from rs_in, so no pass
+ * over the rows is needed for LayerNorm statistics.  Pointers not used by
+ * the epilogue may be NULL; row-sum buffers must be 8-byte aligned. */
+int siglip2_gemm_rowsums(int dtype, int epilogue, const void* a_dev, int lda, const void* b_dev, int ldb,
+                         void* out_dev, int ldo, int M, int N, int K, const float* bias_dev, const void* res_dev,
+                         int ldr, const float* c1_dev, const float* c2_dev, float eps, const float* rs_in_dev,
+                         float* rs_acc_dev, float* rs_zero_dev, void* stream);
 
 /* LayerNorm over the last dimension (fp32 statistics, biased variance).
  * Packed mode (cu_seqlens_dev == NULL): y[r] = LN(x[r]) for r < rows.

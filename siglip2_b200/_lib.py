@@ -24,6 +24,8 @@ SIGNATURES = {
     "siglip2_get_gemm_variant": (_c_int, []),
     "siglip2_gemm": (_c_int, [_c_int, _c_int, _vp, _c_int, _vp, _c_int, _vp, _c_int, _c_int, _c_int, _c_int,
                               _vp, _vp, _c_int, _vp, _vp, _c_float, _vp]),
+    "siglip2_gemm_rowsums": (_c_int, [_c_int, _c_int, _vp, _c_int, _vp, _c_int, _vp, _c_int, _c_int, _c_int, _c_int,
+                                      _vp, _vp, _c_int, _vp, _vp, _c_float, _vp, _vp, _vp, _vp]),
     "siglip2_layernorm": (_c_int, [_c_int, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_float, _vp, _c_int, _vp]),
     "siglip2_token_image": (_c_int, [_vp, _c_int, _c_int, _vp, _vp]),
     "siglip2_posemb": (_c_int, [_c_int, _vp, _c_int, _c_int, _vp, _vp, _vp, _c_int, _vp, _vp]),
@@ -64,6 +66,7 @@ STATUS = {0: "OK", -1: "ERR_ARG", -2: "ERR_ALIGN", -3: "ERR_SHAPE", -4: "ERR_CUD
 
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
 EPI_BIAS, EPI_BIAS_RES, EPI_LN, EPI_LN_GELU, EPI_BIAS_GELU = 0, 1, 2, 3, 4
+EPI_LN_ROWSUMS, EPI_LN_ROWSUMS_GELU, EPI_BIAS_RES_ROWSUMS = 5, 6, 7
 
 _lib = None
 

@@ -30,19 +30,30 @@
 namespace sg {
 
 enum GemmEpilogue : int {
-  kEpiBias = 0,        // out = acc + bias
-  kEpiBiasRes = 1,     // out = acc + bias + res
-  kEpiLn = 2,          // out = rstd (acc - mu c1) + c2
-  kEpiLnGelu = 3,      // out = gelu_tanh(rstd (acc - mu c1) + c2)
-  kEpiBiasGelu = 4,    // out = gelu_tanh(acc + bias)
+  kEpiBias = 0,          // out = acc + bias
+  kEpiBiasRes = 1,       // out = acc + bias + res
+  kEpiLn = 2,            // out = rstd (acc - mu c1) + c2, mu/rstd from statistics warps
+  kEpiLnGelu = 3,        // out = gelu_tanh(rstd (acc - mu c1) + c2), likewise
+  kEpiBiasGelu = 4,      // out = gelu_tanh(acc + bias)
+  kEpiLnRs = 5,          // as kEpiLn, mu/rstd from row sums accumulated by the producer of A
+  kEpiLnRsGelu = 6,      // as kEpiLnGelu, likewise
+  kEpiBiasResRs = 7,     // as kEpiBiasRes, and accumulates the row sums of the rounded output
 };
+
+__host__ __device__ constexpr bool epi_has_stat_warps(int e) { return e == kEpiLn || e == kEpiLnGelu; }
+__host__ __device__ constexpr bool epi_is_ln(int e) { return e == kEpiLn || e == kEpiLnGelu || e == kEpiLnRs || e == kEpiLnRsGelu; }
+__host__ __device__ constexpr bool epi_is_gelu(int e) { return e == kEpiLnGelu || e == kEpiLnRsGelu || e == kEpiBiasGelu; }
+__host__ __device__ constexpr bool epi_has_res(int e) { return e == kEpiBiasRes || e == kEpiBiasResRs; }
 
 struct GemmParams {
   int M, N, K;
-  const float* bias;     // [N] (kEpiBias*, kEpiBiasRes)
-  const float* c1;       // [N] (kEpiLn*)
-  const float* c2;       // [N] (kEpiLn*)
-  float eps;             // LayerNorm epsilon (kEpiLn*)
+  const float* bias;          // [N] (bias epilogues)
+  const float* c1;            // [N] (LayerNorm-folded epilogues)
+  const float* c2;            // [N]
+  float eps;                  // LayerNorm epsilon
+  const float2* rs_in;        // [M] (sum, sum of squares) of A's rows over K (kEpiLnRs*)
+  float2* rs_acc;             // [M] row sums of the output to accumulate into (kEpiBiasResRs)
+  float2* rs_zero;            // [M] optional: zeroed by the CTAs of the first column tile
 };
 
 constexpr int kGemmBM = 128;
@@ -71,9 +82,9 @@ struct GemmCfg {
   static constexpr int kSmemBytes = kOffStats + 2 * 2 * kGemmBM * 4 + 1024 /*alignment slack*/;
 };
 
-template <bool LN>
+template <bool kStatWarps>
 struct GemmThreads {
-  static constexpr int kWarps = LN ? 10 : 6;
+  static constexpr int kWarps = kStatWarps ? 10 : 6;
   static constexpr int kThreads = kWarps * 32;
 };
 
@@ -114,8 +125,12 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
                                               const float* st_mean, const float* st_rstd, volatile int* abort_flag,
                                               int warp, int lane, int first_tile, int tile_step, int num_tiles,
                                               int n_tiles, int rows_per_tile, int row_offset) {
-  constexpr bool kLN = (EPI == kEpiLn || EPI == kEpiLnGelu);
-  constexpr bool kRes = (EPI == kEpiBiasRes);
+  constexpr bool kStat = epi_has_stat_warps(EPI);  // mu/rstd from this kernel's statistics warps
+  constexpr bool kRsIn = (EPI == kEpiLnRs || EPI == kEpiLnRsGelu);  // mu/rstd from row sums
+  constexpr bool kLnMath = epi_is_ln(EPI);
+  constexpr bool kGelu = epi_is_gelu(EPI);
+  constexpr bool kRes = epi_has_res(EPI);
+  constexpr bool kRsOut = (EPI == kEpiBiasResRs);
   constexpr int NCH = BN / kEpiCols;
   const int ew = warp - 2;
   const int q = warp & 3;
@@ -135,7 +150,7 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
     }
     tc_fence_after();
     float mu = 0.f, rstd = 1.f;
-    if constexpr (kLN) {
+    if constexpr (kStat) {
       if (!mbar_wait(&sfull[buf], tph, 122)) {
         *abort_flag = 1;
         break;
@@ -146,6 +161,16 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
       if (lane == 0) mbar_arrive(&sempty[buf]);
     }
     const int row0 = m0 + q * 32;
+    const int my_row = row0 + lane;
+    if constexpr (kRsIn) {
+      // row sums of the raw A row (the previous GEMM's rounded output): fp32
+      // E[x^2] - E[x]^2 over K = D values of O(1) magnitude
+      const float2 rs = my_row < p.M ? p.rs_in[my_row] : make_float2(0.f, 0.f);
+      const float inv_k = 1.f / static_cast<float>(p.K);
+      mu = rs.x * inv_k;
+      rstd = rsqrtf(fmaxf(rs.y * inv_k - mu * mu, 0.f) + p.eps);
+    }
+    float rs1 = 0.f, rs2 = 0.f;  // row sums of this tile's rounded outputs (kRsOut)
     const uint32_t tbase = tmem_base + buf * acc_stride + (static_cast<uint32_t>(q * 32) << 16);
     uint32_t ra[32], rb[32];
     SG_TMEM_LD_32(tbase, ra);
@@ -172,14 +197,14 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(cur[j]);
       if (col0 < p.N) {
-        if constexpr (kLN) {
+        if constexpr (kLnMath) {
           float a[32], b[32];
           load_param32(p.c1, col0, p.N, a);
           load_param32(p.c2, col0, p.N, b);
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             v[j] = fmaf(rstd, fmaf(-mu, a[j], v[j]), b[j]);
-            if constexpr (EPI == kEpiLnGelu) v[j] = gelu_tanh(v[j]);
+            if constexpr (kGelu) v[j] = gelu_tanh(v[j]);
           }
         } else {
           float a[32];
@@ -187,7 +212,7 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             v[j] += a[j];
-            if constexpr (EPI == kEpiBiasGelu) v[j] = gelu_tanh(v[j]);
+            if constexpr (kGelu) v[j] = gelu_tanh(v[j]);
           }
         }
       }
@@ -218,6 +243,18 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
         o.z = Pack2<T>::pack(v[g * 8 + 4], v[g * 8 + 5]);
         o.w = Pack2<T>::pack(v[g * 8 + 6], v[g * 8 + 7]);
         *reinterpret_cast<uint4*>(srow + ((g ^ sw) << 4)) = o;
+        if constexpr (kRsOut) {
+          // statistics of exactly what the next GEMM will read (the rounded values)
+          if (col0 + g * 8 < p.N) {
+            const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+            for (int h2 = 0; h2 < 4; ++h2) {
+              const float2 f = Pack2<T>::unpack(ow[h2]);
+              rs1 += f.x + f.y;
+              rs2 = fmaf(f.x, f.x, fmaf(f.y, f.y, rs2));
+            }
+          }
+        }
       }
       fence_proxy_async_smem();
       __syncwarp();
@@ -233,6 +270,13 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(buf ? tempty_addr1 : tempty_addr0);
+      }
+    }
+    if constexpr (kRsOut) {
+      if (my_row < p.M) {
+        atomicAdd(&p.rs_acc[my_row].x, rs1);
+        atomicAdd(&p.rs_acc[my_row].y, rs2);
+        if (p.rs_zero != nullptr && n0 == 0) p.rs_zero[my_row] = make_float2(0.f, 0.f);
       }
     }
   }
@@ -305,12 +349,12 @@ __device__ __forceinline__ void gemm_row_stats(const GemmParams& p, const uint8_
 }
 
 template <typename T, int BN, int EPI, int SUB>
-__global__ void __launch_bounds__(GemmThreads<(EPI == kEpiLn || EPI == kEpiLnGelu)>::kThreads, 1)
+__global__ void __launch_bounds__(GemmThreads<epi_has_stat_warps(EPI)>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
                    const GemmParams p) {
-  constexpr bool kLN = (EPI == kEpiLn || EPI == kEpiLnGelu);
-  constexpr bool kRes = (EPI == kEpiBiasRes);
+  constexpr bool kLN = epi_has_stat_warps(EPI);  // statistics warps in this kernel
+  constexpr bool kRes = epi_has_res(EPI);
   using Cfg = GemmCfg<BN, SUB>;
   constexpr int STAGES = Cfg::kStages;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
@@ -521,12 +565,12 @@ struct Gemm2Cfg {
 };
 
 template <typename T, int BN, int EPI, int SUB>
-__global__ void __launch_bounds__(GemmThreads<(EPI == kEpiLn || EPI == kEpiLnGelu)>::kThreads, 1)
+__global__ void __launch_bounds__(GemmThreads<epi_has_stat_warps(EPI)>::kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
                     const GemmParams p) {
-  constexpr bool kLN = (EPI == kEpiLn || EPI == kEpiLnGelu);
-  constexpr bool kRes = (EPI == kEpiBiasRes);
+  constexpr bool kLN = epi_has_stat_warps(EPI);  // statistics warps in this kernel
+  constexpr bool kRes = epi_has_res(EPI);
   using Cfg = Gemm2Cfg<BN, SUB>;
   constexpr int STAGES = Cfg::kStages;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;

@@ -32,10 +32,9 @@ int launch_gemm_tc(const GemmIO& io, const GemmParams& p, cudaStream_t stream) {
   SG_TRY(make_tmap_2d(&ta, io.a, 2, p.M, p.K, io.lda, kGemmBM, kGemmBK));
   SG_TRY(make_tmap_2d(&tb, io.b, 2, p.N, p.K, io.ldb, BN, kGemmBK));
   SG_TRY(make_tmap_2d(&to, io.out, 2, p.M, p.N, io.ldo, 32, kEpiCols));
-  if (EPI == kEpiBiasRes) SG_TRY(make_tmap_2d(&tr, io.res, 2, p.M, p.N, io.ldr, 32, kEpiCols));
+  if (epi_has_res(EPI)) SG_TRY(make_tmap_2d(&tr, io.res, 2, p.M, p.N, io.ldr, 32, kEpiCols));
   else tr = to;
-  constexpr bool kLN = (EPI == kEpiLn || EPI == kEpiLnGelu);
-  constexpr int threads = GemmThreads<kLN>::kThreads;
+  constexpr int threads = GemmThreads<epi_has_stat_warps(EPI)>::kThreads;
   constexpr int smem = GemmCfg<BN, SUB>::kSmemBytes;
   auto kern = gemm_tc_kernel<T, BN, EPI, SUB>;
   static bool attr_done = false;  // per instantiation
@@ -57,10 +56,9 @@ int launch_gemm_tc2(const GemmIO& io, const GemmParams& p, cudaStream_t stream) 
   SG_TRY(make_tmap_2d(&ta, io.a, 2, p.M, p.K, io.lda, kGemmBM, kGemmBK));
   SG_TRY(make_tmap_2d(&tb, io.b, 2, p.N, p.K, io.ldb, BN / 2, kGemmBK));
   SG_TRY(make_tmap_2d(&to, io.out, 2, p.M, p.N, io.ldo, 32, kEpiCols));
-  if (EPI == kEpiBiasRes) SG_TRY(make_tmap_2d(&tr, io.res, 2, p.M, p.N, io.ldr, 32, kEpiCols));
+  if (epi_has_res(EPI)) SG_TRY(make_tmap_2d(&tr, io.res, 2, p.M, p.N, io.ldr, 32, kEpiCols));
   else tr = to;
-  constexpr bool kLN = (EPI == kEpiLn || EPI == kEpiLnGelu);
-  constexpr int threads = GemmThreads<kLN>::kThreads;
+  constexpr int threads = GemmThreads<epi_has_stat_warps(EPI)>::kThreads;
   constexpr int smem = Gemm2Cfg<BN, SUB>::kSmemBytes;
   auto kern = gemm_tc2_kernel<T, BN, EPI, SUB>;
   static bool attr_done = false;  // per instantiation
@@ -95,7 +93,7 @@ std::atomic<int> g_gemm_variant{0};
 // read the A stage locally), the others on SM pairs.
 template <typename T, int BN, int EPI>
 int launch_gemm_any(const GemmIO& io, const GemmParams& p, cudaStream_t s) {
-  constexpr bool kLN = (EPI == kEpiLn || EPI == kEpiLnGelu);
+  constexpr bool kLN = epi_has_stat_warps(EPI);
   int v = g_gemm_variant.load();
   if (v == 0) v = kLN ? 1 : 2;
   if (v == 2) return launch_gemm_tc2<T, BN, EPI, 2>(io, p, s);
@@ -111,6 +109,9 @@ int dispatch_epi(int epi, const GemmIO& io, const GemmParams& p, cudaStream_t s)
     case kEpiLn: return launch_gemm_any<T, BN, kEpiLn>(io, p, s);
     case kEpiLnGelu: return launch_gemm_any<T, BN, kEpiLnGelu>(io, p, s);
     case kEpiBiasGelu: return launch_gemm_any<T, BN, kEpiBiasGelu>(io, p, s);
+    case kEpiLnRs: return launch_gemm_any<T, BN, kEpiLnRs>(io, p, s);
+    case kEpiLnRsGelu: return launch_gemm_any<T, BN, kEpiLnRsGelu>(io, p, s);
+    case kEpiBiasResRs: return launch_gemm_any<T, BN, kEpiBiasResRs>(io, p, s);
     default: return set_error(SIGLIP2_ERR_ARG, "unknown epilogue %d", epi);
   }
 }
@@ -126,21 +127,27 @@ int dispatch_bn(int epi, const GemmIO& io, const GemmParams& p, cudaStream_t s) 
 
 int sg_gemm_impl(int dtype, int epi, const void* a, int lda, const void* b, int ldb, void* out, int ldo, int M, int N,
                  int K, const float* bias, const void* res, int ldr, const float* c1, const float* c2, float eps,
-                 cudaStream_t stream) {
+                 cudaStream_t stream, const float2* rs_in = nullptr, float2* rs_acc = nullptr,
+                 float2* rs_zero = nullptr) {
   SG_CHECK_ARG(M >= 0 && N > 0 && K > 0, "bad GEMM shape M=%d N=%d K=%d", M, N, K);
   if (M == 0) return SIGLIP2_OK;
   SG_CHECK_ARG(a && b && out, "null operand");
-  SG_CHECK_ARG(epi >= 0 && epi <= 4, "unknown epilogue %d", epi);
-  const bool ln = (epi == kEpiLn || epi == kEpiLnGelu);
+  SG_CHECK_ARG(epi >= 0 && epi <= 7, "unknown epilogue %d", epi);
+  const bool ln = epi_is_ln(epi);
   SG_CHECK_ARG(!ln || (c1 && c2), "LN epilogue needs c1 and c2");
   SG_CHECK_ARG(ln || bias, "bias epilogue needs bias");
-  SG_CHECK_ARG(epi != kEpiBiasRes || res, "residual epilogue needs res");
-  SG_CHECK_ARG(!ln || K % kGemmBK == 0, "LN-folded GEMM needs K %% 64 == 0 (K=%d)", K);
+  SG_CHECK_ARG(!epi_has_res(epi) || res, "residual epilogue needs res");
+  SG_CHECK_ARG(!epi_has_stat_warps(epi) || K % kGemmBK == 0, "LN-folded GEMM needs K %% 64 == 0 (K=%d)", K);
+  SG_CHECK_ARG(!(epi == kEpiLnRs || epi == kEpiLnRsGelu) || rs_in, "row-sum LN epilogue needs rs_in");
+  SG_CHECK_ARG(epi != kEpiBiasResRs || rs_acc, "row-sum accumulating epilogue needs rs_acc");
+  const auto misaligned8 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 7u) != 0; };
+  if (misaligned8(rs_in) || misaligned8(rs_acc) || misaligned8(rs_zero))
+    return set_error(SIGLIP2_ERR_ALIGN, "row-sum buffers must be 8-byte aligned");
   if (dtype != SIGLIP2_BF16 && dtype != SIGLIP2_F16)
     return set_error(SIGLIP2_ERR_UNSUPPORTED, "tensor-core GEMM supports bf16/f16 only (dtype=%d)", dtype);
-  if (N % 8 || K % 8 || lda % 8 || ldb % 8 || ldo % 8 || (epi == kEpiBiasRes && ldr % 8))
+  if (N % 8 || K % 8 || lda % 8 || ldb % 8 || ldo % 8 || (epi_has_res(epi) && ldr % 8))
     return set_error(SIGLIP2_ERR_ALIGN, "N, K and leading dimensions must be multiples of 8");
-  if (lda < K || ldb < K || ldo < N || (epi == kEpiBiasRes && ldr < N))
+  if (lda < K || ldb < K || ldo < N || (epi_has_res(epi) && ldr < N))
     return set_error(SIGLIP2_ERR_SHAPE, "leading dimension smaller than the row");
   if (!aligned16(out) || (res && !aligned16(res)))
     return set_error(SIGLIP2_ERR_ALIGN, "output/residual must be 16-byte aligned");
@@ -154,6 +161,9 @@ int sg_gemm_impl(int dtype, int epi, const void* a, int lda, const void* b, int 
   p.c1 = c1;
   p.c2 = c2;
   p.eps = eps;
+  p.rs_in = rs_in;
+  p.rs_acc = rs_acc;
+  p.rs_zero = rs_zero;
   GemmIO io{a, lda, b, ldb, out, ldo, res, ldr};
   if (dtype == SIGLIP2_BF16) return dispatch_bn<__nv_bfloat16>(epi, io, p, stream);
   return dispatch_bn<__half>(epi, io, p, stream);
@@ -423,6 +433,13 @@ int sg_forward_impl(const siglip2_config* c, const siglip2_weights* w, const voi
   const int hdp = padded_head_dim(hd);
   const int nqkv = 3 * H * hdp;
 
+  // Row sums of the residual stream for the LayerNorm-folded GEMMs: the GEMM
+  // that writes x accumulates them; two buffers alternate (x after the
+  // embeddings / fc2 -> rs_b, after out-proj -> rs_a) and each producer
+  // zeroes the buffer its consumer has just finished with.
+  float2* rs_a = f.rowsums;
+  float2* rs_b = f.rowsums + N;
+  SG_CUDA(cudaMemsetAsync(f.rowsums, 0, sizeof(float2) * 2 * static_cast<size_t>(N), s));
   // embeddings: x = pos(hw) ; x = patches Wp^T + bp + x
   SG_TRY(sg_token_image_impl(cu, B, N, f.tok_img, s));
   SG_TRY(sg_posemb_impl(dt, w->pos_table, c->pos_grid, D, f.tok_img, hw, cu, N, f.x, s));
@@ -432,19 +449,19 @@ int sg_forward_impl(const siglip2_config* c, const siglip2_weights* w, const voi
     else SG_TRY(launch_gather<__half>(patches, c->patch_dim, P, cu, f.tok_img, N, f.hmid, s));
     prow = f.hmid;
   }
-  SG_TRY(sg_gemm_impl(dt, kEpiBiasRes, prow, c->patch_dim, w->patch_w, c->patch_dim, f.x, D, N, D, c->patch_dim,
-                      w->patch_b, f.x, D, nullptr, nullptr, 0.f, s));
+  SG_TRY(sg_gemm_impl(dt, kEpiBiasResRs, prow, c->patch_dim, w->patch_w, c->patch_dim, f.x, D, N, D, c->patch_dim,
+                      w->patch_b, f.x, D, nullptr, nullptr, 0.f, s, nullptr, rs_b, nullptr));
   for (int l = 0; l < c->layers; ++l) {
     const siglip2_layer_weights& lw = w->layers[l];
-    SG_TRY(sg_gemm_impl(dt, kEpiLn, f.x, D, lw.qkv_w, D, f.qkv, nqkv, N, nqkv, D, nullptr, nullptr, 0, lw.qkv_c1,
-                        lw.qkv_c2, c->eps, s));
+    SG_TRY(sg_gemm_impl(dt, kEpiLnRs, f.x, D, lw.qkv_w, D, f.qkv, nqkv, N, nqkv, D, nullptr, nullptr, 0, lw.qkv_c1,
+                        lw.qkv_c2, c->eps, s, rs_b, nullptr, nullptr));
     SG_TRY(sg_fmha_impl(dt, f.qkv, N, cu, tiles, T, H, hd, f.attn, D, s));
-    SG_TRY(sg_gemm_impl(dt, kEpiBiasRes, f.attn, D, lw.out_w, D, f.x, D, N, D, D, lw.out_b, f.x, D, nullptr, nullptr,
-                        0.f, s));
-    SG_TRY(sg_gemm_impl(dt, kEpiLnGelu, f.x, D, lw.fc1_w, D, f.hmid, I, N, I, D, nullptr, nullptr, 0, lw.fc1_c1,
-                        lw.fc1_c2, c->eps, s));
-    SG_TRY(sg_gemm_impl(dt, kEpiBiasRes, f.hmid, I, lw.fc2_w, I, f.x, D, N, D, I, lw.fc2_b, f.x, D, nullptr, nullptr,
-                        0.f, s));
+    SG_TRY(sg_gemm_impl(dt, kEpiBiasResRs, f.attn, D, lw.out_w, D, f.x, D, N, D, D, lw.out_b, f.x, D, nullptr,
+                        nullptr, 0.f, s, nullptr, rs_a, rs_b));
+    SG_TRY(sg_gemm_impl(dt, kEpiLnRsGelu, f.x, D, lw.fc1_w, D, f.hmid, I, N, I, D, nullptr, nullptr, 0, lw.fc1_c1,
+                        lw.fc1_c2, c->eps, s, rs_a, nullptr, nullptr));
+    SG_TRY(sg_gemm_impl(dt, kEpiBiasResRs, f.hmid, I, lw.fc2_w, I, f.x, D, N, D, I, lw.fc2_b, f.x, D, nullptr,
+                        nullptr, 0.f, s, nullptr, rs_b, rs_a));
   }
   // post-LayerNorm -> last_hidden_state (packed or padded with zero rows)
   SG_TRY(sg_layernorm_impl(dt, f.x, last_hidden, w->post_ln_w, w->post_ln_b, P > 0 ? B * P : N, D, c->eps,
@@ -536,6 +553,15 @@ int siglip2_gemm(int dtype, int epilogue, const void* a_dev, int lda, const void
                  const float* c1_dev, const float* c2_dev, float eps, void* stream) {
   return sg_gemm_impl(dtype, epilogue, a_dev, lda, b_dev, ldb, out_dev, ldo, M, N, K, bias_dev, res_dev, ldr, c1_dev,
                       c2_dev, eps, static_cast<cudaStream_t>(stream));
+}
+
+int siglip2_gemm_rowsums(int dtype, int epilogue, const void* a_dev, int lda, const void* b_dev, int ldb,
+                         void* out_dev, int ldo, int M, int N, int K, const float* bias_dev, const void* res_dev,
+                         int ldr, const float* c1_dev, const float* c2_dev, float eps, const float* rs_in_dev,
+                         float* rs_acc_dev, float* rs_zero_dev, void* stream) {
+  return sg_gemm_impl(dtype, epilogue, a_dev, lda, b_dev, ldb, out_dev, ldo, M, N, K, bias_dev, res_dev, ldr, c1_dev,
+                      c2_dev, eps, static_cast<cudaStream_t>(stream), reinterpret_cast<const float2*>(rs_in_dev),
+                      reinterpret_cast<float2*>(rs_acc_dev), reinterpret_cast<float2*>(rs_zero_dev));
 }
 
 int siglip2_layernorm(int dtype, const void* x_dev, void* y_dev, const float* gamma_dev, const float* beta_dev,

@@ -127,3 +127,20 @@ def head_pool(x: torch.Tensor, u: torch.Tensor, cu_seqlens: torch.Tensor, n_toke
     L.call("siglip2_head_pool", dtype_code(x.dtype), x.data_ptr(), D, H, cu_seqlens.data_ptr(), B, max_patches,
            u.data_ptr(), scores.data_ptr(), pooled.data_ptr(), _stream(x.device))
     return pooled
+
+
+def gemm_rowsums(a: torch.Tensor, w: torch.Tensor, epilogue: int, bias=None, res=None, c1=None, c2=None,
+                 eps: float = 1e-6, rs_in=None, rs_acc=None, rs_zero=None,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """``siglip2_gemm_rowsums``: row-sum LayerNorm epilogues (``rs_*`` are
+    ``[M, 2]`` float32 (sum, sum of squares) buffers)."""
+    _need_cuda(a, w, bias, res, c1, c2, rs_in, rs_acc, rs_zero, out)
+    M, K = a.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=a.dtype, device=a.device)
+    L.call("siglip2_gemm_rowsums", dtype_code(a.dtype), epilogue, a.data_ptr(), a.stride(0), w.data_ptr(),
+           w.stride(0), out.data_ptr(), out.stride(0), M, N, K, _ptr(bias), _ptr(res),
+           res.stride(0) if res is not None else 0, _ptr(c1), _ptr(c2), float(eps), _ptr(rs_in), _ptr(rs_acc),
+           _ptr(rs_zero), _stream(a.device))
+    return out

@@ -95,3 +95,45 @@ def test_gemm_rejects_bad_args():
     with pytest.raises(L.Siglip2Error):
         ops.gemm(a, w, L.EPI_BIAS, bias=torch.zeros(64, device="cuda"))
     L.check(L.load().siglip2_check_device(1))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M,N,K", [(777, 1152, 4304), (300, 1152, 1152), (4097, 768, 3072)])
+def test_gemm_residual_accumulates_row_sums(dtype, M, N, K):
+    g = torch.Generator(device="cuda").manual_seed(M + N)
+    a = torch.randn(M, K, device="cuda", generator=g).to(dtype)
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.03).to(dtype)
+    bias = torch.randn(N, device="cuda", generator=g) * 0.1
+    res = torch.randn(M, N, device="cuda", generator=g).to(dtype)
+    acc = torch.zeros(M, 2, device="cuda")
+    junk = torch.full((M, 2), 7.0, device="cuda")
+    out = ops.gemm_rowsums(a, w, L.EPI_BIAS_RES_ROWSUMS, bias=bias, res=res, rs_acc=acc, rs_zero=junk)
+    torch.cuda.synchronize()
+    _close(out, a.float() @ w.float().T + bias + res.float())
+    o = out.float()  # sums of exactly the stored (rounded) values
+    assert torch.allclose(acc[:, 0], o.sum(1), rtol=1e-4, atol=1e-2)
+    assert torch.allclose(acc[:, 1], (o * o).sum(1), rtol=1e-4, atol=1e-2)
+    assert not junk.any()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M,N,K", [(300, 3840, 1152), (1000, 4304, 1152), (513, 2304, 768)])
+@pytest.mark.parametrize("gelu", [False, True])
+def test_gemm_layernorm_from_row_sums(dtype, M, N, K, gelu):
+    g = torch.Generator(device="cuda").manual_seed(N + K + 1)
+    x = (torch.randn(M, K, device="cuda", generator=g) * (1 + 3 * torch.rand(M, 1, device="cuda", generator=g))
+         + torch.randn(M, 1, device="cuda", generator=g) * 2).to(dtype)
+    w = torch.randn(N, K, device="cuda", generator=g) * 0.03
+    b = torch.randn(N, device="cuda", generator=g) * 0.1
+    gamma = 1 + 0.2 * torch.randn(K, device="cuda", generator=g)
+    beta = 0.1 * torch.randn(K, device="cuda", generator=g)
+    wg, c1, c2 = ops.fold_layernorm(w, b, gamma, beta, dtype)
+    xf = x.float()
+    rs = torch.stack([xf.sum(1), (xf * xf).sum(1)], 1).contiguous()
+    out = ops.gemm_rowsums(x, wg, L.EPI_LN_ROWSUMS_GELU if gelu else L.EPI_LN_ROWSUMS, c1=c1, c2=c2, eps=1e-6,
+                           rs_in=rs)
+    ref = F.layer_norm(xf, (K,), gamma, beta, 1e-6) @ w.T + b
+    if gelu:
+        ref = _gelu(ref)
+    torch.cuda.synchronize()
+    _close(out, ref, tol=2e-2)
