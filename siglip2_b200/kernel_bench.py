@@ -21,7 +21,8 @@ from . import ops
 from . import workloads as W
 
 EPIS = {"bias": L.EPI_BIAS, "bias_res": L.EPI_BIAS_RES, "ln": L.EPI_LN, "ln_gelu": L.EPI_LN_GELU,
-        "bias_gelu": L.EPI_BIAS_GELU}
+        "bias_gelu": L.EPI_BIAS_GELU, "lnrs": L.EPI_LN_ROWSUMS, "lnrs_gelu": L.EPI_LN_ROWSUMS_GELU,
+        "bias_res_rs": L.EPI_BIAS_RES_ROWSUMS}
 
 
 def _time(fn, reps: int, warmup: int = 3) -> float:
@@ -41,9 +42,17 @@ def bench_gemm(m, n, k, epi, reps, dtype=torch.bfloat16, warmup=3):
     a = torch.randn(m, k, device="cuda").to(dtype)
     w = (torch.randn(n, k, device="cuda") * 0.02).to(dtype)
     vec = torch.randn(n, device="cuda") * 0.1
-    res = torch.randn(m, n, device="cuda").to(dtype) if EPIS[epi] == L.EPI_BIAS_RES else None
+    res = torch.randn(m, n, device="cuda").to(dtype) if epi in ("bias_res", "bias_res_rs") else None
     out = torch.empty(m, n, device="cuda", dtype=dtype)
-    ms = _time(lambda: ops.gemm(a, w, EPIS[epi], bias=vec, res=res, c1=vec, c2=vec, out=out), reps, warmup)
+    rs = torch.rand(m, 2, device="cuda") + 1.0
+    if epi in ("lnrs", "lnrs_gelu", "bias_res_rs"):
+        acc = torch.zeros(m, 2, device="cuda") if epi == "bias_res_rs" else None
+        rs_in = rs if epi != "bias_res_rs" else None
+        fn = lambda: ops.gemm_rowsums(a, w, EPIS[epi], bias=vec, res=res, c1=vec, c2=vec, rs_in=rs_in, rs_acc=acc,  # noqa: E731
+                                      out=out)
+    else:
+        fn = lambda: ops.gemm(a, w, EPIS[epi], bias=vec, res=res, c1=vec, c2=vec, out=out)  # noqa: E731
+    ms = _time(fn, reps, warmup)
     return {"kernel": "gemm", "epi": epi, "M": m, "N": n, "K": k, "ms": ms, "tflops": 2 * m * n * k / ms / 1e9}
 
 
@@ -74,8 +83,9 @@ def bench_layer(preset, images, max_patches, reps):
     hdp = ops.padded_head_dim(D // H)
     N = int((lambda s: (s[:, 0] * s[:, 1]).sum())(_shapes(preset, images, max_patches)))
     out = []
-    for name, n, k, epi in (("qkv", 3 * H * hdp, D, "ln"), ("out", D, D, "bias_res"), ("fc1", I, D, "ln_gelu"),
-                            ("fc2", D, I, "bias_res")):
+    # the epilogues the forward uses
+    for name, n, k, epi in (("qkv", 3 * H * hdp, D, "lnrs"), ("out", D, D, "bias_res_rs"), ("fc1", I, D, "lnrs_gelu"),
+                            ("fc2", D, I, "bias_res_rs")):
         r = bench_gemm(N, n, k, epi, reps)
         r["name"] = name
         out.append(r)
