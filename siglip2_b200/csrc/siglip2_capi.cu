@@ -10,6 +10,7 @@
 #include "rowops.cuh"
 #include "fmha.cuh"
 #include "forward.cuh"
+#include "simt_f32.cuh"
 
 using namespace sg;
 
@@ -143,8 +144,32 @@ int sg_gemm_impl(int dtype, int epi, const void* a, int lda, const void* b, int 
   const auto misaligned8 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 7u) != 0; };
   if (misaligned8(rs_in) || misaligned8(rs_acc) || misaligned8(rs_zero))
     return set_error(SIGLIP2_ERR_ALIGN, "row-sum buffers must be 8-byte aligned");
+  if (dtype == SIGLIP2_F32) {
+    if (epi_has_stat_warps(epi))
+      return set_error(SIGLIP2_ERR_UNSUPPORTED, "fp32 GEMM: use the row-sum LayerNorm epilogues (5, 6)");
+    if (epi_has_res(epi) && !res) return set_error(SIGLIP2_ERR_ARG, "residual epilogue needs res");
+    GemmParams p{};
+    p.M = M; p.N = N; p.K = K; p.bias = bias; p.c1 = c1; p.c2 = c2; p.eps = eps;
+    p.rs_in = rs_in; p.rs_acc = rs_acc; p.rs_zero = rs_zero;
+    dim3 grid((N + kSgBN - 1) / kSgBN, (M + kSgBM - 1) / kSgBM);
+    const float* A = static_cast<const float*>(a);
+    const float* Bw = static_cast<const float*>(b);
+    float* O = static_cast<float*>(out);
+    const float* R = static_cast<const float*>(res);
+    switch (epi) {
+      case kEpiBias: gemm_f32_kernel<kEpiBias><<<grid, 256, 0, stream>>>(A, lda, Bw, ldb, O, ldo, R, ldr, p); break;
+      case kEpiBiasRes: gemm_f32_kernel<kEpiBiasRes><<<grid, 256, 0, stream>>>(A, lda, Bw, ldb, O, ldo, R, ldr, p); break;
+      case kEpiBiasGelu: gemm_f32_kernel<kEpiBiasGelu><<<grid, 256, 0, stream>>>(A, lda, Bw, ldb, O, ldo, R, ldr, p); break;
+      case kEpiLnRs: gemm_f32_kernel<kEpiLnRs><<<grid, 256, 0, stream>>>(A, lda, Bw, ldb, O, ldo, R, ldr, p); break;
+      case kEpiLnRsGelu: gemm_f32_kernel<kEpiLnRsGelu><<<grid, 256, 0, stream>>>(A, lda, Bw, ldb, O, ldo, R, ldr, p); break;
+      case kEpiBiasResRs: gemm_f32_kernel<kEpiBiasResRs><<<grid, 256, 0, stream>>>(A, lda, Bw, ldb, O, ldo, R, ldr, p); break;
+      default: return set_error(SIGLIP2_ERR_ARG, "unknown epilogue %d", epi);
+    }
+    SG_LAUNCH_CHECK();
+    return SIGLIP2_OK;
+  }
   if (dtype != SIGLIP2_BF16 && dtype != SIGLIP2_F16)
-    return set_error(SIGLIP2_ERR_UNSUPPORTED, "tensor-core GEMM supports bf16/f16 only (dtype=%d)", dtype);
+    return set_error(SIGLIP2_ERR_UNSUPPORTED, "GEMM supports f32/bf16/f16 (dtype=%d)", dtype);
   if (N % 8 || K % 8 || lda % 8 || ldb % 8 || ldo % 8 || (epi_has_res(epi) && ldr % 8))
     return set_error(SIGLIP2_ERR_ALIGN, "N, K and leading dimensions must be multiples of 8");
   if (lda < K || ldb < K || ldo < N || (epi_has_res(epi) && ldr < N))
@@ -301,7 +326,22 @@ int sg_fmha_impl(int dtype, const void* qkv, int N, const int* cu, const int* ti
   const int2* t2 = reinterpret_cast<const int2*>(tiles);
   if (dtype == SIGLIP2_BF16) return dispatch_fmha<__nv_bfloat16>(qkv, N, cu, t2, n_tiles, H, hd, out, ldo, s);
   if (dtype == SIGLIP2_F16) return dispatch_fmha<__half>(qkv, N, cu, t2, n_tiles, H, hd, out, ldo, s);
-  return set_error(SIGLIP2_ERR_UNSUPPORTED, "tensor-core attention supports bf16/f16 only");
+  if (dtype == SIGLIP2_F32) {
+    // fp32: q | k | v with head_dim columns per head (no padding)
+    dim3 grid(n_tiles, H);
+    const float sc = 1.f / sqrtf(static_cast<float>(hd));
+    const float* q = static_cast<const float*>(qkv);
+    float* o = static_cast<float*>(out);
+    switch (hd) {
+      case 64: fmha_f32_kernel<64><<<grid, 128, 0, s>>>(q, cu, t2, H, sc, o, ldo); break;
+      case 72: fmha_f32_kernel<72><<<grid, 128, 0, s>>>(q, cu, t2, H, sc, o, ldo); break;
+      case 96: fmha_f32_kernel<96><<<grid, 128, 0, s>>>(q, cu, t2, H, sc, o, ldo); break;
+      default: return set_error(SIGLIP2_ERR_UNSUPPORTED, "fp32 attention: head_dim %d not supported (64, 72, 96)", hd);
+    }
+    SG_LAUNCH_CHECK();
+    return SIGLIP2_OK;
+  }
+  return set_error(SIGLIP2_ERR_UNSUPPORTED, "attention supports f32/bf16/f16");
 }
 
 // ---------------------------------------------------------------------------
@@ -397,8 +437,8 @@ int validate_config(const siglip2_config* c) {
                    c->pos_grid > 0,
                "non-positive config field");
   SG_CHECK_ARG(c->head_dim * c->heads == c->hidden, "head_dim * heads != hidden");
-  if (c->dtype != SIGLIP2_BF16 && c->dtype != SIGLIP2_F16)
-    return set_error(SIGLIP2_ERR_UNSUPPORTED, "forward supports bf16/f16 on the tensor-core path (dtype %d)", c->dtype);
+  if (c->dtype != SIGLIP2_BF16 && c->dtype != SIGLIP2_F16 && c->dtype != SIGLIP2_F32)
+    return set_error(SIGLIP2_ERR_UNSUPPORTED, "forward supports f32, bf16 and f16 (dtype %d)", c->dtype);
   if (c->hidden % 64 || c->intermediate % 8 || c->patch_dim % 8)
     return set_error(SIGLIP2_ERR_UNSUPPORTED, "hidden must be a multiple of 64, intermediate/patch_dim of 8");
   if (c->head_dim != 64 && c->head_dim != 72 && c->head_dim != 80 && c->head_dim != 96)
@@ -430,7 +470,7 @@ int sg_forward_impl(const siglip2_config* c, const siglip2_weights* w, const voi
   const int* tiles = meta + meta_tiles_offset(B);
   const int dt = c->dtype;
   const int D = c->hidden, I = c->intermediate, H = c->heads, hd = c->head_dim;
-  const int hdp = padded_head_dim(hd);
+  const int hdp = dt == SIGLIP2_F32 ? hd : padded_head_dim(hd);  // fp32 attention reads unpadded heads
   const int nqkv = 3 * H * hdp;
 
   // Row sums of the residual stream for the LayerNorm-folded GEMMs: the GEMM
@@ -446,7 +486,8 @@ int sg_forward_impl(const siglip2_config* c, const siglip2_weights* w, const voi
   const void* prow = patches;
   if (P > 0) {
     if (dt == SIGLIP2_BF16) SG_TRY(launch_gather<__nv_bfloat16>(patches, c->patch_dim, P, cu, f.tok_img, N, f.hmid, s));
-    else SG_TRY(launch_gather<__half>(patches, c->patch_dim, P, cu, f.tok_img, N, f.hmid, s));
+    else if (dt == SIGLIP2_F16) SG_TRY(launch_gather<__half>(patches, c->patch_dim, P, cu, f.tok_img, N, f.hmid, s));
+    else SG_TRY(launch_gather<float>(patches, c->patch_dim, P, cu, f.tok_img, N, f.hmid, s));
     prow = f.hmid;
   }
   SG_TRY(sg_gemm_impl(dt, kEpiBiasResRs, prow, c->patch_dim, w->patch_w, c->patch_dim, f.x, D, N, D, c->patch_dim,
@@ -471,11 +512,19 @@ int sg_forward_impl(const siglip2_config* c, const siglip2_weights* w, const voi
     SG_TRY(sg_gemm_impl(dt, kEpiBias, f.hpool, D, w->head_v_w, D, f.hY, D, B * H, D, D, w->head_v_b, nullptr, 0,
                         nullptr, nullptr, 0.f, s));
     if (dt == SIGLIP2_BF16) SG_TRY(launch_select<__nv_bfloat16>(f.hY, H, hd, D, B, f.hattn, s));
-    else SG_TRY(launch_select<__half>(f.hY, H, hd, D, B, f.hattn, s));
+    else if (dt == SIGLIP2_F16) SG_TRY(launch_select<__half>(f.hY, H, hd, D, B, f.hattn, s));
+    else SG_TRY(launch_select<float>(f.hY, H, hd, D, B, f.hattn, s));
     SG_TRY(sg_gemm_impl(dt, kEpiBias, f.hattn, D, w->head_o_w, D, f.ha, D, B, D, D, w->head_o_b, nullptr, 0, nullptr,
                         nullptr, 0.f, s));
-    SG_TRY(sg_gemm_impl(dt, kEpiLnGelu, f.ha, D, w->head_fc1_w, D, f.hmid2, I, B, I, D, nullptr, nullptr, 0,
-                        w->head_fc1_c1, w->head_fc1_c2, c->eps, s));
+    if (dt == SIGLIP2_F32) {
+      rowsums_f32_kernel<<<(B + 7) / 8, 256, 0, s>>>(static_cast<const float*>(f.ha), B, D, rs_a);
+      SG_LAUNCH_CHECK();
+      SG_TRY(sg_gemm_impl(dt, kEpiLnRsGelu, f.ha, D, w->head_fc1_w, D, f.hmid2, I, B, I, D, nullptr, nullptr, 0,
+                          w->head_fc1_c1, w->head_fc1_c2, c->eps, s, rs_a, nullptr, nullptr));
+    } else {
+      SG_TRY(sg_gemm_impl(dt, kEpiLnGelu, f.ha, D, w->head_fc1_w, D, f.hmid2, I, B, I, D, nullptr, nullptr, 0,
+                          w->head_fc1_c1, w->head_fc1_c2, c->eps, s));
+    }
     SG_TRY(sg_gemm_impl(dt, kEpiBiasRes, f.hmid2, I, w->head_fc2_w, I, pooled, D, B, D, I, w->head_fc2_b, f.ha, D,
                         nullptr, nullptr, 0.f, s));
   }
