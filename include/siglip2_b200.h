@@ -26,6 +26,8 @@
  *                       fused Linear+GELU                   optimized_siglip2/ops/MLP.py:233-304
  *                       LayerNorm feeding a Linear           model.py:211,219 / ops/layer_norm.py:364-547
  *  siglip2_layernorm -> nn.LayerNorm (post_layernorm)       model.py:256-258,286
+ *  siglip2_patch_embed -> Siglip2SequenceEmbeddings.forward (patch Linear + resized
+ *                       position grid)                       model.py:68-120
  *  siglip2_posemb    -> Siglip2SequenceEmbeddings pos-emb resize loop  model.py:90-119
  *  siglip2_fmha_varlen -> flex_attention + document block mask         model.py:156-163
  *  siglip2_map_head  -> transformers Siglip2MultiheadAttentionPoolingHead.forward
@@ -77,6 +79,13 @@ const char* siglip2_last_error(void);
 /* Number of kernel launches this library has enqueued since it was loaded. */
 unsigned long long siglip2_launch_count(void);
 
+/* Failure-path self-test: enqueues one CTA that waits on an mbarrier nothing
+ * arrives at; after limit_ns (<= 2 s) it gives up exactly as a stalled
+ * pipeline stage would (device error flag, site 901) and returns.  A
+ * following siglip2_check_device() reports SIGLIP2_ERR_TIMEOUT and the
+ * context stays usable. */
+int siglip2_selftest_wait_timeout(long long limit_ns, void* stream);
+
 /* GEMM kernel selection for every later siglip2_gemm / siglip2_forward call of
  * the process: 0 = automatic (default), 1 = one SM per 128 x BN tile,
  * 2 = CTA pairs on two SMs per 256 x BN tile (tcgen05 cta_group::2). */
@@ -108,6 +117,18 @@ int siglip2_gemm_rowsums(int dtype, int epilogue, const void* a_dev, int lda, co
                          void* out_dev, int ldo, int M, int N, int K, const float* bias_dev, const void* res_dev,
                          int ldr, const float* c1_dev, const float* c2_dev, float eps, const float* rs_in_dev,
                          float* rs_acc_dev, float* rs_zero_dev, void* stream);
+
+/* Patch embedding with the position embedding fused into the GEMM epilogue:
+ *   out[t] = patches[t] . W^T + bias + resize(table)(t)      (out [N, D])
+ * where token t is pixel (y, x) = divmod(t - cu[b], w) of image
+ * b = tok_img[t] with grid (h, w) = hw[2b], hw[2b+1], and resize is the
+ * antialiased bilinear interpolation of the grid x grid fp32 table
+ * [grid^2, D].  rs_acc[t] += (sum, sum of squares) of the rounded out row
+ * (float pairs, zero beforehand: the LayerNorm statistics of the first
+ * layer).  Replaces Siglip2SequenceEmbeddings.forward, model.py:68-120. */
+int siglip2_patch_embed(int dtype, const void* patches_dev, int patch_dim, const void* w_dev, const float* bias_dev,
+                        const float* table_dev, int grid, const int* tok_img_dev, const int* hw_dev,
+                        const int* cu_seqlens_dev, int N, int D, void* out_dev, float* rs_acc_dev, void* stream);
 
 /* LayerNorm over the last dimension (fp32 statistics, biased variance).
  * Packed mode (cu_seqlens_dev == NULL): y[r] = LN(x[r]) for r < rows.

@@ -21,11 +21,14 @@ SIGNATURES = {
     "siglip2_check_device": (_c_int, [_c_int]),
     "siglip2_launch_count": (ctypes.c_ulonglong, []),
     "siglip2_set_gemm_variant": (_c_int, [_c_int]),
+    "siglip2_selftest_wait_timeout": (_c_int, [ctypes.c_longlong, _vp]),
     "siglip2_get_gemm_variant": (_c_int, []),
     "siglip2_gemm": (_c_int, [_c_int, _c_int, _vp, _c_int, _vp, _c_int, _vp, _c_int, _c_int, _c_int, _c_int,
                               _vp, _vp, _c_int, _vp, _vp, _c_float, _vp]),
     "siglip2_gemm_rowsums": (_c_int, [_c_int, _c_int, _vp, _c_int, _vp, _c_int, _vp, _c_int, _c_int, _c_int, _c_int,
                                       _vp, _vp, _c_int, _vp, _vp, _c_float, _vp, _vp, _vp, _vp]),
+    "siglip2_patch_embed": (_c_int, [_c_int, _vp, _c_int, _vp, _vp, _vp, _c_int, _vp, _vp, _vp, _c_int, _c_int, _vp,
+                                     _vp, _vp]),
     "siglip2_layernorm": (_c_int, [_c_int, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_float, _vp, _c_int, _vp]),
     "siglip2_token_image": (_c_int, [_vp, _c_int, _c_int, _vp, _vp]),
     "siglip2_posemb": (_c_int, [_c_int, _vp, _c_int, _c_int, _vp, _vp, _vp, _c_int, _vp, _vp]),

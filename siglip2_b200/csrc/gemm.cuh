@@ -25,7 +25,7 @@
 // the row/column terms in fp32.
 #pragma once
 
-#include "ptx.cuh"
+#include "rowops.cuh"
 
 namespace sg {
 
@@ -38,6 +38,7 @@ enum GemmEpilogue : int {
   kEpiLnRs = 5,          // as kEpiLn, mu/rstd from row sums accumulated by the producer of A
   kEpiLnRsGelu = 6,      // as kEpiLnGelu, likewise
   kEpiBiasResRs = 7,     // as kEpiBiasRes, and accumulates the row sums of the rounded output
+  kEpiBiasPosRs = 8,     // out = acc + bias + resized position embedding of the row's token, + row sums
 };
 
 __host__ __device__ constexpr bool epi_has_stat_warps(int e) { return e == kEpiLn || e == kEpiLnGelu; }
@@ -54,6 +55,15 @@ struct GemmParams {
   const float2* rs_in;        // [M] (sum, sum of squares) of A's rows over K (kEpiLnRs*)
   float2* rs_acc;             // [M] row sums of the output to accumulate into (kEpiBiasResRs)
   float2* rs_zero;            // [M] optional: zeroed by the CTAs of the first column tile
+  // kEpiBiasPosRs: row t is a token of image tok_img[t] at (y, x) of its
+  // (h, w) = pos_hw[2b], pos_hw[2b+1] grid (t - cu[b] = y * w + x); the
+  // position embedding is the antialiased bilinear resize of the
+  // pos_grid x pos_grid fp32 table [pos_grid^2, N] evaluated there
+  const float* pos_table;
+  int pos_grid;
+  const int* tok_img;
+  const int* pos_hw;
+  const int* cu;
 };
 
 constexpr int kGemmBM = 128;
@@ -130,7 +140,8 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
   constexpr bool kLnMath = epi_is_ln(EPI);
   constexpr bool kGelu = epi_is_gelu(EPI);
   constexpr bool kRes = epi_has_res(EPI);
-  constexpr bool kRsOut = (EPI == kEpiBiasResRs);
+  constexpr bool kRsOut = (EPI == kEpiBiasResRs || EPI == kEpiBiasPosRs);
+  constexpr bool kPos = (EPI == kEpiBiasPosRs);
   constexpr int NCH = BN / kEpiCols;
   const int ew = warp - 2;
   const int q = warp & 3;
@@ -171,6 +182,16 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
       rstd = rsqrtf(fmaxf(rs.y * inv_k - mu * mu, 0.f) + p.eps);
     }
     float rs1 = 0.f, rs2 = 0.f;  // row sums of this tile's rounded outputs (kRsOut)
+    AxisTaps ay{0, 0, 0.f, 1.f, 0.f}, ax{0, 0, 0.f, 1.f, 0.f};  // position-embedding taps of this row (kPos)
+    if constexpr (kPos) {
+      if (my_row < p.M) {
+        const int b = p.tok_img[my_row];
+        const int w = p.pos_hw[2 * b + 1];
+        const int i = my_row - p.cu[b];
+        ay = axis_taps(i / w, p.pos_hw[2 * b], p.pos_grid);
+        ax = axis_taps(i - (i / w) * w, w, p.pos_grid);
+      }
+    }
     const uint32_t tbase = tmem_base + buf * acc_stride + (static_cast<uint32_t>(q * 32) << 16);
     uint32_t ra[32], rb[32];
     SG_TMEM_LD_32(tbase, ra);
@@ -213,6 +234,28 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
           for (int j = 0; j < 32; ++j) {
             v[j] += a[j];
             if constexpr (kGelu) v[j] = gelu_tanh(v[j]);
+          }
+        }
+        if constexpr (kPos) {
+          // separable triangle-filter taps over the fp32 table (L2-resident):
+          // 2 x 2 taps when upsampling, more when the image side is < grid
+          for (int ya = ay.lo; ya < ay.hi; ++ya) {
+            const float wy = axis_w(ay, ya);
+            for (int xa = ax.lo; xa < ax.hi; ++xa) {
+              const float wgt = wy * axis_w(ax, xa);
+              const float4* src =
+                  reinterpret_cast<const float4*>(p.pos_table + static_cast<size_t>(ya * p.pos_grid + xa) * p.N + col0);
+#pragma unroll
+              for (int q4 = 0; q4 < 8; ++q4) {
+                if (col0 + 4 * q4 < p.N) {
+                  const float4 f = __ldg(src + q4);
+                  v[4 * q4] = fmaf(wgt, f.x, v[4 * q4]);
+                  v[4 * q4 + 1] = fmaf(wgt, f.y, v[4 * q4 + 1]);
+                  v[4 * q4 + 2] = fmaf(wgt, f.z, v[4 * q4 + 2]);
+                  v[4 * q4 + 3] = fmaf(wgt, f.w, v[4 * q4 + 3]);
+                }
+              }
+            }
           }
         }
       }

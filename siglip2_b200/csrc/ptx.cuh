@@ -104,6 +104,27 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int si
   }
 }
 
+// Failure-path self-test: one CTA waits on an mbarrier that nothing arrives
+// at, gives up after `limit_ns`, records `site` and returns normally.
+__global__ void selftest_wait_timeout_kernel(unsigned long long limit_ns, int site) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned long long t0 = globaltimer_ns();
+    while (!mbar_try_wait_sleep(&bar, 0, 100000u)) {
+      if (globaltimer_ns() - t0 > limit_ns) {
+        record_error(site);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+}
+
 // ----------------------------------------------------------------------------
 // fences
 // ----------------------------------------------------------------------------

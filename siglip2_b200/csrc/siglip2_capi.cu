@@ -113,6 +113,7 @@ int dispatch_epi(int epi, const GemmIO& io, const GemmParams& p, cudaStream_t s)
     case kEpiLnRs: return launch_gemm_any<T, BN, kEpiLnRs>(io, p, s);
     case kEpiLnRsGelu: return launch_gemm_any<T, BN, kEpiLnRsGelu>(io, p, s);
     case kEpiBiasResRs: return launch_gemm_any<T, BN, kEpiBiasResRs>(io, p, s);
+    case kEpiBiasPosRs: return launch_gemm_any<T, BN, kEpiBiasPosRs>(io, p, s);
     default: return set_error(SIGLIP2_ERR_ARG, "unknown epilogue %d", epi);
   }
 }
@@ -126,21 +127,36 @@ int dispatch_bn(int epi, const GemmIO& io, const GemmParams& p, cudaStream_t s) 
 
 }  // namespace
 
+// Position-embedding inputs of the fused patch-embedding epilogue (kEpiBiasPosRs).
+struct PosArgs {
+  const float* table;  // [grid^2, N] fp32
+  int grid;
+  const int* tok_img;  // [M] token -> image
+  const int* hw;       // [2B] (h, w)
+  const int* cu;       // [B+1] first token of each image
+};
+
 int sg_gemm_impl(int dtype, int epi, const void* a, int lda, const void* b, int ldb, void* out, int ldo, int M, int N,
                  int K, const float* bias, const void* res, int ldr, const float* c1, const float* c2, float eps,
                  cudaStream_t stream, const float2* rs_in = nullptr, float2* rs_acc = nullptr,
-                 float2* rs_zero = nullptr) {
+                 float2* rs_zero = nullptr, const PosArgs* pos = nullptr) {
   SG_CHECK_ARG(M >= 0 && N > 0 && K > 0, "bad GEMM shape M=%d N=%d K=%d", M, N, K);
   if (M == 0) return SIGLIP2_OK;
   SG_CHECK_ARG(a && b && out, "null operand");
-  SG_CHECK_ARG(epi >= 0 && epi <= 7, "unknown epilogue %d", epi);
+  SG_CHECK_ARG(epi >= 0 && epi <= 8, "unknown epilogue %d", epi);
+  SG_CHECK_ARG(epi != kEpiBiasPosRs ||
+                   (pos && pos->table && pos->grid > 0 && pos->tok_img && pos->hw && pos->cu),
+               "position-embedding epilogue needs table, grid, token->image map, grids and row starts");
+  if (epi == kEpiBiasPosRs && !aligned16(pos->table))
+    return set_error(SIGLIP2_ERR_ALIGN, "position table must be 16-byte aligned");
   const bool ln = epi_is_ln(epi);
   SG_CHECK_ARG(!ln || (c1 && c2), "LN epilogue needs c1 and c2");
   SG_CHECK_ARG(ln || bias, "bias epilogue needs bias");
   SG_CHECK_ARG(!epi_has_res(epi) || res, "residual epilogue needs res");
   SG_CHECK_ARG(!epi_has_stat_warps(epi) || K % kGemmBK == 0, "LN-folded GEMM needs K %% 64 == 0 (K=%d)", K);
   SG_CHECK_ARG(!(epi == kEpiLnRs || epi == kEpiLnRsGelu) || rs_in, "row-sum LN epilogue needs rs_in");
-  SG_CHECK_ARG(epi != kEpiBiasResRs || rs_acc, "row-sum accumulating epilogue needs rs_acc");
+  SG_CHECK_ARG((epi != kEpiBiasResRs && epi != kEpiBiasPosRs) || rs_acc,
+               "row-sum accumulating epilogue needs rs_acc");
   const auto misaligned8 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 7u) != 0; };
   if (misaligned8(rs_in) || misaligned8(rs_acc) || misaligned8(rs_zero))
     return set_error(SIGLIP2_ERR_ALIGN, "row-sum buffers must be 8-byte aligned");
@@ -151,6 +167,9 @@ int sg_gemm_impl(int dtype, int epi, const void* a, int lda, const void* b, int 
     GemmParams p{};
     p.M = M; p.N = N; p.K = K; p.bias = bias; p.c1 = c1; p.c2 = c2; p.eps = eps;
     p.rs_in = rs_in; p.rs_acc = rs_acc; p.rs_zero = rs_zero;
+    if (pos) {
+      p.pos_table = pos->table; p.pos_grid = pos->grid; p.tok_img = pos->tok_img; p.pos_hw = pos->hw; p.cu = pos->cu;
+    }
     dim3 grid((N + kSgBN - 1) / kSgBN, (M + kSgBM - 1) / kSgBM);
     const float* A = static_cast<const float*>(a);
     const float* Bw = static_cast<const float*>(b);
@@ -163,6 +182,7 @@ int sg_gemm_impl(int dtype, int epi, const void* a, int lda, const void* b, int 
       case kEpiLnRs: gemm_f32_kernel<kEpiLnRs><<<grid, 256, 0, stream>>>(A, lda, Bw, ldb, O, ldo, R, ldr, p); break;
       case kEpiLnRsGelu: gemm_f32_kernel<kEpiLnRsGelu><<<grid, 256, 0, stream>>>(A, lda, Bw, ldb, O, ldo, R, ldr, p); break;
       case kEpiBiasResRs: gemm_f32_kernel<kEpiBiasResRs><<<grid, 256, 0, stream>>>(A, lda, Bw, ldb, O, ldo, R, ldr, p); break;
+      case kEpiBiasPosRs: gemm_f32_kernel<kEpiBiasPosRs><<<grid, 256, 0, stream>>>(A, lda, Bw, ldb, O, ldo, R, ldr, p); break;
       default: return set_error(SIGLIP2_ERR_ARG, "unknown epilogue %d", epi);
     }
     SG_LAUNCH_CHECK();
@@ -189,6 +209,16 @@ int sg_gemm_impl(int dtype, int epi, const void* a, int lda, const void* b, int 
   p.rs_in = rs_in;
   p.rs_acc = rs_acc;
   p.rs_zero = rs_zero;
+  p.pos_table = nullptr;
+  p.pos_grid = 0;
+  p.tok_img = p.pos_hw = p.cu = nullptr;
+  if (pos) {
+    p.pos_table = pos->table;
+    p.pos_grid = pos->grid;
+    p.tok_img = pos->tok_img;
+    p.pos_hw = pos->hw;
+    p.cu = pos->cu;
+  }
   GemmIO io{a, lda, b, ldb, out, ldo, res, ldr};
   if (dtype == SIGLIP2_BF16) return dispatch_bn<__nv_bfloat16>(epi, io, p, stream);
   return dispatch_bn<__half>(epi, io, p, stream);
@@ -480,9 +510,9 @@ int sg_forward_impl(const siglip2_config* c, const siglip2_weights* w, const voi
   float2* rs_a = f.rowsums;
   float2* rs_b = f.rowsums + N;
   SG_CUDA(cudaMemsetAsync(f.rowsums, 0, sizeof(float2) * 2 * static_cast<size_t>(N), s));
-  // embeddings: x = pos(hw) ; x = patches Wp^T + bp + x
+  // embeddings: x = patches Wp^T + bp + resized position grid, one GEMM whose
+  // epilogue evaluates the antialiased resize per token (and the row sums)
   SG_TRY(sg_token_image_impl(cu, B, N, f.tok_img, s));
-  SG_TRY(sg_posemb_impl(dt, w->pos_table, c->pos_grid, D, f.tok_img, hw, cu, N, f.x, s));
   const void* prow = patches;
   if (P > 0) {
     if (dt == SIGLIP2_BF16) SG_TRY(launch_gather<__nv_bfloat16>(patches, c->patch_dim, P, cu, f.tok_img, N, f.hmid, s));
@@ -490,8 +520,9 @@ int sg_forward_impl(const siglip2_config* c, const siglip2_weights* w, const voi
     else SG_TRY(launch_gather<float>(patches, c->patch_dim, P, cu, f.tok_img, N, f.hmid, s));
     prow = f.hmid;
   }
-  SG_TRY(sg_gemm_impl(dt, kEpiBiasResRs, prow, c->patch_dim, w->patch_w, c->patch_dim, f.x, D, N, D, c->patch_dim,
-                      w->patch_b, f.x, D, nullptr, nullptr, 0.f, s, nullptr, rs_b, nullptr));
+  const PosArgs pos{w->pos_table, c->pos_grid, f.tok_img, hw, cu};
+  SG_TRY(sg_gemm_impl(dt, kEpiBiasPosRs, prow, c->patch_dim, w->patch_w, c->patch_dim, f.x, D, N, D, c->patch_dim,
+                      w->patch_b, nullptr, 0, nullptr, nullptr, 0.f, s, nullptr, rs_b, nullptr, &pos));
   for (int l = 0; l < c->layers; ++l) {
     const siglip2_layer_weights& lw = w->layers[l];
     SG_TRY(sg_gemm_impl(dt, kEpiLnRs, f.x, D, lw.qkv_w, D, f.qkv, nqkv, N, nqkv, D, nullptr, nullptr, 0, lw.qkv_c1,
@@ -577,6 +608,14 @@ const char* siglip2_last_error(void) { return t_last_error; }
 
 unsigned long long siglip2_launch_count(void) { return launch_counter().load(); }
 
+int siglip2_selftest_wait_timeout(long long limit_ns, void* stream) {
+  SG_CHECK_ARG(limit_ns > 0 && limit_ns <= 2000000000ll, "limit must be in (0, 2 s]");
+  selftest_wait_timeout_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<unsigned long long>(limit_ns), 901);
+  SG_LAUNCH_CHECK();
+  return SIGLIP2_OK;
+}
+
 int siglip2_set_gemm_variant(int variant) {
   SG_CHECK_ARG(variant >= 0 && variant <= 2, "GEMM variant must be 0 (auto), 1 (1-SM) or 2 (SM pairs)");
   g_gemm_variant.store(variant);
@@ -611,6 +650,17 @@ int siglip2_gemm_rowsums(int dtype, int epilogue, const void* a_dev, int lda, co
   return sg_gemm_impl(dtype, epilogue, a_dev, lda, b_dev, ldb, out_dev, ldo, M, N, K, bias_dev, res_dev, ldr, c1_dev,
                       c2_dev, eps, static_cast<cudaStream_t>(stream), reinterpret_cast<const float2*>(rs_in_dev),
                       reinterpret_cast<float2*>(rs_acc_dev), reinterpret_cast<float2*>(rs_zero_dev));
+}
+
+int siglip2_patch_embed(int dtype, const void* patches_dev, int patch_dim, const void* w_dev, const float* bias_dev,
+                        const float* table_dev, int grid, const int* tok_img_dev, const int* hw_dev,
+                        const int* cu_seqlens_dev, int N, int D, void* out_dev, float* rs_acc_dev, void* stream) {
+  SG_CHECK_ARG(patches_dev && w_dev && bias_dev && out_dev && rs_acc_dev && N >= 0 && D > 0 && patch_dim > 0,
+               "bad patch_embed arguments");
+  const PosArgs pos{table_dev, grid, tok_img_dev, hw_dev, cu_seqlens_dev};
+  return sg_gemm_impl(dtype, kEpiBiasPosRs, patches_dev, patch_dim, w_dev, patch_dim, out_dev, D, N, D, patch_dim,
+                      bias_dev, nullptr, 0, nullptr, nullptr, 0.f, static_cast<cudaStream_t>(stream), nullptr,
+                      reinterpret_cast<float2*>(rs_acc_dev), nullptr, &pos);
 }
 
 int siglip2_layernorm(int dtype, const void* x_dev, void* y_dev, const float* gamma_dev, const float* beta_dev,

@@ -56,6 +56,14 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
   for (int i = 0; i < 8; ++i) {
     const int row = m0 + ty * 8 + i;
     if (row >= p.M) continue;
+    AxisTaps ay{0, 0, 0.f, 1.f, 0.f}, ax{0, 0, 0.f, 1.f, 0.f};
+    if constexpr (EPI == kEpiBiasPosRs) {
+      const int b = p.tok_img[row];
+      const int w = p.pos_hw[2 * b + 1];
+      const int t = row - p.cu[b];
+      ay = axis_taps(t / w, p.pos_hw[2 * b], p.pos_grid);
+      ax = axis_taps(t - (t / w) * w, w, p.pos_grid);
+    }
     float mu = 0.f, rstd = 1.f;
     if constexpr (kLnRs) {
       const float2 rs = p.rs_in[row];
@@ -74,13 +82,18 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
       } else {
         v += p.bias[col];
       }
+      if constexpr (EPI == kEpiBiasPosRs) {
+        for (int ya = ay.lo; ya < ay.hi; ++ya)
+          for (int xa = ax.lo; xa < ax.hi; ++xa)
+            v = fmaf(axis_w(ay, ya) * axis_w(ax, xa), p.pos_table[static_cast<size_t>(ya * p.pos_grid + xa) * p.N + col], v);
+      }
       if constexpr (kGelu) v = 0.5f * v * (1.f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v)));
       if constexpr (epi_has_res(EPI)) v += res[static_cast<size_t>(row) * ldr + col];
       out[static_cast<size_t>(row) * ldo + col] = v;
       s1 += v;
       s2 = fmaf(v, v, s2);
     }
-    if constexpr (EPI == kEpiBiasResRs) {
+    if constexpr (EPI == kEpiBiasResRs || EPI == kEpiBiasPosRs) {
       atomicAdd(&p.rs_acc[row].x, s1);
       atomicAdd(&p.rs_acc[row].y, s2);
       if (p.rs_zero != nullptr && n0 == 0 && tx == 0) p.rs_zero[row] = make_float2(0.f, 0.f);

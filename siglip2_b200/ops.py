@@ -144,3 +144,20 @@ def gemm_rowsums(a: torch.Tensor, w: torch.Tensor, epilogue: int, bias=None, res
            res.stride(0) if res is not None else 0, _ptr(c1), _ptr(c2), float(eps), _ptr(rs_in), _ptr(rs_acc),
            _ptr(rs_zero), _stream(a.device))
     return out
+
+
+def patch_embed(patches: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, table_f32: torch.Tensor,
+                hw: torch.Tensor, cu_seqlens: torch.Tensor, tok_img: torch.Tensor, rs_acc: torch.Tensor | None = None):
+    """``siglip2_patch_embed``: patch Linear with the resized position grid
+    added in the GEMM epilogue; also accumulates row sums into ``rs_acc``."""
+    _need_cuda(patches, w, bias, table_f32, hw, cu_seqlens, tok_img)
+    N, C = patches.shape
+    D = w.shape[0]
+    G = int(round(table_f32.shape[0] ** 0.5))
+    out = torch.empty((N, D), dtype=patches.dtype, device=patches.device)
+    if rs_acc is None:
+        rs_acc = torch.zeros((N, 2), dtype=torch.float32, device=patches.device)
+    L.call("siglip2_patch_embed", dtype_code(patches.dtype), patches.data_ptr(), C, w.data_ptr(), bias.data_ptr(),
+           table_f32.data_ptr(), G, tok_img.data_ptr(), hw.data_ptr(), cu_seqlens.data_ptr(), N, D, out.data_ptr(),
+           rs_acc.data_ptr(), _stream(patches.device))
+    return out

@@ -123,3 +123,31 @@ def test_head_pool(dtype, D, H):
     torch.cuda.synchronize()
     tol = 1e-4 if dtype == torch.float32 else 2e-2
     assert (pooled.float() - ref).abs().max().item() < tol
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("D", [1152, 768])
+def test_patch_embed_fused_position_resize(dtype, D):
+    g = torch.Generator(device="cuda").manual_seed(D)
+    grids = [(18, 18), (24, 31), (11, 37), (8, 128), (1, 1), (3, 5), (16, 16), (40, 25)]
+    lens = [h * w for h, w in grids]
+    N = sum(lens)
+    cu = _cu(lens)
+    hw = torch.tensor(grids, dtype=torch.int32, device="cuda").flatten()
+    tok = ops.token_image(cu, N)
+    patches = (torch.rand(N, 768, device="cuda", generator=g) * 2 - 1).to(dtype)
+    w = (torch.randn(D, 768, device="cuda", generator=g) * 0.02).to(dtype)
+    bias = torch.randn(D, device="cuda", generator=g) * 0.02
+    table = torch.randn(256, D, device="cuda", generator=g) * 0.02
+    rs = torch.zeros(N, 2, device="cuda")
+    out = ops.patch_embed(patches, w, bias, table, hw, cu, tok, rs)
+    grid = table.view(16, 16, D).permute(2, 0, 1)[None]
+    pos = torch.cat([F.interpolate(grid, size=(h, w_), mode="bilinear", align_corners=False, antialias=True)[0]
+                     .reshape(D, h * w_).T for h, w_ in grids], 0)
+    ref = patches.float() @ w.float().T + bias + pos
+    torch.cuda.synchronize()
+    tol = 1e-4 if dtype == torch.float32 else 2e-2
+    assert (out.float() - ref).abs().max().item() < tol
+    o = out.float()
+    assert torch.allclose(rs[:, 0], o.sum(1), rtol=1e-4, atol=1e-3)
+    assert torch.allclose(rs[:, 1], (o * o).sum(1), rtol=1e-4, atol=1e-3)
