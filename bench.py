@@ -26,11 +26,8 @@ from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
-import statistics
 import sys
-import threading
 import time
 
 import numpy as np
@@ -40,6 +37,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 from siglip2_b200 import workloads as W  # noqa: E402
+from siglip2_b200.clocks import ClockSampler  # noqa: E402
 
 METRIC = "images/sec/GPU So400m-NaFlex bf16 @1024 patches; % of dense BF16 TC peak"
 UNIT = "images/s"
@@ -66,59 +64,9 @@ def peaks():
         return 1590.0, 6650.0, "fallback"
 
 
-# --------------------------------------------------------------------------- clocks
-class ClockSampler:
-    """Samples SM clock and throttle reasons through NVML while running."""
-
-    REASONS = {
-        "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
-        "hw_power_brake_slowdown": 0x80, "sw_power_cap": 0x4,
-    }
-
-    def __init__(self, index: int):
-        self.samples, self.reasons, self.max_mhz = [], set(), None
-        self._stop = threading.Event()
-        try:
-            import pynvml
-            pynvml.nvmlInit()
-            self.nv = pynvml
-            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
-        except Exception:
-            self.nv = None
-
-    def _run(self):
-        while not self._stop.is_set():
-            try:
-                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
-                r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                for name, bit in self.REASONS.items():
-                    if r & bit:
-                        self.reasons.add(name)
-            except Exception:
-                pass
-            time.sleep(0.1)
-
-    def __enter__(self):
-        if self.nv is not None:
-            self.t = threading.Thread(target=self._run, daemon=True)
-            self.t.start()
-        return self
-
-    def __exit__(self, *a):
-        self._stop.set()
-        if self.nv is not None:
-            self.t.join()
-
-    def summary(self):
-        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
-                "reasons": sorted(self.reasons), "samples": len(self.samples)}
-
-
 # --------------------------------------------------------------------------- workload
 def build_inputs(wl, rank: int):
     shapes = W.sample_spatial_shapes(wl.sampler, wl.batch, wl.max_patches, seed=1337 + rank)
-    cfg_probe = W.PRESETS[wl.preset]
     pv, mask = W.make_pixels(shapes, wl.max_patches, 3 * 16 * 16, seed=1337 + rank, dtype=wl.dtype)
     return shapes, pv, mask
 
@@ -301,7 +249,7 @@ def main():
         w = (torch.randn(I, D, device=dev) * 0.02).to(wl.dtype)
         c1 = torch.randn(I, device=dev)
         c2 = torch.randn(I, device=dev)
-        rs = torch.rand(N, 2, device=dev) + 1.0
+        rs = ops.rowsums_reference(a)
         out = torch.empty(N, I, device=dev, dtype=wl.dtype)
 
         def fc1():

@@ -62,12 +62,12 @@ typedef enum {
   SIGLIP2_EPI_LN_GELU = 3,    /* out = gelu_tanh(rstd(A)*(A.B^T - mu(A)*c1) + c2)      */
   SIGLIP2_EPI_BIAS_GELU = 4,  /* out = gelu_tanh(A.B^T + bias)                        */
   /* siglip2_gemm_rowsums only: LayerNorm statistics come from, or go to,
-   * per-row (sum, sum of squares) float pairs of the residual stream */
-  SIGLIP2_EPI_LN_ROWSUMS = 5,      /* as SIGLIP2_EPI_LN, mu/rstd from rs_in[M] over K columns */
+   * per-row (sum, sum of squares) float pairs of the residual stream, in
+   * column-block slots (siglip2_rowsum_slots) */
+  SIGLIP2_EPI_LN_ROWSUMS = 5,      /* as SIGLIP2_EPI_LN, mu/rstd from rs_in over K columns    */
   SIGLIP2_EPI_LN_ROWSUMS_GELU = 6, /* as SIGLIP2_EPI_LN_GELU, likewise                        */
-  SIGLIP2_EPI_BIAS_RES_ROWSUMS = 7 /* as SIGLIP2_EPI_BIAS_RES, and rs_acc[row] += (sum, sum of
-                                      squares) of the row's rounded outputs; rows of rs_zero
-                                      are set to zero (optional)                              */
+  SIGLIP2_EPI_BIAS_RES_ROWSUMS = 7 /* as SIGLIP2_EPI_BIAS_RES, and rs_acc receives the (sum,
+                                      sum of squares) of the row's rounded outputs            */
 } siglip2_epilogue;
 
 /* Library version (major*10000 + minor*100 + patch). */
@@ -106,26 +106,38 @@ int siglip2_gemm(int dtype, int epilogue, const void* a_dev, int lda, const void
                  int ldo, int M, int N, int K, const float* bias_dev, const void* res_dev, int ldr,
                  const float* c1_dev, const float* c2_dev, float eps, void* stream);
 
+/* Row sums for the LayerNorm-folded GEMMs are kept per column block: a
+ * [rows][S] array of (sum, sum of squares) float pairs, S =
+ * siglip2_rowsum_slots(dtype, width) for rows of `width` columns, slot j
+ * covering columns [j * blk, min((j + 1) * blk, width)) with blk =
+ * siglip2_rowsum_block(dtype, width) (half a GEMM tile).  Each slot is
+ * written once by the GEMM that produces the rows and summed in slot order
+ * by the GEMM that reads them, so results do not depend on scheduling. */
+int siglip2_rowsum_slots(int dtype, int width);
+int siglip2_rowsum_block(int dtype, int width);
+
 /* siglip2_gemm with row-sum LayerNorm plumbing: the GEMM that writes the
- * residual stream (SIGLIP2_EPI_BIAS_RES_ROWSUMS) accumulates each row's sum
- * and sum of squares into rs_acc (float pairs, zero beforehand), and the
- * LayerNorm-folded GEMM that reads it (SIGLIP2_EPI_LN_ROWSUMS[_GELU]) takes
- * mu = sum/K and rstd = 1/sqrt(sumsq/K - mu^2 + eps) from rs_in, so no pass
- * over the rows is needed for LayerNorm statistics.  Pointers not used by
- * the epilogue may be NULL; row-sum buffers must be 8-byte aligned. */
+ * residual stream (SIGLIP2_EPI_BIAS_RES_ROWSUMS) writes each row's sum and
+ * sum of squares into rs_acc ([M][siglip2_rowsum_slots(dtype, N)] pairs),
+ * and the LayerNorm-folded GEMM that reads it (SIGLIP2_EPI_LN_ROWSUMS[_GELU])
+ * takes mu = sum/K and rstd = 1/sqrt(sumsq/K - mu^2 + eps) from rs_in
+ * ([M][siglip2_rowsum_slots(dtype, K)] pairs), so no pass over the rows is
+ * needed for LayerNorm statistics.  Pointers not used by the epilogue may be
+ * NULL; row-sum buffers must be 8-byte aligned. */
 int siglip2_gemm_rowsums(int dtype, int epilogue, const void* a_dev, int lda, const void* b_dev, int ldb,
                          void* out_dev, int ldo, int M, int N, int K, const float* bias_dev, const void* res_dev,
                          int ldr, const float* c1_dev, const float* c2_dev, float eps, const float* rs_in_dev,
-                         float* rs_acc_dev, float* rs_zero_dev, void* stream);
+                         float* rs_acc_dev, void* stream);
 
 /* Patch embedding with the position embedding fused into the GEMM epilogue:
  *   out[t] = patches[t] . W^T + bias + resize(table)(t)      (out [N, D])
  * where token t is pixel (y, x) = divmod(t - cu[b], w) of image
  * b = tok_img[t] with grid (h, w) = hw[2b], hw[2b+1], and resize is the
  * antialiased bilinear interpolation of the grid x grid fp32 table
- * [grid^2, D].  rs_acc[t] += (sum, sum of squares) of the rounded out row
- * (float pairs, zero beforehand: the LayerNorm statistics of the first
- * layer).  Replaces Siglip2SequenceEmbeddings.forward, model.py:68-120. */
+ * [grid^2, D].  rs_acc ([N][siglip2_rowsum_slots(dtype, D)] float pairs)
+ * receives the (sum, sum of squares) of the rounded out rows: the LayerNorm
+ * statistics of the first layer.  Replaces Siglip2SequenceEmbeddings.forward,
+ * model.py:68-120. */
 int siglip2_patch_embed(int dtype, const void* patches_dev, int patch_dim, const void* w_dev, const float* bias_dev,
                         const float* table_dev, int grid, const int* tok_img_dev, const int* hw_dev,
                         const int* cu_seqlens_dev, int N, int D, void* out_dev, float* rs_acc_dev, void* stream);

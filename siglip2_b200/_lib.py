@@ -26,7 +26,9 @@ SIGNATURES = {
     "siglip2_gemm": (_c_int, [_c_int, _c_int, _vp, _c_int, _vp, _c_int, _vp, _c_int, _c_int, _c_int, _c_int,
                               _vp, _vp, _c_int, _vp, _vp, _c_float, _vp]),
     "siglip2_gemm_rowsums": (_c_int, [_c_int, _c_int, _vp, _c_int, _vp, _c_int, _vp, _c_int, _c_int, _c_int, _c_int,
-                                      _vp, _vp, _c_int, _vp, _vp, _c_float, _vp, _vp, _vp, _vp]),
+                                      _vp, _vp, _c_int, _vp, _vp, _c_float, _vp, _vp, _vp]),
+    "siglip2_rowsum_slots": (_c_int, [_c_int, _c_int]),
+    "siglip2_rowsum_block": (_c_int, [_c_int, _c_int]),
     "siglip2_patch_embed": (_c_int, [_c_int, _vp, _c_int, _vp, _vp, _vp, _c_int, _vp, _vp, _vp, _c_int, _c_int, _vp,
                                      _vp, _vp]),
     "siglip2_layernorm": (_c_int, [_c_int, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_float, _vp, _c_int, _vp]),
@@ -105,3 +107,10 @@ def check(code: int) -> None:
 
 def call(name: str, *args) -> None:
     check(getattr(load(), name)(*args))
+
+
+def check_value(value: int) -> int:
+    """For entry points that return a count or a negative status code."""
+    if value < 0:
+        check(value)
+    return value

@@ -60,7 +60,7 @@ struct FwdBuffers {
   void* attn;    // [N, D]
   void* hmid;    // [N, I]   (also the packed patch rows when the input is padded)
   float* scores; // [N, H]
-  float2* rowsums; // 2 x [N] (sum, sum of squares) of the residual stream rows
+  float2* rowsums; // 2 x [N][slots] (sum, sum of squares) of the residual stream rows, per column block
   void* hpool;   // [B H, D]
   void* hY;      // [B H, D]
   void* hattn;   // [B, D]
@@ -81,7 +81,8 @@ inline size_t forward_workspace(const siglip2_config* c, int B, int N, FwdBuffer
   const size_t mid = std::max<size_t>(static_cast<size_t>(I), static_cast<size_t>(c->patch_dim));
   f.hmid = w.take<uint8_t>(e * N * mid);
   f.scores = w.take<float>(sizeof(float) * N * H);
-  f.rowsums = w.take<float2>(sizeof(float2) * 2 * static_cast<size_t>(N));
+  f.rowsums = w.take<float2>(sizeof(float2) * 2 * static_cast<size_t>(N) *
+                              rowsum_slots(c->dtype == SIGLIP2_F32, D));
   f.hpool = w.take<uint8_t>(e * B * H * D);
   f.hY = w.take<uint8_t>(e * B * H * D);
   f.hattn = w.take<uint8_t>(e * B * D);

@@ -2,27 +2,30 @@
 //
 //     out[M, N] = epilogue( A[M, K] . B[N, K]^T )        (A, B row-major, K-major)
 //
-// One CTA per SM walks a static list of 128 x BN output tiles.  Warp roles:
-//   warp 0      TMA producer: A/B tiles (128B swizzle, 64-wide K slabs) into a
-//               STAGES-deep shared-memory ring, one mbarrier per stage.
-//   warp 1      TMEM owner + UMMA issuer (one elected lane): 4 x
-//               tcgen05.mma 128xBNx16 per stage into one of two TMEM
-//               accumulators (2 x 256 columns), tcgen05.commit frees the
-//               stage / publishes the accumulator.
+// One CTA per SM (gemm_tc_kernel, 128 x BN tiles) or one CTA pair per two SMs
+// (gemm_tc2_kernel, 256 x BN tiles, tcgen05 cta_group::2) walks a static
+// list of output tiles.  Warp roles:
+//   warp 0      TMA producer: A/B tiles (128B swizzle, 64-wide K slabs, SUB
+//               slabs per stage) into a STAGES-deep shared-memory ring.
+//   warp 1      TMEM owner + UMMA issuer (one elected lane): 4 * SUB
+//               tcgen05.mma per stage into one of two TMEM accumulators
+//               (2 x 256 columns); tcgen05.commit frees the stage and
+//               publishes the accumulator.
 //   warps 2-5   epilogue: tcgen05.ld 32 columns at a time (each warp owns the
-//               32 TMEM lanes = rows its warp index allows), fused epilogue,
-//               16-byte global stores.  Runs one tile behind the MMA.
-//   warps 6-9   (LayerNorm-folded variants only) row statistics: each thread
-//               owns one row of the A tile and accumulates shifted sum / sum
-//               of squares straight from the swizzled stage while the MMA
-//               consumes it, so LayerNorm costs no extra pass over HBM.
+//               32 TMEM lanes its warp index allows), fused math in fp32,
+//               64B-swizzled staging, TMA stores.  Runs one tile behind the
+//               MMA; the next tile's parameters, row sums and residual are
+//               prefetched while the current one drains.
+//   warps 6-9   (kEpiLn / kEpiLnGelu only) row statistics of the A tiles,
+//               read from the swizzled stages while the MMA consumes them.
 //
 // LayerNorm folding.  For y = LN(x) = (x - mu) * rstd * gamma + beta feeding a
 // Linear(W, b):   y W^T + b = rstd * (x (W*gamma)^T - mu * c1) + c2
 // with c1[n] = sum_k (W*gamma)[n,k] and c2[n] = b[n] + sum_k beta[k] W[n,k].
 // The GEMM runs on the raw residual stream x against the pre-scaled weight
-// W*gamma; mu and rstd come from the statistics warps; the epilogue applies
-// the row/column terms in fp32.
+// W*gamma; mu and rstd come either from the statistics warps or (kEpiLnRs*)
+// from row sums (sum, sum of squares) that the GEMM which produced x
+// accumulated in its own epilogue (kEpiBiasResRs / kEpiBiasPosRs).
 #pragma once
 
 #include "rowops.cuh"
@@ -52,9 +55,13 @@ struct GemmParams {
   const float* c1;            // [N] (LayerNorm-folded epilogues)
   const float* c2;            // [N]
   float eps;                  // LayerNorm epsilon
-  const float2* rs_in;        // [M] (sum, sum of squares) of A's rows over K (kEpiLnRs*)
-  float2* rs_acc;             // [M] row sums of the output to accumulate into (kEpiBiasResRs)
-  float2* rs_zero;            // [M] optional: zeroed by the CTAs of the first column tile
+  // Row sums in slots: [M][rs_ld] (sum, sum of squares) pairs, slot j covering
+  // the j-th column block of the GEMM that produced the rows (see
+  // rowsum_block); each slot is written exactly once and read in slot order,
+  // so the LayerNorm statistics (and the forward) are deterministic.
+  const float2* rs_in;        // A's row sums over K (kEpiLnRs*), rs_ld slots per row
+  float2* rs_acc;             // output row sums to write (kEpiBiasResRs, kEpiBiasPosRs), rs_ld slots per row
+  int rs_ld;
   // kEpiBiasPosRs: row t is a token of image tok_img[t] at (y, x) of its
   // (h, w) = pos_hw[2b], pos_hw[2b+1] grid (t - cu[b] = y * w + x); the
   // position embedding is the antialiased bilinear resize of the
@@ -69,12 +76,35 @@ struct GemmParams {
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;     // 64 x 2B = one 128-byte swizzle row
 constexpr int kEpiCols = 32;    // epilogue chunk: 32 columns = one 64B-swizzled staging row
-constexpr int kEpiWarps = 4;
+constexpr int kEpiBufs = 2;     // staging buffers per epilogue warp
+constexpr int kEpiBufBytes = 32 * kEpiCols * 2;
+constexpr int kSmemLimit = 227 * 1024;
+constexpr int kGemmThreads = 320;  // 10 warps: producer, MMA, 8 epilogue (or 4 epilogue + 4 statistics)
+
+// Epilogue warps: two per TMEM lane quarter (each drains half of the tile's
+// columns) so that two warps per SM sub-partition hide each other's
+// latencies; the statistics-warp variants keep one per quarter.
+__host__ __device__ constexpr int epi_warps(int e) { return epi_has_stat_warps(e) ? 4 : 8; }
+
+// Tile width of the tensor-core GEMM for an output width N: 192 when it
+// divides N exactly and 256 does not (768 is 256-wide; 1152 is 192-wide).
+__host__ __device__ constexpr int gemm_bn_for(int N) { return (N % 192 == 0 && N % 256 != 0) ? 192 : 256; }
+// Column block of one row-sum slot: the columns one epilogue warp drains of
+// a row-sum-producing tile (half the tile), or the SIMT fp32 tile width.
+__host__ __device__ constexpr int rowsum_block(bool f32, int N) { return f32 ? 128 : gemm_bn_for(N) / 2; }
+__host__ __device__ constexpr int rowsum_slots(bool f32, int N) {
+  return (N + rowsum_block(f32, N) - 1) / rowsum_block(f32, N);
+}
+__host__ __device__ constexpr int gemm_stats_smem(int e) { return epi_has_stat_warps(e) ? 2 * 2 * kGemmBM * 4 : 0; }
+// epilogue staging + barriers + statistics + alignment slack: what the stages may not use
+__host__ __device__ constexpr int gemm_fixed_smem(int e) {
+  return epi_warps(e) * kEpiBufs * kEpiBufBytes + 1024 + gemm_stats_smem(e) + 1024;
+}
 
 // SUB = 64-wide K slabs per pipeline stage (1 or 2).  More K per stage means
 // fewer MMA-complete -> refill round trips per FLOP; measured on B200 the
 // round trip, not the stage count, limits the mainloop.
-template <int BN, int SUB = 1>
+template <int BN, int SUB, int EPI>
 struct GemmCfg {
   static constexpr int kSub = SUB;
   static constexpr int kSlabA = kGemmBM * kGemmBK * 2;
@@ -82,20 +112,15 @@ struct GemmCfg {
   static constexpr int kStageA = kSlabA * SUB;
   static constexpr int kStageB = kSlabB * SUB;
   static constexpr int kStageBytes = kStageA + kStageB;
-  static constexpr int kStages = (200 * 1024) / kStageBytes;  // BN=256: 4 (SUB 1) / 2 (SUB 2)
+  static constexpr int kStages = (kSmemLimit - gemm_fixed_smem(EPI)) / kStageBytes;  // BN=256: 4 (SUB 1) / 2 (SUB 2)
   static constexpr int kTmemCols = 512;                        // 2 accumulators, 256-column slots
   static constexpr int kAccStride = 256;
-  static constexpr int kStaging = kEpiWarps * 2 * 32 * kEpiCols * 2;  // 2 x [32 rows][32 cols] per warp
+  static constexpr int kStaging = epi_warps(EPI) * kEpiBufs * kEpiBufBytes;
   static constexpr int kOffStaging = kStages * kStageBytes;
   static constexpr int kOffBars = kOffStaging + kStaging;
   static constexpr int kOffStats = kOffBars + 1024;
-  static constexpr int kSmemBytes = kOffStats + 2 * 2 * kGemmBM * 4 + 1024 /*alignment slack*/;
-};
-
-template <bool kStatWarps>
-struct GemmThreads {
-  static constexpr int kWarps = kStatWarps ? 10 : 6;
-  static constexpr int kThreads = kWarps * 32;
+  static constexpr int kSmemBytes = kOffStats + gemm_stats_smem(EPI) + 1024 /*alignment slack*/;
+  static_assert(kStages >= 2 && kSmemBytes <= kSmemLimit, "GEMM shared-memory budget");
 };
 
 // keeps the compiler from using tcgen05.ld destination registers before the
@@ -121,12 +146,15 @@ __device__ __forceinline__ void load_param32(const float* __restrict__ p, int co
 }
 
 
-// Epilogue of one CTA (4 warps, warp & 3 = TMEM lane quarter = 32 rows each):
-// TMEM -> registers -> fused math -> 64B-swizzled staging -> TMA store, 32
-// columns per chunk, the residual (if any) arriving in the staging buffer by
-// TMA.  `row_base` is the first output row of this CTA's 128-row tile half;
-// `tempty_addr` is the shared::cluster address of the barrier that hands the
-// accumulator back to the MMA issuer.
+// Epilogue of one CTA: EW = epi_warps(EPI) warps; warp w drains TMEM lane
+// quarter w & 3 (32 rows) and, with 8 warps, half of the tile's columns.
+// Per 32-column chunk: TMEM -> registers -> fused math in fp32 ->
+// 64B-swizzled staging -> TMA store; the residual (if any) arrives in the
+// staging buffer by TMA.  At the start of each tile the next tile's bias /
+// LayerNorm vectors and row sums are prefetched into L1 and its residual box
+// into L2.  `row_offset` is the first output row of this CTA's 128-row half
+// of the tile; `tempty_addr*` are the shared::cluster addresses of the
+// barriers that hand each accumulator back to the MMA issuer.
 template <typename T, int BN, int EPI, bool kCluster>
 __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtensorMap* tmO, const CUtensorMap* tmR,
                                               uint32_t tmem_base, uint32_t acc_stride, uint8_t* staging,
@@ -142,25 +170,81 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
   constexpr bool kRes = epi_has_res(EPI);
   constexpr bool kRsOut = (EPI == kEpiBiasResRs || EPI == kEpiBiasPosRs);
   constexpr bool kPos = (EPI == kEpiBiasPosRs);
-  constexpr int NCH = BN / kEpiCols;
+  constexpr int EW = epi_warps(EPI);
+  constexpr int kParts = EW / 4;              // column parts per tile
+  constexpr int kPartCols = BN / kParts;
+  constexpr int NCH = kPartCols / kEpiCols;   // chunks per warp per tile
+  static_assert(kPartCols % kEpiCols == 0, "epilogue column split");
+  static_assert(!kRsOut || kPartCols == BN / 2, "a row-sum slot is half a tile (rowsum_block)");
   const int ew = warp - 2;
-  const int q = warp & 3;
+  const int q = warp & 3;                     // TMEM lane quarter
+  const int part = ew / 4;
   const int row_in_tile = q * 32 + lane;
-  uint8_t* stg = staging + ew * (2 * 32 * kEpiCols * 2);
-  uint64_t* rbar = resbar + 2 * ew;
-  uint32_t rph0 = 0, rph1 = 0;
+  uint8_t* stg = staging + ew * (kEpiBufs * kEpiBufBytes);
+  uint64_t* rbar = resbar + kEpiBufs * ew;
+  uint32_t rph = 0;  // bit b: parity of the next completion of rbar[b]
+  int sb = 0;        // staging buffer of the current chunk
+
+  auto tile_m0 = [&](int tile) { return (tile / n_tiles) * rows_per_tile + row_offset; };
+  auto tile_c0 = [&](int tile) { return (tile % n_tiles) * BN + part * kPartCols; };  // this warp's first column
+  // L1/L2 prefetch of what the epilogue of `tile` reads besides TMEM
+  auto prefetch_tile = [&](int tile) {
+    if (tile >= num_tiles) return;
+    const int pm0 = tile_m0(tile), pc0 = tile_c0(tile);
+    if (q == 0 && lane < NCH && pc0 + lane * 32 < p.N) {  // 32 floats = one 128-byte line per lane
+      if constexpr (kLnMath) {
+        prefetch_l1(p.c1 + pc0 + lane * 32);
+        prefetch_l1(p.c2 + pc0 + lane * 32);
+      } else {
+        prefetch_l1(p.bias + pc0 + lane * 32);
+      }
+    }
+    if constexpr (kRsIn) {
+      if (part == 0 && pm0 + q * 32 + lane < p.M) {
+        const float2* r = p.rs_in + static_cast<size_t>(pm0 + q * 32 + lane) * p.rs_ld;
+        prefetch_l1(r);
+        prefetch_l1(r + p.rs_ld - 1);
+      }
+    }
+    if constexpr (kRes) {
+      if (lane < NCH && pm0 + q * 32 < p.M && pc0 + lane * kEpiCols < p.N)
+        tma_prefetch_l2_2d(tmR, pc0 + lane * kEpiCols, pm0 + q * 32);
+    }
+  };
+
+  prefetch_tile(first_tile);
   int t = 0;
   for (int tile = first_tile; tile < num_tiles; tile += tile_step, ++t) {
     const int buf = t & 1;
     const uint32_t tph = (t >> 1) & 1;
-    const int m0 = (tile / n_tiles) * rows_per_tile + row_offset;
-    const int n0 = (tile % n_tiles) * BN;
+    const int m0 = tile_m0(tile);
+    const int c0 = tile_c0(tile);
+    const int row0 = m0 + q * 32;
+    const int my_row = row0 + lane;
+    prefetch_tile(tile + tile_step);
+    float mu = 0.f, rstd = 1.f;
+    if constexpr (kRsIn) {
+      // row sums of the raw A row (the previous GEMM's rounded output), slot
+      // by slot in a fixed order: fp32 E[x^2] - E[x]^2 over K = D values of
+      // O(1) magnitude
+      float2 rs = make_float2(0.f, 0.f);
+      if (my_row < p.M) {
+        const float2* r = p.rs_in + static_cast<size_t>(my_row) * p.rs_ld;
+        for (int j = 0; j < p.rs_ld; ++j) {
+          const float2 v = r[j];
+          rs.x += v.x;
+          rs.y += v.y;
+        }
+      }
+      const float inv_k = 1.f / static_cast<float>(p.K);
+      mu = rs.x * inv_k;
+      rstd = rsqrtf(fmaxf(rs.y * inv_k - mu * mu, 0.f) + p.eps);
+    }
     if (*abort_flag || !mbar_wait<kCluster>(&tfull[buf], tph, 121)) {
       *abort_flag = 1;
       break;
     }
     tc_fence_after();
-    float mu = 0.f, rstd = 1.f;
     if constexpr (kStat) {
       if (!mbar_wait(&sfull[buf], tph, 122)) {
         *abort_flag = 1;
@@ -171,17 +255,7 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
       __syncwarp();
       if (lane == 0) mbar_arrive(&sempty[buf]);
     }
-    const int row0 = m0 + q * 32;
-    const int my_row = row0 + lane;
-    if constexpr (kRsIn) {
-      // row sums of the raw A row (the previous GEMM's rounded output): fp32
-      // E[x^2] - E[x]^2 over K = D values of O(1) magnitude
-      const float2 rs = my_row < p.M ? p.rs_in[my_row] : make_float2(0.f, 0.f);
-      const float inv_k = 1.f / static_cast<float>(p.K);
-      mu = rs.x * inv_k;
-      rstd = rsqrtf(fmaxf(rs.y * inv_k - mu * mu, 0.f) + p.eps);
-    }
-    float rs1 = 0.f, rs2 = 0.f;  // row sums of this tile's rounded outputs (kRsOut)
+    float rs1 = 0.f, rs2 = 0.f;  // sums over this warp's columns of the rounded outputs (kRsOut)
     AxisTaps ay{0, 0, 0.f, 1.f, 0.f}, ax{0, 0, 0.f, 1.f, 0.f};  // position-embedding taps of this row (kPos)
     if constexpr (kPos) {
       if (my_row < p.M) {
@@ -192,7 +266,8 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
         ax = axis_taps(i - (i / w) * w, w, p.pos_grid);
       }
     }
-    const uint32_t tbase = tmem_base + buf * acc_stride + (static_cast<uint32_t>(q * 32) << 16);
+    const uint32_t tbase =
+        tmem_base + buf * acc_stride + part * kPartCols + (static_cast<uint32_t>(q * 32) << 16);
     uint32_t ra[32], rb[32];
     SG_TMEM_LD_32(tbase, ra);
     tmem_ld_wait();
@@ -202,18 +277,17 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
       uint32_t* cur = (c & 1) ? rb : ra;
       uint32_t* nxt = (c & 1) ? ra : rb;
       if (c + 1 < NCH) SG_TMEM_LD_32(tbase + (c + 1) * kEpiCols, nxt);
-      const int col0 = n0 + c * kEpiCols;
-      const int sb = c & 1;  // staging buffer
-      uint8_t* sbuf = stg + sb * (32 * kEpiCols * 2);
+      const int col0 = c0 + c * kEpiCols;
+      uint8_t* sbuf = stg + sb * kEpiBufBytes;
       // the store issued from this buffer two chunks ago must have read it
       if (lane == 0) tma_store_wait_read<1>();
-      __syncwarp();
       if constexpr (kRes) {
         if (lane == 0) {
-          mbar_arrive_expect_tx(&rbar[sb], 32 * kEpiCols * 2);
+          mbar_arrive_expect_tx(&rbar[sb], kEpiBufBytes);
           tma_load_2d(sbuf, tmR, &rbar[sb], col0, row0);
         }
       }
+      __syncwarp();
       float v[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(cur[j]);
@@ -263,9 +337,8 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
       const int sw = (lane >> 1) & 3;
       uint8_t* srow = sbuf + lane * (kEpiCols * 2);
       if constexpr (kRes) {
-        const uint32_t ph = sb ? rph1 : rph0;
-        if (!mbar_wait(&rbar[sb], ph, 123)) *abort_flag = 1;
-        if (sb) rph1 ^= 1; else rph0 ^= 1;
+        if (!mbar_wait(&rbar[sb], (rph >> sb) & 1, 123)) *abort_flag = 1;
+        rph ^= 1u << sb;
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
           const uint4 rv = *reinterpret_cast<const uint4*>(srow + ((g ^ sw) << 4));
@@ -305,22 +378,20 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
         tma_store_2d(tmO, sbuf, col0, row0);
       }
       if (lane == 0) tma_store_commit();
+      sb ^= 1;
       if (c + 1 < NCH) {
         tmem_ld_wait();
         SG_REG_FENCE_32(nxt);
       } else {
-        // accumulator fully read: hand the TMEM buffer back to the MMA issuer
+        // this warp's part of the accumulator is read: hand it back to the MMA issuer
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(buf ? tempty_addr1 : tempty_addr0);
       }
     }
     if constexpr (kRsOut) {
-      if (my_row < p.M) {
-        atomicAdd(&p.rs_acc[my_row].x, rs1);
-        atomicAdd(&p.rs_acc[my_row].y, rs2);
-        if (p.rs_zero != nullptr && n0 == 0) p.rs_zero[my_row] = make_float2(0.f, 0.f);
-      }
+      // this warp's column block is one slot (block width kPartCols = BN / 2)
+      if (my_row < p.M && c0 < p.N) p.rs_acc[static_cast<size_t>(my_row) * p.rs_ld + c0 / kPartCols] = make_float2(rs1, rs2);
     }
   }
   if (lane == 0) tma_store_wait_all<0>();
@@ -392,13 +463,14 @@ __device__ __forceinline__ void gemm_row_stats(const GemmParams& p, const uint8_
 }
 
 template <typename T, int BN, int EPI, int SUB>
-__global__ void __launch_bounds__(GemmThreads<epi_has_stat_warps(EPI)>::kThreads, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
                    const GemmParams p) {
   constexpr bool kLN = epi_has_stat_warps(EPI);  // statistics warps in this kernel
   constexpr bool kRes = epi_has_res(EPI);
-  using Cfg = GemmCfg<BN, SUB>;
+  using Cfg = GemmCfg<BN, SUB, EPI>;
+  constexpr int EW = epi_warps(EPI);
   constexpr int STAGES = Cfg::kStages;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kIdesc = make_idesc(kGemmBM, BN, kBF16, false, false);
@@ -416,8 +488,8 @@ __global__ void __launch_bounds__(GemmThreads<epi_has_stat_warps(EPI)>::kThreads
   uint64_t* sfull = tempty + 2;          // [2]
   uint64_t* sempty = sfull + 2;          // [2]
   uint64_t* mdone = sempty + 2;          // [1] all issued MMAs complete (teardown)
-  uint64_t* resbar = mdone + 1;          // [kEpiWarps][2] residual chunk landed in staging
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(resbar + 2 * kEpiWarps);
+  uint64_t* resbar = mdone + 1;          // [EW][kEpiBufs] residual chunk landed in staging
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(resbar + kEpiBufs * EW);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   float* st_mean = reinterpret_cast<float*>(smem + Cfg::kOffStats);  // [2][128]
   float* st_rstd = st_mean + 2 * kGemmBM;                              // [2][128]
@@ -436,12 +508,12 @@ __global__ void __launch_bounds__(GemmThreads<epi_has_stat_warps(EPI)>::kThreads
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], kEpiWarps);
+      mbar_init(&tempty[b], EW);
       mbar_init(&sfull[b], kGemmBM);
-      mbar_init(&sempty[b], kEpiWarps);
+      mbar_init(&sempty[b], EW);
     }
     mbar_init(mdone, 1);
-    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&resbar[i], 1);
+    for (int i = 0; i < kEpiBufs * EW; ++i) mbar_init(&resbar[i], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -551,7 +623,7 @@ __global__ void __launch_bounds__(GemmThreads<epi_has_stat_warps(EPI)>::kThreads
       umma_commit(mdone);
       mbar_wait(mdone, 0, 113);
     }
-  } else if (warp < 2 + kEpiWarps) {
+  } else if (warp < 2 + EW) {
     // ------------------------------------------------------------ epilogue
     // Warp (warp & 3) may only touch TMEM lanes 32*(warp&3) .. +31: it owns
     // those 32 rows of the tile, 32 columns per chunk.  Each chunk goes
@@ -565,7 +637,7 @@ __global__ void __launch_bounds__(GemmThreads<epi_has_stat_warps(EPI)>::kThreads
     // ------------------------------------------------------------ LayerNorm row statistics
     if constexpr (kLN) {
       gemm_row_stats<T, STAGES, SUB, false>(p, smA, Cfg::kStageA, full, empty, sfull, sempty, st_mean, st_rstd,
-                                       abort_flag, threadIdx.x - (2 + kEpiWarps) * 32, lane, blockIdx.x, gridDim.x,
+                                       abort_flag, threadIdx.x - (2 + EW) * 32, lane, blockIdx.x, gridDim.x,
                                        num_tiles, nk);
     }
   }
@@ -589,7 +661,7 @@ __global__ void __launch_bounds__(GemmThreads<epi_has_stat_warps(EPI)>::kThreads
 // and reports back to the leader's accumulator-free barrier.  Per SM this
 // halves the B operand's shared-memory footprint and traffic.
 // ============================================================================
-template <int BN, int SUB = 1>
+template <int BN, int SUB, int EPI>
 struct Gemm2Cfg {
   static constexpr int kSub = SUB;
   static constexpr int kSlabA = kGemmBM * kGemmBK * 2;          // this CTA's 128 rows of A
@@ -597,24 +669,26 @@ struct Gemm2Cfg {
   static constexpr int kStageA = kSlabA * SUB;
   static constexpr int kStageB = kSlabB * SUB;
   static constexpr int kStageBytes = kStageA + kStageB;
-  static constexpr int kStages = (196 * 1024) / kStageBytes;    // BN=256: 6 (SUB 1) / 3 (SUB 2)
+  static constexpr int kStages = (kSmemLimit - gemm_fixed_smem(EPI)) / kStageBytes;  // BN=256: 6 (SUB 1) / 3 (SUB 2)
   static constexpr int kTmemCols = 512;
   static constexpr int kAccStride = 256;
-  static constexpr int kStaging = kEpiWarps * 2 * 32 * kEpiCols * 2;
+  static constexpr int kStaging = epi_warps(EPI) * kEpiBufs * kEpiBufBytes;
   static constexpr int kOffStaging = kStages * kStageBytes;
   static constexpr int kOffBars = kOffStaging + kStaging;
   static constexpr int kOffStats = kOffBars + 1024;
-  static constexpr int kSmemBytes = kOffStats + 2 * 2 * kGemmBM * 4 + 1024;
+  static constexpr int kSmemBytes = kOffStats + gemm_stats_smem(EPI) + 1024;
+  static_assert(kStages >= 2 && kSmemBytes <= kSmemLimit, "GEMM shared-memory budget");
 };
 
 template <typename T, int BN, int EPI, int SUB>
-__global__ void __launch_bounds__(GemmThreads<epi_has_stat_warps(EPI)>::kThreads, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
                     const GemmParams p) {
   constexpr bool kLN = epi_has_stat_warps(EPI);  // statistics warps in this kernel
   constexpr bool kRes = epi_has_res(EPI);
-  using Cfg = Gemm2Cfg<BN, SUB>;
+  using Cfg = Gemm2Cfg<BN, SUB, EPI>;
+  constexpr int EW = epi_warps(EPI);
   constexpr int STAGES = Cfg::kStages;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kIdesc = make_idesc(2 * kGemmBM, BN, kBF16, false, false);
@@ -634,8 +708,8 @@ __global__ void __launch_bounds__(GemmThreads<epi_has_stat_warps(EPI)>::kThreads
   uint64_t* sfull = tempty + 2;          // [2]
   uint64_t* sempty = sfull + 2;          // [2]
   uint64_t* mdone = sempty + 2;          // [1]
-  uint64_t* resbar = mdone + 1;          // [kEpiWarps][2]
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(resbar + 2 * kEpiWarps);
+  uint64_t* resbar = mdone + 1;          // [EW][kEpiBufs]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(resbar + kEpiBufs * EW);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   float* st_mean = reinterpret_cast<float*>(smem + Cfg::kOffStats);
   float* st_rstd = st_mean + 2 * kGemmBM;
@@ -659,12 +733,12 @@ __global__ void __launch_bounds__(GemmThreads<epi_has_stat_warps(EPI)>::kThreads
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 2 * kEpiWarps);
+      mbar_init(&tempty[b], 2 * EW);
       mbar_init(&sfull[b], kGemmBM);
-      mbar_init(&sempty[b], kEpiWarps);
+      mbar_init(&sempty[b], EW);
     }
     mbar_init(mdone, 1);
-    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&resbar[i], 1);
+    for (int i = 0; i < kEpiBufs * EW; ++i) mbar_init(&resbar[i], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -774,7 +848,7 @@ __global__ void __launch_bounds__(GemmThreads<epi_has_stat_warps(EPI)>::kThreads
       umma_commit_pair(mdone);
       mbar_wait<true>(mdone, 0, 153);
     }
-  } else if (warp < 2 + kEpiWarps) {
+  } else if (warp < 2 + EW) {
     // ------------------------------------------------------------ epilogue (both CTAs)
     const uint32_t te0 = mapa_shared(smem_u32(&tempty[0]), 0), te1 = mapa_shared(smem_u32(&tempty[1]), 0);
     gemm_epilogue<T, BN, EPI, true>(p, &tmO, &tmR, tmem_base, Cfg::kAccStride, staging, resbar, tfull, te0, te1,
@@ -784,7 +858,7 @@ __global__ void __launch_bounds__(GemmThreads<epi_has_stat_warps(EPI)>::kThreads
     // ------------------------------------------------------------ LayerNorm row statistics (both CTAs)
     if constexpr (kLN) {
       gemm_row_stats<T, STAGES, SUB, true>(p, smA, Cfg::kStageA, aready, empty, sfull, sempty, st_mean, st_rstd,
-                                      abort_flag, threadIdx.x - (2 + kEpiWarps) * 32, lane, pair, num_pairs,
+                                      abort_flag, threadIdx.x - (2 + EW) * 32, lane, pair, num_pairs,
                                       num_tiles, nk);
     }
   }

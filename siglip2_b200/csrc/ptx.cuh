@@ -160,6 +160,18 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// L2 prefetch of one tensor-map box at (x, y): no shared memory, no completion
+// to wait for (used to pull a later epilogue's residual tile toward the SM)
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void prefetch_l1(const void* p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
+}
+
 // shared -> global tensor store (bulk group; out-of-bounds parts are clipped)
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
@@ -412,9 +424,11 @@ __device__ __forceinline__ float tanh_approx(float x) {
 
 // GELU with the tanh approximation: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
 __device__ __forceinline__ float gelu_tanh(float x) {
-  const float k0 = 0.7978845608028654f;
-  const float k1 = 0.044715f;
-  return 0.5f * x * (1.0f + tanh_approx(k0 * (x + k1 * x * x * x)));
+  const float k0 = 0.7978845608028654f;   // sqrt(2/pi)
+  const float k01 = 0.0356774081363001f;  // sqrt(2/pi) * 0.044715
+  const float h = 0.5f * x;
+  const float z = x * fmaf(k01, x * x, k0);  // sqrt(2/pi) (x + 0.044715 x^3)
+  return fmaf(h, tanh_approx(z), h);
 }
 
 }  // namespace sg

@@ -35,8 +35,8 @@ int launch_gemm_tc(const GemmIO& io, const GemmParams& p, cudaStream_t stream) {
   SG_TRY(make_tmap_2d(&to, io.out, 2, p.M, p.N, io.ldo, 32, kEpiCols));
   if (epi_has_res(EPI)) SG_TRY(make_tmap_2d(&tr, io.res, 2, p.M, p.N, io.ldr, 32, kEpiCols));
   else tr = to;
-  constexpr int threads = GemmThreads<epi_has_stat_warps(EPI)>::kThreads;
-  constexpr int smem = GemmCfg<BN, SUB>::kSmemBytes;
+  constexpr int threads = kGemmThreads;
+  constexpr int smem = GemmCfg<BN, SUB, EPI>::kSmemBytes;
   auto kern = gemm_tc_kernel<T, BN, EPI, SUB>;
   static bool attr_done = false;  // per instantiation
   if (!attr_done) {
@@ -59,8 +59,8 @@ int launch_gemm_tc2(const GemmIO& io, const GemmParams& p, cudaStream_t stream) 
   SG_TRY(make_tmap_2d(&to, io.out, 2, p.M, p.N, io.ldo, 32, kEpiCols));
   if (epi_has_res(EPI)) SG_TRY(make_tmap_2d(&tr, io.res, 2, p.M, p.N, io.ldr, 32, kEpiCols));
   else tr = to;
-  constexpr int threads = GemmThreads<epi_has_stat_warps(EPI)>::kThreads;
-  constexpr int smem = Gemm2Cfg<BN, SUB>::kSmemBytes;
+  constexpr int threads = kGemmThreads;
+  constexpr int smem = Gemm2Cfg<BN, SUB, EPI>::kSmemBytes;
   auto kern = gemm_tc2_kernel<T, BN, EPI, SUB>;
   static bool attr_done = false;  // per instantiation
   if (!attr_done) {
@@ -118,10 +118,10 @@ int dispatch_epi(int epi, const GemmIO& io, const GemmParams& p, cudaStream_t s)
   }
 }
 
-// Tile width: 192 when it divides N exactly (1152, 768, 1536 ...), else 256.
+// Tile width: gemm_bn_for (192 when it divides N and 256 does not, e.g. 1152).
 template <typename T>
 int dispatch_bn(int epi, const GemmIO& io, const GemmParams& p, cudaStream_t s) {
-  if (p.N % 192 == 0 && p.N % 256 != 0) return dispatch_epi<T, 192>(epi, io, p, s);
+  if (gemm_bn_for(p.N) == 192) return dispatch_epi<T, 192>(epi, io, p, s);
   return dispatch_epi<T, 256>(epi, io, p, s);
 }
 
@@ -139,7 +139,7 @@ struct PosArgs {
 int sg_gemm_impl(int dtype, int epi, const void* a, int lda, const void* b, int ldb, void* out, int ldo, int M, int N,
                  int K, const float* bias, const void* res, int ldr, const float* c1, const float* c2, float eps,
                  cudaStream_t stream, const float2* rs_in = nullptr, float2* rs_acc = nullptr,
-                 float2* rs_zero = nullptr, const PosArgs* pos = nullptr) {
+                 const PosArgs* pos = nullptr) {
   SG_CHECK_ARG(M >= 0 && N > 0 && K > 0, "bad GEMM shape M=%d N=%d K=%d", M, N, K);
   if (M == 0) return SIGLIP2_OK;
   SG_CHECK_ARG(a && b && out, "null operand");
@@ -158,7 +158,7 @@ int sg_gemm_impl(int dtype, int epi, const void* a, int lda, const void* b, int 
   SG_CHECK_ARG((epi != kEpiBiasResRs && epi != kEpiBiasPosRs) || rs_acc,
                "row-sum accumulating epilogue needs rs_acc");
   const auto misaligned8 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 7u) != 0; };
-  if (misaligned8(rs_in) || misaligned8(rs_acc) || misaligned8(rs_zero))
+  if (misaligned8(rs_in) || misaligned8(rs_acc))
     return set_error(SIGLIP2_ERR_ALIGN, "row-sum buffers must be 8-byte aligned");
   if (dtype == SIGLIP2_F32) {
     if (epi_has_stat_warps(epi))
@@ -166,7 +166,8 @@ int sg_gemm_impl(int dtype, int epi, const void* a, int lda, const void* b, int 
     if (epi_has_res(epi) && !res) return set_error(SIGLIP2_ERR_ARG, "residual epilogue needs res");
     GemmParams p{};
     p.M = M; p.N = N; p.K = K; p.bias = bias; p.c1 = c1; p.c2 = c2; p.eps = eps;
-    p.rs_in = rs_in; p.rs_acc = rs_acc; p.rs_zero = rs_zero;
+    p.rs_in = rs_in; p.rs_acc = rs_acc;
+    p.rs_ld = rs_in ? rowsum_slots(true, K) : rowsum_slots(true, N);
     if (pos) {
       p.pos_table = pos->table; p.pos_grid = pos->grid; p.tok_img = pos->tok_img; p.pos_hw = pos->hw; p.cu = pos->cu;
     }
@@ -208,7 +209,7 @@ int sg_gemm_impl(int dtype, int epi, const void* a, int lda, const void* b, int 
   p.eps = eps;
   p.rs_in = rs_in;
   p.rs_acc = rs_acc;
-  p.rs_zero = rs_zero;
+  p.rs_ld = rs_in ? rowsum_slots(false, K) : rowsum_slots(false, N);
   p.pos_table = nullptr;
   p.pos_grid = 0;
   p.tok_img = p.pos_hw = p.cu = nullptr;
@@ -503,13 +504,13 @@ int sg_forward_impl(const siglip2_config* c, const siglip2_weights* w, const voi
   const int hdp = dt == SIGLIP2_F32 ? hd : padded_head_dim(hd);  // fp32 attention reads unpadded heads
   const int nqkv = 3 * H * hdp;
 
-  // Row sums of the residual stream for the LayerNorm-folded GEMMs: the GEMM
-  // that writes x accumulates them; two buffers alternate (x after the
-  // embeddings / fc2 -> rs_b, after out-proj -> rs_a) and each producer
-  // zeroes the buffer its consumer has just finished with.
+  // Row sums of the residual stream for the LayerNorm-folded GEMMs, in
+  // slots written by the GEMM that writes x: two buffers alternate (x after
+  // the embeddings / fc2 -> rs_b, after out-proj -> rs_a); every slot is
+  // written before it is read, so nothing is cleared.
+  const size_t rs_n = static_cast<size_t>(N) * rowsum_slots(dt == SIGLIP2_F32, D);
   float2* rs_a = f.rowsums;
-  float2* rs_b = f.rowsums + N;
-  SG_CUDA(cudaMemsetAsync(f.rowsums, 0, sizeof(float2) * 2 * static_cast<size_t>(N), s));
+  float2* rs_b = f.rowsums + rs_n;
   // embeddings: x = patches Wp^T + bp + resized position grid, one GEMM whose
   // epilogue evaluates the antialiased resize per token (and the row sums)
   SG_TRY(sg_token_image_impl(cu, B, N, f.tok_img, s));
@@ -522,18 +523,18 @@ int sg_forward_impl(const siglip2_config* c, const siglip2_weights* w, const voi
   }
   const PosArgs pos{w->pos_table, c->pos_grid, f.tok_img, hw, cu};
   SG_TRY(sg_gemm_impl(dt, kEpiBiasPosRs, prow, c->patch_dim, w->patch_w, c->patch_dim, f.x, D, N, D, c->patch_dim,
-                      w->patch_b, nullptr, 0, nullptr, nullptr, 0.f, s, nullptr, rs_b, nullptr, &pos));
+                      w->patch_b, nullptr, 0, nullptr, nullptr, 0.f, s, nullptr, rs_b, &pos));
   for (int l = 0; l < c->layers; ++l) {
     const siglip2_layer_weights& lw = w->layers[l];
     SG_TRY(sg_gemm_impl(dt, kEpiLnRs, f.x, D, lw.qkv_w, D, f.qkv, nqkv, N, nqkv, D, nullptr, nullptr, 0, lw.qkv_c1,
-                        lw.qkv_c2, c->eps, s, rs_b, nullptr, nullptr));
+                        lw.qkv_c2, c->eps, s, rs_b, nullptr));
     SG_TRY(sg_fmha_impl(dt, f.qkv, N, cu, tiles, T, H, hd, f.attn, D, s));
     SG_TRY(sg_gemm_impl(dt, kEpiBiasResRs, f.attn, D, lw.out_w, D, f.x, D, N, D, D, lw.out_b, f.x, D, nullptr,
-                        nullptr, 0.f, s, nullptr, rs_a, rs_b));
+                        nullptr, 0.f, s, nullptr, rs_a));
     SG_TRY(sg_gemm_impl(dt, kEpiLnRsGelu, f.x, D, lw.fc1_w, D, f.hmid, I, N, I, D, nullptr, nullptr, 0, lw.fc1_c1,
-                        lw.fc1_c2, c->eps, s, rs_a, nullptr, nullptr));
+                        lw.fc1_c2, c->eps, s, rs_a, nullptr));
     SG_TRY(sg_gemm_impl(dt, kEpiBiasResRs, f.hmid, I, lw.fc2_w, I, f.x, D, N, D, I, lw.fc2_b, f.x, D, nullptr,
-                        nullptr, 0.f, s, nullptr, rs_b, rs_a));
+                        nullptr, 0.f, s, nullptr, rs_b));
   }
   // post-LayerNorm -> last_hidden_state (packed or padded with zero rows)
   SG_TRY(sg_layernorm_impl(dt, f.x, last_hidden, w->post_ln_w, w->post_ln_b, P > 0 ? B * P : N, D, c->eps,
@@ -548,10 +549,11 @@ int sg_forward_impl(const siglip2_config* c, const siglip2_weights* w, const voi
     SG_TRY(sg_gemm_impl(dt, kEpiBias, f.hattn, D, w->head_o_w, D, f.ha, D, B, D, D, w->head_o_b, nullptr, 0, nullptr,
                         nullptr, 0.f, s));
     if (dt == SIGLIP2_F32) {
-      rowsums_f32_kernel<<<(B + 7) / 8, 256, 0, s>>>(static_cast<const float*>(f.ha), B, D, rs_a);
+      rowsums_f32_kernel<<<(B + 7) / 8, 256, 0, s>>>(static_cast<const float*>(f.ha), B, D, rs_a,
+                                                      rowsum_slots(true, D));
       SG_LAUNCH_CHECK();
       SG_TRY(sg_gemm_impl(dt, kEpiLnRsGelu, f.ha, D, w->head_fc1_w, D, f.hmid2, I, B, I, D, nullptr, nullptr, 0,
-                          w->head_fc1_c1, w->head_fc1_c2, c->eps, s, rs_a, nullptr, nullptr));
+                          w->head_fc1_c1, w->head_fc1_c2, c->eps, s, rs_a, nullptr));
     } else {
       SG_TRY(sg_gemm_impl(dt, kEpiLnGelu, f.ha, D, w->head_fc1_w, D, f.hmid2, I, B, I, D, nullptr, nullptr, 0,
                           w->head_fc1_c1, w->head_fc1_c2, c->eps, s));
@@ -643,13 +645,23 @@ int siglip2_gemm(int dtype, int epilogue, const void* a_dev, int lda, const void
                       c2_dev, eps, static_cast<cudaStream_t>(stream));
 }
 
+int siglip2_rowsum_slots(int dtype, int n) {
+  SG_CHECK_ARG(n > 0, "bad row width %d", n);
+  return rowsum_slots(dtype == SIGLIP2_F32, n);
+}
+
+int siglip2_rowsum_block(int dtype, int n) {
+  SG_CHECK_ARG(n > 0, "bad row width %d", n);
+  return rowsum_block(dtype == SIGLIP2_F32, n);
+}
+
 int siglip2_gemm_rowsums(int dtype, int epilogue, const void* a_dev, int lda, const void* b_dev, int ldb,
                          void* out_dev, int ldo, int M, int N, int K, const float* bias_dev, const void* res_dev,
                          int ldr, const float* c1_dev, const float* c2_dev, float eps, const float* rs_in_dev,
-                         float* rs_acc_dev, float* rs_zero_dev, void* stream) {
+                         float* rs_acc_dev, void* stream) {
   return sg_gemm_impl(dtype, epilogue, a_dev, lda, b_dev, ldb, out_dev, ldo, M, N, K, bias_dev, res_dev, ldr, c1_dev,
                       c2_dev, eps, static_cast<cudaStream_t>(stream), reinterpret_cast<const float2*>(rs_in_dev),
-                      reinterpret_cast<float2*>(rs_acc_dev), reinterpret_cast<float2*>(rs_zero_dev));
+                      reinterpret_cast<float2*>(rs_acc_dev));
 }
 
 int siglip2_patch_embed(int dtype, const void* patches_dev, int patch_dim, const void* w_dev, const float* bias_dev,
@@ -660,7 +672,7 @@ int siglip2_patch_embed(int dtype, const void* patches_dev, int patch_dim, const
   const PosArgs pos{table_dev, grid, tok_img_dev, hw_dev, cu_seqlens_dev};
   return sg_gemm_impl(dtype, kEpiBiasPosRs, patches_dev, patch_dim, w_dev, patch_dim, out_dev, D, N, D, patch_dim,
                       bias_dev, nullptr, 0, nullptr, nullptr, 0.f, static_cast<cudaStream_t>(stream), nullptr,
-                      reinterpret_cast<float2*>(rs_acc_dev), nullptr, &pos);
+                      reinterpret_cast<float2*>(rs_acc_dev), &pos);
 }
 
 int siglip2_layernorm(int dtype, const void* x_dev, void* y_dev, const float* gamma_dev, const float* beta_dev,

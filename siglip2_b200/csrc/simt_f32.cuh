@@ -52,30 +52,41 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
   }
   constexpr bool kLnRs = (EPI == kEpiLnRs || EPI == kEpiLnRsGelu);
   constexpr bool kGelu = epi_is_gelu(EPI);
+  constexpr bool kRsOut = (EPI == kEpiBiasResRs || EPI == kEpiBiasPosRs);
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
+    // uniform across the 16 threads (tx) of this row: the row-sum shuffles below need all of them
     const int row = m0 + ty * 8 + i;
-    if (row >= p.M) continue;
+    const bool row_ok = row < p.M;
     AxisTaps ay{0, 0, 0.f, 1.f, 0.f}, ax{0, 0, 0.f, 1.f, 0.f};
     if constexpr (EPI == kEpiBiasPosRs) {
-      const int b = p.tok_img[row];
-      const int w = p.pos_hw[2 * b + 1];
-      const int t = row - p.cu[b];
-      ay = axis_taps(t / w, p.pos_hw[2 * b], p.pos_grid);
-      ax = axis_taps(t - (t / w) * w, w, p.pos_grid);
+      if (row_ok) {
+        const int b = p.tok_img[row];
+        const int w = p.pos_hw[2 * b + 1];
+        const int t = row - p.cu[b];
+        ay = axis_taps(t / w, p.pos_hw[2 * b], p.pos_grid);
+        ax = axis_taps(t - (t / w) * w, w, p.pos_grid);
+      }
     }
     float mu = 0.f, rstd = 1.f;
     if constexpr (kLnRs) {
-      const float2 rs = p.rs_in[row];
-      const float inv_k = 1.f / static_cast<float>(p.K);
-      mu = rs.x * inv_k;
-      rstd = 1.f / sqrtf(fmaxf(rs.y * inv_k - mu * mu, 0.f) + p.eps);
+      if (row_ok) {
+        float sx = 0.f, sxx = 0.f;  // slot by slot, in order
+        for (int j = 0; j < p.rs_ld; ++j) {
+          const float2 v = p.rs_in[static_cast<size_t>(row) * p.rs_ld + j];
+          sx += v.x;
+          sxx += v.y;
+        }
+        const float inv_k = 1.f / static_cast<float>(p.K);
+        mu = sx * inv_k;
+        rstd = 1.f / sqrtf(fmaxf(sxx * inv_k - mu * mu, 0.f) + p.eps);
+      }
     }
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int col = n0 + tx * 8 + j;
-      if (col >= p.N) continue;
+      if (!row_ok || col >= p.N) continue;
       float v = acc[i][j];
       if constexpr (kLnRs) {
         v = rstd * (v - mu * p.c1[col]) + p.c2[col];
@@ -93,29 +104,36 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
       s1 += v;
       s2 = fmaf(v, v, s2);
     }
-    if constexpr (EPI == kEpiBiasResRs || EPI == kEpiBiasPosRs) {
-      atomicAdd(&p.rs_acc[row].x, s1);
-      atomicAdd(&p.rs_acc[row].y, s2);
-      if (p.rs_zero != nullptr && n0 == 0 && tx == 0) p.rs_zero[row] = make_float2(0.f, 0.f);
+    if constexpr (kRsOut) {
+      // this CTA's 128 columns are one slot: reduce over the 16 threads of the row in a fixed order
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) {
+        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+      }
+      if (tx == 0 && row_ok) p.rs_acc[static_cast<size_t>(row) * p.rs_ld + blockIdx.x] = make_float2(s1, s2);
     }
   }
 }
 
-// Row sums (sum, sum of squares) of a [M, K] fp32 matrix: the statistics the
-// row-sum LayerNorm epilogues read (used where the producer is not a GEMM).
-__global__ void rowsums_f32_kernel(const float* __restrict__ x, int M, int K, float2* __restrict__ rs) {
+// Row sums (sum, sum of squares) of a [M, K] fp32 matrix in 128-column slots
+// ([M][ld] pairs): the statistics the row-sum LayerNorm epilogues read, for
+// rows whose producer is not a GEMM.  One warp per row.
+__global__ void rowsums_f32_kernel(const float* __restrict__ x, int M, int K, float2* __restrict__ rs, int ld) {
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
-  float s1 = 0.f, s2 = 0.f;
-  for (int k = lane; k < K; k += 32) {
-    const float v = x[static_cast<size_t>(row) * K + k];
-    s1 += v;
-    s2 = fmaf(v, v, s2);
+  for (int j = 0; j < ld; ++j) {
+    float s1 = 0.f, s2 = 0.f;
+    for (int k = j * 128 + lane; k < min(K, (j + 1) * 128); k += 32) {
+      const float v = x[static_cast<size_t>(row) * K + k];
+      s1 += v;
+      s2 = fmaf(v, v, s2);
+    }
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2);
+    if (lane == 0) rs[static_cast<size_t>(row) * ld + j] = make_float2(s1, s2);
   }
-  s1 = warp_sum(s1);
-  s2 = warp_sum(s2);
-  if (lane == 0) rs[row] = make_float2(s1, s2);
 }
 
 // Per-image attention in fp32: one thread per query row, one CTA per

@@ -5,8 +5,10 @@ command the ncu summaries under ``profiles/`` were captured with.
     python -m siglip2_b200.kernel_bench fmha --preset so400m --images 64 --max-patches 1024
     python -m siglip2_b200.kernel_bench layer --preset so400m --images 64 --max-patches 1024
 
-Prints one JSON line per measurement: milliseconds per launch and the
-algorithmic TFLOP/s (dense contractions only).
+Prints one JSON line per measurement: milliseconds per launch, the
+algorithmic TFLOP/s (dense contractions only) and the median SM clock seen
+through NVML while the launches ran.  ``gemm --cublas`` adds torch.matmul
+(cuBLAS, no epilogue) on the same operands as a library reference point.
 """
 from __future__ import annotations
 
@@ -19,41 +21,59 @@ import torch
 from . import _lib as L
 from . import ops
 from . import workloads as W
+from .clocks import ClockSampler
 
 EPIS = {"bias": L.EPI_BIAS, "bias_res": L.EPI_BIAS_RES, "ln": L.EPI_LN, "ln_gelu": L.EPI_LN_GELU,
         "bias_gelu": L.EPI_BIAS_GELU, "lnrs": L.EPI_LN_ROWSUMS, "lnrs_gelu": L.EPI_LN_ROWSUMS_GELU,
         "bias_res_rs": L.EPI_BIAS_RES_ROWSUMS}
 
 
+_LAST_CLOCK = {}
+
+
 def _time(fn, reps: int, warmup: int = 3) -> float:
+    """Milliseconds per call over ``reps`` back-to-back calls (CUDA events on
+    the current stream); the SM clock seen meanwhile goes to ``_LAST_CLOCK``."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(reps):
-        fn()
-    e.record()
-    torch.cuda.synchronize()
+    with ClockSampler(torch.cuda.current_device(), period=0.005) as clk:
+        s.record()
+        for _ in range(reps):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+    _LAST_CLOCK.clear()
+    _LAST_CLOCK.update(clk.summary())
     return s.elapsed_time(e) / reps
 
 
-def bench_gemm(m, n, k, epi, reps, dtype=torch.bfloat16, warmup=3):
+def _clock():
+    return {"sm_mhz": _LAST_CLOCK.get("sm_mhz"), "reasons": _LAST_CLOCK.get("reasons")}
+
+
+def bench_gemm(m, n, k, epi, reps, dtype=torch.bfloat16, warmup=3, cublas=False):
     a = torch.randn(m, k, device="cuda").to(dtype)
     w = (torch.randn(n, k, device="cuda") * 0.02).to(dtype)
     vec = torch.randn(n, device="cuda") * 0.1
     res = torch.randn(m, n, device="cuda").to(dtype) if epi in ("bias_res", "bias_res_rs") else None
     out = torch.empty(m, n, device="cuda", dtype=dtype)
-    rs = torch.rand(m, 2, device="cuda") + 1.0
     if epi in ("lnrs", "lnrs_gelu", "bias_res_rs"):
-        acc = torch.zeros(m, 2, device="cuda") if epi == "bias_res_rs" else None
-        rs_in = rs if epi != "bias_res_rs" else None
+        acc = torch.zeros(m, ops.rowsum_slots(dtype, n), 2, device="cuda") if epi == "bias_res_rs" else None
+        rs_in = ops.rowsums_reference(a) if epi != "bias_res_rs" else None
         fn = lambda: ops.gemm_rowsums(a, w, EPIS[epi], bias=vec, res=res, c1=vec, c2=vec, rs_in=rs_in, rs_acc=acc,  # noqa: E731
                                       out=out)
     else:
         fn = lambda: ops.gemm(a, w, EPIS[epi], bias=vec, res=res, c1=vec, c2=vec, out=out)  # noqa: E731
     ms = _time(fn, reps, warmup)
-    return {"kernel": "gemm", "epi": epi, "M": m, "N": n, "K": k, "ms": ms, "tflops": 2 * m * n * k / ms / 1e9}
+    r = {"kernel": "gemm", "epi": epi, "M": m, "N": n, "K": k, "ms": ms, "tflops": 2 * m * n * k / ms / 1e9,
+         **_clock()}
+    if cublas:
+        wt = w.t()
+        ms_c = _time(lambda: torch.matmul(a, wt, out=out), reps, warmup)
+        r["cublas"] = {"ms": ms_c, "tflops": 2 * m * n * k / ms_c / 1e9, **_clock()}
+    return r
 
 
 def _shapes(preset, images, max_patches, seed=1337):
@@ -75,7 +95,8 @@ def bench_fmha(preset, images, max_patches, reps, dtype=torch.bfloat16, warmup=3
     out = torch.empty(N, D, device="cuda", dtype=dtype)
     ms = _time(lambda: ops.fmha_varlen(qkv, cu, tiles, H, hd, out=out), reps, warmup)
     fl = sum(4 * L_ * L_ * D for L_ in lens)
-    return {"kernel": "fmha", "preset": preset, "images": images, "tokens": N, "ms": ms, "tflops": fl / ms / 1e9}
+    return {"kernel": "fmha", "preset": preset, "images": images, "tokens": N, "ms": ms, "tflops": fl / ms / 1e9,
+            **_clock()}
 
 
 def bench_layer(preset, images, max_patches, reps):
@@ -100,7 +121,8 @@ def main():
     g.add_argument("--m", type=int, default=39178)
     g.add_argument("--n", type=int, default=4304)
     g.add_argument("--k", type=int, default=1152)
-    g.add_argument("--epi", default="ln_gelu", choices=sorted(EPIS))
+    g.add_argument("--epi", default="ln_gelu", help="one of %s, or several separated by commas" % ",".join(sorted(EPIS)))
+    g.add_argument("--cublas", action="store_true", help="also time torch.matmul (cuBLAS) on the same operands")
     g.add_argument("--reps", type=int, default=20)
     g.add_argument("--warmup", type=int, default=3)
     f = sub.add_parser("fmha")
@@ -119,7 +141,10 @@ def main():
     a = ap.parse_args()
     L.check(L.load().siglip2_set_gemm_variant(a.variant))
     if a.cmd == "gemm":
-        print(json.dumps(bench_gemm(a.m, a.n, a.k, a.epi, a.reps, warmup=a.warmup)))
+        for epi in a.epi.split(","):
+            if epi not in EPIS:
+                raise SystemExit(f"unknown epilogue {epi!r}")
+            print(json.dumps(bench_gemm(a.m, a.n, a.k, epi, a.reps, warmup=a.warmup, cublas=a.cublas)))
     elif a.cmd == "fmha":
         print(json.dumps(bench_fmha(a.preset, a.images, a.max_patches, a.reps, warmup=a.warmup)))
     else:

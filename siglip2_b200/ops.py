@@ -129,20 +129,47 @@ def head_pool(x: torch.Tensor, u: torch.Tensor, cu_seqlens: torch.Tensor, n_toke
     return pooled
 
 
+def rowsum_slots(dtype: torch.dtype, width: int) -> int:
+    """``siglip2_rowsum_slots``: column-block slots per row of the row-sum
+    buffers for rows of ``width`` columns."""
+    return L.check_value(L.load().siglip2_rowsum_slots(dtype_code(dtype), width))
+
+
+def rowsums_reference(x: torch.Tensor) -> torch.Tensor:
+    """Row sums of ``x`` in the slot layout the LayerNorm-folded GEMMs read
+    (``[M, S, 2]`` float32), computed with torch: for tests and callers whose
+    rows were not produced by a row-sum GEMM."""
+    M, K = x.shape
+    S = rowsum_slots(x.dtype, K)
+    blk = L.check_value(L.load().siglip2_rowsum_block(dtype_code(x.dtype), K))
+    xf = x.float()
+    out = torch.zeros(M, S, 2, dtype=torch.float32, device=x.device)
+    for j in range(S):
+        part = xf[:, j * blk:(j + 1) * blk]
+        out[:, j, 0] = part.sum(1)
+        out[:, j, 1] = (part * part).sum(1)
+    return out
+
+
 def gemm_rowsums(a: torch.Tensor, w: torch.Tensor, epilogue: int, bias=None, res=None, c1=None, c2=None,
-                 eps: float = 1e-6, rs_in=None, rs_acc=None, rs_zero=None,
+                 eps: float = 1e-6, rs_in=None, rs_acc=None,
                  out: torch.Tensor | None = None) -> torch.Tensor:
-    """``siglip2_gemm_rowsums``: row-sum LayerNorm epilogues (``rs_*`` are
-    ``[M, 2]`` float32 (sum, sum of squares) buffers)."""
-    _need_cuda(a, w, bias, res, c1, c2, rs_in, rs_acc, rs_zero, out)
+    """``siglip2_gemm_rowsums``: row-sum LayerNorm epilogues.  ``rs_in`` is
+    ``[M, rowsum_slots(dtype, K), 2]`` and ``rs_acc`` ``[M, rowsum_slots(dtype, N), 2]``
+    float32 (sum, sum of squares) per column block."""
+    _need_cuda(a, w, bias, res, c1, c2, rs_in, rs_acc, out)
     M, K = a.shape
     N = w.shape[0]
+    for t, width in ((rs_in, K), (rs_acc, N)):
+        if t is not None and (t.dtype != torch.float32 or not t.is_contiguous()
+                              or t.numel() != M * rowsum_slots(a.dtype, width) * 2):
+            raise ValueError("row-sum buffer must be contiguous float32 [M, rowsum_slots(dtype, width), 2]")
     if out is None:
         out = torch.empty((M, N), dtype=a.dtype, device=a.device)
     L.call("siglip2_gemm_rowsums", dtype_code(a.dtype), epilogue, a.data_ptr(), a.stride(0), w.data_ptr(),
            w.stride(0), out.data_ptr(), out.stride(0), M, N, K, _ptr(bias), _ptr(res),
            res.stride(0) if res is not None else 0, _ptr(c1), _ptr(c2), float(eps), _ptr(rs_in), _ptr(rs_acc),
-           _ptr(rs_zero), _stream(a.device))
+           _stream(a.device))
     return out
 
 
@@ -156,7 +183,7 @@ def patch_embed(patches: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, tabl
     G = int(round(table_f32.shape[0] ** 0.5))
     out = torch.empty((N, D), dtype=patches.dtype, device=patches.device)
     if rs_acc is None:
-        rs_acc = torch.zeros((N, 2), dtype=torch.float32, device=patches.device)
+        rs_acc = torch.empty((N, rowsum_slots(patches.dtype, D), 2), dtype=torch.float32, device=patches.device)
     L.call("siglip2_patch_embed", dtype_code(patches.dtype), patches.data_ptr(), C, w.data_ptr(), bias.data_ptr(),
            table_f32.data_ptr(), G, tok_img.data_ptr(), hw.data_ptr(), cu_seqlens.data_ptr(), N, D, out.data_ptr(),
            rs_acc.data_ptr(), _stream(patches.device))

@@ -63,3 +63,20 @@ def test_workspace_size_monotone():
     a = lib.siglip2_workspace_size(ctypes.byref(cfg), 64, 30000)
     b = lib.siglip2_workspace_size(ctypes.byref(cfg), 64, 40000)
     assert 0 < a < b
+
+
+def test_rowsum_slots_follow_the_tile_widths():
+    """Row-sum slots are half a GEMM tile wide (192-wide tiles where 192
+    divides the width and 256 does not, else 256) on the tensor-core path and
+    128 wide on the fp32 path; bad widths are rejected without a GPU."""
+    lib = L.load()
+    bf16, f32 = 1, 0
+    assert lib.siglip2_rowsum_slots(bf16, 1152) == 12   # 192-wide tiles, 96-column slots
+    assert lib.siglip2_rowsum_slots(bf16, 768) == 6     # 256-wide tiles, 128-column slots
+    assert lib.siglip2_rowsum_slots(bf16, 1536) == 12
+    assert lib.siglip2_rowsum_slots(bf16, 4304) == 34
+    assert lib.siglip2_rowsum_slots(f32, 768) == 6
+    assert lib.siglip2_rowsum_slots(bf16, 0) < 0
+    assert lib.siglip2_rowsum_block(bf16, 1152) == 96
+    assert lib.siglip2_rowsum_block(bf16, 4304) == 128  # the last of the 34 slots holds 80 columns
+    assert lib.siglip2_rowsum_block(f32, 4304) == 128

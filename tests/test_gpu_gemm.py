@@ -105,15 +105,14 @@ def test_gemm_residual_accumulates_row_sums(dtype, M, N, K):
     w = (torch.randn(N, K, device="cuda", generator=g) * 0.03).to(dtype)
     bias = torch.randn(N, device="cuda", generator=g) * 0.1
     res = torch.randn(M, N, device="cuda", generator=g).to(dtype)
-    acc = torch.zeros(M, 2, device="cuda")
-    junk = torch.full((M, 2), 7.0, device="cuda")
-    out = ops.gemm_rowsums(a, w, L.EPI_BIAS_RES_ROWSUMS, bias=bias, res=res, rs_acc=acc, rs_zero=junk)
+    acc = torch.full((M, ops.rowsum_slots(dtype, N), 2), float("nan"), device="cuda")  # every slot is written
+    out = ops.gemm_rowsums(a, w, L.EPI_BIAS_RES_ROWSUMS, bias=bias, res=res, rs_acc=acc)
     torch.cuda.synchronize()
     _close(out, a.float() @ w.float().T + bias + res.float())
-    o = out.float()  # sums of exactly the stored (rounded) values
-    assert torch.allclose(acc[:, 0], o.sum(1), rtol=1e-4, atol=1e-2)
-    assert torch.allclose(acc[:, 1], (o * o).sum(1), rtol=1e-4, atol=1e-2)
-    assert not junk.any()
+    o = out.float()  # sums of exactly the stored (rounded) values, per column block
+    ref = ops.rowsums_reference(out)
+    assert torch.allclose(acc, ref, rtol=1e-4, atol=1e-2)
+    assert torch.allclose(acc.sum(1)[:, 0], o.sum(1), rtol=1e-4, atol=1e-2)
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
@@ -129,7 +128,7 @@ def test_gemm_layernorm_from_row_sums(dtype, M, N, K, gelu):
     beta = 0.1 * torch.randn(K, device="cuda", generator=g)
     wg, c1, c2 = ops.fold_layernorm(w, b, gamma, beta, dtype)
     xf = x.float()
-    rs = torch.stack([xf.sum(1), (xf * xf).sum(1)], 1).contiguous()
+    rs = ops.rowsums_reference(x)
     out = ops.gemm_rowsums(x, wg, L.EPI_LN_ROWSUMS_GELU if gelu else L.EPI_LN_ROWSUMS, c1=c1, c2=c2, eps=1e-6,
                            rs_in=rs)
     ref = F.layer_norm(xf, (K,), gamma, beta, 1e-6) @ w.T + b
@@ -137,3 +136,45 @@ def test_gemm_layernorm_from_row_sums(dtype, M, N, K, gelu):
         ref = _gelu(ref)
     torch.cuda.synchronize()
     _close(out, ref, tol=2e-2)
+
+
+@pytest.mark.parametrize("N,K", [(1152, 1152), (4304, 1152), (1152, 4304), (3840, 1152)])
+@pytest.mark.parametrize("epi", ["bias", "bias_gelu", "lnrs", "lnrs_gelu", "bias_res_rs_inplace"])
+def test_gemm_many_tiles_per_cta(N, K, epi):
+    """M large enough that every CTA (pair) walks several tiles, so the
+    accumulator, staging-buffer and barrier phases wrap; checked element by
+    element against fp32 math on the same bf16 inputs."""
+    M = 9001
+    g = torch.Generator(device="cuda").manual_seed(N * 3 + K)
+    x = (torch.randn(M, K, device="cuda", generator=g) * 2 + 0.5).bfloat16()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.03).bfloat16()
+    bias = torch.randn(N, device="cuda", generator=g) * 0.1
+    xf, wf = x.float(), w.float()
+    if epi in ("bias", "bias_gelu"):
+        out = ops.gemm(x, w, L.EPI_BIAS if epi == "bias" else L.EPI_BIAS_GELU, bias=bias)
+        ref = xf @ wf.T + bias
+        if epi == "bias_gelu":
+            ref = _gelu(ref)
+    elif epi in ("lnrs", "lnrs_gelu"):
+        rs = ops.rowsums_reference(x)
+        c1 = torch.randn(N, device="cuda", generator=g) * 0.1
+        c2 = torch.randn(N, device="cuda", generator=g) * 0.1
+        out = ops.gemm_rowsums(x, w, L.EPI_LN_ROWSUMS_GELU if epi == "lnrs_gelu" else L.EPI_LN_ROWSUMS, c1=c1, c2=c2,
+                               eps=1e-6, rs_in=rs)
+        tot = rs.sum(1)
+        mu = tot[:, 0:1] / K
+        rstd = torch.rsqrt(tot[:, 1:2] / K - mu * mu + 1e-6)
+        ref = rstd * (xf @ wf.T - mu * c1) + c2
+        if epi == "lnrs_gelu":
+            ref = _gelu(ref)
+    else:  # out-projection / fc2 as the forward runs them: residual updated in place, row sums out
+        res = torch.randn(M, N, device="cuda", generator=g).bfloat16()
+        ref = xf @ wf.T + bias + res.float()
+        acc = torch.full((M, ops.rowsum_slots(torch.bfloat16, N), 2), float("nan"), device="cuda")
+        out = ops.gemm_rowsums(x, w, L.EPI_BIAS_RES_ROWSUMS, bias=bias, res=res, rs_acc=acc, out=res)
+    torch.cuda.synchronize()
+    o = out.float()
+    bad = (o - ref).abs() > 1e-2 * ref.abs() + 2e-3 * ref.abs().max()
+    assert not bad.any(), (bad.nonzero()[:8].tolist(), bad.sum().item())
+    if epi == "bias_res_rs_inplace":
+        assert torch.allclose(acc, ops.rowsums_reference(out), rtol=1e-4, atol=1e-2)

@@ -139,8 +139,9 @@ def test_patch_embed_fused_position_resize(dtype, D):
     w = (torch.randn(D, 768, device="cuda", generator=g) * 0.02).to(dtype)
     bias = torch.randn(D, device="cuda", generator=g) * 0.02
     table = torch.randn(256, D, device="cuda", generator=g) * 0.02
-    rs = torch.zeros(N, 2, device="cuda")
+    rs = torch.full((N, ops.rowsum_slots(dtype, D), 2), float("nan"), device="cuda")  # every slot is written
     out = ops.patch_embed(patches, w, bias, table, hw, cu, tok, rs)
+    rs = rs.sum(1)
     grid = table.view(16, 16, D).permute(2, 0, 1)[None]
     pos = torch.cat([F.interpolate(grid, size=(h, w_), mode="bilinear", align_corners=False, antialias=True)[0]
                      .reshape(D, h * w_).T for h, w_ in grids], 0)

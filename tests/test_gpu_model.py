@@ -130,3 +130,19 @@ def test_fused_qkv_state_dict_loads():
     pv, _ = W.make_pixels(g, 64, 768)
     x = W.pack_rows(pv, g).cuda().bfloat16()
     assert torch.equal(a((x, g)), b((x, g)))
+
+
+@pytest.mark.parametrize("preset", ["b16", "so400m"])
+def test_forward_is_deterministic(preset):
+    """No atomics anywhere on the path: two forwards of the same input are
+    bit-identical (the row sums behind the folded LayerNorms are written in
+    column-block slots and summed in a fixed order)."""
+    cfg, m, _ = _build(preset, 2, torch.bfloat16, seed=11)
+    grids = [(18, 18), (24, 31), (11, 37), (32, 32), (8, 128), (16, 16), (5, 7)] * 6
+    g = torch.tensor(grids)
+    pv, _ = W.make_pixels(g, max(h * w for h, w in grids), cfg.num_channels * cfg.patch_size ** 2, seed=11)
+    x = W.pack_rows(pv, g).cuda().bfloat16()
+    a = m((x, g))
+    b = m((x, g))
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
