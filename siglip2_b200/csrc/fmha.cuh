@@ -9,14 +9,20 @@
 // (head_dim 64 | 72 | 96), split into a 64-wide slab (128B swizzle) plus an
 // R = HDP-64 wide slab (32B / 64B swizzle).
 //
-// One CTA per (128-query tile of one image, head); two CTAs share an SM
-// (256 TMEM columns and <= 96 KB of shared memory each).  Keys come in tiles
-// of KT = 96.  TMEM columns: S [0, 96) fp32, P [96, 144) (bf16/f16 pairs),
+// Persistent: two CTAs per SM (256 TMEM columns and <= 104 KB of shared
+// memory each) walk the work items (128-query tile of one image, head) of
+// the tile list, longest images first, item = blockIdx.x + k * gridDim.x.
+// The TMA warp loads the next item's Q (second buffer where it fits) and K/V
+// tiles while the current item runs, and the next item's first QK^T is
+// issued while the softmax warps still drain this item's O, so the per-item
+// prologue and epilogue overlap the other work.  Keys come in tiles of
+// KT = 96.  TMEM columns: S [0, 96) fp32, P [96, 144) (bf16/f16 pairs),
 // O [144, 144 + HDP) fp32.  Because P has its own columns, S_{j+1} = Q K_{j+1}^T
 // runs on the tensor cores while the softmax warps turn S_j into P_j.
-//   warp 0     TMA: Q once, K and V tiles into 2-deep rings
+//   warp 0     TMA: Q per item, K and V tiles into 2-deep rings
 //   warp 1     TMEM owner + MMA issuer: S_j as soon as the softmax has read
-//              S_{j-1}; then O += P_{j-1} V_{j-1} (P read from TMEM)
+//              S_{j-1}; then O += P_{j-1} V_{j-1} (P read from TMEM); an
+//              item's first PV overwrites O once the previous item's O is read
 //   warps 2-5  softmax: each thread owns one query row (its TMEM lane):
 //              loads S_j into registers and frees it, masks keys past the
 //              image end, online max with lazy rescale (O is rescaled in TMEM
@@ -31,6 +37,7 @@ namespace sg {
 struct FmhaParams {
   const int* cu;      // [B+1] first row of each image in the packed sequence
   const int2* tiles;  // [n_tiles] (image, query-tile index)
+  int n_items;        // n_tiles * heads work items: item w = (tile w / heads, head w % heads)
   int heads;
   int head_dim;
   void* out;          // [N, heads*head_dim]
@@ -55,8 +62,11 @@ struct FmhaCfg {
   static constexpr int kKSlabR = KT * R * 2;
   static constexpr int kKTile = kKSlabA + (kKSlabR + 1023) / 1024 * 1024;
   static constexpr int kStages = 2;
+  // Q double-buffered (the next item's Q lands while this one runs) where
+  // two CTAs still fit in an SM's shared memory
+  static constexpr int kQBufs = 2 * (2 * kQTile + 2 * kStages * kKTile + 2304) <= 226 * 1024 ? 2 : 1;
   static constexpr int kQ = 0;
-  static constexpr int kK = kQTile;
+  static constexpr int kK = kQBufs * kQTile;
   static constexpr int kV = kK + kStages * kKTile;
   static constexpr int kBar = kV + kStages * kKTile;
   static constexpr int kSmem = kBar + 256 + 1024;
@@ -76,6 +86,7 @@ __global__ void __launch_bounds__(192, 2)
   constexpr int R = C::R;
   constexpr int KT = C::KT;
   constexpr int ST = C::kStages;
+  constexpr int QB = C::kQBufs;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kIdescS = make_idesc(128, KT, kBF16, false, false);
   constexpr uint32_t kIdescO64 = make_idesc(128, 64, kBF16, false, true);
@@ -84,33 +95,30 @@ __global__ void __launch_bounds__(192, 2)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBar);
-  uint64_t* q_full = bars;           // 1
-  uint64_t* k_full = bars + 1;       // ST
+  uint64_t* q_full = bars;           // QB: an item's Q landed
+  uint64_t* q_empty = q_full + QB;   // QB: an item's QK^T MMAs are done with its Q
+  uint64_t* k_full = q_empty + QB;   // ST
   uint64_t* k_empty = k_full + ST;   // ST
   uint64_t* v_full = k_empty + ST;   // ST
   uint64_t* v_empty = v_full + ST;   // ST
-  uint64_t* s_full = v_empty + ST;   // 1: S_j computed
-  uint64_t* s_free = s_full + 1;     // 1: S_j read by the softmax (128 arrivals)
-  uint64_t* p_full = s_free + 1;     // 1: P_j written, O rescaled (128 arrivals)
-  uint64_t* pv_done = p_full + 1;    // 1: O += P_j V_j complete
-  uint64_t* mdone = pv_done + 1;     // 1
+  uint64_t* s_full = v_empty + ST;   // 1: S computed
+  uint64_t* s_free = s_full + 1;     // 1: S read by the softmax (128 arrivals)
+  uint64_t* p_full = s_free + 1;     // 1: P written, O rescaled (128 arrivals)
+  uint64_t* pv_done = p_full + 1;    // 1: O += P V complete
+  uint64_t* o_free = pv_done + 1;    // 1: an item's O read by the softmax warps (128 arrivals)
+  uint64_t* mdone = o_free + 1;      // 1
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mdone + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int2 tile = p.tiles[blockIdx.x];
-  const int head = blockIdx.y;
-  const int img_row0 = __ldg(p.cu + tile.x);
-  const int L = __ldg(p.cu + tile.x + 1) - img_row0;
-  const int q_row0 = img_row0 + tile.y * 128;
-  const int n_kv = (L + KT - 1) / KT;
-  const int colQ = head * HDP;
-  const int colK = (p.heads + head) * HDP;
-  const int colV = (2 * p.heads + head) * HDP;
+  const int H = p.heads;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    for (int b = 0; b < QB; ++b) {
+      mbar_init(&q_full[b], 1);
+      mbar_init(&q_empty[b], 1);
+    }
     for (int s = 0; s < ST; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
@@ -121,6 +129,7 @@ __global__ void __launch_bounds__(192, 2)
     mbar_init(s_free, 128);
     mbar_init(p_full, 128);
     mbar_init(pv_done, 1);
+    mbar_init(o_free, 128);
     mbar_init(mdone, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -143,54 +152,74 @@ __global__ void __launch_bounds__(192, 2)
         tma_prefetch_desc(&tmQR);
         tma_prefetch_desc(&tmKR);
       }
-      mbar_arrive_expect_tx(q_full, C::kQBytes);
-      tma_load_2d(smem + C::kQ, &tmQ, q_full, colQ, q_row0);
-      if (R > 0) tma_load_2d(smem + C::kQ + C::kQSlabA, &tmQR, q_full, colQ + 64, q_row0);
-      int issued = 0;
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j % ST;
-        const uint32_t eph = ((j / ST) & 1) ^ 1;
-        const int kv_row = img_row0 + j * KT;
-        if (*abort_flag || !mbar_wait(&k_empty[st], eph, 201)) {
-          *abort_flag = 1;
+      int nq = 0, nk = 0, nv = 0;  // Q, K and V loads issued by this CTA
+      bool ok = true;
+      for (int w = blockIdx.x; w < p.n_items && ok; w += gridDim.x) {
+        const int2 tile = p.tiles[w / H];
+        const int head = w - (w / H) * H;
+        const int img_row0 = __ldg(p.cu + tile.x);
+        const int L = __ldg(p.cu + tile.x + 1) - img_row0;
+        const int n_kv = (L + KT - 1) / KT;
+        const int colQ = head * HDP, colK = (H + head) * HDP, colV = (2 * H + head) * HDP;
+        const int qb = nq % QB;
+        if (*abort_flag || !mbar_wait(&q_empty[qb], ((nq / QB) & 1) ^ 1, 200)) {
+          ok = false;
           break;
         }
-        uint8_t* kb = smem + C::kK + st * C::kKTile;
-        mbar_arrive_expect_tx(&k_full[st], C::kKBytes);
-        tma_load_2d(kb, &tmK, &k_full[st], colK, kv_row);
-        if (R > 0) tma_load_2d(kb + C::kKSlabA, &tmKR, &k_full[st], colK + 64, kv_row);
-        if (*abort_flag || !mbar_wait(&v_empty[st], eph, 202)) {
-          *abort_flag = 1;
-          break;
+        uint8_t* qdst = smem + C::kQ + qb * C::kQTile;
+        mbar_arrive_expect_tx(&q_full[qb], C::kQBytes);
+        tma_load_2d(qdst, &tmQ, &q_full[qb], colQ, img_row0 + tile.y * 128);
+        if (R > 0) tma_load_2d(qdst + C::kQSlabA, &tmQR, &q_full[qb], colQ + 64, img_row0 + tile.y * 128);
+        ++nq;
+        for (int j = 0; j < n_kv; ++j) {
+          const int st = nk % ST;  // nk == nv here
+          const uint32_t eph = ((nk / ST) & 1) ^ 1;
+          const int kv_row = img_row0 + j * KT;
+          if (*abort_flag || !mbar_wait(&k_empty[st], eph, 201)) {
+            ok = false;
+            break;
+          }
+          uint8_t* kb = smem + C::kK + st * C::kKTile;
+          mbar_arrive_expect_tx(&k_full[st], C::kKBytes);
+          tma_load_2d(kb, &tmK, &k_full[st], colK, kv_row);
+          if (R > 0) tma_load_2d(kb + C::kKSlabA, &tmKR, &k_full[st], colK + 64, kv_row);
+          ++nk;
+          if (*abort_flag || !mbar_wait(&v_empty[st], eph, 202)) {
+            ok = false;
+            break;
+          }
+          uint8_t* vb = smem + C::kV + st * C::kKTile;
+          mbar_arrive_expect_tx(&v_full[st], C::kKBytes);
+          tma_load_2d(vb, &tmK, &v_full[st], colV, kv_row);
+          if (R > 0) tma_load_2d(vb + C::kKSlabA, &tmKR, &v_full[st], colV + 64, kv_row);
+          ++nv;
         }
-        uint8_t* vb = smem + C::kV + st * C::kKTile;
-        mbar_arrive_expect_tx(&v_full[st], C::kKBytes);
-        tma_load_2d(vb, &tmK, &v_full[st], colV, kv_row);
-        if (R > 0) tma_load_2d(vb + C::kKSlabA, &tmKR, &v_full[st], colV + 64, kv_row);
-        ++issued;
       }
-      // no TMA write may still be in flight when the CTA exits
-      mbar_wait(q_full, 0, 203);
-      for (int j = (issued > ST ? issued - ST : 0); j < issued; ++j) {
-        mbar_wait(&k_full[j % ST], (j / ST) & 1, 204);
-        mbar_wait(&v_full[j % ST], (j / ST) & 1, 205);
-      }
+      if (!ok) *abort_flag = 1;
+      // No TMA write may still be in flight when the CTA exits: a buffer is
+      // only reloaded after its previous load was consumed, so only the last
+      // load of each buffer can be outstanding.
+      for (int i = (nq > QB ? nq - QB : 0); i < nq; ++i) mbar_wait(&q_full[i % QB], (i / QB) & 1, 203);
+      for (int i = (nk > ST ? nk - ST : 0); i < nk; ++i) mbar_wait(&k_full[i % ST], (i / ST) & 1, 204);
+      for (int i = (nv > ST ? nv - ST : 0); i < nv; ++i) mbar_wait(&v_full[i % ST], (i / ST) & 1, 205);
     }
   } else if (warp == 1) {
     // --------------------------------------------------------------- MMA
     if (lane == 0) {
-      bool ok = mbar_wait(q_full, 0, 211);
-      const uint32_t qa = smem_u32(smem + C::kQ);
-      const uint32_t qr = qa + C::kQSlabA;
-      auto issue_pv = [&](int jj) -> bool {
-        const int st = jj % ST;
-        if (!mbar_wait(p_full, jj & 1, 214) || !mbar_wait(&v_full[st], (jj / ST) & 1, 215)) return false;
+      int kv = 0, g = 0, it = 0;  // K/V tiles, S tiles and items consumed
+      bool ok = true;
+      // O += P V for the K/V tile kvi, the S tile gi of item `item`; the
+      // item's first PV overwrites O once the previous item's O was read
+      auto issue_pv = [&](int kvi, int gi, bool first, int item) -> bool {
+        const int st = kvi % ST;
+        if (!mbar_wait(p_full, gi & 1, 214) || !mbar_wait(&v_full[st], (kvi / ST) & 1, 215)) return false;
+        if (first && item > 0 && !mbar_wait(o_free, (item - 1) & 1, 217)) return false;
         tc_fence_after();
         const uint32_t va = smem_u32(smem + C::kV + st * C::kKTile);
         const uint32_t vr = va + C::kKSlabA;
 #pragma unroll
         for (int s = 0; s < KT / 16; ++s) {  // 16 keys per MMA; P columns [kColP + 8s, +8)
-          const uint32_t acc = (jj > 0 || s > 0) ? 1u : 0u;
+          const uint32_t acc = (!first || s > 0) ? 1u : 0u;
           umma_ts(tmem + C::kColO, tmem + C::kColP + s * 8, mnmajor_desc(va + s * 16 * 128, 128, 0), kIdescO64, acc);
           if constexpr (R > 0)
             umma_ts(tmem + C::kColO + 64, tmem + C::kColP + s * 8, mnmajor_desc(vr + s * 16 * R * 2, R * 2, 0),
@@ -200,28 +229,45 @@ __global__ void __launch_bounds__(192, 2)
         umma_commit(&v_empty[st]);
         return true;
       };
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int st = j % ST;
-        // S_j overwrites S_{j-1}: the softmax must have read it
-        if (*abort_flag || !mbar_wait(&k_full[st], (j / ST) & 1, 212) ||
-            (j > 0 && !mbar_wait(s_free, (j - 1) & 1, 213))) {
+      for (int w = blockIdx.x; w < p.n_items && ok; w += gridDim.x, ++it) {
+        const int2 tile = p.tiles[w / H];
+        const int L = __ldg(p.cu + tile.x + 1) - __ldg(p.cu + tile.x);
+        const int n_kv = (L + KT - 1) / KT;
+        const int qb = it % QB;
+        if (*abort_flag || !mbar_wait(&q_full[qb], (it / QB) & 1, 211)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        const uint32_t ka = smem_u32(smem + C::kK + st * C::kKTile);
-        const uint32_t kr = ka + C::kKSlabA;
+        const uint32_t qa = smem_u32(smem + C::kQ + qb * C::kQTile);
+        const uint32_t qr = qa + C::kQSlabA;
+        for (int j = 0; j < n_kv; ++j, ++kv, ++g) {
+          const int st = kv % ST;
+          // S_g overwrites S_{g-1}: the softmax must have read it
+          if (*abort_flag || !mbar_wait(&k_full[st], (kv / ST) & 1, 212) ||
+              (g > 0 && !mbar_wait(s_free, (g - 1) & 1, 213))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t ka = smem_u32(smem + C::kK + st * C::kKTile);
+          const uint32_t kr = ka + C::kKSlabA;
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          umma_ss(tmem, kmajor_desc(qa + k * 32, 128), kmajor_desc(ka + k * 32, 128), kIdescS, k > 0);
+          for (int k = 0; k < 4; ++k)
+            umma_ss(tmem, kmajor_desc(qa + k * 32, 128), kmajor_desc(ka + k * 32, 128), kIdescS, k > 0);
 #pragma unroll
-        for (int k = 0; k < R / 16; ++k)
-          umma_ss(tmem, kmajor_desc(qr + k * 32, R * 2), kmajor_desc(kr + k * 32, R * 2), kIdescS, 1);
-        umma_commit(s_full);
-        umma_commit(&k_empty[st]);
-        if (j > 0 && !issue_pv(j - 1)) ok = false;
+          for (int k = 0; k < R / 16; ++k)
+            umma_ss(tmem, kmajor_desc(qr + k * 32, R * 2), kmajor_desc(kr + k * 32, R * 2), kIdescS, 1);
+          umma_commit(s_full);
+          umma_commit(&k_empty[st]);
+          if (j > 0 && !issue_pv(kv - 1, g - 1, j == 1, it)) {
+            ok = false;
+            break;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&q_empty[qb]);  // every QK^T of this item issued: Q is free once they finish
+        if (!issue_pv(kv - 1, g - 1, n_kv == 1, it)) ok = false;
       }
-      if (ok && n_kv > 0 && !issue_pv(n_kv - 1)) ok = false;
       if (!ok) *abort_flag = 1;
       umma_commit(mdone);
       mbar_wait(mdone, 0, 216);
@@ -232,90 +278,101 @@ __global__ void __launch_bounds__(192, 2)
     const int r = q * 32 + lane;  // query row within the tile
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const float sc = p.scale_log2;
-    float m_use = 0.f, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      if (*abort_flag || !mbar_wait(s_full, j & 1, 221)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      float s[KT];
-#pragma unroll
-      for (int c = 0; c < KT / 16; c += 2) {
-        uint32_t u[16], u2[16];
-        SG_TMEM_LD_16(tmem + c * 16 + lane_off, u);
-        SG_TMEM_LD_16(tmem + (c + 1) * 16 + lane_off, u2);
-        tmem_ld_wait();
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          s[c * 16 + k] = __uint_as_float(u[k]);
-          s[(c + 1) * 16 + k] = __uint_as_float(u2[k]);
-        }
-      }
-      // S_j is in registers: let the MMA warp compute S_{j+1}
-      tc_fence_before();
-      mbar_arrive(s_free);
-      const int valid = L - j * KT;  // keys of this image in the tile (>= 1)
-      if (valid < KT) {
-#pragma unroll
-        for (int k = 0; k < KT; ++k)
-          if (k >= valid) s[k] = -INFINITY;
-      }
-      float mx[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mx[i] = s[i];
-#pragma unroll
-      for (int k = 8; k < KT; ++k) mx[k & 7] = fmaxf(mx[k & 7], s[k]);
-      float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-      mt *= sc;
-      float alpha = 1.f;
-      if (j == 0) {
-        m_use = mt;
-      } else if (mt > m_use + 8.f) {
-        alpha = ex2_approx(m_use - mt);
-        m_use = mt;
-      }
-      float ps[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) ps[i] = 0.f;
-      uint32_t w[KT / 2];
-#pragma unroll
-      for (int k = 0; k < KT / 2; ++k) {
-        const float p0 = ex2_approx(fmaf(s[2 * k], sc, -m_use));
-        const float p1 = ex2_approx(fmaf(s[2 * k + 1], sc, -m_use));
-        ps[k & 7] += p0 + p1;
-        w[k] = Pack2<T>::pack(p0, p1);
-      }
-      l = l * alpha + (((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7])));
-      if (j > 0) {
-        // PV_{j-1} must be done: P's columns are rewritten and O may be rescaled
-        if (!mbar_wait(pv_done, (j - 1) & 1, 222)) {
+    int g = 0;  // S tiles consumed
+    for (int w = blockIdx.x; w < p.n_items && ok; w += gridDim.x) {
+      const int2 tile = p.tiles[w / H];
+      const int head = w - (w / H) * H;
+      const int img_row0 = __ldg(p.cu + tile.x);
+      const int L = __ldg(p.cu + tile.x + 1) - img_row0;
+      const int n_kv = (L + KT - 1) / KT;
+      float m_use = 0.f, l = 0.f;
+      for (int j = 0; j < n_kv; ++j, ++g) {
+        if (*abort_flag || !mbar_wait(s_full, g & 1, 221)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
-          uint32_t u[16];
+        float s[KT];
 #pragma unroll
-          for (int c = 0; c < HDP / 16; ++c) {
-            SG_TMEM_LD_16(tmem + C::kColO + c * 16 + lane_off, u);
-            tmem_ld_wait();
+        for (int c = 0; c < KT / 16; c += 2) {
+          uint32_t u[16], u2[16];
+          SG_TMEM_LD_16(tmem + c * 16 + lane_off, u);
+          SG_TMEM_LD_16(tmem + (c + 1) * 16 + lane_off, u2);
+          tmem_ld_wait();
 #pragma unroll
-            for (int k = 0; k < 16; ++k) u[k] = __float_as_uint(__uint_as_float(u[k]) * alpha);
-            SG_TMEM_ST_16(tmem + C::kColO + c * 16 + lane_off, u);
+          for (int k = 0; k < 16; ++k) {
+            s[c * 16 + k] = __uint_as_float(u[k]);
+            s[(c + 1) * 16 + k] = __uint_as_float(u2[k]);
           }
         }
-      }
+        // S is in registers: let the MMA warp compute the next S
+        tc_fence_before();
+        mbar_arrive(s_free);
+        const int valid = L - j * KT;  // keys of this image in the tile (>= 1)
+        if (valid < KT) {
 #pragma unroll
-      for (int c = 0; c < KT / 16; ++c) SG_TMEM_ST_8(tmem + C::kColP + c * 8 + lane_off, (w + c * 8));
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(p_full);
-    }
-    if (ok && n_kv > 0 && mbar_wait(pv_done, (n_kv - 1) & 1, 223)) {
+          for (int k = 0; k < KT; ++k)
+            if (k >= valid) s[k] = -INFINITY;
+        }
+        float mx[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx[i] = s[i];
+#pragma unroll
+        for (int k = 8; k < KT; ++k) mx[k & 7] = fmaxf(mx[k & 7], s[k]);
+        float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+        mt *= sc;
+        float alpha = 1.f;
+        if (j == 0) {
+          m_use = mt;
+        } else if (mt > m_use + 8.f) {
+          alpha = ex2_approx(m_use - mt);
+          m_use = mt;
+        }
+        float ps[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ps[i] = 0.f;
+        uint32_t wv[KT / 2];
+#pragma unroll
+        for (int k = 0; k < KT / 2; ++k) {
+          const float p0 = ex2_approx(fmaf(s[2 * k], sc, -m_use));
+          const float p1 = ex2_approx(fmaf(s[2 * k + 1], sc, -m_use));
+          ps[k & 7] += p0 + p1;
+          wv[k] = Pack2<T>::pack(p0, p1);
+        }
+        l = l * alpha + (((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7])));
+        if (j > 0) {
+          // the previous PV must be done: P's columns are rewritten and O may be rescaled
+          // (at j == 0 the previous item's last PV was waited for before its O was read)
+          if (!mbar_wait(pv_done, (g - 1) & 1, 222)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (__any_sync(0xffffffffu, alpha != 1.f)) {
+            uint32_t u[16];
+#pragma unroll
+            for (int c = 0; c < HDP / 16; ++c) {
+              SG_TMEM_LD_16(tmem + C::kColO + c * 16 + lane_off, u);
+              tmem_ld_wait();
+#pragma unroll
+              for (int k = 0; k < 16; ++k) u[k] = __float_as_uint(__uint_as_float(u[k]) * alpha);
+              SG_TMEM_ST_16(tmem + C::kColO + c * 16 + lane_off, u);
+            }
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < KT / 16; ++c) SG_TMEM_ST_8(tmem + C::kColP + c * 8 + lane_off, (wv + c * 8));
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(p_full);
+      }
+      if (!ok || !mbar_wait(pv_done, (g - 1) & 1, 223)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
-      const int row = q_row0 + r;
+      const int row = img_row0 + tile.y * 128 + r;
       const bool row_ok = (tile.y * 128 + r) < L;
       const float inv_l = 1.f / l;
       T* orow = reinterpret_cast<T*>(p.out) + static_cast<size_t>(row) * p.ld_out + head * p.head_dim;
@@ -326,22 +383,24 @@ __global__ void __launch_bounds__(192, 2)
         tmem_ld_wait();
         if (row_ok) {
 #pragma unroll
-          for (int g = 0; g < 2; ++g) {
-            const int d0 = c * 16 + g * 8;
+          for (int gg = 0; gg < 2; ++gg) {
+            const int d0 = c * 16 + gg * 8;
             if (d0 < p.head_dim) {  // head_dim is a multiple of 8
               uint4 o;
-              o.x = Pack2<T>::pack(__uint_as_float(u[g * 8 + 0]) * inv_l, __uint_as_float(u[g * 8 + 1]) * inv_l);
-              o.y = Pack2<T>::pack(__uint_as_float(u[g * 8 + 2]) * inv_l, __uint_as_float(u[g * 8 + 3]) * inv_l);
-              o.z = Pack2<T>::pack(__uint_as_float(u[g * 8 + 4]) * inv_l, __uint_as_float(u[g * 8 + 5]) * inv_l);
-              o.w = Pack2<T>::pack(__uint_as_float(u[g * 8 + 6]) * inv_l, __uint_as_float(u[g * 8 + 7]) * inv_l);
+              o.x = Pack2<T>::pack(__uint_as_float(u[gg * 8 + 0]) * inv_l, __uint_as_float(u[gg * 8 + 1]) * inv_l);
+              o.y = Pack2<T>::pack(__uint_as_float(u[gg * 8 + 2]) * inv_l, __uint_as_float(u[gg * 8 + 3]) * inv_l);
+              o.z = Pack2<T>::pack(__uint_as_float(u[gg * 8 + 4]) * inv_l, __uint_as_float(u[gg * 8 + 5]) * inv_l);
+              o.w = Pack2<T>::pack(__uint_as_float(u[gg * 8 + 6]) * inv_l, __uint_as_float(u[gg * 8 + 7]) * inv_l);
               *reinterpret_cast<uint4*>(orow + d0) = o;
             }
           }
         }
       }
-    } else if (!ok) {
-      *abort_flag = 1;
+      // O is in registers: the next item's first PV may overwrite it
+      tc_fence_before();
+      mbar_arrive(o_free);
     }
+    if (!ok) *abort_flag = 1;
   }
 
   tc_fence_before();

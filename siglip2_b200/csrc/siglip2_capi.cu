@@ -314,6 +314,7 @@ int launch_fmha(const void* qkv, int N, const int* cu, const int2* tiles, int n_
   FmhaParams p;
   p.cu = cu;
   p.tiles = tiles;
+  p.n_items = n_tiles * H;
   p.heads = H;
   p.head_dim = hd;
   p.out = out;
@@ -326,7 +327,8 @@ int launch_fmha(const void* qkv, int N, const int* cu, const int2* tiles, int n_
     SG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     attr_done = true;
   }
-  dim3 grid(n_tiles, H);
+  // persistent: two CTAs per SM walk the (query tile, head) items
+  const int grid = std::min(p.n_items, 2 * sm_count());
   kern<<<grid, 192, smem, s>>>(tq, tqr, tk, tkr, p);
   SG_LAUNCH_CHECK();
   return SIGLIP2_OK;
@@ -350,7 +352,8 @@ int sg_fmha_impl(int dtype, const void* qkv, int N, const int* cu, const int* ti
   SG_CHECK_ARG(qkv && cu && tiles && out && N >= 0 && n_tiles >= 0 && H > 0 && hd > 0, "bad attention arguments");
   SG_CHECK_ARG(hd % 8 == 0 && ldo % 8 == 0 && ldo >= H * hd, "head_dim and ldo must be multiples of 8");
   if (N == 0 || n_tiles == 0) return SIGLIP2_OK;
-  if (H > 65535) return set_error(SIGLIP2_ERR_UNSUPPORTED, "too many heads");
+  if (H > 65535 || static_cast<long long>(n_tiles) * H > (1ll << 30))
+    return set_error(SIGLIP2_ERR_UNSUPPORTED, "too many heads or attention tiles");
   if (!aligned16(out)) return set_error(SIGLIP2_ERR_ALIGN, "attention output must be 16-byte aligned");
   if (reinterpret_cast<uintptr_t>(tiles) & 7u)
     return set_error(SIGLIP2_ERR_ALIGN, "attention tile list must be 8-byte aligned (read as int32 pairs)");
