@@ -160,10 +160,10 @@ int siglip2_token_image(const int* cu_seqlens_dev, int B, int N, int* tok_img_de
 int siglip2_posemb(int dtype, const float* table_dev, int grid, int D, const int* tok_img_dev, const int* hw_dev,
                    const int* cu_seqlens_dev, int N, void* out_dev, void* stream);
 
-/* Per-image attention over the packed sequence.  qkv_dev: [N, 3*heads*HDP]
- * with HDP = siglip2_padded_head_dim(head_dim); column (w*heads + h)*HDP + d
- * holds q (w=0), k (w=1), v (w=2) of head h, dim d, and columns
- * d >= head_dim must be zero.  tiles_dev: n_tiles (image, query_tile) int32
+/* Per-image attention over the packed sequence.  qkv_dev: [N, 3*heads*head_dim],
+ * column (w*heads + h)*head_dim + d holds q (w=0), k (w=1), v (w=2) of head
+ * h, dim d (the fused qkv_proj output of model_optimized.py); row pitch
+ * 3*heads*head_dim, base 16-byte aligned.  tiles_dev: n_tiles (image, query_tile) int32
  * pairs covering ceil(L_b / 128) query tiles of every image.  out_dev:
  * [N, ldo] receives softmax(q k^T / sqrt(head_dim)) v per head at columns
  * h*head_dim ...  Replaces flex_attention with the document mask,
@@ -171,7 +171,8 @@ int siglip2_posemb(int dtype, const float* table_dev, int grid, int D, const int
 int siglip2_fmha_varlen(int dtype, const void* qkv_dev, int N, const int* cu_seqlens_dev, const int* tiles_dev,
                         int n_tiles, int heads, int head_dim, void* out_dev, int ldo, void* stream);
 
-/* Head dimension as stored in the QKV buffer (64 -> 64, 72 -> 80, 96 -> 96). */
+/* Head dimension of the attention kernel's tiles (64 -> 64, 72 -> 80,
+ * 96 -> 96); the padding exists only in shared memory and TMEM. */
 int siglip2_padded_head_dim(int head_dim);
 
 /* Attention pooling of the MAP head, first half: for every image b and head h
@@ -223,9 +224,9 @@ typedef struct {
 } siglip2_config;
 
 /* Device pointers of one encoder layer, pre-packed by the host layer:
- *  qkv_w  [3*H*HDP, D]: rows (w*H + h)*HDP + d = (W_w * ln1.gamma)[h*hd + d]
- *         for d < head_dim, zero rows for the padding d >= head_dim;
- *  qkv_c1 = row sums of qkv_w, qkv_c2 = b + W . ln1.beta (zero in padding);
+ *  qkv_w  [3*D, D]: rows w*D + n = (W_w * ln1.gamma)[n] for w = q, k, v
+ *         (the fused qkv_proj layout);
+ *  qkv_c1 = row sums of qkv_w, qkv_c2 = b + W . ln1.beta;
  *  fc1_w = W1 * ln2.gamma, fc1_c1 / fc1_c2 likewise;
  *  out_w / fc2_w as in the reference, biases float32. */
 typedef struct {

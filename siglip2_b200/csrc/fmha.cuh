@@ -2,12 +2,13 @@
 // sequence: every query row attends only to the keys of its own image, i.e.
 // the block-diagonal document mask of the reference, with no padded rows.
 //
-// Input: the QKV projection output [N, 3*H*HDP] in the head-padded layout the
-// QKV GEMM writes: column (which*H + h)*HDP + d holds q/k/v[which] of head h,
-// dim d; columns d >= head_dim are exact zeros (zero weight rows), so padding
-// the head dimension to HDP changes no dot product.  HDP = 64 | 80 | 96
-// (head_dim 64 | 72 | 96), split into a 64-wide slab (128B swizzle) plus an
-// R = HDP-64 wide slab (32B / 64B swizzle).
+// Input: the QKV projection output [N, 3*H*hd], q | k | v with the heads of
+// each in order (the reference's fused qkv_proj layout).  Each head is read
+// through a 3-D tensor map [N][3H][hd] as a 64-wide slab (128B swizzle) plus
+// an R = HDP-64 wide slab (32B / 64B swizzle), HDP = 64 | 80 | 96 for
+// head_dim 64 | 72 | 96; the columns of the R slab past head_dim are
+// out-of-bounds reads and arrive as zeros, so padding the head dimension
+// changes no dot product and costs no HBM bytes.
 //
 // Persistent: two CTAs per SM (256 TMEM columns and <= 104 KB of shared
 // memory each) walk the work items (128-query tile of one image, head) of
@@ -160,7 +161,6 @@ __global__ void __launch_bounds__(192, 2)
         const int img_row0 = __ldg(p.cu + tile.x);
         const int L = __ldg(p.cu + tile.x + 1) - img_row0;
         const int n_kv = (L + KT - 1) / KT;
-        const int colQ = head * HDP, colK = (H + head) * HDP, colV = (2 * H + head) * HDP;
         const int qb = nq % QB;
         if (*abort_flag || !mbar_wait(&q_empty[qb], ((nq / QB) & 1) ^ 1, 200)) {
           ok = false;
@@ -168,8 +168,8 @@ __global__ void __launch_bounds__(192, 2)
         }
         uint8_t* qdst = smem + C::kQ + qb * C::kQTile;
         mbar_arrive_expect_tx(&q_full[qb], C::kQBytes);
-        tma_load_2d(qdst, &tmQ, &q_full[qb], colQ, img_row0 + tile.y * 128);
-        if (R > 0) tma_load_2d(qdst + C::kQSlabA, &tmQR, &q_full[qb], colQ + 64, img_row0 + tile.y * 128);
+        tma_load_3d(qdst, &tmQ, &q_full[qb], 0, head, img_row0 + tile.y * 128);
+        if (R > 0) tma_load_3d(qdst + C::kQSlabA, &tmQR, &q_full[qb], 64, head, img_row0 + tile.y * 128);
         ++nq;
         for (int j = 0; j < n_kv; ++j) {
           const int st = nk % ST;  // nk == nv here
@@ -181,8 +181,8 @@ __global__ void __launch_bounds__(192, 2)
           }
           uint8_t* kb = smem + C::kK + st * C::kKTile;
           mbar_arrive_expect_tx(&k_full[st], C::kKBytes);
-          tma_load_2d(kb, &tmK, &k_full[st], colK, kv_row);
-          if (R > 0) tma_load_2d(kb + C::kKSlabA, &tmKR, &k_full[st], colK + 64, kv_row);
+          tma_load_3d(kb, &tmK, &k_full[st], 0, H + head, kv_row);
+          if (R > 0) tma_load_3d(kb + C::kKSlabA, &tmKR, &k_full[st], 64, H + head, kv_row);
           ++nk;
           if (*abort_flag || !mbar_wait(&v_empty[st], eph, 202)) {
             ok = false;
@@ -190,8 +190,8 @@ __global__ void __launch_bounds__(192, 2)
           }
           uint8_t* vb = smem + C::kV + st * C::kKTile;
           mbar_arrive_expect_tx(&v_full[st], C::kKBytes);
-          tma_load_2d(vb, &tmK, &v_full[st], colV, kv_row);
-          if (R > 0) tma_load_2d(vb + C::kKSlabA, &tmKR, &v_full[st], colV + 64, kv_row);
+          tma_load_3d(vb, &tmK, &v_full[st], 0, 2 * H + head, kv_row);
+          if (R > 0) tma_load_3d(vb + C::kKSlabA, &tmKR, &v_full[st], 64, 2 * H + head, kv_row);
           ++nv;
         }
       }

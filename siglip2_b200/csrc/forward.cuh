@@ -56,7 +56,7 @@ inline int meta_counts(const int* hw_host, int B, int* n_tokens, int* n_tiles) {
 struct FwdBuffers {
   int* tok_img;
   void* x;       // [N, D] residual stream
-  void* qkv;     // [N, 3 H HDP]
+  void* qkv;     // [N, 3 H hd]  q | k | v
   void* attn;    // [N, D]
   void* hmid;    // [N, I]   (also the packed patch rows when the input is padded)
   float* scores; // [N, H]
@@ -71,12 +71,11 @@ struct FwdBuffers {
 inline size_t forward_workspace(const siglip2_config* c, int B, int N, FwdBuffers* out, uint8_t* base) {
   const size_t e = elem_bytes(c->dtype);
   const int D = c->hidden, I = c->intermediate, H = c->heads;
-  const int hdp = c->dtype == SIGLIP2_F32 ? c->head_dim : padded_head_dim(c->head_dim);
   Ws w{base, 0, 0};
   FwdBuffers f;
   f.tok_img = w.take<int>(sizeof(int) * (N + 1));
   f.x = w.take<uint8_t>(e * N * D);
-  f.qkv = w.take<uint8_t>(e * N * 3 * H * hdp);
+  f.qkv = w.take<uint8_t>(e * N * 3 * H * c->head_dim);
   f.attn = w.take<uint8_t>(e * N * D);
   const size_t mid = std::max<size_t>(static_cast<size_t>(I), static_cast<size_t>(c->patch_dim));
   f.hmid = w.take<uint8_t>(e * N * mid);

@@ -87,8 +87,13 @@ constexpr int kGemmThreads = 320;  // 10 warps: producer, MMA, 8 epilogue (or 4 
 __host__ __device__ constexpr int epi_warps(int e) { return epi_has_stat_warps(e) ? 4 : 8; }
 
 // Tile width of the tensor-core GEMM for an output width N: 192 when it
-// divides N exactly and 256 does not (768 is 256-wide; 1152 is 192-wide).
-__host__ __device__ constexpr int gemm_bn_for(int N) { return (N % 192 == 0 && N % 256 != 0) ? 192 : 256; }
+// divides N and 256-wide tiles would waste more than 8% of the columns
+// (1152 -> 192; 768, 1536, 3456, 4304 -> 256).  256-wide tiles move fewer
+// operand bytes per FLOP, so they win whenever their tail waste is small.
+__host__ __device__ constexpr int gemm_bn_for(int N) {
+  return (N % 192 == 0 && static_cast<long long>((N + 255) / 256) * 256 * 100 > static_cast<long long>(N) * 108) ? 192
+                                                                                                                 : 256;
+}
 // Column block of one row-sum slot: the columns one epilogue warp drains of
 // a row-sum-producing tile (half the tile), or the SIMT fp32 tile width.
 __host__ __device__ constexpr int rowsum_block(bool f32, int N) { return f32 ? 128 : gemm_bn_for(N) / 2; }

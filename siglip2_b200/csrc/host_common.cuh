@@ -114,6 +114,30 @@ inline int make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, int6
   return SIGLIP2_OK;
 }
 
+// 3-D view [d2][d1][d0] (d0 contiguous) with byte strides for d1 and d2.
+// Box elements past d0 (or any other extent) are read as zeros.
+inline int make_tmap_3d(CUtensorMap* map, const void* base, int elem_bytes, int64_t d0, int64_t d1, int64_t d2,
+                        int64_t stride1_bytes, int64_t stride2_bytes, int box0, int box1, int box2) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (!fn) return set_error(SIGLIP2_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  if (!aligned16(base)) return set_error(SIGLIP2_ERR_ALIGN, "TMA base address %p is not 16-byte aligned", base);
+  if (stride1_bytes % 16 != 0 || stride2_bytes % 16 != 0)
+    return set_error(SIGLIP2_ERR_ALIGN, "TMA strides %lld / %lld bytes are not multiples of 16", (long long)stride1_bytes,
+                     (long long)stride2_bytes);
+  const CUtensorMapDataType dt = elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(d0), static_cast<cuuint64_t>(d1), static_cast<cuuint64_t>(d2)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(stride1_bytes), static_cast<cuuint64_t>(stride2_bytes)};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(box0), static_cast<cuuint32_t>(box1), static_cast<cuuint32_t>(box2)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle_for_bytes(box0 * elem_bytes), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(SIGLIP2_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (%d) dims=%lldx%lldx%lld box=%dx%dx%d", (int)r,
+                     (long long)d0, (long long)d1, (long long)d2, box0, box1, box2);
+  return SIGLIP2_OK;
+}
+
 inline int sm_count() {
   static int n = 0;
   static std::once_flag once;

@@ -301,12 +301,15 @@ int launch_fmha(const void* qkv, int N, const int* cu, const int2* tiles, int n_
                 cudaStream_t s) {
   using C = FmhaCfg<HDP>;
   CUtensorMap tq, tqr, tk, tkr;
-  const int ldq = 3 * H * HDP;
-  SG_TRY(make_tmap_2d(&tq, qkv, 2, N, ldq, ldq, 128, 64));
-  SG_TRY(make_tmap_2d(&tk, qkv, 2, N, ldq, ldq, C::KT, 64));
+  // 3-D view [N][3H][hd] of the packed q | k | v columns: the remainder box
+  // (columns 64 .. HDP of a head) reads zeros past hd, so head_dim 72 is
+  // padded to the 80-wide tile in shared memory, not in HBM
+  const int64_t row_bytes = 3ll * H * hd * 2;
+  SG_TRY(make_tmap_3d(&tq, qkv, 2, hd, 3 * H, N, hd * 2, row_bytes, 64, 1, 128));
+  SG_TRY(make_tmap_3d(&tk, qkv, 2, hd, 3 * H, N, hd * 2, row_bytes, 64, 1, C::KT));
   if (HDP > 64) {
-    SG_TRY(make_tmap_2d(&tqr, qkv, 2, N, ldq, ldq, 128, HDP - 64));
-    SG_TRY(make_tmap_2d(&tkr, qkv, 2, N, ldq, ldq, C::KT, HDP - 64));
+    SG_TRY(make_tmap_3d(&tqr, qkv, 2, hd, 3 * H, N, hd * 2, row_bytes, HDP - 64, 1, 128));
+    SG_TRY(make_tmap_3d(&tkr, qkv, 2, hd, 3 * H, N, hd * 2, row_bytes, HDP - 64, 1, C::KT));
   } else {
     tqr = tq;
     tkr = tk;
@@ -504,8 +507,7 @@ int sg_forward_impl(const siglip2_config* c, const siglip2_weights* w, const voi
   const int* tiles = meta + meta_tiles_offset(B);
   const int dt = c->dtype;
   const int D = c->hidden, I = c->intermediate, H = c->heads, hd = c->head_dim;
-  const int hdp = dt == SIGLIP2_F32 ? hd : padded_head_dim(hd);  // fp32 attention reads unpadded heads
-  const int nqkv = 3 * H * hdp;
+  const int nqkv = 3 * H * hd;  // q | k | v, heads of head_dim columns (unpadded)
 
   // Row sums of the residual stream for the LayerNorm-folded GEMMs, in
   // slots written by the GEMM that writes x: two buffers alternate (x after

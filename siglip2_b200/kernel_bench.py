@@ -86,10 +86,7 @@ def bench_fmha(preset, images, max_patches, reps, dtype=torch.bfloat16, warmup=3
     shapes = _shapes(preset, images, max_patches)
     lens = (shapes[:, 0] * shapes[:, 1]).tolist()
     N = sum(lens)
-    hdp = ops.padded_head_dim(hd)
-    qkv = torch.randn(N, 3, H, hdp, device="cuda").to(dtype)
-    qkv[..., hd:] = 0
-    qkv = qkv.view(N, -1)
+    qkv = torch.randn(N, 3 * H * hd, device="cuda").to(dtype)  # q | k | v
     cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0).tolist()), dtype=torch.int32, device="cuda")
     tiles = ops.attention_tiles(lens).cuda()
     out = torch.empty(N, D, device="cuda", dtype=dtype)
@@ -101,11 +98,10 @@ def bench_fmha(preset, images, max_patches, reps, dtype=torch.bfloat16, warmup=3
 
 def bench_layer(preset, images, max_patches, reps):
     D, I, _, H = W.PRESETS[preset]
-    hdp = ops.padded_head_dim(D // H)
     N = int((lambda s: (s[:, 0] * s[:, 1]).sum())(_shapes(preset, images, max_patches)))
     out = []
     # the epilogues the forward uses
-    for name, n, k, epi in (("qkv", 3 * H * hdp, D, "lnrs"), ("out", D, D, "bias_res_rs"), ("fc1", I, D, "lnrs_gelu"),
+    for name, n, k, epi in (("qkv", 3 * D, D, "lnrs"), ("out", D, D, "bias_res_rs"), ("fc1", I, D, "lnrs_gelu"),
                             ("fc2", D, I, "bias_res_rs")):
         r = bench_gemm(N, n, k, epi, reps)
         r["name"] = name

@@ -33,7 +33,7 @@ import torch
 import torch.nn as nn
 
 from . import _lib as L
-from .ops import dtype_code, fold_layernorm, padded_head_dim
+from .ops import dtype_code, fold_layernorm
 
 
 @dataclass
@@ -163,7 +163,6 @@ class _Packed:
             raise RuntimeError("siglip2_b200 runs on CUDA only: move the model with .to('cuda') first")
         D, I, H = cfg.hidden_size, cfg.intermediate_size, cfg.num_attention_heads
         hd = D // H
-        hdp = padded_head_dim(hd) if dt != torch.float32 else hd
         f32 = torch.float32
         keep = []
 
@@ -181,13 +180,10 @@ class _Packed:
             layers = (L.LayerWeights * max(1, cfg.num_hidden_layers))()
             for i, lyr in enumerate(model.encoder.layers):
                 at = lyr.self_attn
-                wp = torch.zeros(3, H, hdp, D, device=dev, dtype=f32)
-                bp = torch.zeros(3, H, hdp, device=dev, dtype=f32)
-                for w_i, lin in enumerate((at.q_proj, at.k_proj, at.v_proj)):
-                    wp[w_i, :, :hd] = lin.weight.float().view(H, hd, D)
-                    bp[w_i, :, :hd] = lin.bias.float().view(H, hd)
-                wg, c1, c2 = fold_layernorm(wp.view(3 * H * hdp, D), bp.view(-1), lyr.layer_norm1.weight,
-                                            lyr.layer_norm1.bias, dt)
+                # q | k | v rows (the fused qkv_proj layout of model_optimized.py), LN1 folded in
+                wp = torch.cat([lin.weight.float() for lin in (at.q_proj, at.k_proj, at.v_proj)], 0)
+                bp = torch.cat([lin.bias.float() for lin in (at.q_proj, at.k_proj, at.v_proj)], 0)
+                wg, c1, c2 = fold_layernorm(wp, bp, lyr.layer_norm1.weight, lyr.layer_norm1.bias, dt)
                 f1, f1c1, f1c2 = fold_layernorm(lyr.mlp.fc1.weight, lyr.mlp.fc1.bias, lyr.layer_norm2.weight,
                                                 lyr.layer_norm2.bias, dt)
                 layers[i] = L.LayerWeights(

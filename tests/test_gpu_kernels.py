@@ -17,12 +17,9 @@ def _cu(lens):
     return torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32, device="cuda")
 
 
-def _pack_qkv(q, k, v, H, hd, hdp):
-    N = q.shape[0]
-    buf = torch.zeros(N, 3, H, hdp, dtype=q.dtype, device=q.device)
-    for w, t in enumerate((q, k, v)):
-        buf[:, w, :, :hd] = t.view(N, H, hd)
-    return buf.view(N, 3 * H * hdp)
+def _pack_qkv(q, k, v):
+    """q | k | v columns, as the fused QKV projection writes them."""
+    return torch.cat([q, k, v], 1).contiguous()
 
 
 def _ref_attn(q, k, v, lens, H, hd):
@@ -46,8 +43,7 @@ def test_fmha_varlen(dtype, H, hd, lens):
     g = torch.Generator(device="cuda").manual_seed(sum(lens) + hd)
     N = sum(lens)
     q, k, v = (torch.randn(N, H * hd, device="cuda", generator=g).to(dtype) for _ in range(3))
-    hdp = ops.padded_head_dim(hd)
-    qkv = _pack_qkv(q, k, v, H, hd, hdp)
+    qkv = _pack_qkv(q, k, v)
     cu = _cu(lens)
     tiles = ops.attention_tiles(lens).cuda()
     out = ops.fmha_varlen(qkv, cu, tiles, H, hd)
@@ -69,7 +65,7 @@ def test_fmha_many_items_per_cta(H, hd):
     N = sum(lens)
     gd = torch.Generator(device="cuda").manual_seed(hd + 1)
     q, k, v = (torch.randn(N, H * hd, device="cuda", generator=gd).bfloat16() for _ in range(3))
-    qkv = _pack_qkv(q, k, v, H, hd, ops.padded_head_dim(hd))
+    qkv = _pack_qkv(q, k, v)
     tiles = ops.attention_tiles(lens).cuda()
     assert tiles.shape[0] * H > 8 * 296
     out = ops.fmha_varlen(qkv, _cu(lens), tiles, H, hd)
