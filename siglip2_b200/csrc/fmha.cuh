@@ -139,9 +139,11 @@ __global__ void __launch_bounds__(192, 2)
     tmem_alloc(tmem_holder, C::kTmemCols);
     tmem_relinquish();
   }
+  pdl_launch_dependents();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();  // the QKV projection is complete and visible from here on
   const uint32_t tmem = *tmem_holder;
 
   if (warp == 0) {

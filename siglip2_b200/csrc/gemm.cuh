@@ -532,9 +532,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tmem_alloc(tmem_holder, Cfg::kTmemCols);
     tmem_relinquish();
   }
+  pdl_launch_dependents();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();  // the previous kernel's outputs are complete and visible from here on
   const uint32_t tmem_base = *tmem_holder;
 
   if (warp == 0) {
@@ -757,9 +759,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tmem_alloc_pair(tmem_holder, Cfg::kTmemCols);
     tmem_relinquish_pair();
   }
+  pdl_launch_dependents();
   tc_fence_before();
   cluster_sync();  // both CTAs' barriers initialised before any remote signal
   tc_fence_after();
+  pdl_wait();  // the previous kernel's outputs are complete and visible from here on
   const uint32_t tmem_base = *tmem_holder;
 
   if (warp == 0) {

@@ -126,6 +126,15 @@ __global__ void selftest_wait_timeout_kernel(unsigned long long limit_ns, int si
 }
 
 // ----------------------------------------------------------------------------
+// programmatic dependent launch: a kernel lets the next kernel of the stream
+// be scheduled as soon as it starts (its CTAs then occupy SMs as this grid
+// drains and run their prologue), and waits for the previous grid to finish
+// and flush before it touches global memory
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// ----------------------------------------------------------------------------
 // fences
 // ----------------------------------------------------------------------------
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -27,6 +27,14 @@ struct GemmIO {
   int ldr;
 };
 
+// Programmatic dependent launch for the persistent GEMM / attention kernels:
+// each may be scheduled while the previous kernel of the stream drains; the
+// kernel itself waits (griddepcontrol.wait) before touching global memory.
+inline void set_pdl_attr(cudaLaunchAttribute* a) {
+  a->id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  a->val.programmaticStreamSerializationAllowed = 1;
+}
+
 template <typename T, int BN, int EPI, int SUB>
 int launch_gemm_tc(const GemmIO& io, const GemmParams& p, cudaStream_t stream) {
   CUtensorMap ta, tb, to, tr;
@@ -45,7 +53,16 @@ int launch_gemm_tc(const GemmIO& io, const GemmParams& p, cudaStream_t stream) {
   }
   const int tiles = ((p.M + kGemmBM - 1) / kGemmBM) * ((p.N + BN - 1) / BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kern<<<grid, threads, smem, stream>>>(ta, tb, to, tr, p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  set_pdl_attr(&attr[0]);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  SG_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, to, tr, p));
   SG_LAUNCH_CHECK();
   return SIGLIP2_OK;
 }
@@ -74,13 +91,14 @@ int launch_gemm_tc2(const GemmIO& io, const GemmParams& p, cudaStream_t stream) 
   cfg.blockDim = dim3(threads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  set_pdl_attr(&attr[1]);
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   SG_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, to, tr, p));
   SG_LAUNCH_CHECK();
   return SIGLIP2_OK;
@@ -332,7 +350,16 @@ int launch_fmha(const void* qkv, int N, const int* cu, const int2* tiles, int n_
   }
   // persistent: two CTAs per SM walk the (query tile, head) items
   const int grid = std::min(p.n_items, 2 * sm_count());
-  kern<<<grid, 192, smem, s>>>(tq, tqr, tk, tkr, p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  set_pdl_attr(&attr[0]);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  SG_CUDA(cudaLaunchKernelEx(&cfg, kern, tq, tqr, tk, tkr, p));
   SG_LAUNCH_CHECK();
   return SIGLIP2_OK;
 }
