@@ -62,15 +62,20 @@ struct FmhaCfg {
   static constexpr int kKSlabA = KT * 64 * 2;         // K / V: 96 rows (12 KB, a multiple of 1 KB)
   static constexpr int kKSlabR = KT * R * 2;
   static constexpr int kKTile = kKSlabA + (kKSlabR + 1023) / 1024 * 1024;
-  static constexpr int kStages = 2;
-  // Q double-buffered (the next item's Q lands while this one runs) where
-  // two CTAs still fit in an SM's shared memory
-  static constexpr int kQBufs = 2 * (2 * kQTile + 2 * kStages * kKTile + 2304) <= 226 * 1024 ? 2 : 1;
+  // Two CTAs share an SM's 228 KB (1 KB reserved per CTA).  Deeper K/V rings
+  // come first (K_{j+1} then loads two tiles ahead of its QK^T), then a
+  // second Q buffer (the next item's Q lands while this one runs):
+  // head_dim 64: 3 stages, 2 Q buffers; 72 (80-wide): 3, 1; 96: 2, 1.
+  static constexpr int kPerCta = 233472 / 2 - 1024;
+  static constexpr int bytes_for(int qb, int st) { return qb * kQTile + 2 * st * kKTile + 256 + 1024; }
+  static constexpr int kStages = bytes_for(1, 3) <= kPerCta ? 3 : 2;
+  static constexpr int kQBufs = bytes_for(2, kStages) <= kPerCta ? 2 : 1;
   static constexpr int kQ = 0;
   static constexpr int kK = kQBufs * kQTile;
   static constexpr int kV = kK + kStages * kKTile;
   static constexpr int kBar = kV + kStages * kKTile;
   static constexpr int kSmem = kBar + 256 + 1024;
+  static_assert(kSmem <= kPerCta, "two attention CTAs per SM");
   static constexpr int kQBytes = kQSlabA + kQSlabR;   // TMA bytes
   static constexpr int kKBytes = kKSlabA + kKSlabR;
   static constexpr uint32_t kTmemCols = 256;
