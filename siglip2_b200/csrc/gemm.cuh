@@ -86,14 +86,10 @@ constexpr int kGemmThreads = 320;  // 10 warps: producer, MMA, 8 epilogue (or 4 
 // latencies; the statistics-warp variants keep one per quarter.
 __host__ __device__ constexpr int epi_warps(int e) { return epi_has_stat_warps(e) ? 4 : 8; }
 
-// Tile width of the tensor-core GEMM for an output width N: 192 when it
-// divides N and 256-wide tiles would waste more than 8% of the columns
-// (1152 -> 192; 768, 1536, 3456, 4304 -> 256).  256-wide tiles move fewer
-// operand bytes per FLOP, so they win whenever their tail waste is small.
-__host__ __device__ constexpr int gemm_bn_for(int N) {
-  return (N % 192 == 0 && static_cast<long long>((N + 255) / 256) * 256 * 100 > static_cast<long long>(N) * 108) ? 192
-                                                                                                                 : 256;
-}
+// Tile width of the tensor-core GEMM: 256 columns (the widest MMA; it moves
+// the fewest operand bytes per FLOP).  The CTA-pair kernel runs a narrower
+// last column tile at its own width, so N need not be a multiple of 256.
+__host__ __device__ constexpr int gemm_bn_for(int) { return 256; }
 // Column block of one row-sum slot: the columns one epilogue warp drains of
 // a row-sum-producing tile (half the tile), or the SIMT fp32 tile width.
 __host__ __device__ constexpr int rowsum_block(bool f32, int N) { return f32 ? 128 : gemm_bn_for(N) / 2; }
@@ -698,7 +694,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   constexpr int EW = epi_warps(EPI);
   constexpr int STAGES = Cfg::kStages;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr uint32_t kIdesc = make_idesc(2 * kGemmBM, BN, kBF16, false, false);
+  // the last column tile may be narrower (N - (n_tiles - 1) * BN, rounded up
+  // to 16): its MMAs run at that width and the pair splits B at half of it
+  const auto tile_width = [&](int n_tile) { return min(BN, (p.N - n_tile * BN + 15) & ~15); };
   constexpr int kTileRows = 2 * kGemmBM;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -775,7 +773,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool ok = true;
       for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
         const int m0 = (tile / n_tiles) * kTileRows + static_cast<int>(rank) * kGemmBM;
-        const int n0 = (tile % n_tiles) * BN + static_cast<int>(rank) * (BN / 2);
+        const int n0 = (tile % n_tiles) * BN + static_cast<int>(rank) * (tile_width(tile % n_tiles) / 2);
         for (int kb = 0; kb < nk; ++kb) {
           if (*abort_flag || !mbar_wait<true>(&empty[stage], phase ^ 1, 141)) {
             ok = false;
@@ -823,6 +821,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * Cfg::kAccStride;
+        const uint32_t idesc = make_idesc(2 * kGemmBM, tile_width(tile % n_tiles), kBF16, false, false);
         for (int kb = 0; kb < nk; ++kb) {
           if (*abort_flag || !mbar_wait<true>(&full[stage], phase, 152)) {
             ok = false;
@@ -842,7 +841,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
             for (int k = 0; k < kGemmBK / 16; ++k) {
               umma_ss_pair(d_tmem, kmajor_desc(a_base + sub * Cfg::kSlabA + k * 32, 128),
-                           kmajor_desc(b_base + sub * Cfg::kSlabB + k * 32, 128), kIdesc, (kb | sub | k) != 0);
+                           kmajor_desc(b_base + sub * Cfg::kSlabB + k * 32, 128), idesc, (kb | sub | k) != 0);
             }
           }
           umma_commit_pair_mc(&empty[stage], 0x3);

@@ -136,10 +136,10 @@ int dispatch_epi(int epi, const GemmIO& io, const GemmParams& p, cudaStream_t s)
   }
 }
 
-// Tile width: gemm_bn_for (192 when it divides N and 256 does not, e.g. 1152).
+// Tile width: gemm_bn_for (256; the pair kernel narrows the last column tile).
 template <typename T>
 int dispatch_bn(int epi, const GemmIO& io, const GemmParams& p, cudaStream_t s) {
-  if (gemm_bn_for(p.N) == 192) return dispatch_epi<T, 192>(epi, io, p, s);
+  static_assert(gemm_bn_for(1) == 256, "one tile width");
   return dispatch_epi<T, 256>(epi, io, p, s);
 }
 

@@ -66,17 +66,17 @@ def test_workspace_size_monotone():
 
 
 def test_rowsum_slots_follow_the_tile_widths():
-    """Row-sum slots are half a GEMM tile wide (192-wide tiles where 192
-    divides the width and 256 does not, else 256) on the tensor-core path and
-    128 wide on the fp32 path; bad widths are rejected without a GPU."""
+    """Row-sum slots are half a GEMM tile wide (256-wide tiles, 128-column
+    slots) on the tensor-core path and 128 wide on the fp32 path; bad widths
+    are rejected without a GPU."""
     lib = L.load()
     bf16, f32 = 1, 0
-    assert lib.siglip2_rowsum_slots(bf16, 1152) == 12   # 192-wide tiles, 96-column slots
-    assert lib.siglip2_rowsum_slots(bf16, 768) == 6     # 256-wide tiles, 128-column slots
+    assert lib.siglip2_rowsum_slots(bf16, 1152) == 9
+    assert lib.siglip2_rowsum_slots(bf16, 768) == 6
     assert lib.siglip2_rowsum_slots(bf16, 1536) == 12
     assert lib.siglip2_rowsum_slots(bf16, 4304) == 34
     assert lib.siglip2_rowsum_slots(f32, 768) == 6
     assert lib.siglip2_rowsum_slots(bf16, 0) < 0
-    assert lib.siglip2_rowsum_block(bf16, 1152) == 96
+    assert lib.siglip2_rowsum_block(bf16, 1152) == 128
     assert lib.siglip2_rowsum_block(bf16, 4304) == 128  # the last of the 34 slots holds 80 columns
     assert lib.siglip2_rowsum_block(f32, 4304) == 128

@@ -73,7 +73,9 @@ def test_tower_packed_vs_oracle(preset, layers, dtype, grids):
                              g.numpy(), dt=np.float32)
     cos, mx = _per_image(out.cpu(), torch.from_numpy(ref32), lens)
     assert cos > 0.999, cos
-    assert mx < 5e-2, mx
+    # sanity bound only (one bf16 ulp at |x| in [8, 16) is 0.0625 and the
+    # reference's own bf16 error is ~0.05); the parity bar is _same_dtype_ok
+    assert mx < 8e-2, mx
     refdt = TR.forward_packed(sdq, cfg, packed, grids, dtype)
     cos2, mx2 = _per_image(out, refdt, lens)
     ok, info = _same_dtype_ok(out, refdt, torch.from_numpy(ref32))
