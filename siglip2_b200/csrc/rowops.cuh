@@ -118,12 +118,16 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const T* __restrict__ x,
   for (int c = 0; c < MAXV; ++c) {
     const int v = lane + c * 32;
     if (v < nvec) {
-      float o[V];
+      float o[V], gv[V], bv[V];
 #pragma unroll
-      for (int k = 0; k < V; ++k) {
-        const int col = v * V + k;
-        o[k] = (f[c][k] - mean) * rstd * __ldg(gamma + col) + __ldg(beta + col);
+      for (int k4 = 0; k4 < V / 4; ++k4) {  // gamma / beta as float4 (16-byte aligned: D % V == 0)
+        const float4 g4 = __ldg(reinterpret_cast<const float4*>(gamma + v * V) + k4);
+        const float4 b4 = __ldg(reinterpret_cast<const float4*>(beta + v * V) + k4);
+        gv[4 * k4] = g4.x; gv[4 * k4 + 1] = g4.y; gv[4 * k4 + 2] = g4.z; gv[4 * k4 + 3] = g4.w;
+        bv[4 * k4] = b4.x; bv[4 * k4 + 1] = b4.y; bv[4 * k4 + 2] = b4.z; bv[4 * k4 + 3] = b4.w;
       }
+#pragma unroll
+      for (int k = 0; k < V; ++k) o[k] = fmaf((f[c][k] - mean) * rstd, gv[k], bv[k]);
       store_vec(yr + v * V, o);
     }
   }

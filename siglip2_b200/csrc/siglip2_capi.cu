@@ -274,7 +274,9 @@ int sg_layernorm_impl(int dtype, const void* x, void* y, const float* g, const f
                       const int* cu, int P, cudaStream_t s) {
   SG_CHECK_ARG(x && y && g && b && rows >= 0 && D > 0, "bad LayerNorm arguments");
   SG_CHECK_ARG(cu == nullptr || P > 0, "padded LayerNorm needs P > 0");
-  if (!aligned16(x) || !aligned16(y)) return set_error(SIGLIP2_ERR_ALIGN, "LayerNorm tensors must be 16-byte aligned");
+  if (!aligned16(x) || !aligned16(y) || !aligned16(g) || !aligned16(b))
+    return set_error(SIGLIP2_ERR_ALIGN, "LayerNorm tensors and gamma / beta must be 16-byte aligned");
+  SG_CHECK_ARG(D % 8 == 0, "LayerNorm width %d must be a multiple of 8", D);
   switch (dtype) {
     case SIGLIP2_BF16: return launch_layernorm<__nv_bfloat16>(x, y, g, b, rows, D, eps, cu, P, s);
     case SIGLIP2_F16: return launch_layernorm<__half>(x, y, g, b, rows, D, eps, cu, P, s);
