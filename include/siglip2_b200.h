@@ -116,6 +116,14 @@ int siglip2_gemm(int dtype, int epilogue, const void* a_dev, int lda, const void
 int siglip2_rowsum_slots(int dtype, int width);
 int siglip2_rowsum_block(int dtype, int width);
 
+/* Row sums of x [M, K] (row pitch ldx elements) in the slot layout above:
+ * rs_dev[r * siglip2_rowsum_slots(dtype, K) + j] = (sum, sum of squares) of
+ * row r over column block j.  For rows no row-sum GEMM produced, e.g. the
+ * input of a stand-alone encoder layer (Siglip2EncoderLayer.forward,
+ * model.py:204-223).  x 16-byte aligned; K and ldx multiples of 8 (bf16,
+ * f16) or 4 (f32); rs_dev 8-byte aligned. */
+int siglip2_rowsums(int dtype, const void* x_dev, int ldx, int M, int K, float* rs_dev, void* stream);
+
 /* siglip2_gemm with row-sum LayerNorm plumbing: the GEMM that writes the
  * residual stream (SIGLIP2_EPI_BIAS_RES_ROWSUMS) writes each row's sum and
  * sum of squares into rs_acc ([M][siglip2_rowsum_slots(dtype, N)] pairs),

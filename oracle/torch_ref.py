@@ -37,43 +37,66 @@ def _qkv(sd, pre, dt, dev):
 
 
 @torch.no_grad()
-def forward_packed(sd, cfg, seq_patches, grids, dtype, device="cuda"):
+def embeddings(sd, cfg, seq_patches, grids, dtype, device="cuda", pre="embeddings."):
+    """``model.py:68-120``: patch Linear + per-image resized position grid."""
+    D = cfg.hidden_size
+    x = F.linear(seq_patches.to(device=device, dtype=dtype), _w(sd, pre + "patch_embedding.weight", dtype, device),
+                 _w(sd, pre + "patch_embedding.bias", dtype, device))
+    g = int(round(cfg.num_patches ** 0.5))
+    table = _w(sd, pre + "position_embedding.weight", dtype, device).reshape(g, g, D).permute(2, 0, 1)[None]
+    pos = torch.cat([F.interpolate(table, size=(int(h), int(w)), mode="bilinear", align_corners=False, antialias=True)
+                     .reshape(D, int(h) * int(w)).transpose(0, 1) for h, w in grids], 0)
+    return x + pos
+
+
+@torch.no_grad()
+def attention(sd, cfg, pre, h, lens, dtype, device="cuda"):
+    """``model.py:144-176`` on packed rows ``h [N, D]``: q/k/v Linear,
+    softmax attention within each run of ``lens`` rows, out Linear."""
     D, H = cfg.hidden_size, cfg.num_attention_heads
     hd = D // H
-    eps = cfg.layer_norm_eps
+    (wq, bq), (wk, bk), (wv, bv) = _qkv(sd, pre, dtype, device)
+    q, k, v = F.linear(h, wq, bq), F.linear(h, wk, bk), F.linear(h, wv, bv)
+    outs = []
+    s = 0
+    for Ln in lens:
+        sl = slice(s, s + Ln)
+        qh, kh, vh = (t[sl].view(Ln, H, hd).transpose(0, 1) for t in (q, k, v))
+        outs.append(F.scaled_dot_product_attention(qh[None], kh[None], vh[None], scale=hd ** -0.5)[0]
+                    .transpose(0, 1).reshape(Ln, D))
+        s += Ln
+    a = torch.cat(outs, 0)
+    return F.linear(a, _w(sd, pre + "out_proj.weight", dtype, device), _w(sd, pre + "out_proj.bias", dtype, device))
+
+
+@torch.no_grad()
+def mlp(sd, pre, h, dtype, device="cuda"):
+    """``model.py:187-191``: fc2(gelu_tanh(fc1 h))."""
+    h = F.gelu(F.linear(h, _w(sd, pre + "fc1.weight", dtype, device), _w(sd, pre + "fc1.bias", dtype, device)),
+               approximate="tanh")
+    return F.linear(h, _w(sd, pre + "fc2.weight", dtype, device), _w(sd, pre + "fc2.bias", dtype, device))
+
+
+@torch.no_grad()
+def encoder_layer(sd, cfg, pre, x, lens, dtype, device="cuda"):
+    """``model.py:204-223`` on packed rows ``x [N, D]``."""
+    D, eps = cfg.hidden_size, cfg.layer_norm_eps
+    h = F.layer_norm(x, (D,), _w(sd, pre + "layer_norm1.weight", dtype, device),
+                     _w(sd, pre + "layer_norm1.bias", dtype, device), eps)
+    x = x + attention(sd, cfg, pre + "self_attn.", h, lens, dtype, device)
+    h = F.layer_norm(x, (D,), _w(sd, pre + "layer_norm2.weight", dtype, device),
+                     _w(sd, pre + "layer_norm2.bias", dtype, device), eps)
+    return x + mlp(sd, pre + "mlp.", h, dtype, device)
+
+
+@torch.no_grad()
+def forward_packed(sd, cfg, seq_patches, grids, dtype, device="cuda"):
+    D, eps = cfg.hidden_size, cfg.layer_norm_eps
     grids = [(int(h), int(w)) for h, w in grids]
     lens = [h * w for h, w in grids]
-    x = F.linear(seq_patches.to(device=device, dtype=dtype), _w(sd, "embeddings.patch_embedding.weight", dtype, device),
-                 _w(sd, "embeddings.patch_embedding.bias", dtype, device))
-    g = int(round(cfg.num_patches ** 0.5))
-    table = _w(sd, "embeddings.position_embedding.weight", dtype, device).reshape(g, g, D).permute(2, 0, 1)[None]
-    pos = torch.cat([F.interpolate(table, size=(h, w), mode="bilinear", align_corners=False, antialias=True)
-                     .reshape(D, h * w).transpose(0, 1) for h, w in grids], 0)
-    x = x + pos
+    x = embeddings(sd, cfg, seq_patches, grids, dtype, device)
     for i in range(cfg.num_hidden_layers):
-        pre = f"encoder.layers.{i}."
-        res = x
-        h = F.layer_norm(x, (D,), _w(sd, pre + "layer_norm1.weight", dtype, device),
-                         _w(sd, pre + "layer_norm1.bias", dtype, device), eps)
-        (wq, bq), (wk, bk), (wv, bv) = _qkv(sd, pre + "self_attn.", dtype, device)
-        q, k, v = F.linear(h, wq, bq), F.linear(h, wk, bk), F.linear(h, wv, bv)
-        outs = []
-        s = 0
-        for Ln in lens:
-            sl = slice(s, s + Ln)
-            qh, kh, vh = (t[sl].view(Ln, H, hd).transpose(0, 1) for t in (q, k, v))
-            outs.append(F.scaled_dot_product_attention(qh[None], kh[None], vh[None], scale=hd ** -0.5)[0]
-                        .transpose(0, 1).reshape(Ln, D))
-            s += Ln
-        a = torch.cat(outs, 0)
-        x = res + F.linear(a, _w(sd, pre + "self_attn.out_proj.weight", dtype, device),
-                           _w(sd, pre + "self_attn.out_proj.bias", dtype, device))
-        res = x
-        h = F.layer_norm(x, (D,), _w(sd, pre + "layer_norm2.weight", dtype, device),
-                         _w(sd, pre + "layer_norm2.bias", dtype, device), eps)
-        h = F.gelu(F.linear(h, _w(sd, pre + "mlp.fc1.weight", dtype, device), _w(sd, pre + "mlp.fc1.bias", dtype, device)),
-                   approximate="tanh")
-        x = res + F.linear(h, _w(sd, pre + "mlp.fc2.weight", dtype, device), _w(sd, pre + "mlp.fc2.bias", dtype, device))
+        x = encoder_layer(sd, cfg, f"encoder.layers.{i}.", x, lens, dtype, device)
     return F.layer_norm(x, (D,), _w(sd, "post_layernorm.weight", dtype, device), _w(sd, "post_layernorm.bias", dtype, device),
                         eps)
 

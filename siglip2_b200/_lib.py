@@ -29,6 +29,7 @@ SIGNATURES = {
                                       _vp, _vp, _c_int, _vp, _vp, _c_float, _vp, _vp, _vp]),
     "siglip2_rowsum_slots": (_c_int, [_c_int, _c_int]),
     "siglip2_rowsum_block": (_c_int, [_c_int, _c_int]),
+    "siglip2_rowsums": (_c_int, [_c_int, _vp, _c_int, _c_int, _c_int, _vp, _vp]),
     "siglip2_patch_embed": (_c_int, [_c_int, _vp, _c_int, _vp, _vp, _vp, _c_int, _vp, _vp, _vp, _c_int, _c_int, _vp,
                                      _vp, _vp]),
     "siglip2_layernorm": (_c_int, [_c_int, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_float, _vp, _c_int, _vp]),

@@ -221,4 +221,36 @@ __global__ void token_image_kernel(const int* __restrict__ cu, int B, int N, int
   tok_img[t] = lo;
 }
 
+// Row sums in the slot layout the LayerNorm-folded GEMMs read: for row r and
+// column block j (columns [j*blk, min((j+1)*blk, K))), rs[r*slots + j] =
+// (sum, sum of squares).  For rows that no row-sum GEMM produced (the input
+// of a stand-alone encoder layer).  One warp per row, 16-byte loads; K, ldx
+// and blk are multiples of the vector width and x is 16-byte aligned (the
+// host checks).
+template <typename T>
+__global__ void __launch_bounds__(256) rowsums_kernel(const T* __restrict__ x, int ldx, int M, int K, int blk,
+                                                      float2* __restrict__ rs, int slots) {
+  constexpr int V = Vec16<T>::N;
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const T* xr = x + static_cast<size_t>(row) * ldx;
+  for (int j = 0; j < slots; ++j) {
+    const int c_end = min(K, (j + 1) * blk);
+    float s1 = 0.f, s2 = 0.f;
+    for (int c = j * blk + lane * V; c < c_end; c += 32 * V) {
+      float f[V];
+      load_vec(xr + c, f);
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        s1 += f[i];
+        s2 = fmaf(f[i], f[i], s2);
+      }
+    }
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2);
+    if (lane == 0) rs[static_cast<size_t>(row) * slots + j] = make_float2(s1, s2);
+  }
+}
+
 }  // namespace sg

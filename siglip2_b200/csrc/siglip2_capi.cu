@@ -306,6 +306,25 @@ int sg_posemb_impl(int dtype, const float* table, int G, int D, const int* tok_i
   return SIGLIP2_OK;
 }
 
+int sg_rowsums_impl(int dtype, const void* x, int ldx, int M, int K, float2* rs, cudaStream_t s) {
+  SG_CHECK_ARG(x && rs && M >= 0 && K > 0 && ldx >= K, "bad rowsums arguments");
+  const bool f32 = dtype == SIGLIP2_F32;
+  const int v = f32 ? 4 : 8;
+  if (!aligned16(x) || K % v || ldx % v || (reinterpret_cast<uintptr_t>(rs) & 7u))
+    return set_error(SIGLIP2_ERR_ALIGN, "rowsums: x 16-byte aligned, K and ldx multiples of %d, rs 8-byte aligned", v);
+  if (M == 0) return SIGLIP2_OK;
+  const int blk = rowsum_block(f32, K), slots = rowsum_slots(f32, K);
+  const dim3 grid((M + 7) / 8);
+  switch (dtype) {
+    case SIGLIP2_BF16: rowsums_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), ldx, M, K, blk, rs, slots); break;
+    case SIGLIP2_F16: rowsums_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(x), ldx, M, K, blk, rs, slots); break;
+    case SIGLIP2_F32: rowsums_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(x), ldx, M, K, blk, rs, slots); break;
+    default: return set_error(SIGLIP2_ERR_ARG, "unknown dtype %d", dtype);
+  }
+  SG_LAUNCH_CHECK();
+  return SIGLIP2_OK;
+}
+
 int sg_token_image_impl(const int* cu, int B, int N, int* tok_img, cudaStream_t s) {
   if (N == 0) return SIGLIP2_OK;
   token_image_kernel<<<(N + 255) / 256, 256, 0, s>>>(cu, B, N, tok_img);
@@ -687,6 +706,11 @@ int siglip2_rowsum_slots(int dtype, int n) {
 int siglip2_rowsum_block(int dtype, int n) {
   SG_CHECK_ARG(n > 0, "bad row width %d", n);
   return rowsum_block(dtype == SIGLIP2_F32, n);
+}
+
+int siglip2_rowsums(int dtype, const void* x_dev, int ldx, int M, int K, float* rs_dev, void* stream) {
+  return sg_rowsums_impl(dtype, x_dev, ldx, M, K, reinterpret_cast<float2*>(rs_dev),
+                         static_cast<cudaStream_t>(stream));
 }
 
 int siglip2_gemm_rowsums(int dtype, int epilogue, const void* a_dev, int lda, const void* b_dev, int ldb,

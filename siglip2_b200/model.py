@@ -33,7 +33,11 @@ import torch
 import torch.nn as nn
 
 from . import _lib as L
+from . import ops
+from . import torch_ops  # noqa: F401  (registers torch.ops.siglip2_b200)
 from .ops import dtype_code, fold_layernorm
+
+_OPS = torch.ops.siglip2_b200
 
 
 @dataclass
@@ -58,12 +62,226 @@ class Siglip2Output(NamedTuple):
 
 
 # ---------------------------------------------------------------------------
-# parameter containers with the reference's names (no forward of their own)
+# packed sequences: which rows attend to which
 # ---------------------------------------------------------------------------
 
 
+def create_document_ids(seq_sizes, device=None) -> torch.Tensor:
+    """``model.py:12-36``: the image index of every packed token, padded to a
+    multiple of 128 entries with ids that name no image (the pad ids count
+    up from the token count)."""
+    sizes = torch.as_tensor(seq_sizes).to(device)
+    ids = torch.repeat_interleave(torch.arange(sizes.numel(), device=sizes.device), sizes)
+    n = ids.numel()
+    pad = (-n) % 128
+    if pad:
+        ids = torch.cat([ids, torch.arange(n, n + pad, device=ids.device, dtype=ids.dtype)])
+    return ids
+
+
+def _mask_runs(mask_mod, b: int, seq_len: int, device) -> list[int]:
+    """Lengths of the contiguous runs of a document mask ``mask_mod(b, h, q,
+    kv)`` over ``seq_len`` rows.  A run starts at row i when row i does not
+    attend to row i-1.  Every row is then checked against both ends of its
+    run and the rows just outside it, and ``mask_mod`` is compared with
+    "same run" on every (row, column) pair up to 4096 rows, on a seeded
+    sample of 64 columns per row above that.  A document mask passes; a
+    causal, sliding-window or interleaved mask does not."""
+    i = torch.arange(seq_len, device=device)
+    bt = torch.full((), b, dtype=torch.int64, device=device)
+    ht = torch.zeros((), dtype=torch.int64, device=device)
+
+    def attends(q, k):
+        return torch.broadcast_to(torch.as_tensor(mask_mod(bt, ht, q, k), device=device), q.shape).to(torch.bool)
+
+    start = torch.ones(seq_len, dtype=torch.bool, device=device)
+    start[1:] = ~attends(i[1:], i[:-1])
+    starts = i[start]
+    ends = torch.cat([starts[1:], torch.tensor([seq_len], device=device)])
+    run = torch.cumsum(start.to(torch.int64), 0) - 1
+    lo, hi = starts[run], ends[run]
+    ok = bool(attends(i, lo).all()) and bool(attends(i, hi - 1).all())
+    left, right = lo > 0, hi < seq_len
+    ok = ok and not bool(attends(i[left], lo[left] - 1).any()) and not bool(attends(i[right], hi[right]).any())
+    if ok and seq_len <= 4096:
+        step = max(1, (1 << 22) // seq_len)
+        for r0 in range(0, seq_len, step):
+            q = i[r0:r0 + step, None].expand(-1, seq_len).reshape(-1)
+            k = i[None, :].expand(min(step, seq_len - r0), -1).reshape(-1)
+            ok = ok and bool(torch.equal(attends(q, k), run[q] == run[k]))
+    elif ok:
+        gen = torch.Generator().manual_seed(seq_len)
+        k = torch.randint(0, seq_len, (seq_len * 64,), generator=gen).to(device)
+        q = i.repeat_interleave(64)
+        ok = bool(torch.equal(attends(q, k), run[q] == run[k]))
+    if not ok:
+        raise NotImplementedError("only document masks (rows attend to exactly their own contiguous run) "
+                                  "are supported")
+    return (ends - starts).tolist()
+
+
+class Sequences:
+    """The independent attention sequences of a row set (one per image and
+    batch entry): their lengths on the host, ``cu_seqlens`` [n+1] and the
+    128-row query tiles (``(sequence, tile)`` int32 pairs, longest sequences
+    first) on the device.  Built once per encoder call and shared by its
+    layers, as ``model_optimized.py:316-338`` shares one block mask."""
+
+    def __init__(self, lengths, device):
+        self.lengths = [int(n) for n in lengths]
+        if not self.lengths or min(self.lengths) <= 0:
+            raise ValueError("every sequence needs at least one row")
+        cu = np.zeros(len(self.lengths) + 1, dtype=np.int64)
+        np.cumsum(self.lengths, out=cu[1:])
+        if cu[-1] >= 2 ** 31:
+            raise ValueError("more than 2^31 - 1 rows")
+        self.n_tokens = int(cu[-1])
+        tiles = ops.attention_tiles(self.lengths).reshape(-1)
+        nc = cu.size + (cu.size & 1)  # the tile pairs are read as 8-byte words
+        host = torch.zeros(nc + tiles.numel(), dtype=torch.int32)
+        host[:cu.size] = torch.from_numpy(cu.astype(np.int32))
+        host[nc:] = tiles
+        dev = host.to(device)
+        self.cu_seqlens = dev[:cu.size]
+        self.tiles = dev[nc:].view(-1, 2)
+
+    @classmethod
+    def full(cls, seq_len: int, batch: int, device) -> "Sequences":
+        return cls([seq_len] * batch, device)
+
+    @classmethod
+    def from_document_ids(cls, document_ids, seq_len: int, batch: int, device) -> "Sequences":
+        """``document_ids[q] == document_ids[kv]`` (``model.py:156-157``) over
+        the first ``seq_len`` ids, the same for every batch entry.  Each
+        document must be one contiguous run of rows."""
+        ids = torch.as_tensor(document_ids).reshape(-1)
+        if ids.numel() < seq_len:
+            raise ValueError(f"document_ids has {ids.numel()} entries for {seq_len} rows")
+        vals, counts = torch.unique_consecutive(ids[:seq_len], return_counts=True)
+        if torch.unique(vals).numel() != vals.numel():
+            raise NotImplementedError("each document must be one contiguous run of rows")
+        return cls(counts.tolist() * batch, device)
+
+    @classmethod
+    def from_block_mask(cls, block_mask, seq_len: int, batch: int, device) -> "Sequences":
+        """The runs of a ``flex_attention`` ``BlockMask`` built from a document
+        mask (``model_optimized.py:323-330``); other masks are refused."""
+        if tuple(block_mask.seq_lengths) != (seq_len, seq_len):
+            raise ValueError(f"block mask is for {tuple(block_mask.seq_lengths)} rows, input has {seq_len}")
+        nb, nh = block_mask.kv_num_blocks.shape[:2]
+        if nh != 1 or nb not in (1, batch):
+            raise NotImplementedError("block masks must have one head entry and 1 or batch batch entries")
+        mdev = block_mask.kv_num_blocks.device
+        runs = [_mask_runs(block_mask.mask_mod, b, seq_len, mdev) for b in range(nb)]
+        if nb == 1:
+            runs = runs * batch
+        return cls([n for r in runs for n in r], device)
+
+
+@torch.compiler.disable
+def _sequences(x: torch.Tensor, document_ids=None, block_mask=None) -> Sequences:
+    if x.dim() != 3:
+        raise ValueError(f"hidden_states must be [batch, rows, hidden], got {tuple(x.shape)}")
+    B, S = x.shape[:2]
+    if block_mask is not None:
+        return Sequences.from_block_mask(block_mask, S, B, x.device)
+    if document_ids is not None:
+        return Sequences.from_document_ids(document_ids, S, B, x.device)
+    return Sequences.full(S, B, x.device)
+
+
+# ---------------------------------------------------------------------------
+# modules with the reference's names; forwards on the library's kernels
+# ---------------------------------------------------------------------------
+
+
+@torch.compiler.disable
+def _derived(module: nn.Module, build):
+    """Tensors derived from a module's parameters (concatenated, folded,
+    cast), rebuilt when a parameter changes address, version, dtype or
+    device."""
+    key = tuple((p.data_ptr(), p._version, p.dtype, p.device) for p in module.parameters())
+    hit = module.__dict__.get("_sg_derived")
+    if hit is None or hit[0] != key:
+        if any(p.device.type != "cuda" for p in module.parameters()):
+            raise RuntimeError("siglip2_b200 runs on CUDA only: move the module with .to('cuda') first")
+        with torch.no_grad():
+            hit = (key, tuple(t.detach().contiguous() for t in build()))
+        module.__dict__["_sg_derived"] = hit
+    return hit[1]
+
+
+def _rows(x: torch.Tensor, dtype) -> torch.Tensor:
+    """``x [..., D]`` as a contiguous ``[rows, D]`` matrix of ``dtype``."""
+    x2 = x.reshape(-1, x.shape[-1])
+    return (x2 if x2.dtype == dtype else x2.to(dtype)).contiguous()
+
+
+def _check_inference(module: nn.Module, dropout: float):
+    if module.training and dropout > 0:
+        raise NotImplementedError("siglip2_b200 implements inference only: call .eval() (or set "
+                                  "attention_dropout=0); the reference applies attention dropout in train mode")
+
+
+class LayerNorm(nn.LayerNorm):
+    """``nn.LayerNorm`` (``model.py:199,201,256``) whose forward is
+    ``siglip2_layernorm``: fp32 statistics, biased variance."""
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        w, b = _derived(self, lambda: (self.weight.float(), self.bias.float()))
+        return _OPS.layernorm(_rows(x, x.dtype), w, b, float(self.eps)).view(x.shape)
+
+
+class LayerNormImproved(nn.Module):
+    """``optimized_siglip2/model_optimized.py:23-80``: LayerNorm with the
+    residual interface of its ``layer_norm_fn``.  ``residual`` is added first
+    (in fp32) and the sum is what is normalised; with ``prenorm`` the sum is
+    returned too, in fp32 when ``residual_in_fp32``, else in the residual's
+    dtype.  As in the reference, ``is_rms_norm`` is not read.  Dropout,
+    ``rowscale``, the second input (``x1``/``weight1``/``bias1``) and
+    zero-centred weights are not implemented and raise."""
+
+    def __init__(self, hidden_size, eps, bias=True, init_fn="ones"):
+        super().__init__()
+        if init_fn not in ("ones", "zeros"):
+            raise ValueError(f"init_fn must be either 'ones' or 'zeros', got {init_fn}")
+        self.hidden_size = hidden_size
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(hidden_size) if init_fn == "ones" else torch.zeros(hidden_size))
+        self.bias = nn.Parameter(torch.randn(hidden_size) if bias else torch.zeros(hidden_size))
+        self.variance_epsilon = eps
+
+    def forward(self, hidden_states, residual=None, x1=None, weight1=None, bias1=None, dropout_p=0.0, rowscale=None,
+                prenorm=False, residual_in_fp32=False, zero_centered_weight=False, is_rms_norm=False,
+                return_dropout_mask=False, out_dtype=None, out=None, residual_out=None):
+        if (x1 is not None or weight1 is not None or bias1 is not None or rowscale is not None or dropout_p
+                or zero_centered_weight or return_dropout_mask):
+            raise NotImplementedError("siglip2_b200 LayerNormImproved: dropout, rowscale, x1/weight1/bias1 and "
+                                      "zero_centered_weight are not implemented")
+        w, b = _derived(self, lambda: (self.weight.float(), self.bias.float()))
+        x = hidden_states
+        if residual is None and not residual_in_fp32:
+            y = _OPS.layernorm(_rows(x, x.dtype), w, b, float(self.variance_epsilon)).view(x.shape)
+            res = x
+        else:
+            s = x.float() if residual is None else x.float() + residual.float()
+            y = _OPS.layernorm(_rows(s, torch.float32), w, b, float(self.variance_epsilon)).view(x.shape)
+            res = s.to(torch.float32 if residual_in_fp32 else residual.dtype)
+        y = y.to(out_dtype or x.dtype)
+        if out is not None:
+            y = out.copy_(y)
+        if residual_out is not None:
+            res = residual_out.copy_(res)
+        return (y, res) if prenorm else y
+
+    def extra_repr(self):
+        return f"{self.hidden_size}, eps={self.eps}"
+
+
 class Siglip2SequenceEmbeddings(nn.Module):
-    """Parameters of ``model.py:52-66``."""
+    """``model.py:52-120``: patch Linear plus the learned position grid
+    resized (antialiased bilinear) to each image, as one ``siglip2_patch_embed``
+    launch."""
 
     def __init__(self, config: Siglip2VisionConfig):
         super().__init__()
@@ -75,13 +293,43 @@ class Siglip2SequenceEmbeddings(nn.Module):
         self.position_embedding_size = int(config.num_patches ** 0.5)
         self.position_embedding = nn.Embedding(config.num_patches, config.hidden_size)
 
+    def forward(self, packed_seq_patches):
+        """``(seq_patches [N, C*p*p], seq_sizes [B], spatial_shapes [B, 2])``
+        -> ``[N, D]``; image b's rows are its ``h*w`` patches, row-major."""
+        seq_patches, seq_sizes, spatial_shapes = packed_seq_patches
+        w, b, table = _derived(self, lambda: (self.patch_embedding.weight, self.patch_embedding.bias.float(),
+                                              self.position_embedding.weight.float()))
+        hw = _grids(spatial_shapes)
+        if seq_sizes is not None:
+            sizes = torch.as_tensor(seq_sizes).detach().to("cpu", torch.int64).reshape(-1).numpy()
+            if not np.array_equal(sizes, hw[:, 0].astype(np.int64) * hw[:, 1]):
+                raise ValueError("seq_sizes must equal h*w of spatial_shapes")
+        meta, N, _ = _metadata(hw, w.device)
+        B = hw.shape[0]
+        cu, hw_dev = meta[:B + 1], meta[B + 1:3 * B + 1]
+        tok = _OPS.token_image(cu, N)
+        return _OPS.patch_embed(_rows(seq_patches, w.dtype), w, b, table, hw_dev, cu, tok)
+
+
+def _attention(m: nn.Module, x: torch.Tensor, seqs: Sequences) -> torch.Tensor:
+    """QKV projection -> per-sequence attention -> out projection
+    (``model.py:144-176``), three launches."""
+    qkv_w, qkv_b, out_w, out_b = _derived(m, lambda: (*m.qkv_params(), m.out_proj.weight, m.out_proj.bias))
+    x2 = _rows(x, qkv_w.dtype)
+    if x2.shape[0] != seqs.n_tokens:
+        raise ValueError(f"{x2.shape[0]} rows but the sequences cover {seqs.n_tokens}")
+    qkv = _OPS.gemm(x2, qkv_w, L.EPI_BIAS, qkv_b.float(), None, None, None, 0.0)
+    a = _OPS.fmha_varlen(qkv, seqs.cu_seqlens, seqs.tiles, m.num_heads, m.head_dim)
+    return _OPS.gemm(a, out_w, L.EPI_BIAS, out_b.float(), None, None, None, 0.0).view(*x.shape[:-1], -1)
+
 
 class Siglip2Attention(nn.Module):
-    """Parameters of ``model.py:123-142``; also loads the fused ``qkv_proj``
-    of ``model_optimized.py:215`` (rows = cat([q, k, v]))."""
+    """``model.py:123-176``; also loads the fused ``qkv_proj`` of
+    ``model_optimized.py:215`` (rows = cat([q, k, v]))."""
 
     def __init__(self, config):
         super().__init__()
+        self.config = config
         self.embed_dim = config.hidden_size
         self.num_heads = config.num_attention_heads
         self.head_dim = self.embed_dim // self.num_heads
@@ -106,53 +354,227 @@ class Siglip2Attention(nn.Module):
         super()._load_from_state_dict(state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
                                       error_msgs)
 
+    def qkv_params(self):
+        """The fused projection ``[3D, D]`` / ``[3D]`` (q | k | v rows)."""
+        lins = (self.q_proj, self.k_proj, self.v_proj)
+        return torch.cat([m.weight for m in lins], 0), torch.cat([m.bias for m in lins], 0)
+
+    def forward(self, hidden_states, document_ids=None, output_attentions=False):
+        """``[B, S, D]`` -> ``(out [B, S, D], None)``; rows q and kv attend
+        when ``document_ids[q] == document_ids[kv]`` (all rows when None)."""
+        _check_inference(self, self.dropout)
+        return _attention(self, hidden_states, _sequences(hidden_states, document_ids=document_ids)), None
+
+
+class Siglip2AttentionImproved(Siglip2Attention):
+    """``optimized_siglip2/model_optimized.py:200-243``: fused ``qkv_proj``;
+    the mask is a ``flex_attention`` ``BlockMask`` built from a document
+    mask (or ``document_ids`` directly)."""
+
+    def __init__(self, config):
+        nn.Module.__init__(self)
+        self.config = config
+        self.embed_dim = config.hidden_size
+        self.num_heads = config.num_attention_heads
+        self.head_dim = self.embed_dim // self.num_heads
+        if self.head_dim * self.num_heads != self.embed_dim:
+            raise ValueError("embed_dim must be divisible by num_heads")
+        self.scale = self.head_dim ** -0.5
+        self.dropout = config.attention_dropout
+        self.qkv_proj = nn.Linear(self.embed_dim, 3 * self.embed_dim)
+        self.out_proj = nn.Linear(self.embed_dim, self.embed_dim)
+
+    def _load_from_state_dict(self, *args, **kwargs):
+        nn.Module._load_from_state_dict(self, *args, **kwargs)
+
+    def qkv_params(self):
+        return self.qkv_proj.weight, self.qkv_proj.bias
+
+    def forward(self, hidden_states, block_mask=None, output_attentions=False, document_ids=None):
+        _check_inference(self, self.dropout)
+        seqs = _sequences(hidden_states, document_ids=document_ids, block_mask=block_mask)
+        return _attention(self, hidden_states, seqs), None
+
 
 class Siglip2MLP(nn.Module):
-    """Parameters of ``model.py:179-185`` (GELU-tanh between fc1 and fc2)."""
+    """``model.py:179-191``: ``fc2(gelu_tanh(fc1 x))`` as two GEMMs, GELU in
+    the first one's epilogue."""
 
     def __init__(self, config):
         super().__init__()
+        self.config = config
         self.fc1 = nn.Linear(config.hidden_size, config.intermediate_size)
         self.fc2 = nn.Linear(config.intermediate_size, config.hidden_size)
 
+    def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
+        w1, b1, w2, b2 = _derived(self, lambda: (self.fc1.weight, self.fc1.bias.float(), self.fc2.weight,
+                                                 self.fc2.bias.float()))
+        h = _OPS.gemm(_rows(hidden_states, w1.dtype), w1, L.EPI_BIAS_GELU, b1, None, None, None, 0.0)
+        return _OPS.gemm(h, w2, L.EPI_BIAS, b2, None, None, None, 0.0).view(*hidden_states.shape[:-1], -1)
+
+
+class MLPImproved(Siglip2MLP):
+    """``optimized_siglip2/model_optimized.py:246-260`` (same parameters and
+    result as ``Siglip2MLP``)."""
+
+
+class Siglip2SequenceEmbeddingsImproved(Siglip2SequenceEmbeddings):
+    """``optimized_siglip2/model_optimized.py:123-197`` (same parameters and
+    result as ``Siglip2SequenceEmbeddings``)."""
+
+
+def _layer_tensors(layer: nn.Module):
+    """The ten per-layer tensors of ``siglip2_layer_weights`` (LAYER_FIELDS
+    order): QKV with LayerNorm 1 folded, out projection, fc1 with LayerNorm 2
+    folded, fc2."""
+    at, mlp = layer.self_attn, layer.mlp
+    wp, bp = at.qkv_params()
+    dt = wp.dtype
+    return (*fold_layernorm(wp, bp, layer.layer_norm1.weight, layer.layer_norm1.bias, dt),
+            at.out_proj.weight.to(dt), at.out_proj.bias.float(),
+            *fold_layernorm(mlp.fc1.weight, mlp.fc1.bias, layer.layer_norm2.weight, layer.layer_norm2.bias, dt),
+            mlp.fc2.weight.to(dt), mlp.fc2.bias.float())
+
+
+def _encoder_layer(layer: nn.Module, x: torch.Tensor, seqs: Sequences, rs: torch.Tensor | None = None):
+    """One pre-LN layer (``model.py:204-223``) as the launch sequence the
+    tower runs: LN1 folded into the QKV GEMM, attention, out projection with
+    the residual, LN2 folded into fc1 (+GELU), fc2 with the residual.  The
+    LayerNorm statistics travel as row sums (``rs`` in, the output's out).
+    Returns ``(y, rs_y)``."""
+    _check_inference(layer, layer.self_attn.dropout)
+    qw, qc1, qc2, ow, ob, f1w, f1c1, f1c2, f2w, f2b = _derived(layer, lambda: _layer_tensors(layer))
+    eps1, eps2 = float(layer.layer_norm1.eps), float(layer.layer_norm2.eps)
+    at = layer.self_attn
+    x2 = _rows(x, qw.dtype)
+    if x2.shape[0] != seqs.n_tokens:
+        raise ValueError(f"{x2.shape[0]} rows but the sequences cover {seqs.n_tokens}")
+    if rs is None:
+        rs = _OPS.rowsums(x2)
+    qkv, _ = _OPS.gemm_rowsums(x2, qw, L.EPI_LN_ROWSUMS, None, None, qc1, qc2, eps1, rs, False)
+    a = _OPS.fmha_varlen(qkv, seqs.cu_seqlens, seqs.tiles, at.num_heads, at.head_dim)
+    h, rs_h = _OPS.gemm_rowsums(a, ow, L.EPI_BIAS_RES_ROWSUMS, ob, x2, None, None, 0.0, None, True)
+    m, _ = _OPS.gemm_rowsums(h, f1w, L.EPI_LN_ROWSUMS_GELU, None, None, f1c1, f1c2, eps2, rs_h, False)
+    y, rs_y = _OPS.gemm_rowsums(m, f2w, L.EPI_BIAS_RES_ROWSUMS, f2b, h, None, None, 0.0, None, True)
+    return y.view(x.shape), rs_y
+
 
 class Siglip2EncoderLayer(nn.Module):
-    """Parameters of ``model.py:194-201``."""
+    """``model.py:194-223``."""
 
     def __init__(self, config: Siglip2VisionConfig):
         super().__init__()
         self.embed_dim = config.hidden_size
         self.self_attn = Siglip2Attention(config)
-        self.layer_norm1 = nn.LayerNorm(self.embed_dim, eps=config.layer_norm_eps)
+        self.layer_norm1 = LayerNorm(self.embed_dim, eps=config.layer_norm_eps)
         self.mlp = Siglip2MLP(config)
-        self.layer_norm2 = nn.LayerNorm(self.embed_dim, eps=config.layer_norm_eps)
+        self.layer_norm2 = LayerNorm(self.embed_dim, eps=config.layer_norm_eps)
+
+    def forward(self, hidden_states: torch.Tensor, document_ids: torch.Tensor | None = None) -> torch.Tensor:
+        return _encoder_layer(self, hidden_states, _sequences(hidden_states, document_ids=document_ids))[0]
+
+
+class Siglip2EncoderLayerImproved(nn.Module):
+    """``optimized_siglip2/model_optimized.py:263-301`` (fused ``qkv_proj``,
+    ``LayerNormImproved``); the mask is a document-mask ``BlockMask``."""
+
+    def __init__(self, config: Siglip2VisionConfig):
+        super().__init__()
+        self.embed_dim = config.hidden_size
+        self.self_attn = Siglip2AttentionImproved(config)
+        self.layer_norm1 = LayerNormImproved(self.embed_dim, eps=config.layer_norm_eps)
+        self.mlp = MLPImproved(config)
+        self.layer_norm2 = LayerNormImproved(self.embed_dim, eps=config.layer_norm_eps)
+
+    def forward(self, hidden_states: torch.Tensor, block_mask=None, document_ids=None) -> torch.Tensor:
+        seqs = _sequences(hidden_states, document_ids=document_ids, block_mask=block_mask)
+        return _encoder_layer(self, hidden_states, seqs)[0]
+
+
+def _encoder(enc: nn.Module, inputs_embeds: torch.Tensor, document_ids) -> torch.Tensor:
+    seqs = _sequences(inputs_embeds, document_ids=document_ids)
+    x, rs = inputs_embeds, None
+    for layer in enc.layers:
+        x, rs = _encoder_layer(layer, x, seqs, rs)
+    return x
 
 
 class Siglip2Encoder(nn.Module):
+    """``model.py:226-247``: the layers over one shared set of sequences."""
+
     def __init__(self, config: Siglip2VisionConfig):
         super().__init__()
+        self.config = config
         self.layers = nn.ModuleList([Siglip2EncoderLayer(config) for _ in range(config.num_hidden_layers)])
+
+    def forward(self, inputs_embeds: torch.Tensor, document_ids: torch.Tensor | None = None) -> torch.Tensor:
+        return _encoder(self, inputs_embeds, document_ids)
+
+
+class Siglip2EncoderImproved(nn.Module):
+    """``optimized_siglip2/model_optimized.py:304-338``."""
+
+    def __init__(self, config: Siglip2VisionConfig):
+        super().__init__()
+        self.config = config
+        self.layers = nn.ModuleList([Siglip2EncoderLayerImproved(config) for _ in range(config.num_hidden_layers)])
+
+    def forward(self, inputs_embeds: torch.Tensor, document_ids: torch.Tensor | None = None) -> torch.Tensor:
+        return _encoder(self, inputs_embeds, document_ids)
 
 
 class Siglip2MultiheadAttentionPoolingHead(nn.Module):
-    """Parameters of ``transformers`` ``modeling_siglip2.py:670-681``."""
+    """Parameters of ``transformers`` ``modeling_siglip2.py:670-681``; runs
+    inside the tower's forward (``pooler_output``)."""
 
     def __init__(self, config: Siglip2VisionConfig):
         super().__init__()
         self.probe = nn.Parameter(torch.randn(1, 1, config.hidden_size))
         self.attention = nn.MultiheadAttention(config.hidden_size, config.num_attention_heads, batch_first=True)
-        self.layernorm = nn.LayerNorm(config.hidden_size, eps=config.layer_norm_eps)
+        self.layernorm = LayerNorm(config.hidden_size, eps=config.layer_norm_eps)
         self.mlp = Siglip2MLP(config)
         self.num_heads = config.num_attention_heads
-
 
 # ---------------------------------------------------------------------------
 # weight packing for the C ABI
 # ---------------------------------------------------------------------------
 
 
+# Flat order of the packed weight tensors: LAYER_FIELDS for every layer,
+# then TOWER_FIELDS, then HEAD_FIELDS when the head is present.
+LAYER_FIELDS = ("qkv_w", "qkv_c1", "qkv_c2", "out_w", "out_b", "fc1_w", "fc1_c1", "fc1_c2", "fc2_w", "fc2_b")
+TOWER_FIELDS = ("patch_w", "patch_b", "pos_table", "post_ln_w", "post_ln_b")
+HEAD_FIELDS = ("head_u", "head_v_w", "head_v_b", "head_o_w", "head_o_b", "head_fc1_w", "head_fc1_c1", "head_fc1_c2",
+               "head_fc2_w", "head_fc2_b")
+# siglip2_config's integer fields, in the order of the dims list
+DIM_FIELDS = ("hidden", "intermediate", "layers", "heads", "head_dim", "patch_dim", "pos_grid", "dtype", "has_head")
+
+
+def weight_structs(dims, eps: float, tensors):
+    """ctypes ``siglip2_config`` / ``siglip2_weights`` (and the layer array
+    they point into) over ``tensors`` in the flat order above.  The structs
+    hold raw pointers: the tensors must outlive every call that uses them."""
+    cfg = L.Config(eps=float(eps), **dict(zip(DIM_FIELDS, (int(d) for d in dims))))
+    n_layers = cfg.layers
+    want = n_layers * len(LAYER_FIELDS) + len(TOWER_FIELDS) + (len(HEAD_FIELDS) if cfg.has_head else 0)
+    if len(tensors) != want:
+        raise ValueError(f"expected {want} packed weight tensors, got {len(tensors)}")
+    ptrs = [t.data_ptr() for t in tensors]
+    layers = (L.LayerWeights * max(1, n_layers))()
+    for i in range(n_layers):
+        layers[i] = L.LayerWeights(*ptrs[i * len(LAYER_FIELDS):(i + 1) * len(LAYER_FIELDS)])
+    rest = ptrs[n_layers * len(LAYER_FIELDS):]
+    w = L.Weights(**dict(zip(TOWER_FIELDS, rest)))
+    w.layers = ctypes.cast(layers, ctypes.POINTER(L.LayerWeights))
+    if cfg.has_head:
+        for name, p in zip(HEAD_FIELDS, rest[len(TOWER_FIELDS):]):
+            setattr(w, name, p)
+    return cfg, w, layers
+
+
 class _Packed:
-    """Device tensors in the layout ``siglip2_weights`` documents, plus the
+    """Device tensors in the layout ``siglip2_weights`` documents (``tensors``,
+    flat in the order of LAYER_FIELDS / TOWER_FIELDS / HEAD_FIELDS), plus the
     ctypes structs pointing at them (kept alive together)."""
 
     def __init__(self, model: "Siglip2SequenceVisionTransformer"):
@@ -163,63 +585,43 @@ class _Packed:
             raise RuntimeError("siglip2_b200 runs on CUDA only: move the model with .to('cuda') first")
         D, I, H = cfg.hidden_size, cfg.intermediate_size, cfg.num_attention_heads
         hd = D // H
-        f32 = torch.float32
-        keep = []
+        ts = []
 
-        def k(t):
-            t = t.contiguous()
-            keep.append(t)
-            return t.data_ptr()
+        def k(*xs):
+            ts.extend(x.detach().contiguous() for x in xs)
 
         with torch.no_grad():
             emb = model.embeddings
-            self.cfg = L.Config(hidden=D, intermediate=I, layers=cfg.num_hidden_layers, heads=H, head_dim=hd,
-                                patch_dim=cfg.num_channels * cfg.patch_size ** 2,
-                                pos_grid=int(round(cfg.num_patches ** 0.5)), eps=float(cfg.layer_norm_eps),
-                                dtype=dtype_code(dt), has_head=int(model.head is not None))
-            layers = (L.LayerWeights * max(1, cfg.num_hidden_layers))()
-            for i, lyr in enumerate(model.encoder.layers):
-                at = lyr.self_attn
-                # q | k | v rows (the fused qkv_proj layout of model_optimized.py), LN1 folded in
-                wp = torch.cat([lin.weight.float() for lin in (at.q_proj, at.k_proj, at.v_proj)], 0)
-                bp = torch.cat([lin.bias.float() for lin in (at.q_proj, at.k_proj, at.v_proj)], 0)
-                wg, c1, c2 = fold_layernorm(wp, bp, lyr.layer_norm1.weight, lyr.layer_norm1.bias, dt)
-                f1, f1c1, f1c2 = fold_layernorm(lyr.mlp.fc1.weight, lyr.mlp.fc1.bias, lyr.layer_norm2.weight,
-                                                lyr.layer_norm2.bias, dt)
-                layers[i] = L.LayerWeights(
-                    qkv_w=k(wg), qkv_c1=k(c1), qkv_c2=k(c2),
-                    out_w=k(at.out_proj.weight.to(dt)), out_b=k(at.out_proj.bias.float()),
-                    fc1_w=k(f1), fc1_c1=k(f1c1), fc1_c2=k(f1c2),
-                    fc2_w=k(lyr.mlp.fc2.weight.to(dt)), fc2_b=k(lyr.mlp.fc2.bias.float()))
-            self.layers = layers
-            w = L.Weights()
-            w.patch_w = k(emb.patch_embedding.weight.to(dt))
-            w.patch_b = k(emb.patch_embedding.bias.float())
-            w.pos_table = k(emb.position_embedding.weight.float())
-            w.layers = ctypes.cast(layers, ctypes.POINTER(L.LayerWeights))
-            w.post_ln_w = k(model.post_layernorm.weight.float())
-            w.post_ln_b = k(model.post_layernorm.bias.float())
+            for lyr in model.encoder.layers:
+                k(*_layer_tensors(lyr))
+            k(emb.patch_embedding.weight.to(dt), emb.patch_embedding.bias.float(),
+              emb.position_embedding.weight.float(), model.post_layernorm.weight.float(),
+              model.post_layernorm.bias.float())
             if model.head is not None:
                 hm = model.head
                 win = hm.attention.in_proj_weight.float()
                 bin_ = hm.attention.in_proj_bias.float()
                 q = win[:D] @ hm.probe.float().reshape(D) + bin_[:D]
                 u = torch.einsum("hd,hdk->hk", q.view(H, hd), win[D:2 * D].view(H, hd, D))
-                u = u * (math.log2(math.e) / math.sqrt(hd))
-                w.head_u = k(u)
-                w.head_v_w = k(win[2 * D:].to(dt))
-                w.head_v_b = k(bin_[2 * D:])
-                w.head_o_w = k(hm.attention.out_proj.weight.to(dt))
-                w.head_o_b = k(hm.attention.out_proj.bias.float())
-                hf1, hc1, hc2 = fold_layernorm(hm.mlp.fc1.weight, hm.mlp.fc1.bias, hm.layernorm.weight,
-                                               hm.layernorm.bias, dt)
-                w.head_fc1_w, w.head_fc1_c1, w.head_fc1_c2 = k(hf1), k(hc1), k(hc2)
-                w.head_fc2_w = k(hm.mlp.fc2.weight.to(dt))
-                w.head_fc2_b = k(hm.mlp.fc2.bias.float())
-            self.w = w
-        self.keep = keep
+                k(u * (math.log2(math.e) / math.sqrt(hd)))
+                k(win[2 * D:].to(dt), bin_[2 * D:])
+                k(hm.attention.out_proj.weight.to(dt), hm.attention.out_proj.bias.float())
+                k(*fold_layernorm(hm.mlp.fc1.weight, hm.mlp.fc1.bias, hm.layernorm.weight, hm.layernorm.bias, dt))
+                k(hm.mlp.fc2.weight.to(dt), hm.mlp.fc2.bias.float())
+        self.dims = [D, I, cfg.num_hidden_layers, H, hd, cfg.num_channels * cfg.patch_size ** 2,
+                     int(round(cfg.num_patches ** 0.5)), dtype_code(dt), int(model.head is not None)]
+        self.eps = float(cfg.layer_norm_eps)
+        self.tensors = ts
+        self.cfg, self.w, self.layers = weight_structs(self.dims, self.eps, ts)
         self.device = dev
         self.dtype = dt
+
+
+def _grids(spatial_shapes) -> np.ndarray:
+    """``[B, 2]`` int32 (h, w) grids on the host (one device read when the
+    shapes live on the GPU)."""
+    t = torch.as_tensor(spatial_shapes).detach().to("cpu", torch.int64)
+    return np.ascontiguousarray(t.numpy(), dtype=np.int32).reshape(-1, 2)
 
 
 def _metadata(hw: np.ndarray, device) -> tuple[torch.Tensor, int, int]:
@@ -236,31 +638,42 @@ def _metadata(hw: np.ndarray, device) -> tuple[torch.Tensor, int, int]:
     return host.to(device, non_blocking=True), n_tok.value, n_tiles.value
 
 
-def tower_forward(packed: _Packed, patches: torch.Tensor, hw: np.ndarray, max_patches: int, want_pooled: bool):
-    """Run ``siglip2_forward``.  ``patches`` packed ``[N, C]`` (max_patches=0)
-    or padded ``[B, P, C]``.  Returns ``(last_hidden_state, pooler_output)``."""
+def run_tower(cfg: L.Config, w: L.Weights, dev, dtype, patches: torch.Tensor, hw: np.ndarray, max_patches: int,
+              want_pooled: bool):
+    """Run ``siglip2_forward`` with the given structs.  ``patches`` packed
+    ``[N, C]`` (max_patches=0) or padded ``[B, P, C]``.  Returns
+    ``(last_hidden_state, pooler_output)`` (the second None unless
+    ``want_pooled``)."""
     lib = L.load()
-    dev = packed.device
-    if patches.device != dev or patches.dtype != packed.dtype:
-        patches = patches.to(device=dev, dtype=packed.dtype)
+    if want_pooled and not cfg.has_head:
+        raise ValueError("pooler_output needs the attention-pooling head")
+    if patches.device != dev or patches.dtype != dtype:
+        patches = patches.to(device=dev, dtype=dtype)
     patches = patches.contiguous()
     B = hw.shape[0]
     meta, N, _ = _metadata(hw, dev)
-    D = packed.cfg.hidden
+    D = cfg.hidden
     if max_patches > 0:
-        last = torch.empty((B, max_patches, D), dtype=packed.dtype, device=dev)
+        if tuple(patches.shape[:2]) != (B, max_patches):
+            raise ValueError(f"pixel_values must be [B, max_patches, C] = [{B}, {max_patches}, C]")
+        last = torch.empty((B, max_patches, D), dtype=dtype, device=dev)
     else:
         if patches.shape[0] != N:
             raise ValueError(f"seq_patches has {patches.shape[0]} rows but token_grids cover {N}")
-        last = torch.empty((N, D), dtype=packed.dtype, device=dev)
-    pooled = torch.empty((B, D), dtype=packed.dtype, device=dev) if want_pooled else None
-    ws_bytes = lib.siglip2_workspace_size(ctypes.byref(packed.cfg), B, N)
+        last = torch.empty((N, D), dtype=dtype, device=dev)
+    pooled = torch.empty((B, D), dtype=dtype, device=dev) if want_pooled else None
+    ws_bytes = lib.siglip2_workspace_size(ctypes.byref(cfg), B, N)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev).cuda_stream
-    L.call("siglip2_forward", ctypes.byref(packed.cfg), ctypes.byref(packed.w), patches.data_ptr(), B, max_patches,
+    L.call("siglip2_forward", ctypes.byref(cfg), ctypes.byref(w), patches.data_ptr(), B, max_patches,
            np.ascontiguousarray(hw, dtype=np.int32).ctypes.data, meta.data_ptr(), last.data_ptr(),
            pooled.data_ptr() if pooled is not None else None, ws.data_ptr(), ws_bytes, stream)
     return last, pooled
+
+
+def tower_forward(packed: _Packed, patches: torch.Tensor, hw: np.ndarray, max_patches: int, want_pooled: bool):
+    """``run_tower`` with a module's packed weights."""
+    return run_tower(packed.cfg, packed.w, packed.device, packed.dtype, patches, hw, max_patches, want_pooled)
 
 
 # ---------------------------------------------------------------------------
@@ -276,7 +689,7 @@ class Siglip2SequenceVisionTransformer(nn.Module):
         self.config = config
         self.embeddings = Siglip2SequenceEmbeddings(config)
         self.encoder = Siglip2Encoder(config)
-        self.post_layernorm = nn.LayerNorm(config.hidden_size, eps=config.layer_norm_eps)
+        self.post_layernorm = LayerNorm(config.hidden_size, eps=config.layer_norm_eps)
         self.head = Siglip2MultiheadAttentionPoolingHead(config) if getattr(config, "vision_use_head", False) else None
         self._packed = None
         self._packed_key = None
@@ -309,6 +722,10 @@ class Siglip2SequenceVisionTransformer(nn.Module):
                 "the reference applies attention dropout in train mode")
 
     # -- forward ----------------------------------------------------------
+    # Opaque to torch.compile: the grids are read on the host and the whole
+    # tower is one library call (torch.ops.siglip2_b200.vision_tower is the
+    # same call as a traceable op).
+    @torch.compiler.disable
     def forward(self, *args, **kwargs):
         self._check_mode()
         if len(args) == 1 and isinstance(args[0], (tuple, list)) and not kwargs:
@@ -326,8 +743,7 @@ class Siglip2SequenceVisionTransformer(nn.Module):
     def forward_packed(self, seq_patches: torch.Tensor, token_grids: torch.Tensor) -> torch.Tensor:
         """``model.py:260-292``: packed rows in, ``[N, D]`` out."""
         pk = self.packed_weights()
-        hw = np.asarray(token_grids.detach().to("cpu", torch.int64).numpy(), dtype=np.int32).reshape(-1, 2)
-        last, _ = tower_forward(pk, seq_patches, hw, 0, False)
+        last, _ = tower_forward(pk, seq_patches, _grids(token_grids), 0, False)
         return last
 
     @torch.no_grad()
@@ -336,7 +752,7 @@ class Siglip2SequenceVisionTransformer(nn.Module):
         ``last_hidden_state [B, P, D]`` (zeros on padded rows) and
         ``pooler_output [B, D]`` (None without a head)."""
         pk = self.packed_weights()
-        hw = np.asarray(spatial_shapes.detach().to("cpu", torch.int64).numpy(), dtype=np.int32).reshape(-1, 2)
+        hw = _grids(spatial_shapes)
         B, P = pixel_values.shape[:2]
         lens = hw[:, 0].astype(np.int64) * hw[:, 1]
         if attention_mask is not None:
@@ -357,5 +773,5 @@ class Siglip2SequenceVisionTransformerOptimized(Siglip2SequenceVisionTransformer
     """Same module under the name of ``optimized_siglip2/model_optimized.py:341``."""
 
 
-# HF / BASELINE name of the tower
+# the transformers name of the tower
 Siglip2VisionTransformer = Siglip2SequenceVisionTransformer

@@ -151,6 +151,18 @@ def rowsums_reference(x: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def rowsums(x: torch.Tensor) -> torch.Tensor:
+    """``siglip2_rowsums``: row sums of ``x [M, K]`` in the slot layout the
+    LayerNorm-folded GEMMs read (``[M, rowsum_slots(dtype, K), 2]`` float32)."""
+    _need_cuda(x)
+    assert x.dim() == 2 and x.stride(1) == 1
+    M, K = x.shape
+    out = torch.empty((M, rowsum_slots(x.dtype, K), 2), dtype=torch.float32, device=x.device)
+    L.call("siglip2_rowsums", dtype_code(x.dtype), x.data_ptr(), x.stride(0), M, K, out.data_ptr(),
+           _stream(x.device))
+    return out
+
+
 def gemm_rowsums(a: torch.Tensor, w: torch.Tensor, epilogue: int, bias=None, res=None, c1=None, c2=None,
                  eps: float = 1e-6, rs_in=None, rs_acc=None,
                  out: torch.Tensor | None = None) -> torch.Tensor:

@@ -1,0 +1,175 @@
+"""The kernels as ``torch.library`` custom ops, namespace ``siglip2_b200``.
+
+Each op runs one C-ABI entry point of ``libsiglip2_b200.so`` on the current
+CUDA stream.  Only a CUDA kernel is registered: called with CPU tensors the
+ops raise, there is no CPU implementation.  Every op has a shape-only fake
+implementation, so ``torch.compile`` / ``torch.export`` trace through the
+module forwards instead of breaking the graph there.  This is the mechanism
+the reference uses for its Triton LayerNorm
+(``optimized_siglip2/ops/layer_norm.py:19-75,425-429``).
+
+Ops (``torch.ops.siglip2_b200.<name>``):
+  gemm, gemm_rowsums, rowsums  -- tensor-core GEMMs with fused epilogues
+  fmha_varlen                  -- per-image attention over packed rows
+  layernorm                    -- LayerNorm over the last dimension
+  token_image, patch_embed     -- patch Linear + resized position grid
+  vision_tower                 -- the whole tower (``siglip2_forward``)
+
+No autograd formula is registered: the ops are inference kernels, and
+back-propagating through one raises.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import numpy as np
+import torch
+from torch import Tensor
+
+from . import _lib as L
+from . import ops
+
+_TORCH_DT = {L.DTYPE_F32: torch.float32, L.DTYPE_BF16: torch.bfloat16, L.DTYPE_F16: torch.float16}
+
+
+def _slots(dtype: torch.dtype, width: int) -> int:
+    return ops.rowsum_slots(dtype, width)
+
+
+# --------------------------------------------------------------------------- gemm
+@torch.library.custom_op("siglip2_b200::gemm", mutates_args=(), device_types="cuda")
+def gemm(a: Tensor, w: Tensor, epilogue: int, bias: Optional[Tensor], res: Optional[Tensor], c1: Optional[Tensor],
+         c2: Optional[Tensor], eps: float) -> Tensor:
+    """``epilogue(a @ w.T)`` (``siglip2_gemm``); a [M, K], w [N, K]."""
+    return ops.gemm(a, w, epilogue, bias, res, c1, c2, eps)
+
+
+@gemm.register_fake
+def _(a, w, epilogue, bias, res, c1, c2, eps):
+    return a.new_empty((a.shape[0], w.shape[0]))
+
+
+@torch.library.custom_op("siglip2_b200::gemm_rowsums", mutates_args=(), device_types="cuda")
+def gemm_rowsums(a: Tensor, w: Tensor, epilogue: int, bias: Optional[Tensor], res: Optional[Tensor],
+                 c1: Optional[Tensor], c2: Optional[Tensor], eps: float, rs_in: Optional[Tensor],
+                 produce_rowsums: bool) -> tuple[Tensor, Tensor]:
+    """``siglip2_gemm_rowsums``: returns ``(out [M, N], rs)`` where ``rs`` is
+    the ``[M, slots(N), 2]`` row sums of ``out`` when ``produce_rowsums``
+    (the epilogue must be a row-sum one), else an empty tensor."""
+    M, N = a.shape[0], w.shape[0]
+    rs = (torch.empty((M, _slots(a.dtype, N), 2), dtype=torch.float32, device=a.device) if produce_rowsums
+          else torch.empty(0, dtype=torch.float32, device=a.device))
+    out = ops.gemm_rowsums(a, w, epilogue, bias, res, c1, c2, eps, rs_in, rs if produce_rowsums else None)
+    return out, rs
+
+
+@gemm_rowsums.register_fake
+def _(a, w, epilogue, bias, res, c1, c2, eps, rs_in, produce_rowsums):
+    M, N = a.shape[0], w.shape[0]
+    rs_shape = (M, _slots(a.dtype, N), 2) if produce_rowsums else (0,)
+    return a.new_empty((M, N)), a.new_empty(rs_shape, dtype=torch.float32)
+
+
+@torch.library.custom_op("siglip2_b200::rowsums", mutates_args=(), device_types="cuda")
+def rowsums(x: Tensor) -> Tensor:
+    """``siglip2_rowsums``: ``[M, slots(K), 2]`` row sums of ``x [M, K]``."""
+    return ops.rowsums(x)
+
+
+@rowsums.register_fake
+def _(x):
+    return x.new_empty((x.shape[0], _slots(x.dtype, x.shape[1]), 2), dtype=torch.float32)
+
+
+# --------------------------------------------------------------------------- attention
+@torch.library.custom_op("siglip2_b200::fmha_varlen", mutates_args=(), device_types="cuda")
+def fmha_varlen(qkv: Tensor, cu_seqlens: Tensor, tiles: Tensor, heads: int, head_dim: int) -> Tensor:
+    """``siglip2_fmha_varlen``: qkv [N, 3*heads*head_dim] -> [N, heads*head_dim]."""
+    return ops.fmha_varlen(qkv, cu_seqlens, tiles, heads, head_dim)
+
+
+@fmha_varlen.register_fake
+def _(qkv, cu_seqlens, tiles, heads, head_dim):
+    return qkv.new_empty((qkv.shape[0], heads * head_dim))
+
+
+# --------------------------------------------------------------------------- row ops
+@torch.library.custom_op("siglip2_b200::layernorm", mutates_args=(), device_types="cuda")
+def layernorm(x: Tensor, weight: Tensor, bias: Tensor, eps: float) -> Tensor:
+    """``siglip2_layernorm`` over the last dimension; weight/bias float32."""
+    return ops.layernorm(x.contiguous(), weight, bias, eps)
+
+
+@layernorm.register_fake
+def _(x, weight, bias, eps):
+    return torch.empty_like(x, memory_format=torch.contiguous_format)
+
+
+@torch.library.custom_op("siglip2_b200::token_image", mutates_args=(), device_types="cuda")
+def token_image(cu_seqlens: Tensor, n_tokens: int) -> Tensor:
+    """``siglip2_token_image``: int32 image index of each packed token."""
+    return ops.token_image(cu_seqlens, n_tokens)
+
+
+@token_image.register_fake
+def _(cu_seqlens, n_tokens):
+    return cu_seqlens.new_empty((n_tokens,), dtype=torch.int32)
+
+
+@torch.library.custom_op("siglip2_b200::patch_embed", mutates_args=(), device_types="cuda")
+def patch_embed(patches: Tensor, w: Tensor, bias: Tensor, table: Tensor, hw: Tensor, cu_seqlens: Tensor,
+                tok_img: Tensor) -> Tensor:
+    """``siglip2_patch_embed``: ``patches @ w.T + bias + resize(table)`` [N, D]."""
+    return ops.patch_embed(patches, w, bias, table, hw, cu_seqlens, tok_img)
+
+
+@patch_embed.register_fake
+def _(patches, w, bias, table, hw, cu_seqlens, tok_img):
+    return patches.new_empty((patches.shape[0], w.shape[0]))
+
+
+# --------------------------------------------------------------------------- whole tower
+_STRUCTS: dict = {}
+
+
+def _structs_for(dims, eps, weights):
+    """ctypes structs over ``weights``, cached by their addresses (a few
+    entries): rebuilding them costs more than the launch sequence."""
+    from .model import weight_structs
+    key = (tuple(dims), float(eps), tuple(t.data_ptr() for t in weights))
+    hit = _STRUCTS.get(key)
+    if hit is None:
+        if len(_STRUCTS) >= 4:
+            _STRUCTS.pop(next(iter(_STRUCTS)))
+        hit = _STRUCTS[key] = weight_structs(dims, eps, weights)
+    return hit
+
+
+@torch.library.custom_op("siglip2_b200::vision_tower", mutates_args=(), device_types="cuda")
+def vision_tower(patches: Tensor, hw: Tensor, max_patches: int, want_pooled: bool, weights: list[Tensor],
+                 dims: list[int], eps: float) -> tuple[Tensor, Tensor]:
+    """``siglip2_forward``.  ``patches`` packed [N, C] (max_patches = 0) or
+    padded [B, max_patches, C]; ``hw`` the [B, 2] grids (read on the host);
+    ``weights`` the packed tensors in the flat order of
+    ``model.LAYER_FIELDS`` / ``TOWER_FIELDS`` / ``HEAD_FIELDS``; ``dims`` the
+    integer fields of ``siglip2_config`` (``model.DIM_FIELDS``).  Returns
+    ``(last_hidden_state, pooler_output)``; the second is empty when
+    ``want_pooled`` is false."""
+    from .model import run_tower
+    cfg, w, _ = _structs_for(dims, eps, weights)
+    hw_np = np.ascontiguousarray(hw.detach().to("cpu", torch.int32).numpy()).reshape(-1, 2)
+    last, pooled = run_tower(cfg, w, patches.device, _TORCH_DT[int(dims[7])], patches, hw_np, max_patches,
+                             want_pooled)
+    if pooled is None:
+        pooled = last.new_empty((0, int(dims[0])))
+    return last, pooled
+
+
+@vision_tower.register_fake
+def _(patches, hw, max_patches, want_pooled, weights, dims, eps):
+    D, dt = int(dims[0]), _TORCH_DT[int(dims[7])]
+    B = hw.shape[0]
+    shape = (patches.shape[0], D) if max_patches == 0 else (B, max_patches, D)
+    last = patches.new_empty(shape, dtype=dt)
+    pooled = patches.new_empty((B, D) if want_pooled else (0, D), dtype=dt)
+    return last, pooled
