@@ -38,7 +38,10 @@ def _ref_attn(q, k, v, lens, H, hd):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("H,hd", [(16, 72), (12, 64), (16, 96), (2, 72)])
-@pytest.mark.parametrize("lens", [[1, 7, 129, 300, 1024, 128, 256, 65], [576], [900, 3, 1000]])
+@pytest.mark.parametrize("lens", [[1, 7, 129, 300, 1024, 128, 256, 65], [576], [900, 3, 1000],
+                                  # an image's last key tile ends on / just past 16-key chunks, and its last
+                                  # query tile ends on / just past 32-row warps
+                                  [16, 17, 31, 32, 33, 48, 95, 97, 112, 113, 160, 161, 191, 192, 193, 224, 225]])
 def test_fmha_varlen(dtype, H, hd, lens):
     g = torch.Generator(device="cuda").manual_seed(sum(lens) + hd)
     N = sum(lens)
