@@ -158,6 +158,36 @@ int siglip2_patch_embed(int dtype, const void* patches_dev, int patch_dim, const
 int siglip2_layernorm(int dtype, const void* x_dev, void* y_dev, const float* gamma_dev, const float* beta_dev,
                       int rows, int D, float eps, const int* cu_seqlens_dev, int max_patches, void* stream);
 
+/* Patch grid (grid_h, grid_w) of a height x width image under a budget of
+ * max_patches patches of patch x patch pixels: the largest scale whose
+ * patch-rounded size fits, found by the binary search of transformers'
+ * get_image_size_for_max_num_patches (models/siglip2/image_processing_siglip2.py),
+ * restated step for step so that the grids agree exactly. Host only. */
+int siglip2_image_grid(int height, int width, int patch, int max_patches, int* grid_h, int* grid_w);
+
+/* The preprocessing in front of the tower (transformers Siglip2ImageProcessor,
+ * torchvision backend, image_processing_siglip2.py _preprocess): for image b,
+ * uint8 pixels at images_dev + offsets_dev[b], channels first (C x H x W) or
+ * channels last (H x W x C), source size src_hw[2b], src_hw[2b+1]:
+ *   - resize to (grid_h * patch, grid_w * patch) with antialiased bilinear
+ *     filtering and round half to even (torchvision's resize of a uint8 CUDA
+ *     tensor), skipped when the size already matches; downscaling by more
+ *     than 19x per axis is rejected;
+ *   - normalise channel c to (x - mean[c]) / std_dev_values[c] in fp32, where
+ *     mean and std are in uint8 units (image_mean / rescale_factor, e.g. 127.5);
+ *   - write patch (y, x) as row y * grid_w + x of pixel_values [batch,
+ *     max_patches, patch * patch * channels] (element (py, px, c) at
+ *     (py * patch + px) * channels + c, in dtype), rows past grid_h * grid_w
+ *     zero, and mask [batch, max_patches] int32 = 1 for the valid rows.
+ * Sizes and grids are passed twice: on the host (checks, shared-memory size)
+ * and on the device (read by the kernel). channels 1..4, patch <= 32,
+ * patch * patch * channels a multiple of 8, pixel_values 16-byte aligned.
+ * One launch; HBM-bound without a resize. */
+int siglip2_patchify(int dtype, const uint8_t* images_dev, const long long* offsets_dev, const int* src_hw_host,
+                     const int* src_hw_dev, const int* grid_hw_host, const int* grid_hw_dev, int batch, int channels,
+                     int patch, int channels_last, const float* mean, const float* std_dev_values, int max_patches,
+                     void* pixel_values_dev, int* mask_dev, void* stream);
+
 /* tok_img[t] = image index of packed token t (cu_seqlens_dev has B+1 entries). */
 int siglip2_token_image(const int* cu_seqlens_dev, int B, int N, int* tok_img_dev, void* stream);
 

@@ -34,6 +34,9 @@ SIGNATURES = {
                                      _vp, _vp]),
     "siglip2_layernorm": (_c_int, [_c_int, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_float, _vp, _c_int, _vp]),
     "siglip2_token_image": (_c_int, [_vp, _c_int, _c_int, _vp, _vp]),
+    "siglip2_image_grid": (_c_int, [_c_int, _c_int, _c_int, _c_int, _vp, _vp]),
+    "siglip2_patchify": (_c_int, [_c_int, _vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp,
+                                  _c_int, _vp, _vp, _vp]),
     "siglip2_posemb": (_c_int, [_c_int, _vp, _c_int, _c_int, _vp, _vp, _vp, _c_int, _vp, _vp]),
     "siglip2_fmha_varlen": (_c_int, [_c_int, _vp, _c_int, _vp, _vp, _c_int, _c_int, _c_int, _vp, _c_int, _vp]),
     "siglip2_padded_head_dim": (_c_int, [_c_int]),

@@ -2,6 +2,7 @@
 // One translation unit: every kernel header is included here and compiled
 // for sm_100a only.
 #include <algorithm>
+#include <cmath>
 #include <type_traits>
 #include <vector>
 
@@ -11,6 +12,7 @@
 #include "fmha.cuh"
 #include "forward.cuh"
 #include "simt_f32.cuh"
+#include "patchify.cuh"
 
 using namespace sg;
 
@@ -323,6 +325,126 @@ int sg_rowsums_impl(int dtype, const void* x, int ldx, int M, int K, float2* rs,
   }
   SG_LAUNCH_CHECK();
   return SIGLIP2_OK;
+}
+
+// ---------------------------------------------------------------------------
+// image -> patch rows (preprocessing in front of the tower)
+// ---------------------------------------------------------------------------
+// Patch grid of an H x W image under a patch budget: the binary search over a
+// scale factor of transformers' get_image_size_for_max_num_patches
+// (models/siglip2/image_processing_siglip2.py), in the same double-precision
+// steps so that the grids agree exactly.
+static int sg_scaled_side(double scale, int size, int patch) {
+  double s = static_cast<double>(size) * scale;
+  s = std::ceil(s / patch) * patch;
+  if (s < patch) s = patch;
+  return static_cast<int>(s);
+}
+
+int sg_image_grid(int H, int W, int patch, int max_patches, int* h, int* w) {
+  SG_CHECK_ARG(H > 0 && W > 0 && patch > 0 && max_patches > 0 && h && w, "bad image_grid arguments");
+  const double eps = 1e-5;
+  double lo = eps / 10, hi = 100.0;
+  while (hi - lo >= eps) {
+    const double mid = (lo + hi) / 2;
+    const int th = sg_scaled_side(mid, H, patch), tw = sg_scaled_side(mid, W, patch);
+    const double n = (static_cast<double>(th) / patch) * (static_cast<double>(tw) / patch);
+    if (n <= max_patches) lo = mid;
+    else hi = mid;
+  }
+  *h = sg_scaled_side(lo, H, patch) / patch;
+  *w = sg_scaled_side(lo, W, patch) / patch;
+  return SIGLIP2_OK;
+}
+
+template <typename T>
+int launch_patchify(const PatchifyArgs& a, bool fast, bool any_resize, size_t smem, long long n_rows, void* out,
+                    int* mask, cudaStream_t s) {
+  T* o = static_cast<T*>(out);
+  if (fast) {
+    int dev = 0, sms = 148;
+    SG_CUDA(cudaGetDevice(&dev));
+    SG_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const long long blocks = std::min<long long>((n_rows + 7) / 8, 8ll * sms);  // 8 CTAs of 8 warps per SM
+    patchify16x3_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, s>>>(a, o, mask);
+    SG_LAUNCH_CHECK();
+    if (!any_resize) return SIGLIP2_OK;
+    SG_CUDA(cudaFuncSetAttribute(patchify_kernel<T, 3, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(smem)));
+    patchify_kernel<T, 3, 16><<<static_cast<unsigned>(n_rows), kPatchifyThreads, smem, s>>>(a, o, mask);
+  } else {
+    SG_CUDA(cudaFuncSetAttribute(patchify_kernel<T, 0, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(smem)));
+    patchify_kernel<T, 0, 0><<<static_cast<unsigned>(n_rows), kPatchifyThreads, smem, s>>>(a, o, mask);
+  }
+  SG_LAUNCH_CHECK();
+  return SIGLIP2_OK;
+}
+
+int sg_patchify_impl(int dtype, const uint8_t* images, const long long* offsets_dev, const int* src_hw_host,
+                     const int* src_hw_dev, const int* grid_hw_host, const int* grid_hw_dev, int B, int C, int patch,
+                     int channels_last, const float* mean, const float* stdv, int max_patches, void* out, int* mask,
+                     cudaStream_t s) {
+  SG_CHECK_ARG(images && offsets_dev && src_hw_host && src_hw_dev && grid_hw_host && grid_hw_dev && mean && stdv &&
+                   out && mask && B > 0 && max_patches > 0,
+               "bad patchify arguments");
+  SG_CHECK_ARG(C >= 1 && C <= 4, "patchify: 1 to 4 channels (got %d)", C);
+  SG_CHECK_ARG(patch >= 1 && patch <= kPatchifyMaxPatch, "patchify: patch side 1..%d (got %d)", kPatchifyMaxPatch,
+               patch);
+  SG_CHECK_ARG((patch * patch * C) % 8 == 0, "patchify: patch * patch * channels must be a multiple of 8");
+  if (!aligned16(out)) return set_error(SIGLIP2_ERR_ALIGN, "pixel_values must be 16-byte aligned");
+  PatchifyArgs a{};
+  a.images = images;
+  a.offsets = offsets_dev;
+  a.src_hw = src_hw_dev;
+  a.grid_hw = grid_hw_dev;
+  a.batch = B;
+  a.channels = C;
+  a.patch = patch;
+  a.channels_last = channels_last ? 1 : 0;
+  a.max_patches = max_patches;
+  int rows = 1;
+  for (int b = 0; b < B; ++b) {
+    const int H = src_hw_host[2 * b], W = src_hw_host[2 * b + 1];
+    const int h = grid_hw_host[2 * b], w = grid_hw_host[2 * b + 1];
+    SG_CHECK_ARG(H > 0 && W > 0 && h > 0 && w > 0, "patchify: image %d has an empty size or grid", b);
+    if (static_cast<long long>(h) * w > max_patches)
+      return set_error(SIGLIP2_ERR_SHAPE, "patchify: image %d grid %dx%d exceeds %d patches", b, h, w, max_patches);
+    const double sy = static_cast<double>(H) / (h * patch), sx = static_cast<double>(W) / (w * patch);
+    // taps per axis <= 2 * max(scale, 1) + 2
+    if (2 * std::max(sy, 1.0) + 2 > kPatchifyMaxTaps || 2 * std::max(sx, 1.0) + 2 > kPatchifyMaxTaps)
+      return set_error(SIGLIP2_ERR_UNSUPPORTED, "patchify: image %d is downscaled more than %dx", b,
+                       (kPatchifyMaxTaps - 2) / 2);
+    if (H != h * patch || W != w * patch)  // source rows under one patch row: p output rows plus the filter reach
+      rows = std::max(rows, static_cast<int>(std::ceil(sy * (patch - 1) + 2 * std::max(sy, 1.0))) + 3);
+  }
+  rows = std::min(rows, 1 << 20);
+  a.max_rows = rows;
+  for (int c = 0; c < 4; ++c) {
+    a.mean[c] = c < C ? mean[c] : 0.f;
+    a.stdv[c] = c < C ? stdv[c] : 1.f;
+  }
+  const size_t smem = (2 * patch * kPatchifyMaxTaps) * sizeof(float) + 4 * patch * sizeof(int) +
+                      static_cast<size_t>(rows) * patch * C * sizeof(float);
+  if (smem > static_cast<size_t>(kSmemLimit))
+    return set_error(SIGLIP2_ERR_UNSUPPORTED, "patchify: %zu bytes of shared memory needed", smem);
+  // 3 x 16 x 16: a warp-per-row kernel for the padded rows and the images
+  // already at their grid size, then the resize kernel for the others (if
+  // any); other shapes: the general kernel for every row
+  const bool fast = C == 3 && patch == 16;
+  bool any_resize = false;
+  for (int b = 0; b < B; ++b)
+    any_resize = any_resize || src_hw_host[2 * b] != grid_hw_host[2 * b] * patch ||
+                 src_hw_host[2 * b + 1] != grid_hw_host[2 * b + 1] * patch;
+  const long long n_rows = static_cast<long long>(B) * max_patches;
+  if (n_rows > (1ll << 31) - 8) return set_error(SIGLIP2_ERR_SHAPE, "patchify: too many rows");
+  a.resize_only = fast ? 1 : 0;
+  switch (dtype) {
+    case SIGLIP2_BF16: return launch_patchify<__nv_bfloat16>(a, fast, any_resize, smem, n_rows, out, mask, s);
+    case SIGLIP2_F16: return launch_patchify<__half>(a, fast, any_resize, smem, n_rows, out, mask, s);
+    case SIGLIP2_F32: return launch_patchify<float>(a, fast, any_resize, smem, n_rows, out, mask, s);
+    default: return set_error(SIGLIP2_ERR_ARG, "unknown dtype %d", dtype);
+  }
 }
 
 int sg_token_image_impl(const int* cu, int B, int N, int* tok_img, cudaStream_t s) {
@@ -737,6 +859,19 @@ int siglip2_layernorm(int dtype, const void* x_dev, void* y_dev, const float* ga
                       int rows, int D, float eps, const int* cu_seqlens_dev, int max_patches, void* stream) {
   return sg_layernorm_impl(dtype, x_dev, y_dev, gamma_dev, beta_dev, rows, D, eps, cu_seqlens_dev, max_patches,
                            static_cast<cudaStream_t>(stream));
+}
+
+int siglip2_image_grid(int height, int width, int patch, int max_patches, int* grid_h, int* grid_w) {
+  return sg_image_grid(height, width, patch, max_patches, grid_h, grid_w);
+}
+
+int siglip2_patchify(int dtype, const uint8_t* images_dev, const long long* offsets_dev, const int* src_hw_host,
+                     const int* src_hw_dev, const int* grid_hw_host, const int* grid_hw_dev, int batch, int channels,
+                     int patch, int channels_last, const float* mean, const float* std_dev_values, int max_patches,
+                     void* pixel_values_dev, int* mask_dev, void* stream) {
+  return sg_patchify_impl(dtype, images_dev, offsets_dev, src_hw_host, src_hw_dev, grid_hw_host, grid_hw_dev, batch,
+                          channels, patch, channels_last, mean, std_dev_values, max_patches, pixel_values_dev,
+                          mask_dev, static_cast<cudaStream_t>(stream));
 }
 
 int siglip2_token_image(const int* cu_seqlens_dev, int B, int N, int* tok_img_dev, void* stream) {

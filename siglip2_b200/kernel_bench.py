@@ -4,6 +4,7 @@ command the ncu summaries under ``profiles/`` were captured with.
     python -m siglip2_b200.kernel_bench gemm --epi ln_gelu --m 39178 --n 4304 --k 1152
     python -m siglip2_b200.kernel_bench fmha --preset so400m --images 64 --max-patches 1024
     python -m siglip2_b200.kernel_bench layer --preset so400m --images 64 --max-patches 1024
+    python -m siglip2_b200.kernel_bench patchify --images 64 --height 768 --width 1024 --max-patches 1024
 
 Prints one JSON line per measurement: milliseconds per launch, the
 algorithmic TFLOP/s (dense contractions only) and the median SM clock seen
@@ -110,6 +111,44 @@ def bench_layer(preset, images, max_patches, reps):
     return out
 
 
+def bench_patchify(images: int, height: int, width: int, max_patches: int, reps: int, warmup: int = 3,
+                   channels_last: bool = True) -> dict:
+    """``siglip2_patchify`` on ``images`` random uint8 images of one size
+    already on the device (the kernel alone: the grids are computed and the
+    metadata uploaded once).  HBM bytes: the uint8 source read once plus the
+    bf16 ``pixel_values`` written."""
+    import ctypes as ct
+
+    import numpy as np
+
+    from .image_processor import image_grid
+    g = torch.Generator(device="cuda").manual_seed(0)
+    shape = (images, height, width, 3) if channels_last else (images, 3, height, width)
+    pix = torch.randint(0, 256, shape, dtype=torch.uint8, device="cuda", generator=g)
+    gh, gw = image_grid(height, width, 16, max_patches)
+    src = np.tile(np.array([height, width], dtype=np.int32), images)
+    grid = np.tile(np.array([gh, gw], dtype=np.int32), images)
+    offs = np.arange(images, dtype=np.int64) * (height * width * 3)
+    meta = torch.from_numpy(np.concatenate([offs.view(np.int32), src, grid])).cuda()
+    out = torch.empty((images, max_patches, 768), dtype=torch.bfloat16, device="cuda")
+    mask = torch.empty((images, max_patches), dtype=torch.int32, device="cuda")
+    mean = np.full(3, 127.5, dtype=np.float32)
+    std = np.full(3, 127.5, dtype=np.float32)
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def run():
+        L.call("siglip2_patchify", L.DTYPE_BF16, pix.data_ptr(), meta.data_ptr(), src.ctypes.data,
+               meta[2 * images:].data_ptr(), grid.ctypes.data, meta[4 * images:].data_ptr(), images, 3, 16,
+               int(channels_last), mean.ctypes.data, std.ctypes.data, max_patches, out.data_ptr(),
+               mask.data_ptr(), ct.c_void_p(stream))
+
+    ms = _time(run, reps, warmup)
+    nbytes = pix.numel() + out.numel() * 2 + mask.numel() * 4
+    return {"kernel": "patchify", "images": images, "src": [height, width], "grid": [gh, gw],
+            "max_patches": max_patches, "resize": (gh * 16, gw * 16) != (height, width), "ms": ms,
+            "gbs": nbytes / ms / 1e6, **_LAST_CLOCK}
+
+
 def main():
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -134,6 +173,15 @@ def main():
     y.add_argument("--reps", type=int, default=20)
     for sp in (g, f, y):
         sp.add_argument("--variant", type=int, default=0, help="GEMM kernel: 0 auto, 1 one SM, 2 SM pairs")
+    pz = sub.add_parser("patchify")
+    pz.add_argument("--images", type=int, default=64)
+    pz.add_argument("--height", type=int, default=512)
+    pz.add_argument("--width", type=int, default=512)
+    pz.add_argument("--max-patches", type=int, default=1024)
+    pz.add_argument("--channels-first", action="store_true")
+    pz.add_argument("--reps", type=int, default=20)
+    pz.add_argument("--warmup", type=int, default=3)
+    pz.add_argument("--variant", type=int, default=0)
     a = ap.parse_args()
     L.check(L.load().siglip2_set_gemm_variant(a.variant))
     if a.cmd == "gemm":
@@ -141,6 +189,9 @@ def main():
             if epi not in EPIS:
                 raise SystemExit(f"unknown epilogue {epi!r}")
             print(json.dumps(bench_gemm(a.m, a.n, a.k, epi, a.reps, warmup=a.warmup, cublas=a.cublas)))
+    elif a.cmd == "patchify":
+        print(json.dumps(bench_patchify(a.images, a.height, a.width, a.max_patches, a.reps, a.warmup,
+                                        channels_last=not a.channels_first)))
     elif a.cmd == "fmha":
         print(json.dumps(bench_fmha(a.preset, a.images, a.max_patches, a.reps, warmup=a.warmup)))
     else:
