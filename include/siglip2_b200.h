@@ -188,6 +188,16 @@ int siglip2_patchify(int dtype, const uint8_t* images_dev, const long long* offs
                      int patch, int channels_last, const float* mean, const float* std_dev_values, int max_patches,
                      void* pixel_values_dev, int* mask_dev, void* stream);
 
+/* y[r] = scale * x[r] / ||x[r]||_2 for rows r < rows of width D (fp32 sum of
+ * squares; an all-zero row gives zeros).  The embedding normalisation before
+ * the image-text logits of transformers' Siglip2Model.forward
+ * (models/siglip2/modeling_siglip2.py:964-972), with exp(logit_scale) passed
+ * as scale for one side; the logits are then one siglip2_gemm with the bias
+ * epilogue (bias = logit_bias).  x, y 16-byte aligned; D, ldx, ldy multiples
+ * of 8 (bf16, f16) or 4 (f32). */
+int siglip2_l2_normalize(int dtype, const void* x_dev, int ldx, int rows, int D, float scale, void* y_dev, int ldy,
+                         void* stream);
+
 /* tok_img[t] = image index of packed token t (cu_seqlens_dev has B+1 entries). */
 int siglip2_token_image(const int* cu_seqlens_dev, int B, int N, int* tok_img_dev, void* stream);
 

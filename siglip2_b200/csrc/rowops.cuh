@@ -1,7 +1,9 @@
 // Bandwidth-bound row kernels: the stand-alone LayerNorm (post_layernorm,
-// whose output is last_hidden_state) and the per-image antialiased resize of
-// the learned position grid.  Both move 16 bytes per thread per access
-// (8 x bf16/f16, 4 x f32) and reduce with warp shuffles.
+// whose output is last_hidden_state), the per-image antialiased resize of
+// the learned position grid, LayerNorm row sums for rows no GEMM produced,
+// and the L2 normalisation of embeddings before the image-text logits.  They
+// move 16 bytes per thread per access (8 x bf16/f16, 4 x f32) and reduce
+// with warp shuffles.
 #pragma once
 
 #include "ptx.cuh"
@@ -219,6 +221,37 @@ __global__ void token_image_kernel(const int* __restrict__ cu, int B, int N, int
     if (cu[mid] <= t) lo = mid; else hi = mid;
   }
   tok_img[t] = lo;
+}
+
+// y[r] = scale * x[r] / ||x[r]||_2 (fp32 sum of squares, one rounding to T;
+// an all-zero row gives zeros).  One warp per row, 16-byte accesses; D, ldx
+// and ldy multiples of the vector width, x and y 16-byte aligned.  The
+// normalisation of the embeddings before the image-text logits.
+template <typename T>
+__global__ void __launch_bounds__(256) l2norm_kernel(const T* __restrict__ x, int ldx, int rows, int D, float scale,
+                                                     T* __restrict__ y, int ldy) {
+  constexpr int V = Vec16<T>::N;
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const T* xr = x + static_cast<size_t>(row) * ldx;
+  float ss = 0.f;
+  for (int c = lane * V; c < D; c += 32 * V) {
+    float f[V];
+    load_vec(xr + c, f);
+#pragma unroll
+    for (int i = 0; i < V; ++i) ss = fmaf(f[i], f[i], ss);
+  }
+  ss = warp_sum(ss);
+  const float k = ss > 0.f ? scale / sqrtf(ss) : 0.f;
+  T* yr = y + static_cast<size_t>(row) * ldy;
+  for (int c = lane * V; c < D; c += 32 * V) {
+    float f[V];
+    load_vec(xr + c, f);
+#pragma unroll
+    for (int i = 0; i < V; ++i) f[i] *= k;
+    store_vec(yr + c, f);
+  }
 }
 
 // Row sums in the slot layout the LayerNorm-folded GEMMs read: for row r and

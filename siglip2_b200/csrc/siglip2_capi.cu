@@ -447,6 +447,24 @@ int sg_patchify_impl(int dtype, const uint8_t* images, const long long* offsets_
   }
 }
 
+int sg_l2_normalize_impl(int dtype, const void* x, int ldx, int rows, int D, float scale, void* y, int ldy,
+                         cudaStream_t s) {
+  SG_CHECK_ARG(x && y && rows >= 0 && D > 0 && ldx >= D && ldy >= D, "bad l2_normalize arguments");
+  const int v = dtype == SIGLIP2_F32 ? 4 : 8;
+  if (!aligned16(x) || !aligned16(y) || D % v || ldx % v || ldy % v)
+    return set_error(SIGLIP2_ERR_ALIGN, "l2_normalize: 16-byte aligned rows, D and strides multiples of %d", v);
+  if (rows == 0) return SIGLIP2_OK;
+  const dim3 grid((rows + 7) / 8);
+  switch (dtype) {
+    case SIGLIP2_BF16: l2norm_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), ldx, rows, D, scale, static_cast<__nv_bfloat16*>(y), ldy); break;
+    case SIGLIP2_F16: l2norm_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(x), ldx, rows, D, scale, static_cast<__half*>(y), ldy); break;
+    case SIGLIP2_F32: l2norm_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(x), ldx, rows, D, scale, static_cast<float*>(y), ldy); break;
+    default: return set_error(SIGLIP2_ERR_ARG, "unknown dtype %d", dtype);
+  }
+  SG_LAUNCH_CHECK();
+  return SIGLIP2_OK;
+}
+
 int sg_token_image_impl(const int* cu, int B, int N, int* tok_img, cudaStream_t s) {
   if (N == 0) return SIGLIP2_OK;
   token_image_kernel<<<(N + 255) / 256, 256, 0, s>>>(cu, B, N, tok_img);
@@ -872,6 +890,11 @@ int siglip2_patchify(int dtype, const uint8_t* images_dev, const long long* offs
   return sg_patchify_impl(dtype, images_dev, offsets_dev, src_hw_host, src_hw_dev, grid_hw_host, grid_hw_dev, batch,
                           channels, patch, channels_last, mean, std_dev_values, max_patches, pixel_values_dev,
                           mask_dev, static_cast<cudaStream_t>(stream));
+}
+
+int siglip2_l2_normalize(int dtype, const void* x_dev, int ldx, int rows, int D, float scale, void* y_dev, int ldy,
+                         void* stream) {
+  return sg_l2_normalize_impl(dtype, x_dev, ldx, rows, D, scale, y_dev, ldy, static_cast<cudaStream_t>(stream));
 }
 
 int siglip2_token_image(const int* cu_seqlens_dev, int B, int N, int* tok_img_dev, void* stream) {
