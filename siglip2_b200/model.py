@@ -217,6 +217,13 @@ def _rows(x: torch.Tensor, dtype) -> torch.Tensor:
     return (x2 if x2.dtype == dtype else x2.to(dtype)).contiguous()
 
 
+def _needs_grad(module: nn.Module, *xs) -> bool:
+    """Autograd is recording something: the forward then passes the live
+    parameters (the ops' backward reaches them) instead of the cached copies."""
+    return torch.is_grad_enabled() and (any(x is not None and x.requires_grad for x in xs)
+                                        or any(p.requires_grad for p in module.parameters()))
+
+
 def _check_inference(module: nn.Module, dropout: float):
     if module.training and dropout > 0:
         raise NotImplementedError("siglip2_b200 implements inference only: call .eval() (or set "
@@ -228,7 +235,10 @@ class LayerNorm(nn.LayerNorm):
     ``siglip2_layernorm``: fp32 statistics, biased variance."""
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        w, b = _derived(self, lambda: (self.weight.float(), self.bias.float()))
+        if _needs_grad(self, x):
+            w, b = self.weight.float(), self.bias.float()
+        else:
+            w, b = _derived(self, lambda: (self.weight.float(), self.bias.float()))
         return _OPS.layernorm(_rows(x, x.dtype), w, b, float(self.eps)).view(x.shape)
 
 
@@ -258,8 +268,11 @@ class LayerNormImproved(nn.Module):
                 or zero_centered_weight or return_dropout_mask):
             raise NotImplementedError("siglip2_b200 LayerNormImproved: dropout, rowscale, x1/weight1/bias1 and "
                                       "zero_centered_weight are not implemented")
-        w, b = _derived(self, lambda: (self.weight.float(), self.bias.float()))
         x = hidden_states
+        if _needs_grad(self, x, residual):
+            w, b = self.weight.float(), self.bias.float()
+        else:
+            w, b = _derived(self, lambda: (self.weight.float(), self.bias.float()))
         if residual is None and not residual_in_fp32:
             y = _OPS.layernorm(_rows(x, x.dtype), w, b, float(self.variance_epsilon)).view(x.shape)
             res = x
@@ -407,8 +420,11 @@ class Siglip2MLP(nn.Module):
         self.fc2 = nn.Linear(config.intermediate_size, config.hidden_size)
 
     def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
-        w1, b1, w2, b2 = _derived(self, lambda: (self.fc1.weight, self.fc1.bias.float(), self.fc2.weight,
-                                                 self.fc2.bias.float()))
+        if _needs_grad(self, hidden_states):
+            w1, b1, w2, b2 = self.fc1.weight, self.fc1.bias.float(), self.fc2.weight, self.fc2.bias.float()
+        else:
+            w1, b1, w2, b2 = _derived(self, lambda: (self.fc1.weight, self.fc1.bias.float(), self.fc2.weight,
+                                                     self.fc2.bias.float()))
         h = _OPS.gemm(_rows(hidden_states, w1.dtype), w1, L.EPI_BIAS_GELU, b1, None, None, None, 0.0)
         return _OPS.gemm(h, w2, L.EPI_BIAS, b2, None, None, None, 0.0).view(*hidden_states.shape[:-1], -1)
 

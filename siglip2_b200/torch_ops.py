@@ -15,11 +15,13 @@ Ops (``torch.ops.siglip2_b200.<name>``):
   token_image, patch_embed     -- patch Linear + resized position grid
   vision_tower                 -- the whole tower (``siglip2_forward``)
 
-No autograd formula is registered: the ops are inference kernels, and
-back-propagating through one raises.
+Backward: ``gemm`` (bias, bias + GELU-tanh and bias + residual epilogues)
+and ``layernorm`` have a stop-gap autograd formula (below); back-propagating
+through any other op raises.
 """
 from __future__ import annotations
 
+import math
 from typing import Optional
 
 import numpy as np
@@ -47,6 +49,62 @@ def gemm(a: Tensor, w: Tensor, epilogue: int, bias: Optional[Tensor], res: Optio
 @gemm.register_fake
 def _(a, w, epilogue, bias, res, c1, c2, eps):
     return a.new_empty((a.shape[0], w.shape[0]))
+
+
+# Stop-gap backward of the plain epilogues (bias, bias + GELU-tanh, bias +
+# residual), so that the MLP can be trained through these kernels: dgrad and
+# wgrad run on the library's own GEMM (on transposed copies, the contracted
+# dimension zero-padded to a multiple of 8); the bias sums and the GELU-tanh
+# derivative (at the recomputed pre-activation) are fp32 torch arithmetic.
+_GELU_K0 = math.sqrt(2.0 / math.pi)
+_GELU_K1 = 0.044715
+
+
+def _gelu_tanh_grad(z: Tensor) -> Tensor:
+    """d/dz of 0.5 z (1 + tanh(k0 (z + k1 z^3))), fp32."""
+    t = torch.tanh(_GELU_K0 * (z + _GELU_K1 * z * z * z))
+    return 0.5 * (1 + t) + 0.5 * z * (1 - t * t) * _GELU_K0 * (1 + 3 * _GELU_K1 * z * z)
+
+
+def _matmul_nt(a: Tensor, b: Tensor) -> Tensor:
+    """``a [M, K] @ b [N, K].T`` on ``siglip2_gemm`` (K and N zero-padded to
+    multiples of 8 for the tensor-core path)."""
+    mult = 1 if a.dtype == torch.float32 else 8
+    M, K = a.shape
+    N = b.shape[0]
+    Kp, Np = -(-K // mult) * mult, -(-N // mult) * mult
+    if Kp != K or not a.is_contiguous():
+        a = torch.nn.functional.pad(a, (0, Kp - K)).contiguous()
+    if Kp != K or Np != N or not b.is_contiguous():
+        b = torch.nn.functional.pad(b, (0, Kp - K, 0, Np - N)).contiguous()
+    zero = torch.zeros(Np, dtype=torch.float32, device=a.device)
+    # through the registered op, so that the backward traces under torch.compile
+    return gemm(a, b, L.EPI_BIAS, zero, None, None, None, 0.0)[:, :N]
+
+
+def _gemm_setup(ctx, inputs, output):
+    a, w, epilogue, bias, res, c1, c2, eps = inputs
+    ctx.epilogue = epilogue
+    ctx.save_for_backward(a, w, bias)
+
+
+def _gemm_backward(ctx, grad):
+    a, w, bias = ctx.saved_tensors
+    if ctx.epilogue not in (L.EPI_BIAS, L.EPI_BIAS_GELU, L.EPI_BIAS_RES):
+        raise NotImplementedError("siglip2_b200::gemm: backward exists for the bias, bias+GELU and bias+residual "
+                                  "epilogues only")
+    g = grad
+    if ctx.epilogue == L.EPI_BIAS_GELU:
+        z = gemm(a.contiguous(), w.contiguous(), L.EPI_BIAS, bias, None, None, None, 0.0)
+        g = (grad.float() * _gelu_tanh_grad(z.float())).to(grad.dtype)
+    da = _matmul_nt(g, w.t()) if ctx.needs_input_grad[0] else None
+    dw = _matmul_nt(g.t(), a.t()) if ctx.needs_input_grad[1] else None
+    db = g.float().sum(0) if ctx.needs_input_grad[3] else None
+    dres = grad if ctx.needs_input_grad[4] else None
+    return da, dw, None, db, dres, None, None, None
+
+
+gemm.register_autograd(_gemm_backward, setup_context=_gemm_setup)
 
 
 @torch.library.custom_op("siglip2_b200::gemm_rowsums", mutates_args=(), device_types="cuda")
@@ -103,6 +161,32 @@ def layernorm(x: Tensor, weight: Tensor, bias: Tensor, eps: float) -> Tensor:
 @layernorm.register_fake
 def _(x, weight, bias, eps):
     return torch.empty_like(x, memory_format=torch.contiguous_format)
+
+
+def _layernorm_setup(ctx, inputs, output):
+    x, weight, bias, eps = inputs
+    ctx.eps = eps
+    ctx.save_for_backward(x, weight)
+
+
+def _layernorm_backward(ctx, grad):
+    """Stop-gap LayerNorm backward in fp32 torch arithmetic (statistics
+    recomputed from x): dx = rstd (g - mean(g) - xh mean(g xh)), g = dy * w."""
+    x, weight = ctx.saved_tensors
+    xf = x.float()
+    mu = xf.mean(-1, keepdim=True)
+    rstd = torch.rsqrt(((xf - mu) ** 2).mean(-1, keepdim=True) + ctx.eps)
+    xh = (xf - mu) * rstd
+    dy = grad.float()
+    gy = dy * weight.float()
+    dx = rstd * (gy - gy.mean(-1, keepdim=True) - xh * (gy * xh).mean(-1, keepdim=True))
+    rows = dy.reshape(-1, dy.shape[-1])
+    dw = (rows * xh.reshape(rows.shape)).sum(0) if ctx.needs_input_grad[1] else None
+    db = rows.sum(0) if ctx.needs_input_grad[2] else None
+    return dx.to(x.dtype) if ctx.needs_input_grad[0] else None, dw, db, None
+
+
+layernorm.register_autograd(_layernorm_backward, setup_context=_layernorm_setup)
 
 
 @torch.library.custom_op("siglip2_b200::token_image", mutates_args=(), device_types="cuda")

@@ -278,3 +278,41 @@ def test_torch_compile_traces_the_submodules():
     torch._dynamo.reset()
     assert torch.equal(torch.compile(mlp, backend="aot_eager")(x), mlp(x))
     assert torch.equal(torch.compile(layer, backend="aot_eager")(x, ids), layer(x, ids))
+
+
+@pytest.mark.parametrize("dtype", [F32, BF16])
+def test_mlp_and_layernorm_backward(dtype):
+    """The stop-gap backward (``run_tests.py:74-82`` back-propagates through
+    MLPImproved and LayerNormImproved): gradients of the input and of every
+    parameter against torch autograd on the same weights in fp32."""
+    cfg, pre = _cfg("b16"), "encoder.layers.0.mlp."
+    sd = _sd(cfg)
+    mlp = _load(S.MLPImproved(cfg), _sub(sd, pre), dtype)
+    ln = _load(S.LayerNormImproved(cfg.hidden_size, eps=1e-6), {"weight": 1 + 0.1 * torch.randn(cfg.hidden_size),
+                                                                 "bias": 0.1 * torch.randn(cfg.hidden_size)}, dtype)
+    x = _rand((3, 67, cfg.hidden_size), dtype).requires_grad_(True)
+    r = _rand((3, 67, cfg.hidden_size), dtype, seed=7)
+    g = torch.Generator().manual_seed(8)
+    up = torch.randn(3, 67, cfg.hidden_size, generator=g).to("cuda", dtype)
+    h, res = ln(x, residual=r, prenorm=True, residual_in_fp32=True)
+    out = mlp(h)
+    (out.float() * up.float()).sum().backward()
+    # torch reference in fp32 on the same (rounded) parameters
+    xr = x.detach().float().requires_grad_(True)
+    params = {n: p.detach().float().requires_grad_(True) for n, p in
+              [("ln.w", ln.weight), ("ln.b", ln.bias), ("fc1.w", mlp.fc1.weight), ("fc1.b", mlp.fc1.bias),
+               ("fc2.w", mlp.fc2.weight), ("fc2.b", mlp.fc2.bias)]}
+    hr = F.layer_norm(xr + r.float(), (cfg.hidden_size,), params["ln.w"], params["ln.b"], 1e-6)
+    hr = F.gelu(F.linear(hr, params["fc1.w"], params["fc1.b"]), approximate="tanh")
+    outr = F.linear(hr, params["fc2.w"], params["fc2.b"])
+    (outr * up.float()).sum().backward()
+    got = {"x": x.grad, "ln.w": ln.weight.grad, "ln.b": ln.bias.grad, "fc1.w": mlp.fc1.weight.grad,
+           "fc1.b": mlp.fc1.bias.grad, "fc2.w": mlp.fc2.weight.grad, "fc2.b": mlp.fc2.bias.grad}
+    want = {"x": xr.grad, **{k: v.grad for k, v in params.items()}}
+    for k in got:
+        a, b = got[k].float().flatten(), want[k].flatten()
+        cos = F.cosine_similarity(a, b, dim=0).item()
+        rel = ((a - b).norm() / b.norm()).item()
+        print(f"\n[grad] {dtype} {k}: cos {cos:.6f} rel {rel:.2e}")
+        assert cos > (0.99999 if dtype == F32 else 0.999) and rel < (1e-4 if dtype == F32 else 4e-2), (k, cos, rel)
+    assert res.dtype == F32
