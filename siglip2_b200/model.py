@@ -310,8 +310,9 @@ class Siglip2SequenceEmbeddings(nn.Module):
         """``(seq_patches [N, C*p*p], seq_sizes [B], spatial_shapes [B, 2])``
         -> ``[N, D]``; image b's rows are its ``h*w`` patches, row-major."""
         seq_patches, seq_sizes, spatial_shapes = packed_seq_patches
-        w, b, table = _derived(self, lambda: (self.patch_embedding.weight, self.patch_embedding.bias.float(),
-                                              self.position_embedding.weight.float()))
+        params = lambda: (self.patch_embedding.weight, self.patch_embedding.bias.float(),  # noqa: E731
+                          self.position_embedding.weight.float())
+        w, b, table = params() if _needs_grad(self, seq_patches) else _derived(self, params)
         hw = _grids(spatial_shapes)
         if seq_sizes is not None:
             sizes = torch.as_tensor(seq_sizes).detach().to("cpu", torch.int64).reshape(-1).numpy()
@@ -321,18 +322,20 @@ class Siglip2SequenceEmbeddings(nn.Module):
         B = hw.shape[0]
         cu, hw_dev = meta[:B + 1], meta[B + 1:3 * B + 1]
         tok = _OPS.token_image(cu, N)
-        return _OPS.patch_embed(_rows(seq_patches, w.dtype), w, b, table, hw_dev, cu, tok)
+        return _OPS.patch_embed(_rows(seq_patches, w.dtype), w, b, table, hw_dev, cu, tok,
+                                [int(v) for v in hw.reshape(-1)])
 
 
 def _attention(m: nn.Module, x: torch.Tensor, seqs: Sequences) -> torch.Tensor:
     """QKV projection -> per-sequence attention -> out projection
     (``model.py:144-176``), three launches."""
-    qkv_w, qkv_b, out_w, out_b = _derived(m, lambda: (*m.qkv_params(), m.out_proj.weight, m.out_proj.bias))
+    params = lambda: (*m.qkv_params(), m.out_proj.weight, m.out_proj.bias)  # noqa: E731
+    qkv_w, qkv_b, out_w, out_b = params() if _needs_grad(m, x) else _derived(m, params)
     x2 = _rows(x, qkv_w.dtype)
     if x2.shape[0] != seqs.n_tokens:
         raise ValueError(f"{x2.shape[0]} rows but the sequences cover {seqs.n_tokens}")
     qkv = _OPS.gemm(x2, qkv_w, L.EPI_BIAS, qkv_b.float(), None, None, None, 0.0)
-    a = _OPS.fmha_varlen(qkv, seqs.cu_seqlens, seqs.tiles, m.num_heads, m.head_dim)
+    a = _OPS.fmha_varlen(qkv, seqs.cu_seqlens, seqs.tiles, m.num_heads, m.head_dim, seqs.lengths)
     return _OPS.gemm(a, out_w, L.EPI_BIAS, out_b.float(), None, None, None, 0.0).view(*x.shape[:-1], -1)
 
 
@@ -459,6 +462,8 @@ def _encoder_layer(layer: nn.Module, x: torch.Tensor, seqs: Sequences, rs: torch
     LayerNorm statistics travel as row sums (``rs`` in, the output's out).
     Returns ``(y, rs_y)``."""
     _check_inference(layer, layer.self_attn.dropout)
+    if _needs_grad(layer, x):
+        return _encoder_layer_unfused(layer, x, seqs), None
     qw, qc1, qc2, ow, ob, f1w, f1c1, f1c2, f2w, f2b = _derived(layer, lambda: _layer_tensors(layer))
     eps1, eps2 = float(layer.layer_norm1.eps), float(layer.layer_norm2.eps)
     at = layer.self_attn
@@ -468,11 +473,31 @@ def _encoder_layer(layer: nn.Module, x: torch.Tensor, seqs: Sequences, rs: torch
     if rs is None:
         rs = _OPS.rowsums(x2)
     qkv, _ = _OPS.gemm_rowsums(x2, qw, L.EPI_LN_ROWSUMS, None, None, qc1, qc2, eps1, rs, False)
-    a = _OPS.fmha_varlen(qkv, seqs.cu_seqlens, seqs.tiles, at.num_heads, at.head_dim)
+    a = _OPS.fmha_varlen(qkv, seqs.cu_seqlens, seqs.tiles, at.num_heads, at.head_dim, seqs.lengths)
     h, rs_h = _OPS.gemm_rowsums(a, ow, L.EPI_BIAS_RES_ROWSUMS, ob, x2, None, None, 0.0, None, True)
     m, _ = _OPS.gemm_rowsums(h, f1w, L.EPI_LN_ROWSUMS_GELU, None, None, f1c1, f1c2, eps2, rs_h, False)
     y, rs_y = _OPS.gemm_rowsums(m, f2w, L.EPI_BIAS_RES_ROWSUMS, f2b, h, None, None, 0.0, None, True)
     return y.view(x.shape), rs_y
+
+
+def _encoder_layer_unfused(layer: nn.Module, x: torch.Tensor, seqs: Sequences) -> torch.Tensor:
+    """The layer for autograd: the same arithmetic as ``model.py:204-223``
+    with the LayerNorms as their own launches (folding them into the GEMM
+    weights has no backward here), every op one with a backward formula."""
+    at, mlp = layer.self_attn, layer.mlp
+    x2 = _rows(x, at.out_proj.weight.dtype)
+    if x2.shape[0] != seqs.n_tokens:
+        raise ValueError(f"{x2.shape[0]} rows but the sequences cover {seqs.n_tokens}")
+    ln1, ln2 = layer.layer_norm1, layer.layer_norm2
+    h = _OPS.layernorm(x2, ln1.weight.float(), ln1.bias.float(), float(ln1.eps))
+    wq, bq = at.qkv_params()
+    qkv = _OPS.gemm(h, wq, L.EPI_BIAS, bq.float(), None, None, None, 0.0)
+    a = _OPS.fmha_varlen(qkv, seqs.cu_seqlens, seqs.tiles, at.num_heads, at.head_dim, seqs.lengths)
+    r = _OPS.gemm(a, at.out_proj.weight, L.EPI_BIAS_RES, at.out_proj.bias.float(), x2, None, None, 0.0)
+    h = _OPS.layernorm(r, ln2.weight.float(), ln2.bias.float(), float(ln2.eps))
+    m = _OPS.gemm(h, mlp.fc1.weight, L.EPI_BIAS_GELU, mlp.fc1.bias.float(), None, None, None, 0.0)
+    y = _OPS.gemm(m, mlp.fc2.weight, L.EPI_BIAS_RES, mlp.fc2.bias.float(), r, None, None, 0.0)
+    return y.view(x.shape)
 
 
 class Siglip2EncoderLayer(nn.Module):

@@ -15,9 +15,9 @@ Ops (``torch.ops.siglip2_b200.<name>``):
   token_image, patch_embed     -- patch Linear + resized position grid
   vision_tower                 -- the whole tower (``siglip2_forward``)
 
-Backward: ``gemm`` (bias, bias + GELU-tanh and bias + residual epilogues)
-and ``layernorm`` have a stop-gap autograd formula (below); back-propagating
-through any other op raises.
+Backward: ``gemm`` (bias, bias + GELU-tanh and bias + residual epilogues),
+``layernorm``, ``fmha_varlen`` and ``patch_embed`` have a stop-gap autograd
+formula (below); back-propagating through any other op raises.
 """
 from __future__ import annotations
 
@@ -141,14 +141,47 @@ def _(x):
 
 # --------------------------------------------------------------------------- attention
 @torch.library.custom_op("siglip2_b200::fmha_varlen", mutates_args=(), device_types="cuda")
-def fmha_varlen(qkv: Tensor, cu_seqlens: Tensor, tiles: Tensor, heads: int, head_dim: int) -> Tensor:
-    """``siglip2_fmha_varlen``: qkv [N, 3*heads*head_dim] -> [N, heads*head_dim]."""
+def fmha_varlen(qkv: Tensor, cu_seqlens: Tensor, tiles: Tensor, heads: int, head_dim: int,
+                lengths: list[int]) -> Tensor:
+    """``siglip2_fmha_varlen``: qkv [N, 3*heads*head_dim] -> [N, heads*head_dim].
+    ``lengths``: the sequence lengths on the host (``cu_seqlens`` is their
+    device prefix sum), read only by the backward."""
     return ops.fmha_varlen(qkv, cu_seqlens, tiles, heads, head_dim)
 
 
 @fmha_varlen.register_fake
-def _(qkv, cu_seqlens, tiles, heads, head_dim):
+def _(qkv, cu_seqlens, tiles, heads, head_dim, lengths):
     return qkv.new_empty((qkv.shape[0], heads * head_dim))
+
+
+def _fmha_setup(ctx, inputs, output):
+    qkv, cu_seqlens, tiles, heads, head_dim, lengths = inputs
+    ctx.heads, ctx.head_dim, ctx.lengths = heads, head_dim, list(lengths)
+    ctx.save_for_backward(qkv)
+
+
+def _fmha_backward(ctx, grad):
+    """Stop-gap attention backward: every sequence is recomputed with torch's
+    scaled_dot_product_attention and differentiated there (softmax(q k^T /
+    sqrt(hd)) v, the forward's definition), one sequence at a time."""
+    (qkv,) = ctx.saved_tensors
+    H, hd = ctx.heads, ctx.head_dim
+    N = qkv.shape[0]
+    x = qkv.detach().view(N, 3, H, hd)
+    g = grad.reshape(N, H, hd)
+    parts = []
+    s = 0
+    for n in ctx.lengths:
+        with torch.enable_grad():
+            q, k, v = (x[s:s + n, i].transpose(0, 1)[None].requires_grad_(True) for i in range(3))
+            o = torch.nn.functional.scaled_dot_product_attention(q, k, v, scale=hd ** -0.5)
+            dq, dk, dv = torch.autograd.grad(o, (q, k, v), g[s:s + n].transpose(0, 1)[None])
+        parts.append(torch.stack([t[0].transpose(0, 1) for t in (dq, dk, dv)], 1))
+        s += n
+    return torch.cat(parts, 0).reshape(N, 3 * H * hd), None, None, None, None, None
+
+
+fmha_varlen.register_autograd(_fmha_backward, setup_context=_fmha_setup)
 
 
 # --------------------------------------------------------------------------- row ops
@@ -202,14 +235,51 @@ def _(cu_seqlens, n_tokens):
 
 @torch.library.custom_op("siglip2_b200::patch_embed", mutates_args=(), device_types="cuda")
 def patch_embed(patches: Tensor, w: Tensor, bias: Tensor, table: Tensor, hw: Tensor, cu_seqlens: Tensor,
-                tok_img: Tensor) -> Tensor:
-    """``siglip2_patch_embed``: ``patches @ w.T + bias + resize(table)`` [N, D]."""
+                tok_img: Tensor, grids: list[int]) -> Tensor:
+    """``siglip2_patch_embed``: ``patches @ w.T + bias + resize(table)`` [N, D].
+    ``grids``: the (h, w) pairs on the host (``hw`` on the device), read only
+    by the backward."""
     return ops.patch_embed(patches, w, bias, table, hw, cu_seqlens, tok_img)
 
 
 @patch_embed.register_fake
-def _(patches, w, bias, table, hw, cu_seqlens, tok_img):
+def _(patches, w, bias, table, hw, cu_seqlens, tok_img, grids):
     return patches.new_empty((patches.shape[0], w.shape[0]))
+
+
+def _patch_embed_setup(ctx, inputs, output):
+    patches, w, bias, table, hw, cu_seqlens, tok_img, grids = inputs
+    ctx.grids = list(grids)
+    ctx.save_for_backward(patches, w, table)
+
+
+def _patch_embed_backward(ctx, grad):
+    """Stop-gap backward: patch and weight gradients on the library GEMM; the
+    position table's gradient is the adjoint of the per-image antialiased
+    bilinear resize, taken through torch's interpolate (one image at a time)."""
+    patches, w, table = ctx.saved_tensors
+    d_patches = _matmul_nt(grad, w.t()) if ctx.needs_input_grad[0] else None
+    dw = _matmul_nt(grad.t(), patches.t()) if ctx.needs_input_grad[1] else None
+    db = grad.float().sum(0) if ctx.needs_input_grad[2] else None
+    dtable = None
+    if ctx.needs_input_grad[3]:
+        G2, D = table.shape
+        G = int(round(G2 ** 0.5))
+        grids = ctx.grids
+        with torch.enable_grad():
+            t = table.detach().float().reshape(G, G, D).permute(2, 0, 1)[None].requires_grad_(True)
+            outs, s = [], 0
+            for i in range(0, len(grids), 2):
+                h, wd = grids[i], grids[i + 1]
+                outs.append(torch.nn.functional.interpolate(t, size=(h, wd), mode="bilinear", align_corners=False,
+                                                            antialias=True).reshape(D, h * wd))
+            r = torch.cat(outs, 1)  # [D, N]
+            (dt,) = torch.autograd.grad(r, (t,), grad.float().t())
+        dtable = dt[0].permute(1, 2, 0).reshape(G2, D).to(table.dtype)
+    return d_patches, dw, db, dtable, None, None, None, None
+
+
+patch_embed.register_autograd(_patch_embed_backward, setup_context=_patch_embed_setup)
 
 
 # --------------------------------------------------------------------------- whole tower

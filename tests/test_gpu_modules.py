@@ -184,12 +184,17 @@ def test_encoder_layer(preset, dtype):
     N = sum(LENS)
     x = _rand((1, N, cfg.hidden_size), dtype)
     ids = S.create_document_ids(torch.tensor(LENS), "cuda")
-    out = layer(x, ids)
-    assert out.shape == x.shape
-    _check(out, TR.encoder_layer(sdq, cfg, pre, x[0], LENS, dtype),
-           TR.encoder_layer(sdq, cfg, pre, x[0].float(), LENS, F32), dtype, f"encoder layer {preset}")
+    ref_dt = TR.encoder_layer(sdq, cfg, pre, x[0], LENS, dtype)
+    ref32 = TR.encoder_layer(sdq, cfg, pre, x[0].float(), LENS, F32)
     li = _load(S.Siglip2EncoderLayerImproved(cfg), _sub(_fuse_qkv(sd), pre), dtype)
-    assert torch.equal(li(x, _doc_block_mask(ids, N)), out)
+    with torch.no_grad():  # inference: LayerNorms folded into the GEMMs, row sums carried
+        out = layer(x, ids)
+        assert out.shape == x.shape
+        _check(out, ref_dt, ref32, dtype, f"encoder layer {preset}")
+        assert torch.equal(li(x, _doc_block_mask(ids, N)), out)
+    out_g = layer(x, ids)  # autograd recording: the unfused layer
+    _check(out_g, ref_dt, ref32, dtype, f"encoder layer {preset} (unfused)")
+    assert torch.equal(li(x, _doc_block_mask(ids, N)), out_g)
 
 
 @pytest.mark.parametrize("preset", ["b16", "so400m"])
@@ -221,7 +226,8 @@ def test_submodules_compose_to_the_tower(preset):
         s += n
     assert (ours.float() - ref.float()).abs().max().item() < 0.1
     enc = _load(S.Siglip2EncoderImproved(cfg), _sub(_fuse_qkv(sd), "encoder."), BF16)
-    assert torch.equal(enc(x[None], ids), y)
+    with torch.no_grad():
+        assert torch.equal(enc(x[None], ids), y)
 
 
 def test_vision_tower_op_matches_the_module():
@@ -259,7 +265,7 @@ def test_registered_ops_pass_opcheck():
     torch.library.opcheck(O.layernorm, (a, gam, bet, 1e-6), test_utils=tests)
     sq = S.Sequences([120, 80], "cuda")
     qkv = _rand((200, 3 * 4 * 64), BF16, seed=6)
-    torch.library.opcheck(O.fmha_varlen, (qkv, sq.cu_seqlens, sq.tiles, 4, 64), test_utils=tests)
+    torch.library.opcheck(O.fmha_varlen, (qkv, sq.cu_seqlens, sq.tiles, 4, 64, sq.lengths), test_utils=tests)
     torch.library.opcheck(O.token_image, (sq.cu_seqlens, 200), test_utils=tests)
     _, rs = O.gemm_rowsums(h, w2, L.EPI_BIAS_RES_ROWSUMS, bias[:256].contiguous(), a, None, None, 0.0, None, True)
     assert rs.shape == (200, ops.rowsum_slots(BF16, 256), 2)
@@ -316,3 +322,82 @@ def test_mlp_and_layernorm_backward(dtype):
         print(f"\n[grad] {dtype} {k}: cos {cos:.6f} rel {rel:.2e}")
         assert cos > (0.99999 if dtype == F32 else 0.999) and rel < (1e-4 if dtype == F32 else 4e-2), (k, cos, rel)
     assert res.dtype == F32
+
+
+def _grad_check(got, want, dtype, what):
+    for k in got:
+        a, b = got[k].float().flatten(), want[k].float().flatten()
+        if k == "self_attn.k_proj.bias":
+            # the key bias shifts every score of a query row equally: softmax
+            # ignores it, its gradient is zero up to rounding on both sides
+            scale = max(got["self_attn.v_proj.bias"].float().norm().item(), 1e-30)
+            assert a.norm().item() < 1e-2 * scale and b.norm().item() < 1e-2 * scale, (k, a.norm(), b.norm())
+            continue
+        cos = F.cosine_similarity(a, b, dim=0).item()
+        rel = ((a - b).norm() / b.norm()).item()
+        print(f"\n[grad] {what} {dtype} {k}: cos {cos:.6f} rel {rel:.2e}")
+        assert cos > (0.99999 if dtype == F32 else 0.999) and rel < (1e-3 if dtype == F32 else 5e-2), (k, cos, rel)
+
+
+@pytest.mark.parametrize("dtype", [F32, BF16])
+def test_encoder_layer_and_embeddings_backward(dtype):
+    """Encoder layer (document ids, and the BlockMask form) and embeddings
+    back-propagate: gradients of the input and every parameter against torch
+    autograd in fp32 on the same weights (``model.py:68-120, 144-223``)."""
+    cfg, pre = _cfg("b16"), "encoder.layers.0."
+    sd = _sd(cfg, seed=6)
+    lens = [200, 1, 129, 64]
+    N, D, H = sum(lens), cfg.hidden_size, cfg.num_attention_heads
+    hd = D // H
+    ids = S.create_document_ids(torch.tensor(lens), "cuda")
+    g = torch.Generator().manual_seed(9)
+    up = torch.randn(1, N, D, generator=g).to("cuda")
+    for layer in (_load(S.Siglip2EncoderLayer(cfg), _sub(sd, pre), dtype),
+                  _load(S.Siglip2EncoderLayerImproved(cfg), _sub(_fuse_qkv(sd), pre), dtype)):
+        x = _rand((1, N, D), dtype, seed=10).requires_grad_(True)
+        improved = isinstance(layer, S.Siglip2EncoderLayerImproved)
+        out = layer(x, _doc_block_mask(ids, N)) if improved else layer(x, ids)
+        (out.float() * up).sum().backward()
+        params = {n: p.detach().float().requires_grad_(True) for n, p in layer.named_parameters()}
+        xr = x.detach().float().requires_grad_(True)
+        P = params
+        h = F.layer_norm(xr[0], (D,), P["layer_norm1.weight"], P["layer_norm1.bias"], cfg.layer_norm_eps)
+        if improved:
+            qkv = F.linear(h, P["self_attn.qkv_proj.weight"], P["self_attn.qkv_proj.bias"])
+        else:
+            qkv = torch.cat([F.linear(h, P[f"self_attn.{n}_proj.weight"], P[f"self_attn.{n}_proj.bias"])
+                             for n in "qkv"], 1)
+        q, k, v = qkv.view(N, 3, H, hd).unbind(1)
+        outs, s0 = [], 0
+        for n in lens:
+            sl = slice(s0, s0 + n)
+            o = F.scaled_dot_product_attention(*(t[sl].transpose(0, 1)[None] for t in (q, k, v)), scale=hd ** -0.5)
+            outs.append(o[0].transpose(0, 1).reshape(n, D))
+            s0 += n
+        r = xr[0] + F.linear(torch.cat(outs, 0), P["self_attn.out_proj.weight"], P["self_attn.out_proj.bias"])
+        h = F.layer_norm(r, (D,), P["layer_norm2.weight"], P["layer_norm2.bias"], cfg.layer_norm_eps)
+        h = F.gelu(F.linear(h, P["mlp.fc1.weight"], P["mlp.fc1.bias"]), approximate="tanh")
+        ref = r + F.linear(h, P["mlp.fc2.weight"], P["mlp.fc2.bias"])
+        (ref[None] * up).sum().backward()
+        got = {"x": x.grad, **{n: p.grad for n, p in layer.named_parameters()}}
+        want = {"x": xr.grad, **{n: p.grad for n, p in params.items()}}
+        _grad_check(got, want, dtype, "layer (improved)" if improved else "layer")
+    # embeddings: patch Linear + resized position grid
+    emb = _load(S.Siglip2SequenceEmbeddings(cfg), _sub(sd, "embeddings."), dtype)
+    grids = [(18, 18), (11, 37), (5, 3), (20, 12)]
+    gt = torch.tensor(grids)
+    n_tok = sum(a * b for a, b in grids)
+    pv = _rand((n_tok, 768), dtype, seed=11).requires_grad_(True)
+    out = emb((pv, gt.prod(-1), gt))
+    up2 = torch.randn(n_tok, D, generator=g).to("cuda")
+    (out.float() * up2).sum().backward()
+    P = {n: p.detach().float().requires_grad_(True) for n, p in emb.named_parameters()}
+    pr = pv.detach().float().requires_grad_(True)
+    G = int(cfg.num_patches ** 0.5)
+    table = P["position_embedding.weight"].reshape(G, G, D).permute(2, 0, 1)[None]
+    pos = torch.cat([F.interpolate(table, size=hw, mode="bilinear", align_corners=False, antialias=True)
+                     .reshape(D, -1).t() for hw in grids], 0)
+    ref = F.linear(pr, P["patch_embedding.weight"], P["patch_embedding.bias"]) + pos
+    (ref * up2).sum().backward()
+    _grad_check({"x": pv.grad, **{n: p.grad for n, p in emb.named_parameters()}},
+                {"x": pr.grad, **{n: p.grad for n, p in P.items()}}, dtype, "embeddings")

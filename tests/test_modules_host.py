@@ -110,12 +110,12 @@ def test_fake_shapes_of_the_registered_ops():
     assert O.rowsums(_meta(7, 4304)).shape == (7, 34, 2)
     assert O.rowsums(_meta(7, 768, dtype=torch.float32)).shape == (7, 6, 2)
     cu, tiles = _meta(3, dtype=torch.int32), _meta(4, 2, dtype=torch.int32)
-    assert O.fmha_varlen(_meta(300, 3456), cu, tiles, 16, 72).shape == (300, 1152)
+    assert O.fmha_varlen(_meta(300, 3456), cu, tiles, 16, 72, [100, 200]).shape == (300, 1152)
     assert O.layernorm(a, _meta(1152, dtype=torch.float32), _meta(1152, dtype=torch.float32), 1e-6).shape == a.shape
     tok = O.token_image(cu, 300)
     assert tok.shape == (300,) and tok.dtype == torch.int32
     pe = O.patch_embed(_meta(300, 768), _meta(1152, 768), _meta(1152, dtype=torch.float32),
-                       _meta(256, 1152, dtype=torch.float32), _meta(4, dtype=torch.int32), cu, tok)
+                       _meta(256, 1152, dtype=torch.float32), _meta(4, dtype=torch.int32), cu, tok, [10, 10, 10, 20])
     assert pe.shape == (300, 1152)
 
 
