@@ -362,10 +362,12 @@ int launch_patchify(const PatchifyArgs& a, bool fast, bool any_resize, size_t sm
                     int* mask, cudaStream_t s) {
   T* o = static_cast<T*>(out);
   if (fast) {
-    int dev = 0, sms = 148;
+    int dev = 0, sms = 148, per_sm = 1;
     SG_CUDA(cudaGetDevice(&dev));
     SG_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    const long long blocks = std::min<long long>((n_rows + 7) / 8, 8ll * sms);  // 8 CTAs of 8 warps per SM
+    // persistent: exactly the CTAs that are resident at once (one wave)
+    SG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, patchify16x3_kernel<T>, 256, 0));
+    const long long blocks = std::min<long long>((n_rows + 7) / 8, static_cast<long long>(std::max(per_sm, 1)) * sms);
     patchify16x3_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, s>>>(a, o, mask);
     SG_LAUNCH_CHECK();
     if (!any_resize) return SIGLIP2_OK;
