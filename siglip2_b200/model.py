@@ -565,8 +565,9 @@ class Siglip2EncoderImproved(nn.Module):
 
 
 class Siglip2MultiheadAttentionPoolingHead(nn.Module):
-    """Parameters of ``transformers`` ``modeling_siglip2.py:670-681``; runs
-    inside the tower's forward (``pooler_output``)."""
+    """``transformers`` ``modeling_siglip2.py:670-713``: the attention-pooling
+    (MAP) head.  Runs inside the tower's forward (``pooler_output``); its own
+    forward does the same on padded rows."""
 
     def __init__(self, config: Siglip2VisionConfig):
         super().__init__()
@@ -575,6 +576,58 @@ class Siglip2MultiheadAttentionPoolingHead(nn.Module):
         self.layernorm = LayerNorm(config.hidden_size, eps=config.layer_norm_eps)
         self.mlp = Siglip2MLP(config)
         self.num_heads = config.num_attention_heads
+
+    def _tensors(self):
+        """Per-head key vectors of the probe (base-2 scores: the query
+        projection of the probe through each head's key rows, times
+        log2(e) / sqrt(head_dim); the key bias shifts all scores of a head
+        equally and drops out), then the value / out projections, LayerNorm
+        and MLP parameters."""
+        D = self.probe.shape[-1]
+        H = self.num_heads
+        hd = D // H
+        win = self.attention.in_proj_weight.float()
+        bin_ = self.attention.in_proj_bias.float()
+        q = win[:D] @ self.probe.float().reshape(D) + bin_[:D]
+        u = torch.einsum("hd,hdk->hk", q.view(H, hd), win[D:2 * D].view(H, hd, D)) * (math.log2(math.e) /
+                                                                                      math.sqrt(hd))
+        dt = self.attention.in_proj_weight.dtype
+        return (u, self.attention.in_proj_weight[2 * D:], bin_[2 * D:], self.attention.out_proj.weight,
+                self.attention.out_proj.bias.float(), self.layernorm.weight.float(), self.layernorm.bias.float(),
+                self.mlp.fc1.weight.to(dt), self.mlp.fc1.bias.float(), self.mlp.fc2.weight.to(dt),
+                self.mlp.fc2.bias.float())
+
+    def forward(self, hidden_state: torch.Tensor, attention_mask: torch.Tensor | None = None) -> torch.Tensor:
+        """``hidden_state [B, P, D]`` -> ``[B, D]``: the probe attends over each
+        image's valid rows (``siglip2_head_pool``), then the value and out
+        projections, LayerNorm, MLP and residual (library GEMMs).  The valid
+        rows of an image must be its first ones, as ``attention_mask`` marks
+        them in the padded forward (other masks raise); without a mask every
+        row is valid.  Inference only (no backward)."""
+        if hidden_state.requires_grad and torch.is_grad_enabled():
+            raise NotImplementedError("the attention-pooling head has no backward in siglip2_b200")
+        B, P, D = hidden_state.shape
+        H = self.num_heads
+        if attention_mask is None:
+            lens = torch.full((B,), P, dtype=torch.int64)
+        else:
+            m = attention_mask.detach().to("cpu", torch.int64).reshape(B, P)
+            lens = m.sum(1)
+            if not torch.equal(m, (torch.arange(P)[None] < lens[:, None]).to(m.dtype)) or bool((lens == 0).any()):
+                raise NotImplementedError("attention_mask must mark a non-empty prefix of every image's rows")
+        (u, wv, bv, wo, bo, lw, lb, w1, b1, w2, b2) = _derived(self, self._tensors)
+        x = hidden_state.to(wv.dtype).contiguous()
+        cu = torch.zeros(B + 1, dtype=torch.int32)
+        cu[1:] = torch.cumsum(lens, 0).to(torch.int32)
+        cu = cu.to(x.device)
+        with torch.no_grad():
+            pooled = ops.head_pool(x, u, cu, B * P, max_patches=P)                 # [B, H, D]
+            v = ops.gemm(pooled.view(B * H, D), wv, L.EPI_BIAS, bias=bv).view(B, H, H, D // H)
+            idx = torch.arange(H, device=x.device)
+            a = ops.gemm(v[:, idx, idx, :].reshape(B, D).contiguous(), wo, L.EPI_BIAS, bias=bo)
+            h = ops.layernorm(a, lw, lb, float(self.layernorm.eps))
+            h = ops.gemm(h, w1, L.EPI_BIAS_GELU, bias=b1)
+            return ops.gemm(h, w2, L.EPI_BIAS_RES, bias=b2, res=a)
 
 # ---------------------------------------------------------------------------
 # weight packing for the C ABI

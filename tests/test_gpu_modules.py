@@ -401,3 +401,33 @@ def test_encoder_layer_and_embeddings_backward(dtype):
     (ref * up2).sum().backward()
     _grad_check({"x": pv.grad, **{n: p.grad for n, p in emb.named_parameters()}},
                 {"x": pr.grad, **{n: p.grad for n, p in P.items()}}, dtype, "embeddings")
+
+
+@pytest.mark.parametrize("dtype", [F32, BF16])
+def test_map_head_module(dtype):
+    """The attention-pooling head's own forward (transformers
+    ``modeling_siglip2.py:684-713``) on padded rows against the torch replay
+    of it on each image's valid rows; padded rows (random here) are ignored."""
+    cfg = _cfg("b16")
+    sd = W.init_state_dict(cfg, seed=12, with_head=True, random_affine=True)
+    sdq = {k: v.to(dtype).float() for k, v in sd.items()}
+    head = _load(S.Siglip2MultiheadAttentionPoolingHead(cfg), _sub(sd, "head."), dtype)
+    lens, P, D = [200, 37, 256, 1], 256, cfg.hidden_size
+    x = _rand((len(lens), P, D), dtype, seed=13)
+    mask = (torch.arange(P)[None] < torch.tensor(lens)[:, None]).to(torch.int64)
+    out = head(x, mask.cuda())
+    assert out.shape == (len(lens), D)
+    packed = torch.cat([x[b, :n] for b, n in enumerate(lens)], 0)
+    grids = [(n, 1) for n in lens]
+    _check(out, TR.map_head(sdq, cfg, packed, grids, dtype), TR.map_head(sdq, cfg, packed.float(), grids, F32),
+           dtype, "MAP head")
+    full = head(x[:, :100])  # no mask: every row valid
+    ref_full = TR.map_head(sdq, cfg, x[:, :100].reshape(-1, D).float(), [(100, 1)] * len(lens), F32)
+    _check(full, TR.map_head(sdq, cfg, x[:, :100].reshape(-1, D), [(100, 1)] * len(lens), dtype), ref_full, dtype,
+           "MAP head, no mask")
+    bad = mask.clone()
+    bad[0, 0] = 0
+    with pytest.raises(NotImplementedError):
+        head(x, bad)
+    with pytest.raises(NotImplementedError):
+        head(x.clone().requires_grad_(True), mask)
