@@ -10,7 +10,15 @@ is one forward of the 64 images through the HF-style public API
 ``model(pixel_values, attention_mask, spatial_shapes)`` followed (N > 1) by the
 NCCL all-gather of the pooled embeddings.
 
-``value``: images/s over all ranks with inputs already in HBM.  ``e2e``: the
+Multi-GPU (weak scaling): one global batch of ``images_per_gpu * N`` images
+(the same seeded grid draw, so N = 1 is the first 64 of it) is split over the
+ranks by ``parallel.shard_images`` (cost-balanced, longest first); each rank
+runs the forward on its shard and ``parallel.PooledGather`` all-gathers the
+pooled embeddings back into global order (the path's only collective), timed
+separately as ``allgather_ms_per_step``.
+
+``value``: images/s over all ranks (whole job) with inputs already in HBM;
+``value_per_gpu`` = value / N, the metric's per-GPU figure.  ``e2e``: the
 same with pixel_values in pinned host memory (H2D inside every step, on a copy
 stream one step ahead of the forward, double-buffered) and the pooled
 embeddings read back to the host every step.  ``roofline``: the dominant kernel
@@ -66,9 +74,23 @@ def peaks():
 
 
 # --------------------------------------------------------------------------- workload
-def build_inputs(wl, rank: int):
-    shapes = W.sample_spatial_shapes(wl.sampler, wl.batch, wl.max_patches, seed=1337 + rank)
-    pv, mask = W.make_pixels(shapes, wl.max_patches, 3 * 16 * 16, seed=1337 + rank, dtype=wl.dtype)
+def global_shapes(wl, world: int):
+    """(h, w) of the whole job's images: ``images_per_gpu * world`` draws."""
+    return W.sample_spatial_shapes(wl.sampler, wl.batch * world, wl.max_patches, seed=1337)
+
+
+def shard(wl, world: int):
+    """Global grids and, per rank, the global indices of the images it owns."""
+    from siglip2_b200.parallel import shard_images
+    d, i, _, _ = W.PRESETS[wl.preset]
+    shapes_all = global_shapes(wl, world)
+    return shapes_all, shard_images(shapes_all.tolist(), world, d, i)
+
+
+def build_inputs(wl, shapes_all, ids):
+    """Padded pixels of the images ``ids`` of the global batch."""
+    shapes = shapes_all[ids]
+    pv, mask = W.make_pixels_indexed(shapes, ids, wl.max_patches, 3 * 16 * 16, seed=1337, dtype=wl.dtype)
     return shapes, pv, mask
 
 
@@ -99,7 +121,7 @@ def cpu_sample(wl, seconds: float):
         limiter = None
     cfg = W.preset_config(wl.preset, config_cls=O.OracleConfig)
     sd = {k: v.float().numpy() for k, v in W.init_state_dict(cfg, seed=1337, with_head=True).items()}
-    shapes, pv, mask = build_inputs(wl, 0)
+    shapes, pv, mask = build_inputs(wl, global_shapes(wl, 1), list(range(wl.batch)))
     pv = pv.float().numpy()
     done, t0 = 0, time.perf_counter()
     while done < wl.batch:
@@ -122,7 +144,7 @@ def run_reference_arm(args, wl, rank, world):
     cores = os.cpu_count() or 1
     cfg = W.preset_config(wl.preset, config_cls=O.OracleConfig)
     sd = {k: v.float().numpy() for k, v in W.init_state_dict(cfg, seed=1337, with_head=True).items()}
-    shapes, pv, mask = build_inputs(wl, 0)
+    shapes, pv, mask = build_inputs(wl, global_shapes(wl, 1), list(range(wl.batch)))
     pv = pv.float().numpy()
     per_step = 1  # one image of the batch per step keeps K + W steps within minutes
 
@@ -170,26 +192,44 @@ def main():
     from siglip2_b200 import _lib as L
     from siglip2_b200 import ops
 
+    from siglip2_b200.parallel import PooledGather
+
     cfg, model = build_model(wl, dev)
-    shapes, pv_cpu, mask_cpu = build_inputs(wl, rank)
+    shapes_all, owned = shard(wl, world)
+    mine = owned[rank]
+    shapes, pv_cpu, mask_cpu = build_inputs(wl, shapes_all, mine)
     shapes_cpu = shapes.to(torch.int64)
     pv = pv_cpu.to(dev)
     mask = mask_cpu.to(dev)
     pv_pinned = pv_cpu.pin_memory()
     mask_pinned = mask_cpu.pin_memory()
-    B, D = wl.batch, cfg.hidden_size
-    gathered = torch.empty((world * B, D), dtype=wl.dtype, device=dev) if world > 1 else None
+    B, D = len(mine), cfg.hidden_size
+    B_all = shapes_all.shape[0]
+    gather = PooledGather(owned, D, wl.dtype, dev) if world > 1 else None
+    g_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
 
-    def step(pixels, msk):
+    def step(pixels, msk, timed=None):
         out = model(pixels, msk, shapes_cpu)
-        if world > 1:
-            dist.all_gather_into_tensor(gathered, out.pooler_output)
-        return out
+        if world == 1:
+            return out.pooler_output
+        if timed is not None:
+            g_ev[timed][0].record()
+        res = gather(out.pooler_output)
+        if timed is not None:
+            g_ev[timed][1].record()
+        return res
 
     def sync_all():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
 
     # ---- device-resident throughput
     for _ in range(args.warmup):
@@ -201,27 +241,29 @@ def main():
     with ClockSampler(local) as clk:
         sync_all()
         e0.record()
-        for _ in range(args.steps):
-            step(pv, mask)
+        for i in range(args.steps):
+            step(pv, mask, timed=i)
         e1.record()
         sync_all()
     launches = (lib.siglip2_launch_count() - n0)
-    ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms_rank = e0.elapsed_time(e1)
+    gather_ms_rank = sum(a.elapsed_time(b) for a, b in g_ev) / args.steps if world > 1 else 0.0
+    fwd_ms_rank = ms_rank / args.steps - gather_ms_rank  # this rank's forward (and launch gaps) per step
+    ms = max_over_ranks(ms_rank)
+    gather_ms = max_over_ranks(gather_ms_rank)
+    fwd_ms_max = max_over_ranks(fwd_ms_rank)
+    fwd_ms_min = -max_over_ranks(-fwd_ms_rank)
     ms_step = ms / args.steps
-    images = world * B * args.steps
+    images = B_all * args.steps
     value = images / (ms / 1e3)
     peak_tf, peak_hbm, peak_kind = peaks()
-    fl = flops_forward(cfg, shapes)
+    fl = flops_forward(cfg, shapes_all)  # whole job
     tflops = fl / (ms_step / 1e3) / 1e12
 
     # ---- end-to-end through the public API from pinned host memory
     h2d = pv_pinned.numel() * pv_pinned.element_size() + mask_pinned.numel() * mask_pinned.element_size()
-    d2h = B * D * torch.tensor([], dtype=wl.dtype).element_size()
-    host_out = torch.empty((B, D), dtype=wl.dtype, pin_memory=True)
+    d2h = B_all * D * torch.tensor([], dtype=wl.dtype).element_size()  # every rank reads back the gathered rows
+    host_out = torch.empty((B_all, D), dtype=wl.dtype, pin_memory=True)
     # as a data loader feeds a model: each step's inputs are uploaded from
     # pinned memory on a copy stream into one of two device buffers, one step
     # ahead, so the upload of step i+1 overlaps the forward of step i; every
@@ -249,7 +291,7 @@ def main():
             cur.wait_event(ready[i % 2])
             o = step(*bufs[i % 2])
             consumed[i % 2].record(cur)
-            host_out.copy_(o.pooler_output, non_blocking=True)
+            host_out.copy_(o, non_blocking=True)
 
     e2e_steps(2)
     sync_all()
@@ -258,18 +300,14 @@ def main():
     e2e_steps(args.steps)
     e3.record()
     sync_all()
-    ms_e2e = e2.elapsed_time(e3)
-    if world > 1:
-        t = torch.tensor([ms_e2e], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_e2e = float(t.item())
+    ms_e2e = max_over_ranks(e2.elapsed_time(e3))
     e2e_value = images / (ms_e2e / 1e3)
 
     # ---- dominant kernel alone: the fc1 GEMM as the forward runs it (LayerNorm
     # folded from row sums, GELU epilogue, CTA pairs) on this batch's token count
     roofline = None
     if rank == 0:
-        N = int((shapes[:, 0] * shapes[:, 1]).sum())
+        N = int((shapes[:, 0] * shapes[:, 1]).sum())  # this rank's valid tokens
         I = cfg.intermediate_size
         a = torch.randn(N, D, device=dev).to(wl.dtype)
         w = (torch.randn(I, D, device=dev) * 0.02).to(wl.dtype)
@@ -313,17 +351,23 @@ def main():
         cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
 
     if rank == 0:
+        tok_all = int((shapes_all[:, 0] * shapes_all[:, 1]).sum())
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16" if wl.dtype == torch.bfloat16 else str(wl.dtype).split(".")[-1],
             "data": "synthetic (seeded NaFlex grids, U[-1,1] pixels, trunc-normal weights)",
-            "config": {"workload": wl.name, "images_per_gpu": B, "max_patches": wl.max_patches,
-                       "valid_tokens_per_gpu": int((shapes[:, 0] * shapes[:, 1]).sum()),
-                       "padding_frac": round(1 - float((shapes[:, 0] * shapes[:, 1]).sum()) / (B * wl.max_patches), 4),
-                       "parallelism": f"dp{world} (images sharded, NCCL all-gather of pooled embeddings)",
+            "config": {"workload": wl.name, "images_per_gpu": wl.batch, "images_total": B_all,
+                       "max_patches": wl.max_patches, "valid_tokens_total": tok_all,
+                       "padding_frac": round(1 - tok_all / (B_all * wl.max_patches), 4),
+                       "parallelism": f"dp{world} (global batch sharded by image cost, NCCL all-gather of "
+                                      f"pooled embeddings)",
                        "l2": "working set (inputs 100 MB + weights 0.86 GB per step) larger than L2"},
-            "tflops_algorithmic": round(tflops, 1), "pct_of_peak": round(100 * tflops / peak_tf, 2),
+            "value_per_gpu": value / world,
+            "tflops_algorithmic": round(tflops, 1), "pct_of_peak": round(100 * tflops / (world * peak_tf), 2),
+            "tflops_note": "whole job; pct_of_peak against n_gpus x the per-GPU peak",
+            "forward_ms_per_step": {"max_rank": round(fwd_ms_max, 4), "min_rank": round(fwd_ms_min, 4)},
+            "allgather_ms_per_step": round(gather_ms, 4) if world > 1 else None,
             "peak": {"bf16_tflops": peak_tf, "kind": peak_kind},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": int(launches),

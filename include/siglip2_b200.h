@@ -62,12 +62,12 @@ typedef enum {
   SIGLIP2_EPI_LN_GELU = 3,    /* out = gelu_tanh(rstd(A)*(A.B^T - mu(A)*c1) + c2)      */
   SIGLIP2_EPI_BIAS_GELU = 4,  /* out = gelu_tanh(A.B^T + bias)                        */
   /* siglip2_gemm_rowsums only: LayerNorm statistics come from, or go to,
-   * per-row (sum, sum of squares) float pairs of the residual stream, in
-   * column-block slots (siglip2_rowsum_slots) */
+   * per-row (mean, centred sum of squares) float pairs of the residual
+   * stream, in column-block slots (siglip2_rowsum_slots) */
   SIGLIP2_EPI_LN_ROWSUMS = 5,      /* as SIGLIP2_EPI_LN, mu/rstd from rs_in over K columns    */
   SIGLIP2_EPI_LN_ROWSUMS_GELU = 6, /* as SIGLIP2_EPI_LN_GELU, likewise                        */
-  SIGLIP2_EPI_BIAS_RES_ROWSUMS = 7 /* as SIGLIP2_EPI_BIAS_RES, and rs_acc receives the (sum,
-                                      sum of squares) of the row's rounded outputs            */
+  SIGLIP2_EPI_BIAS_RES_ROWSUMS = 7 /* as SIGLIP2_EPI_BIAS_RES, and rs_acc receives the slot
+                                      statistics of the row's rounded outputs                 */
 } siglip2_epilogue;
 
 /* Library version (major*10000 + minor*100 + patch). */
@@ -93,8 +93,10 @@ int siglip2_set_gemm_variant(int variant);
 int siglip2_get_gemm_variant(void);
 
 /* Synchronises the current device and returns SIGLIP2_ERR_TIMEOUT if a kernel
- * gave up on a bounded wait since the last reset (the failing site id is in
- * siglip2_last_error()).  reset != 0 clears the flag. */
+ * gave up on a bounded wait since the last reset, or SIGLIP2_ERR_SHAPE if a
+ * kernel found an index outside a buffer it was given and skipped the access
+ * (the failing site id is in siglip2_last_error()).  reset != 0 clears the
+ * flag. */
 int siglip2_check_device(int reset);
 
 /* out[M,N] = epilogue(A[M,K] . B[N,K]^T).
@@ -106,31 +108,34 @@ int siglip2_gemm(int dtype, int epilogue, const void* a_dev, int lda, const void
                  int ldo, int M, int N, int K, const float* bias_dev, const void* res_dev, int ldr,
                  const float* c1_dev, const float* c2_dev, float eps, void* stream);
 
-/* Row sums for the LayerNorm-folded GEMMs are kept per column block: a
- * [rows][S] array of (sum, sum of squares) float pairs, S =
- * siglip2_rowsum_slots(dtype, width) for rows of `width` columns, slot j
- * covering columns [j * blk, min((j + 1) * blk, width)) with blk =
- * siglip2_rowsum_block(dtype, width) (half a GEMM tile).  Each slot is
- * written once by the GEMM that produces the rows and summed in slot order
- * by the GEMM that reads them, so results do not depend on scheduling. */
+/* LayerNorm statistics for the LayerNorm-folded GEMMs are kept per column
+ * block ("slots"): a [rows][S] array of float pairs (mean, centred sum of
+ * squares) of the block's values, S = siglip2_rowsum_slots(dtype, width) for
+ * rows of `width` columns, slot j covering columns [j * blk, min((j + 1) *
+ * blk, width)) with blk = siglip2_rowsum_block(dtype, width) (half a GEMM
+ * tile).  Each slot is written once by the GEMM that produces the rows (from
+ * sums shifted by the block's first value, so a large row mean does not
+ * cancel the variance) and merged in slot order by the GEMM that reads them
+ * (mean = sum n_j mean_j / width, M2 = sum M2_j + n_j (mean_j - mean)^2), so
+ * results do not depend on scheduling. */
 int siglip2_rowsum_slots(int dtype, int width);
 int siglip2_rowsum_block(int dtype, int width);
 
-/* Row sums of x [M, K] (row pitch ldx elements) in the slot layout above:
- * rs_dev[r * siglip2_rowsum_slots(dtype, K) + j] = (sum, sum of squares) of
- * row r over column block j.  For rows no row-sum GEMM produced, e.g. the
+/* Slot statistics of x [M, K] (row pitch ldx elements) in the layout above:
+ * rs_dev[r * siglip2_rowsum_slots(dtype, K) + j] = (mean, centred sum of
+ * squares) of row r over column block j.  For rows no row-sum GEMM produced, e.g. the
  * input of a stand-alone encoder layer (Siglip2EncoderLayer.forward,
  * model.py:204-223).  x 16-byte aligned; K and ldx multiples of 8 (bf16,
  * f16) or 4 (f32); rs_dev 8-byte aligned. */
 int siglip2_rowsums(int dtype, const void* x_dev, int ldx, int M, int K, float* rs_dev, void* stream);
 
 /* siglip2_gemm with row-sum LayerNorm plumbing: the GEMM that writes the
- * residual stream (SIGLIP2_EPI_BIAS_RES_ROWSUMS) writes each row's sum and
- * sum of squares into rs_acc ([M][siglip2_rowsum_slots(dtype, N)] pairs),
- * and the LayerNorm-folded GEMM that reads it (SIGLIP2_EPI_LN_ROWSUMS[_GELU])
- * takes mu = sum/K and rstd = 1/sqrt(sumsq/K - mu^2 + eps) from rs_in
- * ([M][siglip2_rowsum_slots(dtype, K)] pairs), so no pass over the rows is
- * needed for LayerNorm statistics.  Pointers not used by the epilogue may be
+ * residual stream (SIGLIP2_EPI_BIAS_RES_ROWSUMS) writes each row's slot
+ * statistics into rs_acc ([M][siglip2_rowsum_slots(dtype, N)] pairs), and the
+ * LayerNorm-folded GEMM that reads it (SIGLIP2_EPI_LN_ROWSUMS[_GELU]) merges
+ * rs_in ([M][siglip2_rowsum_slots(dtype, K)] pairs) into mu and rstd =
+ * 1/sqrt(M2/K + eps), so no pass over the rows is needed for LayerNorm
+ * statistics.  Pointers not used by the epilogue may be
  * NULL; row-sum buffers must be 8-byte aligned. */
 int siglip2_gemm_rowsums(int dtype, int epilogue, const void* a_dev, int lda, const void* b_dev, int ldb,
                          void* out_dev, int ldo, int M, int N, int K, const float* bias_dev, const void* res_dev,
@@ -143,7 +148,7 @@ int siglip2_gemm_rowsums(int dtype, int epilogue, const void* a_dev, int lda, co
  * b = tok_img[t] with grid (h, w) = hw[2b], hw[2b+1], and resize is the
  * antialiased bilinear interpolation of the grid x grid fp32 table
  * [grid^2, D].  rs_acc ([N][siglip2_rowsum_slots(dtype, D)] float pairs)
- * receives the (sum, sum of squares) of the rounded out rows: the LayerNorm
+ * receives the slot statistics of the rounded out rows: the LayerNorm
  * statistics of the first layer.  Replaces Siglip2SequenceEmbeddings.forward,
  * model.py:68-120. */
 int siglip2_patch_embed(int dtype, const void* patches_dev, int patch_dim, const void* w_dev, const float* bias_dev,
@@ -241,10 +246,14 @@ int siglip2_head_pool(int dtype, const void* x_dev, int D, int heads, const int*
  * allocator, where a cudaMalloc per call would synchronise the device).  No
  * counterpart in the reference.  Same inputs and result as
  * siglip2_head_pool, but the score scratch is a fixed 4 MiB device array
- * inside the library (1,048,576 floats, reserved on every GPU that loads the
- * library until exit): n_tokens * heads above that is rejected with
- * SIGLIP2_ERR_SHAPE.  n_tokens must equal cu_seqlens[B].  Nothing is
- * allocated (no cudaMalloc/cudaFree).  The first call on each device looks up
+ * inside the library (1,048,576 floats, reserved on each GPU once the
+ * library's kernels are first used there, until exit): n_tokens * heads
+ * above that is rejected with SIGLIP2_ERR_SHAPE.  n_tokens must equal
+ * cu_seqlens[B]; cu_seqlens lives on the device, so the kernel itself checks
+ * each image's score rows against n_tokens: an image reaching past it writes
+ * nothing (its pooled rows are left as they were) and the next
+ * siglip2_check_device() returns SIGLIP2_ERR_SHAPE.  Nothing is allocated (no
+ * cudaMalloc/cudaFree).  The first call on each device looks up
  * the array's device address once (cudaGetSymbolAddress) with that device
  * current; make that first call before any stream capture.  All calls share
  * the one array, so calls that overlap on the GPU (other streams, other host

@@ -1,10 +1,10 @@
 """Per-kernel timing driver at the tower's shapes (CUDA events), also the
 command the ncu summaries under ``profiles/`` were captured with.
 
-    python -m siglip2_b200.kernel_bench gemm --epi ln_gelu --m 39178 --n 4304 --k 1152
-    python -m siglip2_b200.kernel_bench fmha --preset so400m --images 64 --max-patches 1024
-    python -m siglip2_b200.kernel_bench layer --preset so400m --images 64 --max-patches 1024
-    python -m siglip2_b200.kernel_bench patchify --images 64 --height 768 --width 1024 --max-patches 1024
+    python kernel_bench.py gemm --epi ln_gelu --m 39178 --n 4304 --k 1152
+    python kernel_bench.py fmha --preset so400m --images 64 --max-patches 1024
+    python kernel_bench.py layer --preset so400m --images 64 --max-patches 1024
+    python kernel_bench.py patchify --images 64 --height 768 --width 1024 --max-patches 1024
 
 Prints one JSON line per measurement: milliseconds per launch, the
 algorithmic TFLOP/s (dense contractions only) and the median SM clock seen
@@ -16,13 +16,17 @@ from __future__ import annotations
 import argparse
 import json
 import math
+import os
+import sys
 
 import torch
 
-from . import _lib as L
-from . import ops
-from . import workloads as W
-from .clocks import ClockSampler
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+
+from siglip2_b200 import _lib as L  # noqa: E402
+from siglip2_b200 import ops  # noqa: E402
+from siglip2_b200 import workloads as W  # noqa: E402
+from siglip2_b200.clocks import ClockSampler  # noqa: E402
 
 EPIS = {"bias": L.EPI_BIAS, "bias_res": L.EPI_BIAS_RES, "ln": L.EPI_LN, "ln_gelu": L.EPI_LN_GELU,
         "bias_gelu": L.EPI_BIAS_GELU, "lnrs": L.EPI_LN_ROWSUMS, "lnrs_gelu": L.EPI_LN_ROWSUMS_GELU,
@@ -121,7 +125,7 @@ def bench_patchify(images: int, height: int, width: int, max_patches: int, reps:
 
     import numpy as np
 
-    from .image_processor import image_grid
+    from siglip2_b200.image_processor import image_grid
     g = torch.Generator(device="cuda").manual_seed(0)
     shape = (images, height, width, 3) if channels_last else (images, 3, height, width)
     pix = torch.randint(0, 256, shape, dtype=torch.uint8, device="cuda", generator=g)

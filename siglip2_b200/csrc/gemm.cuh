@@ -24,8 +24,9 @@
 // with c1[n] = sum_k (W*gamma)[n,k] and c2[n] = b[n] + sum_k beta[k] W[n,k].
 // The GEMM runs on the raw residual stream x against the pre-scaled weight
 // W*gamma; mu and rstd come either from the statistics warps or (kEpiLnRs*)
-// from row sums (sum, sum of squares) that the GEMM which produced x
-// accumulated in its own epilogue (kEpiBiasResRs / kEpiBiasPosRs).
+// from per-column-block slot statistics (mean, centred sum of squares; see
+// rowops.cuh) that the GEMM which produced x wrote in its own epilogue
+// (kEpiBiasResRs / kEpiBiasPosRs).
 #pragma once
 
 #include "rowops.cuh"
@@ -55,10 +56,10 @@ struct GemmParams {
   const float* c1;            // [N] (LayerNorm-folded epilogues)
   const float* c2;            // [N]
   float eps;                  // LayerNorm epsilon
-  // Row sums in slots: [M][rs_ld] (sum, sum of squares) pairs, slot j covering
-  // the j-th column block of the GEMM that produced the rows (see
-  // rowsum_block); each slot is written exactly once and read in slot order,
-  // so the LayerNorm statistics (and the forward) are deterministic.
+  // Row statistics in slots: [M][rs_ld] (mean, centred sum of squares) pairs,
+  // slot j covering the j-th column block of the GEMM that produced the rows
+  // (see rowsum_block); each slot is written exactly once and merged in slot
+  // order, so the LayerNorm statistics (and the forward) are deterministic.
   const float2* rs_in;        // A's row sums over K (kEpiLnRs*), rs_ld slots per row
   float2* rs_acc;             // output row sums to write (kEpiBiasResRs, kEpiBiasPosRs), rs_ld slots per row
   int rs_ld;
@@ -92,7 +93,8 @@ __host__ __device__ constexpr int epi_warps(int e) { return epi_has_stat_warps(e
 __host__ __device__ constexpr int gemm_bn_for(int) { return 256; }
 // Column block of one row-sum slot: the columns one epilogue warp drains of
 // a row-sum-producing tile (half the tile), or the SIMT fp32 tile width.
-__host__ __device__ constexpr int rowsum_block(bool f32, int N) { return f32 ? 128 : gemm_bn_for(N) / 2; }
+__host__ __device__ constexpr int rowsum_block(bool f32, int N) { return f32 ? kRowSumBlock : gemm_bn_for(N) / 2; }
+static_assert(gemm_bn_for(1) / 2 == kRowSumBlock, "slot width of the tensor-core epilogue");
 __host__ __device__ constexpr int rowsum_slots(bool f32, int N) {
   return (N + rowsum_block(f32, N) - 1) / rowsum_block(f32, N);
 }
@@ -225,21 +227,9 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
     prefetch_tile(tile + tile_step);
     float mu = 0.f, rstd = 1.f;
     if constexpr (kRsIn) {
-      // row sums of the raw A row (the previous GEMM's rounded output), slot
-      // by slot in a fixed order: fp32 E[x^2] - E[x]^2 over K = D values of
-      // O(1) magnitude
-      float2 rs = make_float2(0.f, 0.f);
-      if (my_row < p.M) {
-        const float2* r = p.rs_in + static_cast<size_t>(my_row) * p.rs_ld;
-        for (int j = 0; j < p.rs_ld; ++j) {
-          const float2 v = r[j];
-          rs.x += v.x;
-          rs.y += v.y;
-        }
-      }
-      const float inv_k = 1.f / static_cast<float>(p.K);
-      mu = rs.x * inv_k;
-      rstd = rsqrtf(fmaxf(rs.y * inv_k - mu * mu, 0.f) + p.eps);
+      // LayerNorm statistics of the raw A row (the previous GEMM's rounded
+      // output) merged from its column-block slots in a fixed order
+      if (my_row < p.M) slot_stats_merge(p.rs_in + static_cast<size_t>(my_row) * p.rs_ld, p.rs_ld, p.K, p.eps, mu, rstd);
     }
     if (*abort_flag || !mbar_wait<kCluster>(&tfull[buf], tph, 121)) {
       *abort_flag = 1;
@@ -256,7 +246,10 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
       __syncwarp();
       if (lane == 0) mbar_arrive(&sempty[buf]);
     }
-    float rs1 = 0.f, rs2 = 0.f;  // sums over this warp's columns of the rounded outputs (kRsOut)
+    // sums over this warp's columns of the rounded outputs minus the first of
+    // them (kRsOut): shifted sums keep the slot variance exact when the row's
+    // mean is large against its spread
+    float rs1 = 0.f, rs2 = 0.f, rs_shift = 0.f;
     AxisTaps ay{0, 0, 0.f, 1.f, 0.f}, ax{0, 0, 0.f, 1.f, 0.f};  // position-embedding taps of this row (kPos)
     if constexpr (kPos) {
       if (my_row < p.M) {
@@ -367,8 +360,10 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
 #pragma unroll
             for (int h2 = 0; h2 < 4; ++h2) {
               const float2 f = Pack2<T>::unpack(ow[h2]);
-              rs1 += f.x + f.y;
-              rs2 = fmaf(f.x, f.x, fmaf(f.y, f.y, rs2));
+              if (c == 0 && g == 0 && h2 == 0) rs_shift = f.x;
+              const float a0 = f.x - rs_shift, a1 = f.y - rs_shift;
+              rs1 += a0 + a1;
+              rs2 = fmaf(a0, a0, fmaf(a1, a1, rs2));
             }
           }
         }
@@ -392,7 +387,9 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
     }
     if constexpr (kRsOut) {
       // this warp's column block is one slot (block width kPartCols = BN / 2)
-      if (my_row < p.M && c0 < p.N) p.rs_acc[static_cast<size_t>(my_row) * p.rs_ld + c0 / kPartCols] = make_float2(rs1, rs2);
+      if (my_row < p.M && c0 < p.N)
+        p.rs_acc[static_cast<size_t>(my_row) * p.rs_ld + c0 / kPartCols] =
+            slot_stats_from_shifted(rs1, rs2, rs_shift, min(kPartCols, p.N - c0));
     }
   }
   if (lane == 0) tma_store_wait_all<0>();

@@ -22,11 +22,16 @@ namespace sg {
 //   x:       rows of the image are base + i, i < L (base = cu[b], or b * P
 //            when the hidden state is stored padded)
 //   u:       [H, D] float32, already scaled by log2(e) / sqrt(hd)
-//   scores:  [N_rows_total, H] float32 scratch (indexed by packed token)
+//   scores:  [score_rows, H] float32 scratch (indexed by packed token)
 //   pooled:  [B, H, D] element type T
+// An image whose score rows [cu[b], cu[b+1]) do not lie inside
+// [0, score_rows) writes nothing: its CTA records kSiteHeadPoolScores in the
+// device error flag and returns (the scratch may be a fixed array whose
+// size the caller does not control).
 template <typename T>
 __global__ void head_pool_kernel(const T* __restrict__ x, int D, int H, const int* __restrict__ cu, int pad_P,
-                                 const float* __restrict__ u, float* __restrict__ scores, T* __restrict__ pooled) {
+                                 const float* __restrict__ u, float* __restrict__ scores, int score_rows,
+                                 T* __restrict__ pooled) {
   extern __shared__ float sh[];  // u: [H][D], then m[H], inv[H]
   float* su = sh;
   float* sm = su + H * D;
@@ -34,6 +39,10 @@ __global__ void head_pool_kernel(const T* __restrict__ x, int D, int H, const in
   const int b = blockIdx.x;
   const int t0 = cu[b];
   const int L = cu[b + 1] - t0;
+  if (t0 < 0 || L < 0 || static_cast<long long>(t0) + L > score_rows) {  // uniform over the CTA
+    if (threadIdx.x == 0) record_error(kSiteHeadPoolScores);
+    return;
+  }
   const size_t base = pad_P > 0 ? static_cast<size_t>(b) * pad_P : static_cast<size_t>(t0);
   const int nthr = blockDim.x;
   for (int i = threadIdx.x; i < H * D; i += nthr) su[i] = u[i];

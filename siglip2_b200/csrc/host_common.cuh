@@ -9,7 +9,9 @@
 #include <stdio.h>
 
 #include <atomic>
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "../../include/siglip2_b200.h"
 
@@ -138,16 +140,41 @@ inline int make_tmap_3d(CUtensorMap* map, const void* base, int elem_bytes, int6
   return SIGLIP2_OK;
 }
 
+// Per-device host caches: one process may drive several GPUs (one host
+// thread per device, or cudaSetDevice between calls), so anything learnt from
+// or set on a device is kept per device ordinal.
+constexpr int kMaxDevices = 64;
+
+// SM count of the current device (queried once per device).
 inline int sm_count() {
-  static int n = 0;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
-  });
+  static std::atomic<int> cache[kMaxDevices];  // zero-initialised: not yet queried
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+  const bool cached = dev >= 0 && dev < kMaxDevices;
+  int n = cached ? cache[dev].load(std::memory_order_relaxed) : 0;
+  if (n == 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    if (cached) cache[dev].store(n, std::memory_order_relaxed);
+  }
   return n;
+}
+
+// cudaFuncAttributeMaxDynamicSharedMemorySize holds per kernel and per
+// device: raise it on the current device when a launch needs more than was
+// set there before (never lowers it, so launches of different sizes can
+// interleave).
+inline int ensure_dynamic_smem(const void* kern, int bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> set_bytes;  // (kernel, device) -> attribute value
+  int dev = 0;
+  SG_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  int& cur = set_bytes[std::make_pair(kern, dev)];
+  if (bytes > cur) {
+    SG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    cur = bytes;
+  }
+  return SIGLIP2_OK;
 }
 
 }  // namespace sg

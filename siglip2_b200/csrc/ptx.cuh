@@ -20,6 +20,12 @@ namespace sg {
 // ----------------------------------------------------------------------------
 __device__ int g_device_error = 0;   // 0 = ok, else first failing site id
 
+// Site ids from kSiteBoundsFirst on mark a kernel that found an index outside
+// the buffer it was given, skipped the access and returned (the host reports
+// those as SIGLIP2_ERR_SHAPE; lower ids are bounded waits that gave up).
+constexpr int kSiteBoundsFirst = 1000;
+constexpr int kSiteHeadPoolScores = 1001;  // head_pool_kernel: score row past score_rows
+
 // 4 s: far above any legitimate wait inside one launch, short enough that a
 // broken pipeline returns an error instead of holding the GPU.
 constexpr unsigned long long kWaitLimitNs = 4000000000ull;

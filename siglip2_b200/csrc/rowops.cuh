@@ -58,6 +58,39 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 // ---------------------------------------------------------------------------
+// LayerNorm statistics in column-block slots.  Slot j of a row holds
+// (mean, centred sum of squares) of the row's columns [j*blk, min((j+1)*blk, K)):
+// producers that see a block once (the GEMM epilogues) accumulate sums of
+// x - s with s the block's first value, so the variance does not cancel when
+// the row's mean is large against its spread; the reader merges the slots
+// with the pairwise update of Chan, Golub and LeVeque (1979):
+//   mean = sum_j n_j mean_j / K,   M2 = sum_j (M2_j + n_j (mean_j - mean)^2).
+// ---------------------------------------------------------------------------
+constexpr int kRowSumBlock = 128;  // columns per slot
+
+__device__ __forceinline__ float2 slot_stats_from_shifted(float s1, float s2, float shift, int n) {
+  const float inv_n = 1.f / static_cast<float>(n);
+  const float d = s1 * inv_n;  // mean - shift
+  return make_float2(shift + d, fmaxf(s2 - s1 * d, 0.f));
+}
+
+// (mu, rstd) of a K-column row from its `slots` slot statistics (blocks of kRowSumBlock)
+__device__ __forceinline__ void slot_stats_merge(const float2* __restrict__ r, int slots, int K, float eps, float& mu,
+                                                 float& rstd) {
+  float sm = 0.f;
+  for (int j = 0; j < slots; ++j) sm = fmaf(static_cast<float>(min(kRowSumBlock, K - j * kRowSumBlock)), r[j].x, sm);
+  const float m = sm / static_cast<float>(K);
+  float m2 = 0.f;
+  for (int j = 0; j < slots; ++j) {
+    const float2 v = r[j];
+    const float dm = v.x - m;
+    m2 += fmaf(static_cast<float>(min(kRowSumBlock, K - j * kRowSumBlock)) * dm, dm, v.y);
+  }
+  mu = m;
+  rstd = rsqrtf(m2 / static_cast<float>(K) + eps);
+}
+
+// ---------------------------------------------------------------------------
 // LayerNorm, one warp per row, two-pass (mean, then centred variance) from
 // registers; D <= 32 * 8 * MAXV elements.
 //
@@ -254,12 +287,13 @@ __global__ void __launch_bounds__(256) l2norm_kernel(const T* __restrict__ x, in
   }
 }
 
-// Row sums in the slot layout the LayerNorm-folded GEMMs read: for row r and
-// column block j (columns [j*blk, min((j+1)*blk, K))), rs[r*slots + j] =
-// (sum, sum of squares).  For rows that no row-sum GEMM produced (the input
-// of a stand-alone encoder layer).  One warp per row, 16-byte loads; K, ldx
-// and blk are multiples of the vector width and x is 16-byte aligned (the
-// host checks).
+// Slot statistics in the layout the LayerNorm-folded GEMMs read: for row r
+// and column block j (columns [j*blk, min((j+1)*blk, K))), rs[r*slots + j] =
+// (mean, centred sum of squares), two passes over the block (the second
+// reads it from L1).  For rows that no row-sum GEMM produced (the input of a
+// stand-alone encoder layer).  One warp per row, 16-byte loads; K, ldx and
+// blk are multiples of the vector width and x is 16-byte aligned (the host
+// checks).
 template <typename T>
 __global__ void __launch_bounds__(256) rowsums_kernel(const T* __restrict__ x, int ldx, int M, int K, int blk,
                                                       float2* __restrict__ rs, int slots) {
@@ -270,19 +304,26 @@ __global__ void __launch_bounds__(256) rowsums_kernel(const T* __restrict__ x, i
   const T* xr = x + static_cast<size_t>(row) * ldx;
   for (int j = 0; j < slots; ++j) {
     const int c_end = min(K, (j + 1) * blk);
-    float s1 = 0.f, s2 = 0.f;
+    float s1 = 0.f;
+    for (int c = j * blk + lane * V; c < c_end; c += 32 * V) {
+      float f[V];
+      load_vec(xr + c, f);
+#pragma unroll
+      for (int i = 0; i < V; ++i) s1 += f[i];
+    }
+    const float mean = warp_sum(s1) / static_cast<float>(c_end - j * blk);
+    float s2 = 0.f;
     for (int c = j * blk + lane * V; c < c_end; c += 32 * V) {
       float f[V];
       load_vec(xr + c, f);
 #pragma unroll
       for (int i = 0; i < V; ++i) {
-        s1 += f[i];
-        s2 = fmaf(f[i], f[i], s2);
+        const float d = f[i] - mean;
+        s2 = fmaf(d, d, s2);
       }
     }
-    s1 = warp_sum(s1);
     s2 = warp_sum(s2);
-    if (lane == 0) rs[static_cast<size_t>(row) * slots + j] = make_float2(s1, s2);
+    if (lane == 0) rs[static_cast<size_t>(row) * slots + j] = make_float2(mean, s2);
   }
 }
 

@@ -2,6 +2,7 @@
 // One translation unit: every kernel header is included here and compiled
 // for sm_100a only.
 #include <algorithm>
+#include <climits>
 #include <cmath>
 #include <type_traits>
 #include <vector>
@@ -48,11 +49,7 @@ int launch_gemm_tc(const GemmIO& io, const GemmParams& p, cudaStream_t stream) {
   constexpr int threads = kGemmThreads;
   constexpr int smem = GemmCfg<BN, SUB, EPI>::kSmemBytes;
   auto kern = gemm_tc_kernel<T, BN, EPI, SUB>;
-  static bool attr_done = false;  // per instantiation
-  if (!attr_done) {
-    SG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr_done = true;
-  }
+  SG_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem));
   const int tiles = ((p.M + kGemmBM - 1) / kGemmBM) * ((p.N + BN - 1) / BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
   cudaLaunchConfig_t cfg = {};
@@ -81,11 +78,7 @@ int launch_gemm_tc2(const GemmIO& io, const GemmParams& p, cudaStream_t stream) 
   constexpr int threads = kGemmThreads;
   constexpr int smem = Gemm2Cfg<BN, SUB, EPI>::kSmemBytes;
   auto kern = gemm_tc2_kernel<T, BN, EPI, SUB>;
-  static bool attr_done = false;  // per instantiation
-  if (!attr_done) {
-    SG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr_done = true;
-  }
+  SG_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem));
   const int tiles = ((p.M + 2 * kGemmBM - 1) / (2 * kGemmBM)) * ((p.N + BN - 1) / BN);
   const int pairs = std::min(tiles, sm_count() / 2);
   cudaLaunchConfig_t cfg = {};
@@ -371,12 +364,10 @@ int launch_patchify(const PatchifyArgs& a, bool fast, bool any_resize, size_t sm
     patchify16x3_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, s>>>(a, o, mask);
     SG_LAUNCH_CHECK();
     if (!any_resize) return SIGLIP2_OK;
-    SG_CUDA(cudaFuncSetAttribute(patchify_kernel<T, 3, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(smem)));
+    SG_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(patchify_kernel<T, 3, 16>), static_cast<int>(smem)));
     patchify_kernel<T, 3, 16><<<static_cast<unsigned>(n_rows), kPatchifyThreads, smem, s>>>(a, o, mask);
   } else {
-    SG_CUDA(cudaFuncSetAttribute(patchify_kernel<T, 0, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(smem)));
+    SG_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(patchify_kernel<T, 0, 0>), static_cast<int>(smem)));
     patchify_kernel<T, 0, 0><<<static_cast<unsigned>(n_rows), kPatchifyThreads, smem, s>>>(a, o, mask);
   }
   SG_LAUNCH_CHECK();
@@ -506,11 +497,7 @@ int launch_fmha(const void* qkv, int N, const int* cu, const int2* tiles, int n_
   p.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(hd));
   auto kern = fmha_varlen_kernel<T, HDP>;
   constexpr int smem = FmhaCfg<HDP>::kSmem;
-  static bool attr_done = false;
-  if (!attr_done) {
-    SG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr_done = true;
-  }
+  SG_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem));
   // persistent: two CTAs per SM walk the (query tile, head) items
   const int grid = std::min(p.n_items, 2 * sm_count());
   cudaLaunchConfig_t cfg = {};
@@ -579,7 +566,7 @@ int launch_head_pool_parallel(const void* x, int D, int H, const int* cu, int B,
                               const float* u, float* scores, void* pooled, cudaStream_t s) {
   const int smem = H * D * 4;
   auto ks = head_scores_kernel<T>;
-  SG_CUDA(cudaFuncSetAttribute(ks, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  SG_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(ks), smem));
   const int warps = 16;
   int blocks = (N + warps - 1) / warps;
   blocks = std::min(blocks, 4 * sm_count());
@@ -609,7 +596,7 @@ int sg_head_pool_parallel(int dtype, const void* x, int D, int H, const int* cu,
 }
 
 int sg_head_pool_impl(int dtype, const void* x, int D, int H, const int* cu, int B, int pad_P, const float* u,
-                      float* scores, void* pooled, cudaStream_t s) {
+                      float* scores, int score_rows, void* pooled, cudaStream_t s) {
   SG_CHECK_ARG(H % 4 == 0 && H <= 16 && D % 8 == 0, "head pooling needs H %% 4 == 0, H <= 16, D %% 8 == 0");
   const int threads = (D / 8) * (H / 4);
   SG_CHECK_ARG(threads <= 1024, "head pooling: D=%d H=%d needs too many threads", D, H);
@@ -618,20 +605,23 @@ int sg_head_pool_impl(int dtype, const void* x, int D, int H, const int* cu, int
   switch (dtype) {
     case SIGLIP2_BF16: {
       auto k = head_pool_kernel<__nv_bfloat16>;
-      SG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      k<<<B, nt, smem, s>>>(static_cast<const __nv_bfloat16*>(x), D, H, cu, pad_P, u, scores, static_cast<__nv_bfloat16*>(pooled));
+      SG_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(k), smem));
+      k<<<B, nt, smem, s>>>(static_cast<const __nv_bfloat16*>(x), D, H, cu, pad_P, u, scores, score_rows,
+                             static_cast<__nv_bfloat16*>(pooled));
       break;
     }
     case SIGLIP2_F16: {
       auto k = head_pool_kernel<__half>;
-      SG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      k<<<B, nt, smem, s>>>(static_cast<const __half*>(x), D, H, cu, pad_P, u, scores, static_cast<__half*>(pooled));
+      SG_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(k), smem));
+      k<<<B, nt, smem, s>>>(static_cast<const __half*>(x), D, H, cu, pad_P, u, scores, score_rows,
+                             static_cast<__half*>(pooled));
       break;
     }
     case SIGLIP2_F32: {
       auto k = head_pool_kernel<float>;
-      SG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      k<<<B, nt, smem, s>>>(static_cast<const float*>(x), D, H, cu, pad_P, u, scores, static_cast<float*>(pooled));
+      SG_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(k), smem));
+      k<<<B, nt, smem, s>>>(static_cast<const float*>(x), D, H, cu, pad_P, u, scores, score_rows,
+                             static_cast<float*>(pooled));
       break;
     }
     default: return set_error(SIGLIP2_ERR_ARG, "unknown dtype %d", dtype);
@@ -829,6 +819,8 @@ int siglip2_check_device(int reset) {
     const int zero = 0;
     SG_CUDA(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)));
   }
+  if (flag >= kSiteBoundsFirst)
+    return set_error(SIGLIP2_ERR_SHAPE, "a kernel skipped an index outside the buffer it was given (site %d)", flag);
   if (flag) return set_error(SIGLIP2_ERR_TIMEOUT, "a kernel gave up on a bounded wait (site %d)", flag);
   return SIGLIP2_OK;
 }
@@ -931,8 +923,11 @@ int siglip2_head_pool_noalloc(int dtype, const void* x_dev, int D, int heads, co
     return set_error(SIGLIP2_ERR_ALIGN, "head_pool tensors must be 16-byte aligned");
   float* scores = nullptr;
   SG_TRY(noalloc_scores_ptr(&scores));
-  return sg_head_pool_impl(dtype, x_dev, D, heads, cu_seqlens_dev, B, max_patches, u_dev, scores, pooled_dev,
-                           static_cast<cudaStream_t>(stream));
+  // the kernel writes score rows cu[b] .. cu[b+1]-1 only when they lie below
+  // n_tokens (checked above to fit the fixed array); an image past it is
+  // skipped and reported by siglip2_check_device as SIGLIP2_ERR_SHAPE
+  return sg_head_pool_impl(dtype, x_dev, D, heads, cu_seqlens_dev, B, max_patches, u_dev, scores, n_tokens,
+                           pooled_dev, static_cast<cudaStream_t>(stream));
 }
 
 int siglip2_head_pool(int dtype, const void* x_dev, int D, int heads, const int* cu_seqlens_dev, int B,
@@ -941,8 +936,8 @@ int siglip2_head_pool(int dtype, const void* x_dev, int D, int heads, const int*
                "bad head_pool arguments");
   if (!aligned16(x_dev) || !aligned16(pooled_dev))
     return set_error(SIGLIP2_ERR_ALIGN, "head_pool tensors must be 16-byte aligned");
-  return sg_head_pool_impl(dtype, x_dev, D, heads, cu_seqlens_dev, B, max_patches, u_dev, scores_dev, pooled_dev,
-                           static_cast<cudaStream_t>(stream));
+  return sg_head_pool_impl(dtype, x_dev, D, heads, cu_seqlens_dev, B, max_patches, u_dev, scores_dev, INT_MAX,
+                           pooled_dev, static_cast<cudaStream_t>(stream));
 }
 
 int siglip2_metadata_size(const int32_t* hw_host, int batch, int* n_tokens, int* n_tiles) {

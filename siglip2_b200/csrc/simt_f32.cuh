@@ -70,22 +70,13 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
     }
     float mu = 0.f, rstd = 1.f;
     if constexpr (kLnRs) {
-      if (row_ok) {
-        float sx = 0.f, sxx = 0.f;  // slot by slot, in order
-        for (int j = 0; j < p.rs_ld; ++j) {
-          const float2 v = p.rs_in[static_cast<size_t>(row) * p.rs_ld + j];
-          sx += v.x;
-          sxx += v.y;
-        }
-        const float inv_k = 1.f / static_cast<float>(p.K);
-        mu = sx * inv_k;
-        rstd = 1.f / sqrtf(fmaxf(sxx * inv_k - mu * mu, 0.f) + p.eps);
-      }
+      if (row_ok) slot_stats_merge(p.rs_in + static_cast<size_t>(row) * p.rs_ld, p.rs_ld, p.K, p.eps, mu, rstd);
     }
-    float s1 = 0.f, s2 = 0.f;
+    float vout[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int col = n0 + tx * 8 + j;
+      vout[j] = 0.f;
       if (!row_ok || col >= p.N) continue;
       float v = acc[i][j];
       if constexpr (kLnRs) {
@@ -101,38 +92,51 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
       if constexpr (kGelu) v = 0.5f * v * (1.f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v)));
       if constexpr (epi_has_res(EPI)) v += res[static_cast<size_t>(row) * ldr + col];
       out[static_cast<size_t>(row) * ldo + col] = v;
-      s1 += v;
-      s2 = fmaf(v, v, s2);
+      vout[j] = v;
     }
     if constexpr (kRsOut) {
-      // this CTA's 128 columns are one slot: reduce over the 16 threads of the row in a fixed order
+      // this CTA's 128 columns are one slot: (mean, centred sum of squares),
+      // two passes over the row's values, reduced over the 16 threads of the
+      // row in a fixed order
+      const int n_valid = min(kSgBN, p.N - n0);
+      float s1 = 0.f;
 #pragma unroll
-      for (int o = 8; o > 0; o >>= 1) {
-        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-        s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+      for (int j = 0; j < 8; ++j) s1 += vout[j];
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+      const float mean = s1 / static_cast<float>(n_valid);
+      float s2 = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = n0 + tx * 8 + j < p.N ? vout[j] - mean : 0.f;
+        s2 = fmaf(d, d, s2);
       }
-      if (tx == 0 && row_ok) p.rs_acc[static_cast<size_t>(row) * p.rs_ld + blockIdx.x] = make_float2(s1, s2);
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+      if (tx == 0 && row_ok) p.rs_acc[static_cast<size_t>(row) * p.rs_ld + blockIdx.x] = make_float2(mean, s2);
     }
   }
 }
 
-// Row sums (sum, sum of squares) of a [M, K] fp32 matrix in 128-column slots
-// ([M][ld] pairs): the statistics the row-sum LayerNorm epilogues read, for
-// rows whose producer is not a GEMM.  One warp per row.
+// Slot statistics (mean, centred sum of squares) of a [M, K] fp32 matrix in
+// 128-column slots ([M][ld] pairs): what the row-sum LayerNorm epilogues
+// read, for rows whose producer is not a GEMM.  One warp per row, two passes.
 __global__ void rowsums_f32_kernel(const float* __restrict__ x, int M, int K, float2* __restrict__ rs, int ld) {
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
   for (int j = 0; j < ld; ++j) {
-    float s1 = 0.f, s2 = 0.f;
-    for (int k = j * 128 + lane; k < min(K, (j + 1) * 128); k += 32) {
-      const float v = x[static_cast<size_t>(row) * K + k];
-      s1 += v;
-      s2 = fmaf(v, v, s2);
+    const int k_end = min(K, (j + 1) * kRowSumBlock);
+    float s1 = 0.f;
+    for (int k = j * kRowSumBlock + lane; k < k_end; k += 32) s1 += x[static_cast<size_t>(row) * K + k];
+    const float mean = warp_sum(s1) / static_cast<float>(k_end - j * kRowSumBlock);
+    float s2 = 0.f;
+    for (int k = j * kRowSumBlock + lane; k < k_end; k += 32) {
+      const float d = x[static_cast<size_t>(row) * K + k] - mean;
+      s2 = fmaf(d, d, s2);
     }
-    s1 = warp_sum(s1);
     s2 = warp_sum(s2);
-    if (lane == 0) rs[static_cast<size_t>(row) * ld + j] = make_float2(s1, s2);
+    if (lane == 0) rs[static_cast<size_t>(row) * ld + j] = make_float2(mean, s2);
   }
 }
 

@@ -603,9 +603,13 @@ class Siglip2MultiheadAttentionPoolingHead(nn.Module):
         projections, LayerNorm, MLP and residual (library GEMMs).  The valid
         rows of an image must be its first ones, as ``attention_mask`` marks
         them in the padded forward (other masks raise); without a mask every
-        row is valid.  Inference only (no backward)."""
-        if hidden_state.requires_grad and torch.is_grad_enabled():
-            raise NotImplementedError("the attention-pooling head has no backward in siglip2_b200")
+        row is valid.  Inference only (no backward): with autograd recording
+        (grad mode on and the input or any of the head's parameters requiring
+        grad) it raises rather than leave gradients silently missing; call it
+        under ``torch.no_grad()`` / ``torch.inference_mode()``."""
+        if _needs_grad(self, hidden_state):
+            raise NotImplementedError("the attention-pooling head has no backward in siglip2_b200: call it under "
+                                      "torch.no_grad() or torch.inference_mode()")
         B, P, D = hidden_state.shape
         H = self.num_heads
         if attention_mask is None:

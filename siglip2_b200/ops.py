@@ -136,9 +136,10 @@ def rowsum_slots(dtype: torch.dtype, width: int) -> int:
 
 
 def rowsums_reference(x: torch.Tensor) -> torch.Tensor:
-    """Row sums of ``x`` in the slot layout the LayerNorm-folded GEMMs read
-    (``[M, S, 2]`` float32), computed with torch: for tests and callers whose
-    rows were not produced by a row-sum GEMM."""
+    """Slot statistics of ``x`` in the layout the LayerNorm-folded GEMMs read
+    (``[M, S, 2]`` float32: per column block the mean and the centred sum of
+    squares), computed with torch: for tests and callers whose rows were not
+    produced by a row-sum GEMM."""
     M, K = x.shape
     S = rowsum_slots(x.dtype, K)
     blk = L.check_value(L.load().siglip2_rowsum_block(dtype_code(x.dtype), K))
@@ -146,13 +147,24 @@ def rowsums_reference(x: torch.Tensor) -> torch.Tensor:
     out = torch.zeros(M, S, 2, dtype=torch.float32, device=x.device)
     for j in range(S):
         part = xf[:, j * blk:(j + 1) * blk]
-        out[:, j, 0] = part.sum(1)
-        out[:, j, 1] = (part * part).sum(1)
+        mean = part.mean(1)
+        out[:, j, 0] = mean
+        out[:, j, 1] = ((part - mean[:, None]) ** 2).sum(1)
     return out
 
 
+def slot_stats_merge(rs: torch.Tensor, width: int, blk: int = 128) -> tuple[torch.Tensor, torch.Tensor]:
+    """Row mean and biased variance from ``[M, S, 2]`` slot statistics (the
+    merge the LayerNorm-folded GEMMs do), for tests."""
+    n = torch.tensor([min(blk, width - j * blk) for j in range(rs.shape[1])], dtype=torch.float32,
+                     device=rs.device)
+    mean = (rs[..., 0] * n).sum(1) / width
+    m2 = (rs[..., 1] + n * (rs[..., 0] - mean[:, None]) ** 2).sum(1)
+    return mean, m2 / width
+
+
 def rowsums(x: torch.Tensor) -> torch.Tensor:
-    """``siglip2_rowsums``: row sums of ``x [M, K]`` in the slot layout the
+    """``siglip2_rowsums``: slot statistics of ``x [M, K]`` in the layout the
     LayerNorm-folded GEMMs read (``[M, rowsum_slots(dtype, K), 2]`` float32)."""
     _need_cuda(x)
     assert x.dim() == 2 and x.stride(1) == 1
@@ -168,7 +180,7 @@ def gemm_rowsums(a: torch.Tensor, w: torch.Tensor, epilogue: int, bias=None, res
                  out: torch.Tensor | None = None) -> torch.Tensor:
     """``siglip2_gemm_rowsums``: row-sum LayerNorm epilogues.  ``rs_in`` is
     ``[M, rowsum_slots(dtype, K), 2]`` and ``rs_acc`` ``[M, rowsum_slots(dtype, N), 2]``
-    float32 (sum, sum of squares) per column block."""
+    float32 (mean, centred sum of squares) per column block."""
     _need_cuda(a, w, bias, res, c1, c2, rs_in, rs_acc, out)
     M, K = a.shape
     N = w.shape[0]
@@ -188,7 +200,8 @@ def gemm_rowsums(a: torch.Tensor, w: torch.Tensor, epilogue: int, bias=None, res
 def patch_embed(patches: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, table_f32: torch.Tensor,
                 hw: torch.Tensor, cu_seqlens: torch.Tensor, tok_img: torch.Tensor, rs_acc: torch.Tensor | None = None):
     """``siglip2_patch_embed``: patch Linear with the resized position grid
-    added in the GEMM epilogue; also accumulates row sums into ``rs_acc``."""
+    added in the GEMM epilogue; also writes the slot statistics of its rows
+    into ``rs_acc``."""
     _need_cuda(patches, w, bias, table_f32, hw, cu_seqlens, tok_img)
     N, C = patches.shape
     D = w.shape[0]

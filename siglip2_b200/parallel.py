@@ -36,20 +36,35 @@ def shard_images(shapes, world: int, d_model: int = 1152, mlp: int = 4304) -> li
     return [sorted(o) for o in owned]
 
 
+class PooledGather:
+    """The path's one collective, set up once per sharding: every rank's
+    ``[B_r, D]`` pooled rows are padded to the largest shard, gathered with
+    one ``all_gather_into_tensor`` and put back into global image order with
+    one precomputed ``index_select`` (no host work or host-to-device copy per
+    call)."""
+
+    def __init__(self, owned: list[list[int]], dim: int, dtype, device, group=None):
+        self.world = len(owned)
+        self.bmax = max(len(o) for o in owned)
+        self.group = group
+        self.send = torch.zeros((self.bmax, dim), dtype=dtype, device=device)
+        self.recv = torch.empty((self.world * self.bmax, dim), dtype=dtype, device=device)
+        pos = {}
+        for r, idx in enumerate(owned):
+            for k, i in enumerate(idx):
+                pos[i] = r * self.bmax + k
+        total = sum(len(o) for o in owned)
+        assert sorted(pos) == list(range(total)), "shards must cover every image exactly once"
+        self.index = torch.tensor([pos[i] for i in range(total)], dtype=torch.int64, device=device)
+
+    def __call__(self, pooled_local: torch.Tensor) -> torch.Tensor:
+        n = pooled_local.shape[0]
+        self.send[:n].copy_(pooled_local)
+        dist.all_gather_into_tensor(self.recv, self.send, group=self.group)
+        return self.recv.index_select(0, self.index)
+
+
 def gather_pooled(pooled_local: torch.Tensor, owned: list[list[int]], group=None) -> torch.Tensor:
     """All-gather every rank's ``[B_r, D]`` pooled rows and return ``[B, D]``
-    in global image order.  Ranks are padded to the largest shard so one
-    ``all_gather_into_tensor`` suffices."""
-    world = len(owned)
-    bmax = max(len(o) for o in owned)
-    D = pooled_local.shape[1]
-    send = torch.zeros((bmax, D), dtype=pooled_local.dtype, device=pooled_local.device)
-    send[: pooled_local.shape[0]] = pooled_local
-    recv = torch.empty((world * bmax, D), dtype=pooled_local.dtype, device=pooled_local.device)
-    dist.all_gather_into_tensor(recv, send, group=group)
-    total = sum(len(o) for o in owned)
-    out = torch.empty((total, D), dtype=pooled_local.dtype, device=pooled_local.device)
-    for r, idx in enumerate(owned):
-        if idx:
-            out[torch.tensor(idx, device=out.device)] = recv[r * bmax: r * bmax + len(idx)]
-    return out
+    in global image order (one-shot form of ``PooledGather``)."""
+    return PooledGather(owned, pooled_local.shape[1], pooled_local.dtype, pooled_local.device, group)(pooled_local)

@@ -109,6 +109,24 @@ def make_pixels(spatial_shapes: torch.Tensor, max_patches: int, patch_dim: int, 
     return pv.to(dtype), mask
 
 
+def make_pixels_indexed(spatial_shapes: torch.Tensor, image_ids, max_patches: int, patch_dim: int,
+                        seed: int = 1337, dtype=torch.float32):
+    """As ``make_pixels``, but image ``i`` of a global batch draws its rows
+    from a generator of its own (seeded by ``seed`` and its global index
+    ``image_ids[k]``), so any subset of the batch, e.g. one rank's shard,
+    gets exactly the pixels it has in the whole batch."""
+    B = spatial_shapes.shape[0]
+    assert len(image_ids) == B
+    pv = torch.zeros((B, max_patches, patch_dim), dtype=dtype)
+    mask = torch.zeros((B, max_patches), dtype=torch.int32)
+    for k, i in enumerate(image_ids):
+        L = int(spatial_shapes[k, 0] * spatial_shapes[k, 1])
+        g = torch.Generator().manual_seed((seed + 1) * 1_000_003 + int(i))
+        pv[k, :L] = (torch.rand((L, patch_dim), generator=g) * 2.0 - 1.0).to(dtype)
+        mask[k, :L] = 1
+    return pv, mask
+
+
 def pack_rows(pixel_values: torch.Tensor, spatial_shapes: torch.Tensor) -> torch.Tensor:
     """Padded ``[B, P, C]`` -> packed ``[sum h*w, C]`` (valid rows only)."""
     lens = (spatial_shapes[:, 0] * spatial_shapes[:, 1]).tolist()

@@ -2,7 +2,7 @@
 
 Run once, in a container that has the reference checkout and transformers:
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <path to the tohskai/SigLIP-2 checkout>
 
 It imports the reference's own ``model.py`` (tohskai/SigLIP-2) on the CPU in
 fp32 and runs its packed forward (``model.py:260-292``).  Two adjustments are
@@ -123,4 +123,6 @@ def main(ref_root: str):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path to a tohskai/SigLIP-2 checkout>")
+    main(sys.argv[1])

@@ -415,19 +415,24 @@ def test_map_head_module(dtype):
     lens, P, D = [200, 37, 256, 1], 256, cfg.hidden_size
     x = _rand((len(lens), P, D), dtype, seed=13)
     mask = (torch.arange(P)[None] < torch.tensor(lens)[:, None]).to(torch.int64)
-    out = head(x, mask.cuda())
+    with pytest.raises(NotImplementedError):  # autograd recording (parameters require grad): refused
+        head(x, mask.cuda())
+    with torch.no_grad():
+        out = head(x, mask.cuda())
+        full = head(x[:, :100])  # no mask: every row valid
     assert out.shape == (len(lens), D)
     packed = torch.cat([x[b, :n] for b, n in enumerate(lens)], 0)
     grids = [(n, 1) for n in lens]
     _check(out, TR.map_head(sdq, cfg, packed, grids, dtype), TR.map_head(sdq, cfg, packed.float(), grids, F32),
            dtype, "MAP head")
-    full = head(x[:, :100])  # no mask: every row valid
     ref_full = TR.map_head(sdq, cfg, x[:, :100].reshape(-1, D).float(), [(100, 1)] * len(lens), F32)
     _check(full, TR.map_head(sdq, cfg, x[:, :100].reshape(-1, D), [(100, 1)] * len(lens), dtype), ref_full, dtype,
            "MAP head, no mask")
     bad = mask.clone()
     bad[0, 0] = 0
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(NotImplementedError), torch.no_grad():
         head(x, bad)
+    for p_ in head.parameters():
+        p_.requires_grad_(False)
     with pytest.raises(NotImplementedError):
         head(x.clone().requires_grad_(True), mask)
