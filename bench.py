@@ -209,7 +209,8 @@ def main():
     g_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
 
     def step(pixels, msk, timed=None):
-        out = model(pixels, msk, shapes_cpu)
+        with torch.inference_mode():  # the metric's protocol: eval() + inference_mode
+            out = model(pixels, msk, shapes_cpu)
         if world == 1:
             return out.pooler_output
         if timed is not None:

@@ -224,6 +224,28 @@ int siglip2_posemb(int dtype, const float* table_dev, int grid, int D, const int
 int siglip2_fmha_varlen(int dtype, const void* qkv_dev, int N, const int* cu_seqlens_dev, const int* tiles_dev,
                         int n_tiles, int heads, int head_dim, void* out_dev, int ldo, void* stream);
 
+/* siglip2_fmha_varlen in train mode: the reference's attention-output
+ * dropout (model.py:166-169, nn.functional.dropout of the per-head output
+ * before out_proj) applied in the same launch, as the output is stored:
+ * element e = row * heads*head_dim + col of the logical output is kept and
+ * scaled by 1 / (1 - p) when u(e) >= p, else zeroed, with u(e) in [0, 1)
+ * from the counter-based generator Philox4x32-10 (counter = (e / 4, offset),
+ * key = seed, word e % 4, u = (word >> 8) * 2^-24).  The mask is a pure
+ * function of (seed, offset, e): siglip2_dropout with the same arguments
+ * regenerates it (the backward applies it to the incoming gradient).
+ * 0 <= p < 1. */
+int siglip2_fmha_varlen_dropout(int dtype, const void* qkv_dev, int N, const int* cu_seqlens_dev, const int* tiles_dev,
+                                int n_tiles, int heads, int head_dim, void* out_dev, int ldo, float p,
+                                unsigned long long seed, unsigned long long offset, void* stream);
+
+/* y[r, c] = x[r, c] * keep(r * width + c) / (1 - p) for r < rows, c < width,
+ * with the mask of siglip2_fmha_varlen_dropout (x and y may be the same
+ * buffer).  width a multiple of 8; rows 16-byte aligned with pitches
+ * multiples of 8 (bf16, f16) or 4 (f32) elements.  Replaces
+ * nn.functional.dropout at model.py:166-169 (and its gradient). */
+int siglip2_dropout(int dtype, const void* x_dev, int ldx, int rows, int width, float p, unsigned long long seed,
+                    unsigned long long offset, void* y_dev, int ldy, void* stream);
+
 /* Head dimension of the attention kernel's tiles (64 -> 64, 72 -> 80,
  * 96 -> 96); the padding exists only in shared memory and TMEM. */
 int siglip2_padded_head_dim(int head_dim);

@@ -285,3 +285,47 @@ def flops_per_image(cfg, L: int, with_head: bool = True) -> float:
     if with_head:
         f += 4 * D * D + 4 * L * D * D + 4 * L * D + 4 * D * I
     return float(f)
+
+
+# ---------------------------------------------------------------------------
+# Train-mode attention-output dropout mask (model.py:166-169 applies
+# nn.functional.dropout to the attention output; the kernels draw its mask
+# from a counter-based generator so that the backward can regenerate it).
+# Philox4x32-10 as published by Salmon, Moraes, Dror and Shaw ("Parallel
+# random numbers: as easy as 1, 2, 3", SC 2011): ten rounds of two 32x32->64
+# multiplications with the round multipliers below, the key bumped by the
+# Weyl increments between rounds.
+# ---------------------------------------------------------------------------
+_PHILOX_M = (np.uint64(0xD2511F53), np.uint64(0xCD9E8D57))
+_PHILOX_W = (np.uint32(0x9E3779B9), np.uint32(0xBB67AE85))
+
+
+def philox4x32_10(ctr: np.ndarray, key: tuple[int, int]) -> np.ndarray:
+    """``ctr``: uint32 ``[n, 4]`` counters; returns the uint32 ``[n, 4]`` outputs."""
+    c = [ctr[:, i].astype(np.uint64) for i in range(4)]
+    k0, k1 = np.uint32(key[0] & 0xFFFFFFFF), np.uint32(key[1] & 0xFFFFFFFF)
+    mask = np.uint64(0xFFFFFFFF)
+    for _ in range(10):
+        p0 = _PHILOX_M[0] * c[0]
+        p1 = _PHILOX_M[1] * c[2]
+        hi0, lo0 = p0 >> np.uint64(32), p0 & mask
+        hi1, lo1 = p1 >> np.uint64(32), p1 & mask
+        c = [hi1 ^ c[1] ^ np.uint64(k0), lo1, hi0 ^ c[3] ^ np.uint64(k1), lo0]
+        k0 = np.uint32((int(k0) + int(_PHILOX_W[0])) & 0xFFFFFFFF)
+        k1 = np.uint32((int(k1) + int(_PHILOX_W[1])) & 0xFFFFFFFF)
+    return np.stack(c, 1).astype(np.uint32)
+
+
+def dropout_keep(seed: int, offset: int, first: int, count: int, p: float) -> np.ndarray:
+    """Keep flags of elements ``first .. first+count-1`` of the logical
+    ``[rows, width]`` attention output (element e = row * width + col): u(e)
+    = (word e % 4 of Philox4x32-10(counter = (e / 4, offset), key = seed)
+    >> 8) * 2^-24, kept when u >= p (in fp32, as the kernels compare)."""
+    e = np.arange(first, first + count, dtype=np.uint64)
+    q = e >> np.uint64(2)
+    ctr = np.stack([q & np.uint64(0xFFFFFFFF), q >> np.uint64(32),
+                    np.full_like(q, offset & 0xFFFFFFFF), np.full_like(q, (offset >> 32) & 0xFFFFFFFF)], 1)
+    out = philox4x32_10(ctr.astype(np.uint32), (seed & 0xFFFFFFFF, (seed >> 32) & 0xFFFFFFFF))
+    word = out[np.arange(count), (e & np.uint64(3)).astype(np.int64)]
+    u = (word >> np.uint32(8)).astype(np.float32) * np.float32(1.0 / 16777216.0)
+    return u >= np.float32(p)

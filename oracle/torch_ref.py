@@ -4,7 +4,9 @@ TEST INFRASTRUCTURE ONLY (see ``oracle/siglip2_oracle.py``).  The reference's
 ``model.py`` cannot be shipped to the GPU host, so this module replays its op
 sequence with the same torch ops and in the same dtype (bf16/fp16 on the GPU),
 which is what "the reference run at the same dtype" means in the parity
-tests.  Ops, in order (tohskai/SigLIP-2):
+tests.  The functions are differentiable (autograd records when the weights
+or inputs require grad), so the same replay is the gradient reference of the
+training tests.  Ops, in order (tohskai/SigLIP-2):
 
 * ``model.py:86-87``   patch Linear in the weight dtype;
 * ``model.py:90-119``  position grid ``F.interpolate(bilinear, antialias)`` per
@@ -36,7 +38,6 @@ def _qkv(sd, pre, dt, dev):
     return [(_w(sd, pre + f"{n}_proj.weight", dt, dev), _w(sd, pre + f"{n}_proj.bias", dt, dev)) for n in "qkv"]
 
 
-@torch.no_grad()
 def embeddings(sd, cfg, seq_patches, grids, dtype, device="cuda", pre="embeddings."):
     """``model.py:68-120``: patch Linear + per-image resized position grid."""
     D = cfg.hidden_size
@@ -49,7 +50,6 @@ def embeddings(sd, cfg, seq_patches, grids, dtype, device="cuda", pre="embedding
     return x + pos
 
 
-@torch.no_grad()
 def attention(sd, cfg, pre, h, lens, dtype, device="cuda"):
     """``model.py:144-176`` on packed rows ``h [N, D]``: q/k/v Linear,
     softmax attention within each run of ``lens`` rows, out Linear."""
@@ -69,7 +69,6 @@ def attention(sd, cfg, pre, h, lens, dtype, device="cuda"):
     return F.linear(a, _w(sd, pre + "out_proj.weight", dtype, device), _w(sd, pre + "out_proj.bias", dtype, device))
 
 
-@torch.no_grad()
 def mlp(sd, pre, h, dtype, device="cuda"):
     """``model.py:187-191``: fc2(gelu_tanh(fc1 h))."""
     h = F.gelu(F.linear(h, _w(sd, pre + "fc1.weight", dtype, device), _w(sd, pre + "fc1.bias", dtype, device)),
@@ -77,7 +76,6 @@ def mlp(sd, pre, h, dtype, device="cuda"):
     return F.linear(h, _w(sd, pre + "fc2.weight", dtype, device), _w(sd, pre + "fc2.bias", dtype, device))
 
 
-@torch.no_grad()
 def encoder_layer(sd, cfg, pre, x, lens, dtype, device="cuda"):
     """``model.py:204-223`` on packed rows ``x [N, D]``."""
     D, eps = cfg.hidden_size, cfg.layer_norm_eps
@@ -89,7 +87,6 @@ def encoder_layer(sd, cfg, pre, x, lens, dtype, device="cuda"):
     return x + mlp(sd, pre + "mlp.", h, dtype, device)
 
 
-@torch.no_grad()
 def forward_packed(sd, cfg, seq_patches, grids, dtype, device="cuda"):
     D, eps = cfg.hidden_size, cfg.layer_norm_eps
     grids = [(int(h), int(w)) for h, w in grids]
@@ -101,7 +98,6 @@ def forward_packed(sd, cfg, seq_patches, grids, dtype, device="cuda"):
                         eps)
 
 
-@torch.no_grad()
 def map_head(sd, cfg, last_packed, grids, dtype, device="cuda"):
     D, H = cfg.hidden_size, cfg.num_attention_heads
     hd = D // H

@@ -29,8 +29,13 @@
 //              image end, online max with lazy rescale (O is rescaled in TMEM
 //              only when the running max grows by more than 2^8), writes
 //              P = exp2(S*scale*log2e - m) packed in pairs, final O / l.
+//
+// Train mode: with drop.p > 0 the output store applies the reference's
+// attention-output dropout (model.py:166-169) with the counter-based mask of
+// dropout.cuh over the logical [N, heads*head_dim] output.
 #pragma once
 
+#include "dropout.cuh"
 #include "ptx.cuh"
 
 namespace sg {
@@ -44,6 +49,7 @@ struct FmhaParams {
   void* out;          // [N, heads*head_dim]
   int ld_out;
   float scale_log2;   // head_dim^-0.5 * log2(e)
+  DropoutParams drop; // attention-output dropout (p = 0: off)
 };
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -393,11 +399,22 @@ __global__ void __launch_bounds__(192, 2)
           for (int gg = 0; gg < 2; ++gg) {
             const int d0 = c * 16 + gg * 8;
             if (d0 < p.head_dim) {  // head_dim is a multiple of 8
+              float f[8];
+#pragma unroll
+              for (int k = 0; k < 8; ++k) f[k] = inv_l;
+              if (p.drop.p > 0.f) {
+                float keep[8];
+                dropout_factors8(p.drop,
+                                 static_cast<unsigned long long>(row) * (H * p.head_dim) + head * p.head_dim + d0,
+                                 keep);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) f[k] *= keep[k];
+              }
               uint4 o;
-              o.x = Pack2<T>::pack(__uint_as_float(u[gg * 8 + 0]) * inv_l, __uint_as_float(u[gg * 8 + 1]) * inv_l);
-              o.y = Pack2<T>::pack(__uint_as_float(u[gg * 8 + 2]) * inv_l, __uint_as_float(u[gg * 8 + 3]) * inv_l);
-              o.z = Pack2<T>::pack(__uint_as_float(u[gg * 8 + 4]) * inv_l, __uint_as_float(u[gg * 8 + 5]) * inv_l);
-              o.w = Pack2<T>::pack(__uint_as_float(u[gg * 8 + 6]) * inv_l, __uint_as_float(u[gg * 8 + 7]) * inv_l);
+              o.x = Pack2<T>::pack(__uint_as_float(u[gg * 8 + 0]) * f[0], __uint_as_float(u[gg * 8 + 1]) * f[1]);
+              o.y = Pack2<T>::pack(__uint_as_float(u[gg * 8 + 2]) * f[2], __uint_as_float(u[gg * 8 + 3]) * f[3]);
+              o.z = Pack2<T>::pack(__uint_as_float(u[gg * 8 + 4]) * f[4], __uint_as_float(u[gg * 8 + 5]) * f[5]);
+              o.w = Pack2<T>::pack(__uint_as_float(u[gg * 8 + 6]) * f[6], __uint_as_float(u[gg * 8 + 7]) * f[7]);
               *reinterpret_cast<uint4*>(orow + d0) = o;
             }
           }

@@ -470,7 +470,7 @@ int sg_token_image_impl(const int* cu, int B, int N, int* tok_img, cudaStream_t 
 // ---------------------------------------------------------------------------
 template <typename T, int HDP>
 int launch_fmha(const void* qkv, int N, const int* cu, const int2* tiles, int n_tiles, int H, int hd, void* out, int ldo,
-                cudaStream_t s) {
+                const DropoutParams& drop, cudaStream_t s) {
   using C = FmhaCfg<HDP>;
   CUtensorMap tq, tqr, tk, tkr;
   // 3-D view [N][3H][hd] of the packed q | k | v columns: the remainder box
@@ -495,6 +495,7 @@ int launch_fmha(const void* qkv, int N, const int* cu, const int2* tiles, int n_
   p.out = out;
   p.ld_out = ldo;
   p.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(hd));
+  p.drop = drop;
   auto kern = fmha_varlen_kernel<T, HDP>;
   constexpr int smem = FmhaCfg<HDP>::kSmem;
   SG_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem));
@@ -516,19 +517,53 @@ int launch_fmha(const void* qkv, int N, const int* cu, const int2* tiles, int n_
 
 template <typename T>
 int dispatch_fmha(const void* qkv, int N, const int* cu, const int2* tiles, int n_tiles, int H, int hd, void* out,
-                  int ldo, cudaStream_t s) {
+                  int ldo, const DropoutParams& d, cudaStream_t s) {
   switch (hd) {
-    case 64: return launch_fmha<T, 64>(qkv, N, cu, tiles, n_tiles, H, hd, out, ldo, s);
-    case 72: return launch_fmha<T, 80>(qkv, N, cu, tiles, n_tiles, H, hd, out, ldo, s);
-    case 80: return launch_fmha<T, 80>(qkv, N, cu, tiles, n_tiles, H, hd, out, ldo, s);
-    case 96: return launch_fmha<T, 96>(qkv, N, cu, tiles, n_tiles, H, hd, out, ldo, s);
+    case 64: return launch_fmha<T, 64>(qkv, N, cu, tiles, n_tiles, H, hd, out, ldo, d, s);
+    case 72: return launch_fmha<T, 80>(qkv, N, cu, tiles, n_tiles, H, hd, out, ldo, d, s);
+    case 80: return launch_fmha<T, 80>(qkv, N, cu, tiles, n_tiles, H, hd, out, ldo, d, s);
+    case 96: return launch_fmha<T, 96>(qkv, N, cu, tiles, n_tiles, H, hd, out, ldo, d, s);
     default: return set_error(SIGLIP2_ERR_UNSUPPORTED, "head_dim %d not supported (64, 72, 80, 96)", hd);
   }
 }
 
+// Dropout parameters from the entry-point arguments (p in [0, 1)).
+int make_dropout(float p, unsigned long long seed, unsigned long long offset, DropoutParams* d) {
+  SG_CHECK_ARG(p >= 0.f && p < 1.f, "dropout probability %g outside [0, 1)", static_cast<double>(p));
+  d->p = p;
+  d->scale = 1.f / (1.f - p);
+  d->seed_lo = static_cast<uint32_t>(seed);
+  d->seed_hi = static_cast<uint32_t>(seed >> 32);
+  d->off_lo = static_cast<uint32_t>(offset);
+  d->off_hi = static_cast<uint32_t>(offset >> 32);
+  return SIGLIP2_OK;
+}
+
+int sg_dropout_impl(int dtype, const void* x, int ldx, int rows, int width, const DropoutParams& d, void* y, int ldy,
+                    cudaStream_t s) {
+  SG_CHECK_ARG(x && y && rows >= 0 && width > 0 && ldx >= width && ldy >= width, "bad dropout arguments");
+  SG_CHECK_ARG(width % 8 == 0, "dropout width %d must be a multiple of 8", width);
+  const int v = dtype == SIGLIP2_F32 ? 4 : 8;
+  if (!aligned16(x) || !aligned16(y) || ldx % v || ldy % v)
+    return set_error(SIGLIP2_ERR_ALIGN, "dropout: 16-byte aligned rows with strides multiples of %d", v);
+  const long long n = static_cast<long long>(rows) * (width / 8);
+  if (n == 0) return SIGLIP2_OK;
+  if (n > (1ll << 40)) return set_error(SIGLIP2_ERR_SHAPE, "dropout: too many elements");
+  const unsigned blocks = static_cast<unsigned>((n + 255) / 256);
+  switch (dtype) {
+    case SIGLIP2_BF16: dropout_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), ldx, rows, width, d, static_cast<__nv_bfloat16*>(y), ldy); break;
+    case SIGLIP2_F16: dropout_kernel<__half><<<blocks, 256, 0, s>>>(static_cast<const __half*>(x), ldx, rows, width, d, static_cast<__half*>(y), ldy); break;
+    case SIGLIP2_F32: dropout_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(x), ldx, rows, width, d, static_cast<float*>(y), ldy); break;
+    default: return set_error(SIGLIP2_ERR_ARG, "unknown dtype %d", dtype);
+  }
+  SG_LAUNCH_CHECK();
+  return SIGLIP2_OK;
+}
 
 int sg_fmha_impl(int dtype, const void* qkv, int N, const int* cu, const int* tiles, int n_tiles, int H, int hd,
-                 void* out, int ldo, cudaStream_t s) {
+                 void* out, int ldo, cudaStream_t s, const DropoutParams* drop = nullptr) {
+  DropoutParams d{};
+  if (drop) d = *drop;
   SG_CHECK_ARG(qkv && cu && tiles && out && N >= 0 && n_tiles >= 0 && H > 0 && hd > 0, "bad attention arguments");
   SG_CHECK_ARG(hd % 8 == 0 && ldo % 8 == 0 && ldo >= H * hd, "head_dim and ldo must be multiples of 8");
   if (N == 0 || n_tiles == 0) return SIGLIP2_OK;
@@ -538,8 +573,8 @@ int sg_fmha_impl(int dtype, const void* qkv, int N, const int* cu, const int* ti
   if (reinterpret_cast<uintptr_t>(tiles) & 7u)
     return set_error(SIGLIP2_ERR_ALIGN, "attention tile list must be 8-byte aligned (read as int32 pairs)");
   const int2* t2 = reinterpret_cast<const int2*>(tiles);
-  if (dtype == SIGLIP2_BF16) return dispatch_fmha<__nv_bfloat16>(qkv, N, cu, t2, n_tiles, H, hd, out, ldo, s);
-  if (dtype == SIGLIP2_F16) return dispatch_fmha<__half>(qkv, N, cu, t2, n_tiles, H, hd, out, ldo, s);
+  if (dtype == SIGLIP2_BF16) return dispatch_fmha<__nv_bfloat16>(qkv, N, cu, t2, n_tiles, H, hd, out, ldo, d, s);
+  if (dtype == SIGLIP2_F16) return dispatch_fmha<__half>(qkv, N, cu, t2, n_tiles, H, hd, out, ldo, d, s);
   if (dtype == SIGLIP2_F32) {
     // fp32: q | k | v with head_dim columns per head (no padding)
     dim3 grid(n_tiles, H);
@@ -553,6 +588,8 @@ int sg_fmha_impl(int dtype, const void* qkv, int N, const int* cu, const int* ti
       default: return set_error(SIGLIP2_ERR_UNSUPPORTED, "fp32 attention: head_dim %d not supported (64, 72, 96)", hd);
     }
     SG_LAUNCH_CHECK();
+    // fp32: the same dropout mask as a second (in-place) launch
+    if (d.p > 0.f) return sg_dropout_impl(dtype, out, ldo, N, H * hd, d, out, ldo, s);
     return SIGLIP2_OK;
   }
   return set_error(SIGLIP2_ERR_UNSUPPORTED, "attention supports f32/bf16/f16");
@@ -906,6 +943,22 @@ int siglip2_fmha_varlen(int dtype, const void* qkv_dev, int N, const int* cu_seq
                         int n_tiles, int heads, int head_dim, void* out_dev, int ldo, void* stream) {
   return sg_fmha_impl(dtype, qkv_dev, N, cu_seqlens_dev, tiles_dev, n_tiles, heads, head_dim, out_dev, ldo,
                       static_cast<cudaStream_t>(stream));
+}
+
+int siglip2_fmha_varlen_dropout(int dtype, const void* qkv_dev, int N, const int* cu_seqlens_dev, const int* tiles_dev,
+                                int n_tiles, int heads, int head_dim, void* out_dev, int ldo, float p,
+                                unsigned long long seed, unsigned long long offset, void* stream) {
+  DropoutParams d{};
+  SG_TRY(make_dropout(p, seed, offset, &d));
+  return sg_fmha_impl(dtype, qkv_dev, N, cu_seqlens_dev, tiles_dev, n_tiles, heads, head_dim, out_dev, ldo,
+                      static_cast<cudaStream_t>(stream), &d);
+}
+
+int siglip2_dropout(int dtype, const void* x_dev, int ldx, int rows, int width, float p, unsigned long long seed,
+                    unsigned long long offset, void* y_dev, int ldy, void* stream) {
+  DropoutParams d{};
+  SG_TRY(make_dropout(p, seed, offset, &d));
+  return sg_dropout_impl(dtype, x_dev, ldx, rows, width, d, y_dev, ldy, static_cast<cudaStream_t>(stream));
 }
 
 int siglip2_padded_head_dim(int head_dim) { return padded_head_dim(head_dim); }

@@ -17,9 +17,12 @@ Accepted ``state_dict`` layouts: ``model.py`` (``self_attn.{q,k,v}_proj``),
 the fused ``self_attn.qkv_proj`` of ``model_optimized.py:215`` (chunk order
 Q, K, V), and ``head.*`` from ``transformers``.
 
-Only inference is implemented: the forward runs without autograd, and
-``train()`` mode with ``attention_dropout > 0`` is refused (the reference
-applies dropout there, ``model.py:166-169``).
+Inference (``eval()`` under ``torch.no_grad()`` / ``torch.inference_mode()``)
+runs the whole tower as one library call.  When autograd records (grad mode
+on and the input or a parameter requires grad) or in ``train()`` mode, the
+forward runs through the submodules instead, one registered op per launch,
+each with a backward formula, and ``train()`` mode applies the reference's
+attention-output dropout (``model.py:166-169``) inside the attention kernel.
 """
 from __future__ import annotations
 
@@ -31,6 +34,7 @@ from typing import NamedTuple
 import numpy as np
 import torch
 import torch.nn as nn
+import torch.nn.functional as F
 
 from . import _lib as L
 from . import ops
@@ -224,10 +228,16 @@ def _needs_grad(module: nn.Module, *xs) -> bool:
                                         or any(p.requires_grad for p in module.parameters()))
 
 
-def _check_inference(module: nn.Module, dropout: float):
-    if module.training and dropout > 0:
-        raise NotImplementedError("siglip2_b200 implements inference only: call .eval() (or set "
-                                  "attention_dropout=0); the reference applies attention dropout in train mode")
+@torch.compiler.disable
+def _dropout_args(module: nn.Module, p: float) -> tuple[float, int]:
+    """``(p, seed)`` of the attention-output dropout of one call: active in
+    ``train()`` mode as in ``model.py:166-169``; the 63-bit seed of the
+    counter-based mask comes from torch's default CPU generator (so
+    ``torch.manual_seed`` makes it reproducible) and travels to the backward,
+    which regenerates the same mask."""
+    if not (module.training and p > 0):
+        return 0.0, 0
+    return float(p), int(torch.randint(0, 2 ** 63 - 1, (1,), dtype=torch.int64).item())
 
 
 class LayerNorm(nn.LayerNorm):
@@ -335,7 +345,8 @@ def _attention(m: nn.Module, x: torch.Tensor, seqs: Sequences) -> torch.Tensor:
     if x2.shape[0] != seqs.n_tokens:
         raise ValueError(f"{x2.shape[0]} rows but the sequences cover {seqs.n_tokens}")
     qkv = _OPS.gemm(x2, qkv_w, L.EPI_BIAS, qkv_b.float(), None, None, None, 0.0)
-    a = _OPS.fmha_varlen(qkv, seqs.cu_seqlens, seqs.tiles, m.num_heads, m.head_dim, seqs.lengths)
+    a = _OPS.fmha_varlen(qkv, seqs.cu_seqlens, seqs.tiles, m.num_heads, m.head_dim, seqs.lengths,
+                         *_dropout_args(m, m.dropout))
     return _OPS.gemm(a, out_w, L.EPI_BIAS, out_b.float(), None, None, None, 0.0).view(*x.shape[:-1], -1)
 
 
@@ -377,8 +388,9 @@ class Siglip2Attention(nn.Module):
 
     def forward(self, hidden_states, document_ids=None, output_attentions=False):
         """``[B, S, D]`` -> ``(out [B, S, D], None)``; rows q and kv attend
-        when ``document_ids[q] == document_ids[kv]`` (all rows when None)."""
-        _check_inference(self, self.dropout)
+        when ``document_ids[q] == document_ids[kv]`` (all rows when None).
+        In ``train()`` mode the attention output is dropped out with
+        probability ``attention_dropout`` before ``out_proj``."""
         return _attention(self, hidden_states, _sequences(hidden_states, document_ids=document_ids)), None
 
 
@@ -407,7 +419,6 @@ class Siglip2AttentionImproved(Siglip2Attention):
         return self.qkv_proj.weight, self.qkv_proj.bias
 
     def forward(self, hidden_states, block_mask=None, output_attentions=False, document_ids=None):
-        _check_inference(self, self.dropout)
         seqs = _sequences(hidden_states, document_ids=document_ids, block_mask=block_mask)
         return _attention(self, hidden_states, seqs), None
 
@@ -461,7 +472,6 @@ def _encoder_layer(layer: nn.Module, x: torch.Tensor, seqs: Sequences, rs: torch
     the residual, LN2 folded into fc1 (+GELU), fc2 with the residual.  The
     LayerNorm statistics travel as row sums (``rs`` in, the output's out).
     Returns ``(y, rs_y)``."""
-    _check_inference(layer, layer.self_attn.dropout)
     if _needs_grad(layer, x):
         return _encoder_layer_unfused(layer, x, seqs), None
     qw, qc1, qc2, ow, ob, f1w, f1c1, f1c2, f2w, f2b = _derived(layer, lambda: _layer_tensors(layer))
@@ -473,7 +483,8 @@ def _encoder_layer(layer: nn.Module, x: torch.Tensor, seqs: Sequences, rs: torch
     if rs is None:
         rs = _OPS.rowsums(x2)
     qkv, _ = _OPS.gemm_rowsums(x2, qw, L.EPI_LN_ROWSUMS, None, None, qc1, qc2, eps1, rs, False)
-    a = _OPS.fmha_varlen(qkv, seqs.cu_seqlens, seqs.tiles, at.num_heads, at.head_dim, seqs.lengths)
+    a = _OPS.fmha_varlen(qkv, seqs.cu_seqlens, seqs.tiles, at.num_heads, at.head_dim, seqs.lengths,
+                         *_dropout_args(at, at.dropout))
     h, rs_h = _OPS.gemm_rowsums(a, ow, L.EPI_BIAS_RES_ROWSUMS, ob, x2, None, None, 0.0, None, True)
     m, _ = _OPS.gemm_rowsums(h, f1w, L.EPI_LN_ROWSUMS_GELU, None, None, f1c1, f1c2, eps2, rs_h, False)
     y, rs_y = _OPS.gemm_rowsums(m, f2w, L.EPI_BIAS_RES_ROWSUMS, f2b, h, None, None, 0.0, None, True)
@@ -492,7 +503,8 @@ def _encoder_layer_unfused(layer: nn.Module, x: torch.Tensor, seqs: Sequences) -
     h = _OPS.layernorm(x2, ln1.weight.float(), ln1.bias.float(), float(ln1.eps))
     wq, bq = at.qkv_params()
     qkv = _OPS.gemm(h, wq, L.EPI_BIAS, bq.float(), None, None, None, 0.0)
-    a = _OPS.fmha_varlen(qkv, seqs.cu_seqlens, seqs.tiles, at.num_heads, at.head_dim, seqs.lengths)
+    a = _OPS.fmha_varlen(qkv, seqs.cu_seqlens, seqs.tiles, at.num_heads, at.head_dim, seqs.lengths,
+                         *_dropout_args(at, at.dropout))
     r = _OPS.gemm(a, at.out_proj.weight, L.EPI_BIAS_RES, at.out_proj.bias.float(), x2, None, None, 0.0)
     h = _OPS.layernorm(r, ln2.weight.float(), ln2.bias.float(), float(ln2.eps))
     m = _OPS.gemm(h, mlp.fc1.weight, L.EPI_BIAS_GELU, mlp.fc1.bias.float(), None, None, None, 0.0)
@@ -603,13 +615,9 @@ class Siglip2MultiheadAttentionPoolingHead(nn.Module):
         projections, LayerNorm, MLP and residual (library GEMMs).  The valid
         rows of an image must be its first ones, as ``attention_mask`` marks
         them in the padded forward (other masks raise); without a mask every
-        row is valid.  Inference only (no backward): with autograd recording
-        (grad mode on and the input or any of the head's parameters requiring
-        grad) it raises rather than leave gradients silently missing; call it
-        under ``torch.no_grad()`` / ``torch.inference_mode()``."""
-        if _needs_grad(self, hidden_state):
-            raise NotImplementedError("the attention-pooling head has no backward in siglip2_b200: call it under "
-                                      "torch.no_grad() or torch.inference_mode()")
+        row is valid.  With autograd recording (grad mode on and the input
+        or a parameter requiring grad) the head runs as differentiable steps
+        instead (``_forward_autograd``)."""
         B, P, D = hidden_state.shape
         H = self.num_heads
         if attention_mask is None:
@@ -619,6 +627,8 @@ class Siglip2MultiheadAttentionPoolingHead(nn.Module):
             lens = m.sum(1)
             if not torch.equal(m, (torch.arange(P)[None] < lens[:, None]).to(m.dtype)) or bool((lens == 0).any()):
                 raise NotImplementedError("attention_mask must mark a non-empty prefix of every image's rows")
+        if _needs_grad(self, hidden_state):
+            return self._forward_autograd(hidden_state, lens)
         (u, wv, bv, wo, bo, lw, lb, w1, b1, w2, b2) = _derived(self, self._tensors)
         x = hidden_state.to(wv.dtype).contiguous()
         cu = torch.zeros(B + 1, dtype=torch.int32)
@@ -632,6 +642,31 @@ class Siglip2MultiheadAttentionPoolingHead(nn.Module):
             h = ops.layernorm(a, lw, lb, float(self.layernorm.eps))
             h = ops.gemm(h, w1, L.EPI_BIAS_GELU, bias=b1)
             return ops.gemm(h, w2, L.EPI_BIAS_RES, bias=b2, res=a)
+
+    def _forward_autograd(self, hidden_state: torch.Tensor, lens: torch.Tensor) -> torch.Tensor:
+        """The head (``modeling_siglip2.py:684-713``) as differentiable steps
+        for training: the key/value projection of every row, the out
+        projection and the MLP on the library GEMM ops (each with a backward),
+        the probe's attention over each image's valid keys through torch's
+        scaled_dot_product_attention with a key-padding mask, LayerNorm on
+        the LayerNorm op."""
+        B, P, D = hidden_state.shape
+        H = self.num_heads
+        hd = D // H
+        att = self.attention
+        dt = att.in_proj_weight.dtype
+        win, bin_ = att.in_proj_weight, att.in_proj_bias
+        q = F.linear(self.probe.reshape(1, D).to(dt), win[:D], bin_[:D].to(dt))                      # [1, D]
+        kv = _OPS.gemm(_rows(hidden_state, dt), win[D:], L.EPI_BIAS, bin_[D:].float(), None, None, None, 0.0)
+        k, v = kv.view(B, P, 2, H, hd).unbind(2)                                                     # [B, P, H, hd]
+        keep = (torch.arange(P)[None] < lens[:, None]).to(hidden_state.device)[:, None, None, :]     # [B, 1, 1, P]
+        o = F.scaled_dot_product_attention(q.view(1, H, 1, hd).expand(B, H, 1, hd), k.transpose(1, 2),
+                                           v.transpose(1, 2), attn_mask=keep)                        # [B, H, 1, hd]
+        a = _OPS.gemm(o.reshape(B, D).contiguous(), att.out_proj.weight, L.EPI_BIAS, att.out_proj.bias.float(),
+                      None, None, None, 0.0)
+        h = self.layernorm(a)
+        h = _OPS.gemm(h, self.mlp.fc1.weight, L.EPI_BIAS_GELU, self.mlp.fc1.bias.float(), None, None, None, 0.0)
+        return _OPS.gemm(h, self.mlp.fc2.weight, L.EPI_BIAS_RES, self.mlp.fc2.bias.float(), a, None, None, 0.0)
 
 # ---------------------------------------------------------------------------
 # weight packing for the C ABI
@@ -813,11 +848,24 @@ class Siglip2SequenceVisionTransformer(nn.Module):
         self._packed = None
         return res
 
-    def _check_mode(self):
-        if self.training and self.config.attention_dropout > 0:
-            raise NotImplementedError(
-                "siglip2_b200 implements inference only: call .eval() (or set attention_dropout=0); "
-                "the reference applies attention dropout in train mode")
+    def _submodule_path(self, x: torch.Tensor) -> bool:
+        """Autograd records (the submodule ops carry the backward) or
+        ``train()`` mode applies dropout: run the submodules instead of the
+        one-call inference forward."""
+        return _needs_grad(self, x) or (self.training and self.config.attention_dropout > 0)
+
+    def _forward_rows(self, rows: torch.Tensor, hw: np.ndarray) -> torch.Tensor:
+        """Packed rows through the submodules (``model.py:260-292`` step by
+        step): embeddings, every encoder layer over one shared set of
+        sequences, post-LayerNorm.  Each step is a registered op with a
+        backward; in ``train()`` mode the attention output is dropped out."""
+        x = self.embeddings((rows, None, torch.from_numpy(np.ascontiguousarray(hw))))
+        lens = (hw[:, 0].astype(np.int64) * hw[:, 1]).tolist()
+        seqs = Sequences(lens, x.device)
+        rs = None
+        for layer in self.encoder.layers:
+            x, rs = _encoder_layer(layer, x, seqs, rs)
+        return self.post_layernorm(x)
 
     # -- forward ----------------------------------------------------------
     # Opaque to torch.compile: the grids are read on the host and the whole
@@ -825,7 +873,6 @@ class Siglip2SequenceVisionTransformer(nn.Module):
     # same call as a traceable op).
     @torch.compiler.disable
     def forward(self, *args, **kwargs):
-        self._check_mode()
         if len(args) == 1 and isinstance(args[0], (tuple, list)) and not kwargs:
             seq_patches, token_grids = args[0]
             return self.forward_packed(seq_patches, token_grids)
@@ -837,19 +884,20 @@ class Siglip2SequenceVisionTransformer(nn.Module):
                             "(pixel_values, attention_mask, spatial_shapes)")
         return self.forward_padded(vals["pixel_values"], vals["attention_mask"], vals["spatial_shapes"])
 
-    @torch.no_grad()
     def forward_packed(self, seq_patches: torch.Tensor, token_grids: torch.Tensor) -> torch.Tensor:
         """``model.py:260-292``: packed rows in, ``[N, D]`` out."""
-        pk = self.packed_weights()
-        last, _ = tower_forward(pk, seq_patches, _grids(token_grids), 0, False)
+        hw = _grids(token_grids)
+        if self._submodule_path(seq_patches):
+            dt = self.embeddings.patch_embedding.weight.dtype
+            return self._forward_rows(seq_patches.to(dt), hw)
+        with torch.no_grad():
+            last, _ = tower_forward(self.packed_weights(), seq_patches, hw, 0, False)
         return last
 
-    @torch.no_grad()
     def forward_padded(self, pixel_values, attention_mask, spatial_shapes) -> Siglip2Output:
         """HF ``Siglip2VisionTransformer.forward``: padded rows in;
         ``last_hidden_state [B, P, D]`` (zeros on padded rows) and
         ``pooler_output [B, D]`` (None without a head)."""
-        pk = self.packed_weights()
         hw = _grids(spatial_shapes)
         B, P = pixel_values.shape[:2]
         lens = hw[:, 0].astype(np.int64) * hw[:, 1]
@@ -863,7 +911,19 @@ class Siglip2SequenceVisionTransformer(nn.Module):
                 m = attention_mask.detach()
                 if not torch.equal(m.sum(1).to(torch.int64), torch.from_numpy(lens)):
                     raise ValueError("attention_mask must mark exactly the first h*w rows of every image")
-        last, pooled = tower_forward(pk, pixel_values, hw, P, self.head is not None)
+        if self._submodule_path(pixel_values):
+            dt = self.embeddings.patch_embedding.weight.dtype
+            rows = torch.cat([pixel_values[b, :int(n)] for b, n in enumerate(lens)], 0).to(dt)
+            x = self._forward_rows(rows, hw)
+            idx = torch.cat([torch.arange(int(n)) + b * P for b, n in enumerate(lens)]).to(x.device)
+            last = x.new_zeros((B * P, x.shape[-1])).index_copy(0, idx, x).view(B, P, -1)
+            pooled = None
+            if self.head is not None:
+                mask = (torch.arange(P)[None] < torch.from_numpy(lens)[:, None]).to(torch.int64)
+                pooled = self.head(last, mask)
+            return Siglip2Output(last, pooled)
+        with torch.no_grad():
+            last, pooled = tower_forward(self.packed_weights(), pixel_values, hw, P, self.head is not None)
         return Siglip2Output(last, pooled)
 
 

@@ -105,13 +105,35 @@ def attention_tiles(lens) -> torch.Tensor:
 
 
 def fmha_varlen(qkv: torch.Tensor, cu_seqlens: torch.Tensor, tiles: torch.Tensor, heads: int, head_dim: int,
-                out: torch.Tensor | None = None) -> torch.Tensor:
+                out: torch.Tensor | None = None, dropout_p: float = 0.0, seed: int = 0,
+                offset: int = 0) -> torch.Tensor:
+    """Per-sequence attention (``siglip2_fmha_varlen``); with ``dropout_p > 0``
+    the attention-output dropout of train mode is applied as the output is
+    stored (``siglip2_fmha_varlen_dropout``, mask from ``seed``/``offset``)."""
     _need_cuda(qkv, cu_seqlens, tiles)
     N = qkv.shape[0]
     if out is None:
         out = torch.empty((N, heads * head_dim), dtype=qkv.dtype, device=qkv.device)
-    L.call("siglip2_fmha_varlen", dtype_code(qkv.dtype), qkv.data_ptr(), N, cu_seqlens.data_ptr(), tiles.data_ptr(),
-           tiles.shape[0], heads, head_dim, out.data_ptr(), out.stride(0), _stream(qkv.device))
+    if dropout_p > 0:
+        L.call("siglip2_fmha_varlen_dropout", dtype_code(qkv.dtype), qkv.data_ptr(), N, cu_seqlens.data_ptr(),
+               tiles.data_ptr(), tiles.shape[0], heads, head_dim, out.data_ptr(), out.stride(0), float(dropout_p),
+               int(seed) & (2 ** 64 - 1), int(offset) & (2 ** 64 - 1), _stream(qkv.device))
+    else:
+        L.call("siglip2_fmha_varlen", dtype_code(qkv.dtype), qkv.data_ptr(), N, cu_seqlens.data_ptr(),
+               tiles.data_ptr(), tiles.shape[0], heads, head_dim, out.data_ptr(), out.stride(0), _stream(qkv.device))
+    return out
+
+
+def dropout(x: torch.Tensor, p: float, seed: int, offset: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``siglip2_dropout``: ``x * keep / (1 - p)`` with the counter-based mask of
+    the attention kernel's train mode (same ``seed``/``offset``, element index
+    ``row * width + col`` of the ``[rows, width]`` matrix)."""
+    _need_cuda(x)
+    assert x.dim() == 2 and x.stride(1) == 1
+    if out is None:
+        out = torch.empty_like(x)
+    L.call("siglip2_dropout", dtype_code(x.dtype), x.data_ptr(), x.stride(0), x.shape[0], x.shape[1], float(p),
+           int(seed) & (2 ** 64 - 1), int(offset) & (2 ** 64 - 1), out.data_ptr(), out.stride(0), _stream(x.device))
     return out
 
 

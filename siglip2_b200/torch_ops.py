@@ -10,7 +10,8 @@ the reference uses for its Triton LayerNorm
 
 Ops (``torch.ops.siglip2_b200.<name>``):
   gemm, gemm_rowsums, rowsums  -- tensor-core GEMMs with fused epilogues
-  fmha_varlen                  -- per-image attention over packed rows
+  fmha_varlen                  -- per-image attention over packed rows (with
+                                  the train-mode output dropout)
   layernorm                    -- LayerNorm over the last dimension
   token_image, patch_embed     -- patch Linear + resized position grid
   vision_tower                 -- the whole tower (``siglip2_forward``)
@@ -142,32 +143,39 @@ def _(x):
 # --------------------------------------------------------------------------- attention
 @torch.library.custom_op("siglip2_b200::fmha_varlen", mutates_args=(), device_types="cuda")
 def fmha_varlen(qkv: Tensor, cu_seqlens: Tensor, tiles: Tensor, heads: int, head_dim: int,
-                lengths: list[int]) -> Tensor:
+                lengths: list[int], dropout_p: float = 0.0, seed: int = 0) -> Tensor:
     """``siglip2_fmha_varlen``: qkv [N, 3*heads*head_dim] -> [N, heads*head_dim].
     ``lengths``: the sequence lengths on the host (``cu_seqlens`` is their
-    device prefix sum), read only by the backward."""
-    return ops.fmha_varlen(qkv, cu_seqlens, tiles, heads, head_dim)
+    device prefix sum), read only by the backward.  ``dropout_p > 0``: the
+    train-mode attention-output dropout (``model.py:166-169``) with the
+    counter-based mask of ``seed``, applied as the output is stored."""
+    return ops.fmha_varlen(qkv, cu_seqlens, tiles, heads, head_dim, dropout_p=dropout_p, seed=seed)
 
 
 @fmha_varlen.register_fake
-def _(qkv, cu_seqlens, tiles, heads, head_dim, lengths):
+def _(qkv, cu_seqlens, tiles, heads, head_dim, lengths, dropout_p=0.0, seed=0):
     return qkv.new_empty((qkv.shape[0], heads * head_dim))
 
 
 def _fmha_setup(ctx, inputs, output):
-    qkv, cu_seqlens, tiles, heads, head_dim, lengths = inputs
+    qkv, cu_seqlens, tiles, heads, head_dim, lengths, dropout_p, seed = inputs
     ctx.heads, ctx.head_dim, ctx.lengths = heads, head_dim, list(lengths)
+    ctx.dropout_p, ctx.seed = dropout_p, seed
     ctx.save_for_backward(qkv)
 
 
 def _fmha_backward(ctx, grad):
-    """Stop-gap attention backward: every sequence is recomputed with torch's
+    """Stop-gap attention backward: the incoming gradient goes through the
+    forward's dropout mask (regenerated from the seed by ``siglip2_dropout``),
+    then every sequence is recomputed with torch's
     scaled_dot_product_attention and differentiated there (softmax(q k^T /
     sqrt(hd)) v, the forward's definition), one sequence at a time."""
     (qkv,) = ctx.saved_tensors
     H, hd = ctx.heads, ctx.head_dim
     N = qkv.shape[0]
     x = qkv.detach().view(N, 3, H, hd)
+    if ctx.dropout_p > 0:
+        grad = ops.dropout(grad.contiguous(), ctx.dropout_p, ctx.seed)
     g = grad.reshape(N, H, hd)
     parts = []
     s = 0
@@ -178,7 +186,7 @@ def _fmha_backward(ctx, grad):
             dq, dk, dv = torch.autograd.grad(o, (q, k, v), g[s:s + n].transpose(0, 1)[None])
         parts.append(torch.stack([t[0].transpose(0, 1) for t in (dq, dk, dv)], 1))
         s += n
-    return torch.cat(parts, 0).reshape(N, 3 * H * hd), None, None, None, None, None
+    return torch.cat(parts, 0).reshape(N, 3 * H * hd), None, None, None, None, None, None, None
 
 
 fmha_varlen.register_autograd(_fmha_backward, setup_context=_fmha_setup)

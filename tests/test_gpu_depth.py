@@ -90,7 +90,8 @@ def _run(name):
     pv, mask = W.make_pixels_indexed(shapes, ids, wl.max_patches, 3 * 16 * 16, seed=1337, dtype=dtype)
     grids = [(int(h), int(w)) for h, w in shapes.tolist()]
     lens = [h * w for h, w in grids]
-    out = model(pv.cuda(), mask.cuda(), shapes)
+    with torch.inference_mode():
+        out = model(pv.cuda(), mask.cuda(), shapes)
     torch.cuda.synchronize()
     last = torch.cat([out.last_hidden_state[b, :L] for b, L in enumerate(lens)], 0).float().cpu()
     pooled = out.pooler_output.float().cpu()

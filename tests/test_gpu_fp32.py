@@ -24,7 +24,8 @@ def test_cfg0_fp32_matches_reference_outputs(golden_dir):
     m.load_state_dict(sd)
     m = m.cuda().float().eval()
     pv, mask = W.make_pixels(grids, wl.max_patches, 768, seed=1337)
-    out = m(pv.cuda(), mask, grids)
+    with torch.inference_mode():
+        out = m(pv.cuda(), mask, grids)
     torch.cuda.synchronize()
     lens = (grids[:, 0] * grids[:, 1]).tolist()
     valid = torch.cat([out.last_hidden_state[b, :L] for b, L in enumerate(lens)], 0).cpu().numpy()
@@ -47,7 +48,8 @@ def test_fp32_tower_vs_oracle_random_affine(preset, layers):
     grids = torch.tensor([(21, 8), (3, 5), (16, 16), (1, 1), (30, 9)])
     P = 300
     pv, mask = W.make_pixels(grids, P, 768, seed=5)
-    out = m(pv.cuda(), mask, grids)
+    with torch.inference_mode():
+        out = m(pv.cuda(), mask, grids)
     torch.cuda.synchronize()
     last, pooled = O.forward_padded({k: v.numpy() for k, v in sd.items()}, O.OracleConfig(**cfg.__dict__),
                                     pv.numpy(), mask.numpy(), grids.numpy(), dt=np.float64)

@@ -67,7 +67,8 @@ def test_tower_packed_vs_oracle(preset, layers, dtype, grids):
     lens = [h * w for h, w in grids]
     pv, _ = W.make_pixels(g, max(lens), cfg.num_channels * cfg.patch_size ** 2)
     packed = W.pack_rows(pv, g)
-    out = m((packed.to("cuda", dtype), g.cuda()))
+    with torch.inference_mode():
+        out = m((packed.to("cuda", dtype), g.cuda()))
     torch.cuda.synchronize()
     ref32 = O.forward_packed({k: v.numpy() for k, v in sdq.items()}, cfg, packed.to(dtype).float().numpy(),
                              g.numpy(), dt=np.float32)
@@ -90,7 +91,8 @@ def test_tower_padded_with_head(preset, dtype):
     g = torch.tensor(grids)
     P = 256
     pv, mask = W.make_pixels(g, P, cfg.num_channels * cfg.patch_size ** 2, seed=7)
-    out = m(pv.to("cuda", dtype), mask.cuda(), g.cuda())
+    with torch.inference_mode():
+        out = m(pv.to("cuda", dtype), mask.cuda(), g.cuda())
     torch.cuda.synchronize()
     lens = [h * w for h, w in grids]
     last = out.last_hidden_state
@@ -131,7 +133,8 @@ def test_fused_qkv_state_dict_loads():
     g = torch.tensor([(8, 8), (4, 12)])
     pv, _ = W.make_pixels(g, 64, 768)
     x = W.pack_rows(pv, g).cuda().bfloat16()
-    assert torch.equal(a((x, g)), b((x, g)))
+    with torch.inference_mode():
+        assert torch.equal(a((x, g)), b((x, g)))
 
 
 @pytest.mark.parametrize("preset", ["b16", "so400m"])
@@ -144,7 +147,8 @@ def test_forward_is_deterministic(preset):
     g = torch.tensor(grids)
     pv, _ = W.make_pixels(g, max(h * w for h, w in grids), cfg.num_channels * cfg.patch_size ** 2, seed=11)
     x = W.pack_rows(pv, g).cuda().bfloat16()
-    a = m((x, g))
-    b = m((x, g))
+    with torch.inference_mode():
+        a = m((x, g))
+        b = m((x, g))
     torch.cuda.synchronize()
     assert torch.equal(a, b)

@@ -170,9 +170,20 @@ def test_modules_refuse_cpu_parameters():
         S.Siglip2MLP(cfg)(torch.randn(4, cfg.hidden_size))
 
 
-def test_train_mode_with_dropout_is_refused():
+def test_train_mode_dropout_arguments():
+    """Attention-output dropout is active in train() mode only (as
+    ``model.py:166-169``); each call draws its mask seed from torch's CPU
+    generator, so ``torch.manual_seed`` reproduces it."""
+    from siglip2_b200.model import _dropout_args
     cfg = W.preset_config("b16", config_cls=S.Siglip2VisionConfig, num_hidden_layers=1)
     cfg.attention_dropout = 0.1
-    attn = S.Siglip2Attention(cfg).train()
-    with pytest.raises(NotImplementedError, match="inference"):
-        attn(torch.randn(1, 4, cfg.hidden_size))
+    attn = S.Siglip2Attention(cfg)
+    assert _dropout_args(attn.eval(), attn.dropout) == (0.0, 0)
+    attn.train()
+    torch.manual_seed(5)
+    p, s1 = _dropout_args(attn, attn.dropout)
+    _, s2 = _dropout_args(attn, attn.dropout)
+    torch.manual_seed(5)
+    _, s3 = _dropout_args(attn, attn.dropout)
+    assert p == pytest.approx(0.1) and s1 == s3 and s1 != s2 and 0 <= s1 < 2 ** 63
+    assert _dropout_args(attn, 0.0) == (0.0, 0)

@@ -88,3 +88,26 @@ def test_flop_model():
     assert abs(O.flops_per_image(cfg, 1024) / 1e9 - 979.6) < 0.5
     cfg = W.preset_config("b16", config_cls=O.OracleConfig)
     assert abs(O.flops_per_image(cfg, 256) / 1e9 - 46.8) < 0.2
+
+
+def test_philox_known_answers():
+    """The oracle's Philox4x32-10 against the generator's published
+    known-answer vectors (counter, key -> output)."""
+    kat = [((0, 0, 0, 0), (0, 0), (0x6627e8d5, 0xe169c58d, 0xbc57ac4c, 0x9b00dbd8)),
+           ((0xffffffff,) * 4, (0xffffffff, 0xffffffff), (0x408f276d, 0x41c83b0e, 0xa20bc7c6, 0x6d5451fd)),
+           ((0x243f6a88, 0x85a308d3, 0x13198a2e, 0x03707344), (0xa4093822, 0x299f31d0),
+            (0xd16cfe09, 0x94fdcceb, 0x5001e420, 0x24126ea1))]
+    for ctr, key, want in kat:
+        got = O.philox4x32_10(np.array([ctr], dtype=np.uint32), key)[0]
+        assert tuple(int(v) for v in got) == want
+
+
+def test_dropout_keep_rate_and_streams():
+    keep = O.dropout_keep(seed=0x1234_5678_9abc, offset=0, first=0, count=1 << 20, p=0.1)
+    rate = keep.mean()
+    assert abs(rate - 0.9) < 5 * (0.9 * 0.1 / keep.size) ** 0.5, rate
+    other = O.dropout_keep(seed=0x1234_5678_9abc, offset=1, first=0, count=1 << 20, p=0.1)
+    assert (keep != other).mean() > 0.1  # another offset is another stream
+    tail = O.dropout_keep(seed=0x1234_5678_9abc, offset=0, first=1000, count=500, p=0.1)
+    assert np.array_equal(tail, keep[1000:1500])  # a pure function of the element index
+    assert O.dropout_keep(seed=7, offset=0, first=0, count=4096, p=0.0).all()
