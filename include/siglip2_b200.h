@@ -92,6 +92,13 @@ int siglip2_selftest_wait_timeout(long long limit_ns, void* stream);
 int siglip2_set_gemm_variant(int variant);
 int siglip2_get_gemm_variant(void);
 
+/* Attention kernel selection for every later attention launch of the
+ * process: 0 = automatic (default: paired query tiles), 1 = one 128-row
+ * query tile per CTA (two CTAs per SM), 2 = two query tiles of the same
+ * image and head per CTA sharing each K/V tile (one CTA per SM). */
+int siglip2_set_fmha_variant(int variant);
+int siglip2_get_fmha_variant(void);
+
 /* Synchronises the current device and returns SIGLIP2_ERR_TIMEOUT if a kernel
  * gave up on a bounded wait since the last reset, or SIGLIP2_ERR_SHAPE if a
  * kernel found an index outside a buffer it was given and skipped the access

@@ -177,6 +177,8 @@ def main():
     y.add_argument("--reps", type=int, default=20)
     for sp in (g, f, y):
         sp.add_argument("--variant", type=int, default=0, help="GEMM kernel: 0 auto, 1 one SM, 2 SM pairs")
+    f.add_argument("--fmha-variant", type=int, default=0,
+                   help="attention kernel: 0 auto, 1 one query tile per CTA, 2 query-tile pairs")
     pz = sub.add_parser("patchify")
     pz.add_argument("--images", type=int, default=64)
     pz.add_argument("--height", type=int, default=512)
@@ -197,7 +199,10 @@ def main():
         print(json.dumps(bench_patchify(a.images, a.height, a.width, a.max_patches, a.reps, a.warmup,
                                         channels_last=not a.channels_first)))
     elif a.cmd == "fmha":
-        print(json.dumps(bench_fmha(a.preset, a.images, a.max_patches, a.reps, warmup=a.warmup)))
+        L.check(L.load().siglip2_set_fmha_variant(a.fmha_variant))
+        r = bench_fmha(a.preset, a.images, a.max_patches, a.reps, warmup=a.warmup)
+        r["fmha_variant"] = a.fmha_variant
+        print(json.dumps(r))
     else:
         for r in bench_layer(a.preset, a.images, a.max_patches, a.reps):
             print(json.dumps(r))

@@ -23,6 +23,8 @@ SIGNATURES = {
     "siglip2_set_gemm_variant": (_c_int, [_c_int]),
     "siglip2_selftest_wait_timeout": (_c_int, [ctypes.c_longlong, _vp]),
     "siglip2_get_gemm_variant": (_c_int, []),
+    "siglip2_set_fmha_variant": (_c_int, [_c_int]),
+    "siglip2_get_fmha_variant": (_c_int, []),
     "siglip2_gemm": (_c_int, [_c_int, _c_int, _vp, _c_int, _vp, _c_int, _vp, _c_int, _c_int, _c_int, _c_int,
                               _vp, _vp, _c_int, _vp, _vp, _c_float, _vp]),
     "siglip2_gemm_rowsums": (_c_int, [_c_int, _c_int, _vp, _c_int, _vp, _c_int, _vp, _c_int, _c_int, _c_int, _c_int,

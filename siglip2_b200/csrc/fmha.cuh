@@ -218,73 +218,90 @@ __global__ void __launch_bounds__(192, 2)
     }
   } else if (warp == 1) {
     // --------------------------------------------------------------- MMA
-    if (lane == 0) {
-      int kv = 0, g = 0, it = 0;  // K/V tiles, S tiles and items consumed
-      bool ok = true;
-      // O += P V for the K/V tile kvi, the S tile gi of item `item`; the
-      // item's first PV overwrites O once the previous item's O was read
-      auto issue_pv = [&](int kvi, int gi, bool first, int item) -> bool {
-        const int st = kvi % ST;
-        if (!mbar_wait(p_full, gi & 1, 214) || !mbar_wait(&v_full[st], (kvi / ST) & 1, 215)) return false;
-        if (first && item > 0 && !mbar_wait(o_free, (item - 1) & 1, 217)) return false;
-        tc_fence_after();
-        const uint32_t va = smem_u32(smem + C::kV + st * C::kKTile);
-        const uint32_t vr = va + C::kKSlabA;
+    // The whole warp runs the loop (warp-uniform control flow keeps the
+    // descriptor arithmetic in uniform registers); one elected lane issues
+    // each tcgen05.mma / commit.  Descriptors are built once per buffer and
+    // stepped by adding the K offset (in 16-byte address units): the MMA
+    // issue latency, not the tensor pipe, sets this warp's pace.
+    int kv = 0, g = 0, it = 0;  // K/V tiles, S tiles and items consumed
+    bool ok = true;
+    auto wait_all = [&](uint64_t* bar, uint32_t parity, int site) -> bool {
+      const bool w = !*abort_flag && mbar_wait(bar, parity, site);
+      return __all_sync(0xffffffffu, w);
+    };
+    // O += P V for the K/V tile kvi, the S tile gi of item `item`; the
+    // item's first PV overwrites O once the previous item's O was read
+    auto issue_pv = [&](int kvi, int gi, bool first, int item) -> bool {
+      const int st = kvi % ST;
+      if (!wait_all(p_full, gi & 1, 214) || !wait_all(&v_full[st], (kvi / ST) & 1, 215)) return false;
+      if (first && item > 0 && !wait_all(o_free, (item - 1) & 1, 217)) return false;
+      tc_fence_after();
+      const uint32_t va = smem_u32(smem + C::kV + st * C::kKTile);
+      const uint64_t vd = mnmajor_desc(va, 128, 0);
+      const uint64_t vrd = mnmajor_desc(va + C::kKSlabA, R > 0 ? R * 2 : 32, 0);
+      if (elect_one()) {
 #pragma unroll
         for (int s = 0; s < KT / 16; ++s) {  // 16 keys per MMA; P columns [kColP + 8s, +8)
           const uint32_t acc = (!first || s > 0) ? 1u : 0u;
-          umma_ts(tmem + C::kColO, tmem + C::kColP + s * 8, mnmajor_desc(va + s * 16 * 128, 128, 0), kIdescO64, acc);
+          umma_ts(tmem + C::kColO, tmem + C::kColP + s * 8, vd + static_cast<uint64_t>(s * 16 * 128 / 16), kIdescO64,
+                  acc);
           if constexpr (R > 0)
-            umma_ts(tmem + C::kColO + 64, tmem + C::kColP + s * 8, mnmajor_desc(vr + s * 16 * R * 2, R * 2, 0),
+            umma_ts(tmem + C::kColO + 64, tmem + C::kColP + s * 8, vrd + static_cast<uint64_t>(s * 16 * R * 2 / 16),
                     kIdescOR, acc);
         }
         umma_commit(pv_done);
         umma_commit(&v_empty[st]);
-        return true;
-      };
-      for (int w = blockIdx.x; w < p.n_items && ok; w += gridDim.x, ++it) {
-        const int2 tile = p.tiles[w / H];
-        const int L = __ldg(p.cu + tile.x + 1) - __ldg(p.cu + tile.x);
-        const int n_kv = (L + KT - 1) / KT;
-        const int qb = it % QB;
-        if (*abort_flag || !mbar_wait(&q_full[qb], (it / QB) & 1, 211)) {
+      }
+      __syncwarp();
+      return true;
+    };
+    for (int w = blockIdx.x; w < p.n_items && ok; w += gridDim.x, ++it) {
+      const int2 tile = p.tiles[w / H];
+      const int L = __ldg(p.cu + tile.x + 1) - __ldg(p.cu + tile.x);
+      const int n_kv = (L + KT - 1) / KT;
+      const int qb = it % QB;
+      if (!wait_all(&q_full[qb], (it / QB) & 1, 211)) {
+        ok = false;
+        break;
+      }
+      const uint32_t qa = smem_u32(smem + C::kQ + qb * C::kQTile);
+      const uint64_t qd = kmajor_desc(qa, 128), qrd = kmajor_desc(qa + C::kQSlabA, R > 0 ? R * 2 : 32);
+      for (int j = 0; j < n_kv; ++j, ++kv, ++g) {
+        const int st = kv % ST;
+        // S_g overwrites S_{g-1}: the softmax must have read it
+        if (!wait_all(&k_full[st], (kv / ST) & 1, 212) || (g > 0 && !wait_all(s_free, (g - 1) & 1, 213))) {
           ok = false;
           break;
         }
-        const uint32_t qa = smem_u32(smem + C::kQ + qb * C::kQTile);
-        const uint32_t qr = qa + C::kQSlabA;
-        for (int j = 0; j < n_kv; ++j, ++kv, ++g) {
-          const int st = kv % ST;
-          // S_g overwrites S_{g-1}: the softmax must have read it
-          if (*abort_flag || !mbar_wait(&k_full[st], (kv / ST) & 1, 212) ||
-              (g > 0 && !mbar_wait(s_free, (g - 1) & 1, 213))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t ka = smem_u32(smem + C::kK + st * C::kKTile);
-          const uint32_t kr = ka + C::kKSlabA;
+        tc_fence_after();
+        const uint32_t ka = smem_u32(smem + C::kK + st * C::kKTile);
+        const uint64_t kd = kmajor_desc(ka, 128), krd = kmajor_desc(ka + C::kKSlabA, R > 0 ? R * 2 : 32);
+        if (elect_one()) {
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
-            umma_ss(tmem, kmajor_desc(qa + k * 32, 128), kmajor_desc(ka + k * 32, 128), kIdescS, k > 0);
+          for (int k = 0; k < 4; ++k)  // 16 K-elements = 32 bytes = 2 address units per step
+            umma_ss(tmem, qd + 2 * k, kd + 2 * k, kIdescS, k > 0);
 #pragma unroll
-          for (int k = 0; k < R / 16; ++k)
-            umma_ss(tmem, kmajor_desc(qr + k * 32, R * 2), kmajor_desc(kr + k * 32, R * 2), kIdescS, 1);
+          for (int k = 0; k < R / 16; ++k) umma_ss(tmem, qrd + 2 * k, krd + 2 * k, kIdescS, 1);
           umma_commit(s_full);
           umma_commit(&k_empty[st]);
-          if (j > 0 && !issue_pv(kv - 1, g - 1, j == 1, it)) {
-            ok = false;
-            break;
-          }
         }
-        if (!ok) break;
-        umma_commit(&q_empty[qb]);  // every QK^T of this item issued: Q is free once they finish
-        if (!issue_pv(kv - 1, g - 1, n_kv == 1, it)) ok = false;
+        __syncwarp();
+        if (j > 0 && !issue_pv(kv - 1, g - 1, j == 1, it)) {
+          ok = false;
+          break;
+        }
       }
-      if (!ok) *abort_flag = 1;
+      if (!ok) break;
+      if (elect_one()) umma_commit(&q_empty[qb]);  // every QK^T of this item issued: Q is free once they finish
+      __syncwarp();
+      if (!issue_pv(kv - 1, g - 1, n_kv == 1, it)) ok = false;
+    }
+    if (!ok && lane == 0) *abort_flag = 1;
+    if (elect_one()) {
       umma_commit(mdone);
       mbar_wait(mdone, 0, 216);
     }
+    __syncwarp();
   } else {
     // --------------------------------------------------------------- softmax + epilogue
     const int q = warp & 3;       // TMEM lane quarter of this warp

@@ -243,6 +243,18 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
       : "memory");
 }
 
+// One lane of a converged warp (elect.sync): the lane that issues a warp's
+// tcgen05.mma / commit while the whole warp runs the (warp-uniform) loop.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // Arrive (once) on an mbarrier when every previously issued tcgen05.mma of
 // this thread has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {

@@ -11,6 +11,7 @@
 #include "gemm.cuh"
 #include "rowops.cuh"
 #include "fmha.cuh"
+#include "fmha_pair.cuh"
 #include "forward.cuh"
 #include "simt_f32.cuh"
 #include "patchify.cuh"
@@ -101,6 +102,9 @@ int launch_gemm_tc2(const GemmIO& io, const GemmParams& p, cudaStream_t stream) 
 
 // GEMM kernel selection: 0 = automatic, 1 = one SM per tile, 2 = SM pairs.
 std::atomic<int> g_gemm_variant{0};
+// Attention kernel selection: 0 = automatic (one query tile per CTA), 1 = one
+// query tile per CTA, 2 = paired query tiles.
+std::atomic<int> g_fmha_variant{0};
 
 // Automatic choice (measured on B200 at the tower's shapes, K = 128 per stage
 // in both): LayerNorm-folded GEMMs on one SM per tile (their statistics warps
@@ -496,14 +500,16 @@ int launch_fmha(const void* qkv, int N, const int* cu, const int2* tiles, int n_
   p.ld_out = ldo;
   p.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(hd));
   p.drop = drop;
-  auto kern = fmha_varlen_kernel<T, HDP>;
-  constexpr int smem = FmhaCfg<HDP>::kSmem;
+  const bool pair = g_fmha_variant.load() == 2;
+  auto kern = pair ? fmha_pair_kernel<T, HDP> : fmha_varlen_kernel<T, HDP>;
+  const int smem = pair ? FmhaPairCfg<HDP>::kSmem : FmhaCfg<HDP>::kSmem;
   SG_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem));
-  // persistent: two CTAs per SM walk the (query tile, head) items
-  const int grid = std::min(p.n_items, 2 * sm_count());
+  // persistent: one CTA per SM walks the (query tile pair, head) items, or
+  // (single-tile kernel) two CTAs per SM walk the (query tile, head) items
+  const int grid = std::min(p.n_items, (pair ? 1 : 2) * sm_count());
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
-  cfg.blockDim = dim3(192, 1, 1);
+  cfg.blockDim = dim3(pair ? FmhaPairCfg<HDP>::kThreads : 192, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -847,6 +853,14 @@ int siglip2_set_gemm_variant(int variant) {
 }
 
 int siglip2_get_gemm_variant(void) { return g_gemm_variant.load(); }
+
+int siglip2_set_fmha_variant(int variant) {
+  SG_CHECK_ARG(variant >= 0 && variant <= 2, "attention variant must be 0 (auto), 1 (single tile) or 2 (tile pairs)");
+  g_fmha_variant.store(variant);
+  return SIGLIP2_OK;
+}
+
+int siglip2_get_fmha_variant(void) { return g_fmha_variant.load(); }
 
 int siglip2_check_device(int reset) {
   SG_CUDA(cudaDeviceSynchronize());

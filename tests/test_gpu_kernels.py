@@ -10,7 +10,19 @@ import torch.nn.functional as F
 pytestmark = pytest.mark.gpu
 
 from oracle import siglip2_oracle as O  # noqa: E402
+from siglip2_b200 import _lib as L  # noqa: E402
 from siglip2_b200 import ops  # noqa: E402
+
+
+@pytest.fixture(params=[1, 2], ids=["single_tile", "tile_pairs"])
+def fmha_variant(request):
+    """Attention tests run on both kernels: one 128-row query tile per CTA
+    (two CTAs per SM) and two query tiles per CTA sharing each K/V tile."""
+    lib = L.load()
+    old = lib.siglip2_get_fmha_variant()
+    L.check(lib.siglip2_set_fmha_variant(request.param))
+    yield request.param
+    L.check(lib.siglip2_set_fmha_variant(old))
 
 
 def _cu(lens):
@@ -42,7 +54,7 @@ def _ref_attn(q, k, v, lens, H, hd):
                                   # an image's last key tile ends on / just past 16-key chunks, and its last
                                   # query tile ends on / just past 32-row warps
                                   [16, 17, 31, 32, 33, 48, 95, 97, 112, 113, 160, 161, 191, 192, 193, 224, 225]])
-def test_fmha_varlen(dtype, H, hd, lens):
+def test_fmha_varlen(dtype, H, hd, lens, fmha_variant):
     g = torch.Generator(device="cuda").manual_seed(sum(lens) + hd)
     N = sum(lens)
     q, k, v = (torch.randn(N, H * hd, device="cuda", generator=g).to(dtype) for _ in range(3))
@@ -59,7 +71,7 @@ def test_fmha_varlen(dtype, H, hd, lens):
 
 
 @pytest.mark.parametrize("H,hd", [(16, 72), (12, 64), (16, 96)])
-def test_fmha_many_items_per_cta(H, hd):
+def test_fmha_many_items_per_cta(H, hd, fmha_variant):
     """The persistent attention kernel walks many (query tile, head) items
     per CTA (about 13 here), across image sizes from 1 to 1024 tokens, so Q
     buffers, K/V ring stages and the TMEM O hand-off all wrap many times."""
