@@ -66,8 +66,12 @@ typedef enum {
    * stream, in column-block slots (siglip2_rowsum_slots) */
   SIGLIP2_EPI_LN_ROWSUMS = 5,      /* as SIGLIP2_EPI_LN, mu/rstd from rs_in over K columns    */
   SIGLIP2_EPI_LN_ROWSUMS_GELU = 6, /* as SIGLIP2_EPI_LN_GELU, likewise                        */
-  SIGLIP2_EPI_BIAS_RES_ROWSUMS = 7 /* as SIGLIP2_EPI_BIAS_RES, and rs_acc receives the slot
+  SIGLIP2_EPI_BIAS_RES_ROWSUMS = 7, /* as SIGLIP2_EPI_BIAS_RES, and rs_acc receives the slot
                                       statistics of the row's rounded outputs                 */
+  /* 8 is the patch embedding's position epilogue (siglip2_patch_embed) */
+  SIGLIP2_EPI_BIAS_GELU_GRAD = 9   /* out = res * gelu_tanh'(A.B^T + bias): the GELU backward
+                                      fused into the GEMM that recomputes the pre-activation
+                                      (res = the gradient w.r.t. the GELU output)            */
 } siglip2_epilogue;
 
 /* Library version (major*10000 + minor*100 + patch). */
@@ -114,6 +118,23 @@ int siglip2_check_device(int reset);
 int siglip2_gemm(int dtype, int epilogue, const void* a_dev, int lda, const void* b_dev, int ldb, void* out_dev,
                  int ldo, int M, int N, int K, const float* bias_dev, const void* res_dev, int ldr,
                  const float* c1_dev, const float* c2_dev, float eps, void* stream);
+
+/* Backward GEMMs on the tensor cores without transposed copies:
+ *   out[M, N] = epilogue(op(A) . op(B)^T)
+ * op(A) = A stored [M][K] (trans_a = 0) or A stored [K][M] (trans_a = 1);
+ * op(B) = B stored [N][K] (trans_b = 0) or B stored [K][N] (trans_b = 1).
+ * dgrad of y = x W^T:  dx = dy . W    -> trans_a = 0, trans_b = 1 (B = W [N_out][K_in]);
+ * wgrad:               dW = dy^T . x  -> trans_a = 1 (A = dy [tokens][N_out]),
+ *                                         trans_b = 1 (B = x [tokens][K_in]).
+ * Epilogues: SIGLIP2_EPI_BIAS (bias may be NULL) and SIGLIP2_EPI_BIAS_GELU_GRAD.
+ * bf16/f16; M, N, K and leading dimensions multiples of 8.  The transposed
+ * operand arrives by 64 x 64 TMA boxes and the tcgen05 MMA reads it as an
+ * MN-major operand.  Replaces the matmuls of the autograd backward of the
+ * reference's Linear layers (model.py:138-141, 183-184; the fused
+ * linear+GELU backward of optimized_siglip2/ops/MLP.py:409-553). */
+int siglip2_gemm_t(int dtype, int epilogue, int trans_a, int trans_b, const void* a_dev, int lda, const void* b_dev,
+                   int ldb, void* out_dev, int ldo, int M, int N, int K, const float* bias_dev, const void* res_dev,
+                   int ldr, void* stream);
 
 /* LayerNorm statistics for the LayerNorm-folded GEMMs are kept per column
  * block ("slots"): a [rows][S] array of float pairs (mean, centred sum of

@@ -29,6 +29,8 @@ SIGNATURES = {
                               _vp, _vp, _c_int, _vp, _vp, _c_float, _vp]),
     "siglip2_gemm_rowsums": (_c_int, [_c_int, _c_int, _vp, _c_int, _vp, _c_int, _vp, _c_int, _c_int, _c_int, _c_int,
                                       _vp, _vp, _c_int, _vp, _vp, _c_float, _vp, _vp, _vp]),
+    "siglip2_gemm_t": (_c_int, [_c_int, _c_int, _c_int, _c_int, _vp, _c_int, _vp, _c_int, _vp, _c_int, _c_int,
+                                _c_int, _c_int, _vp, _vp, _c_int, _vp]),
     "siglip2_rowsum_slots": (_c_int, [_c_int, _c_int]),
     "siglip2_rowsum_block": (_c_int, [_c_int, _c_int]),
     "siglip2_rowsums": (_c_int, [_c_int, _vp, _c_int, _c_int, _c_int, _vp, _vp]),
@@ -83,6 +85,7 @@ STATUS = {0: "OK", -1: "ERR_ARG", -2: "ERR_ALIGN", -3: "ERR_SHAPE", -4: "ERR_CUD
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
 EPI_BIAS, EPI_BIAS_RES, EPI_LN, EPI_LN_GELU, EPI_BIAS_GELU = 0, 1, 2, 3, 4
 EPI_LN_ROWSUMS, EPI_LN_ROWSUMS_GELU, EPI_BIAS_RES_ROWSUMS = 5, 6, 7
+EPI_BIAS_GELU_GRAD = 9
 
 _lib = None
 

@@ -43,12 +43,16 @@ enum GemmEpilogue : int {
   kEpiLnRsGelu = 6,      // as kEpiLnGelu, likewise
   kEpiBiasResRs = 7,     // as kEpiBiasRes, and accumulates the row sums of the rounded output
   kEpiBiasPosRs = 8,     // out = acc + bias + resized position embedding of the row's token, + row sums
+  kEpiBiasGeluGrad = 9,  // out = res * gelu_tanh'(acc + bias): the GELU backward fused into the GEMM that
+                         // recomputes the pre-activation (res = the incoming gradient)
 };
 
 __host__ __device__ constexpr bool epi_has_stat_warps(int e) { return e == kEpiLn || e == kEpiLnGelu; }
 __host__ __device__ constexpr bool epi_is_ln(int e) { return e == kEpiLn || e == kEpiLnGelu || e == kEpiLnRs || e == kEpiLnRsGelu; }
 __host__ __device__ constexpr bool epi_is_gelu(int e) { return e == kEpiLnGelu || e == kEpiLnRsGelu || e == kEpiBiasGelu; }
-__host__ __device__ constexpr bool epi_has_res(int e) { return e == kEpiBiasRes || e == kEpiBiasResRs; }
+__host__ __device__ constexpr bool epi_has_res(int e) {
+  return e == kEpiBiasRes || e == kEpiBiasResRs || e == kEpiBiasGeluGrad;
+}
 
 struct GemmParams {
   int M, N, K;
@@ -198,7 +202,7 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
       if constexpr (kLnMath) {
         prefetch_l1(p.c1 + pc0 + lane * 32);
         prefetch_l1(p.c2 + pc0 + lane * 32);
-      } else {
+      } else if (p.bias) {
         prefetch_l1(p.bias + pc0 + lane * 32);
       }
     }
@@ -297,7 +301,12 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
           }
         } else {
           float a[32];
-          load_param32(p.bias, col0, p.N, a);
+          if (p.bias) {
+            load_param32(p.bias, col0, p.N, a);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) a[j] = 0.f;
+          }
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             v[j] += a[j];
@@ -340,8 +349,13 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
 #pragma unroll
           for (int h = 0; h < 4; ++h) {
             const float2 f = Pack2<T>::unpack(rw[h]);
-            v[g * 8 + 2 * h] += f.x;
-            v[g * 8 + 2 * h + 1] += f.y;
+            if constexpr (EPI == kEpiBiasGeluGrad) {
+              v[g * 8 + 2 * h] = f.x * gelu_tanh_grad(v[g * 8 + 2 * h]);
+              v[g * 8 + 2 * h + 1] = f.y * gelu_tanh_grad(v[g * 8 + 2 * h + 1]);
+            } else {
+              v[g * 8 + 2 * h] += f.x;
+              v[g * 8 + 2 * h + 1] += f.y;
+            }
           }
         }
       }
@@ -460,18 +474,27 @@ __device__ __forceinline__ void gemm_row_stats(const GemmParams& p, const uint8_
   }
 }
 
-template <typename T, int BN, int EPI, int SUB>
+// kAT / kBT: the operand is stored transposed ("MN-major"): A as [K][M]
+// (M contiguous) and/or B as [K][N], as the backward's dgrad (B = the
+// forward weight [N_out][K_in] read as [K][N]) and wgrad (A = the output
+// gradient [tokens][N_out], B = the forward input [tokens][K_in]) need them.
+// Such a tile arrives as 64-column TMA boxes of 64 K-rows (128B swizzle),
+// one 8 KB chunk per 64 M (N) columns, and the UMMA reads it through an
+// MN-major descriptor (chunk stride 8 KB, 8-row groups 1 KB apart).
+template <typename T, int BN, int EPI, int SUB, bool kAT = false, bool kBT = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
                    const GemmParams p) {
   constexpr bool kLN = epi_has_stat_warps(EPI);  // statistics warps in this kernel
   constexpr bool kRes = epi_has_res(EPI);
+  static_assert(!(kAT && kLN), "the statistics warps read K-major A tiles");
   using Cfg = GemmCfg<BN, SUB, EPI>;
   constexpr int EW = epi_warps(EPI);
   constexpr int STAGES = Cfg::kStages;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr uint32_t kIdesc = make_idesc(kGemmBM, BN, kBF16, false, false);
+  constexpr uint32_t kIdesc = make_idesc(kGemmBM, BN, kBF16, kAT, kBT);
+  constexpr int kChunk = 64 * kGemmBK * 2;  // one MN-major chunk: 64 columns x 64 K-rows
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -552,8 +575,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int sub = 0; sub < SUB; ++sub) {
             const int kx = (kb * SUB + sub) * kGemmBK;
-            tma_load_2d(smA + stage * Cfg::kStageA + sub * Cfg::kSlabA, &tmA, &full[stage], kx, m0);
-            tma_load_2d(smB + stage * Cfg::kStageB + sub * Cfg::kSlabB, &tmB, &full[stage], kx, n0);
+            uint8_t* sa = smA + stage * Cfg::kStageA + sub * Cfg::kSlabA;
+            uint8_t* sb = smB + stage * Cfg::kStageB + sub * Cfg::kSlabB;
+            if constexpr (kAT) {
+#pragma unroll
+              for (int c = 0; c < kGemmBM / 64; ++c) tma_load_2d(sa + c * kChunk, &tmA, &full[stage], m0 + 64 * c, kx);
+            } else {
+              tma_load_2d(sa, &tmA, &full[stage], kx, m0);
+            }
+            if constexpr (kBT) {
+#pragma unroll
+              for (int c = 0; c < BN / 64; ++c) tma_load_2d(sb + c * kChunk, &tmB, &full[stage], n0 + 64 * c, kx);
+            } else {
+              tma_load_2d(sb, &tmB, &full[stage], kx, n0);
+            }
           }
           ++issued;
           if (++stage == STAGES) {
@@ -605,8 +640,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int sub = 0; sub < SUB; ++sub) {
 #pragma unroll
             for (int k = 0; k < kGemmBK / 16; ++k) {
-              umma_ss(d_tmem, kmajor_desc(a_base + sub * Cfg::kSlabA + k * 32, 128),
-                      kmajor_desc(b_base + sub * Cfg::kSlabB + k * 32, 128), kIdesc, (kb | sub | k) != 0);
+              // K-major: 16 K-elements = 32 bytes along the row; MN-major: 16 K-rows = 2 KB
+              const uint64_t ad = kAT ? smem_desc(a_base + sub * Cfg::kSlabA + k * 2048, kChunk, 1024, kSw128)
+                                      : kmajor_desc(a_base + sub * Cfg::kSlabA + k * 32, 128);
+              const uint64_t bd = kBT ? smem_desc(b_base + sub * Cfg::kSlabB + k * 2048, kChunk, 1024, kSw128)
+                                      : kmajor_desc(b_base + sub * Cfg::kSlabB + k * 32, 128);
+              umma_ss(d_tmem, ad, bd, kIdesc, (kb | sub | k) != 0);
             }
           }
           umma_commit(&empty[stage]);

@@ -458,4 +458,14 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   return fmaf(h, tanh_approx(z), h);
 }
 
+// d/dx of gelu_tanh: 0.5 (1 + t) + 0.5 x (1 - t^2) sqrt(2/pi) (1 + 3 * 0.044715 x^2), t = tanh(...)
+__device__ __forceinline__ float gelu_tanh_grad(float x) {
+  const float k0 = 0.7978845608028654f;   // sqrt(2/pi)
+  const float k01 = 0.0356774081363001f;  // sqrt(2/pi) * 0.044715
+  const float x2 = x * x;
+  const float t = tanh_approx(x * fmaf(k01, x2, k0));
+  const float dz = fmaf(3.f * k01, x2, k0);  // d/dx of the tanh argument
+  return fmaf(0.5f * x * dz, fmaf(-t, t, 1.f), 0.5f * (1.f + t));
+}
+
 }  // namespace sg

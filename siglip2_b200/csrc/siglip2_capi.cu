@@ -39,17 +39,20 @@ inline void set_pdl_attr(cudaLaunchAttribute* a) {
   a->val.programmaticStreamSerializationAllowed = 1;
 }
 
-template <typename T, int BN, int EPI, int SUB>
+template <typename T, int BN, int EPI, int SUB, bool kAT = false, bool kBT = false>
 int launch_gemm_tc(const GemmIO& io, const GemmParams& p, cudaStream_t stream) {
   CUtensorMap ta, tb, to, tr;
-  SG_TRY(make_tmap_2d(&ta, io.a, 2, p.M, p.K, io.lda, kGemmBM, kGemmBK));
-  SG_TRY(make_tmap_2d(&tb, io.b, 2, p.N, p.K, io.ldb, BN, kGemmBK));
+  // transposed operands are [K][M] / [K][N] in memory: 64 x 64 boxes
+  if (kAT) SG_TRY(make_tmap_2d(&ta, io.a, 2, p.K, p.M, io.lda, kGemmBK, 64));
+  else SG_TRY(make_tmap_2d(&ta, io.a, 2, p.M, p.K, io.lda, kGemmBM, kGemmBK));
+  if (kBT) SG_TRY(make_tmap_2d(&tb, io.b, 2, p.K, p.N, io.ldb, kGemmBK, 64));
+  else SG_TRY(make_tmap_2d(&tb, io.b, 2, p.N, p.K, io.ldb, BN, kGemmBK));
   SG_TRY(make_tmap_2d(&to, io.out, 2, p.M, p.N, io.ldo, 32, kEpiCols));
   if (epi_has_res(EPI)) SG_TRY(make_tmap_2d(&tr, io.res, 2, p.M, p.N, io.ldr, 32, kEpiCols));
   else tr = to;
   constexpr int threads = kGemmThreads;
   constexpr int smem = GemmCfg<BN, SUB, EPI>::kSmemBytes;
-  auto kern = gemm_tc_kernel<T, BN, EPI, SUB>;
+  auto kern = gemm_tc_kernel<T, BN, EPI, SUB, kAT, kBT>;
   SG_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem));
   const int tiles = ((p.M + kGemmBM - 1) / kGemmBM) * ((p.N + BN - 1) / BN);
   const int grid = tiles < sm_count() ? tiles : sm_count();
@@ -131,7 +134,18 @@ int dispatch_epi(int epi, const GemmIO& io, const GemmParams& p, cudaStream_t s)
     case kEpiLnRsGelu: return launch_gemm_any<T, BN, kEpiLnRsGelu>(io, p, s);
     case kEpiBiasResRs: return launch_gemm_any<T, BN, kEpiBiasResRs>(io, p, s);
     case kEpiBiasPosRs: return launch_gemm_any<T, BN, kEpiBiasPosRs>(io, p, s);
+    case kEpiBiasGeluGrad: return launch_gemm_any<T, BN, kEpiBiasGeluGrad>(io, p, s);
     default: return set_error(SIGLIP2_ERR_ARG, "unknown epilogue %d", epi);
+  }
+}
+
+// Transposed-operand GEMMs of the backward (one SM per 128 x 256 tile).
+template <typename T, bool kAT, bool kBT>
+int dispatch_epi_t(int epi, const GemmIO& io, const GemmParams& p, cudaStream_t s) {
+  switch (epi) {
+    case kEpiBias: return launch_gemm_tc<T, 256, kEpiBias, 2, kAT, kBT>(io, p, s);
+    case kEpiBiasGeluGrad: return launch_gemm_tc<T, 256, kEpiBiasGeluGrad, 2, kAT, kBT>(io, p, s);
+    default: return set_error(SIGLIP2_ERR_UNSUPPORTED, "transposed-operand GEMM: epilogue %d not supported", epi);
   }
 }
 
@@ -160,7 +174,7 @@ int sg_gemm_impl(int dtype, int epi, const void* a, int lda, const void* b, int 
   SG_CHECK_ARG(M >= 0 && N > 0 && K > 0, "bad GEMM shape M=%d N=%d K=%d", M, N, K);
   if (M == 0) return SIGLIP2_OK;
   SG_CHECK_ARG(a && b && out, "null operand");
-  SG_CHECK_ARG(epi >= 0 && epi <= 8, "unknown epilogue %d", epi);
+  SG_CHECK_ARG(epi >= 0 && epi <= 9, "unknown epilogue %d", epi);
   SG_CHECK_ARG(epi != kEpiBiasPosRs ||
                    (pos && pos->table && pos->grid > 0 && pos->tok_img && pos->hw && pos->cu),
                "position-embedding epilogue needs table, grid, token->image map, grids and row starts");
@@ -178,6 +192,8 @@ int sg_gemm_impl(int dtype, int epi, const void* a, int lda, const void* b, int 
   if (misaligned8(rs_in) || misaligned8(rs_acc))
     return set_error(SIGLIP2_ERR_ALIGN, "row-sum buffers must be 8-byte aligned");
   if (dtype == SIGLIP2_F32) {
+    if (epi == kEpiBiasGeluGrad)
+      return set_error(SIGLIP2_ERR_UNSUPPORTED, "fp32 GEMM: the GELU-gradient epilogue is tensor-core only");
     if (epi_has_stat_warps(epi))
       return set_error(SIGLIP2_ERR_UNSUPPORTED, "fp32 GEMM: use the row-sum LayerNorm epilogues (5, 6)");
     if (epi_has_res(epi) && !res) return set_error(SIGLIP2_ERR_ARG, "residual epilogue needs res");
@@ -242,6 +258,45 @@ int sg_gemm_impl(int dtype, int epi, const void* a, int lda, const void* b, int 
   return dispatch_bn<__half>(epi, io, p, stream);
 }
 
+
+// out[M, N] = epi(op(A) . op(B)^T) with op(A) = A [M][K] or, trans_a, A
+// stored [K][M]; op(B) = B [N][K] or, trans_b, B stored [K][N].
+int sg_gemm_t_impl(int dtype, int epi, int trans_a, int trans_b, const void* a, int lda, const void* b, int ldb,
+                   void* out, int ldo, int M, int N, int K, const float* bias, const void* res, int ldr,
+                   cudaStream_t stream) {
+  SG_CHECK_ARG(M >= 0 && N > 0 && K > 0, "bad GEMM shape M=%d N=%d K=%d", M, N, K);
+  if (M == 0) return SIGLIP2_OK;
+  SG_CHECK_ARG(a && b && out, "null operand");
+  SG_CHECK_ARG(epi == kEpiBias || epi == kEpiBiasGeluGrad, "transposed-operand GEMM: epilogue %d not supported", epi);
+  SG_CHECK_ARG(epi != kEpiBiasGeluGrad || (bias && res), "GELU-gradient epilogue needs bias and res");
+  if (dtype != SIGLIP2_BF16 && dtype != SIGLIP2_F16)
+    return set_error(SIGLIP2_ERR_UNSUPPORTED, "transposed-operand GEMM supports bf16/f16 (dtype=%d)", dtype);
+  // TMA wants 16-byte row pitches and the output / residual rows are stored
+  // by TMA too; the extents themselves are free (out-of-range boxes read
+  // zeros, stores are clipped), so token counts need no rounding
+  if (N % 8 || lda % 8 || ldb % 8 || ldo % 8 || (res && ldr % 8))
+    return set_error(SIGLIP2_ERR_ALIGN, "N and leading dimensions must be multiples of 8");
+  if (lda < (trans_a ? M : K) || ldb < (trans_b ? N : K) || ldo < N || (res && ldr < N))
+    return set_error(SIGLIP2_ERR_SHAPE, "leading dimension smaller than the row");
+  if (!aligned16(out) || (res && !aligned16(res)) || (bias && !aligned16(bias)))
+    return set_error(SIGLIP2_ERR_ALIGN, "output / residual / bias must be 16-byte aligned");
+  GemmParams p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.bias = bias;
+  GemmIO io{a, lda, b, ldb, out, ldo, res, ldr};
+  const bool bf = dtype == SIGLIP2_BF16;
+  if (!trans_a && !trans_b)
+    return sg_gemm_impl(dtype, epi, a, lda, b, ldb, out, ldo, M, N, K, bias, res, ldr, nullptr, nullptr, 0.f, stream);
+  if (!trans_a && trans_b)
+    return bf ? dispatch_epi_t<__nv_bfloat16, false, true>(epi, io, p, stream)
+              : dispatch_epi_t<__half, false, true>(epi, io, p, stream);
+  if (trans_a && trans_b)
+    return bf ? dispatch_epi_t<__nv_bfloat16, true, true>(epi, io, p, stream)
+              : dispatch_epi_t<__half, true, true>(epi, io, p, stream);
+  return set_error(SIGLIP2_ERR_UNSUPPORTED, "transposed A with K-major B is not built");
+}
 
 // ---------------------------------------------------------------------------
 // LayerNorm
@@ -881,6 +936,13 @@ int siglip2_gemm(int dtype, int epilogue, const void* a_dev, int lda, const void
                  const float* c1_dev, const float* c2_dev, float eps, void* stream) {
   return sg_gemm_impl(dtype, epilogue, a_dev, lda, b_dev, ldb, out_dev, ldo, M, N, K, bias_dev, res_dev, ldr, c1_dev,
                       c2_dev, eps, static_cast<cudaStream_t>(stream));
+}
+
+int siglip2_gemm_t(int dtype, int epilogue, int trans_a, int trans_b, const void* a_dev, int lda, const void* b_dev,
+                   int ldb, void* out_dev, int ldo, int M, int N, int K, const float* bias_dev, const void* res_dev,
+                   int ldr, void* stream) {
+  return sg_gemm_t_impl(dtype, epilogue, trans_a, trans_b, a_dev, lda, b_dev, ldb, out_dev, ldo, M, N, K, bias_dev,
+                        res_dev, ldr, static_cast<cudaStream_t>(stream));
 }
 
 int siglip2_rowsum_slots(int dtype, int n) {

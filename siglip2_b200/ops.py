@@ -49,6 +49,25 @@ def gemm(a: torch.Tensor, w: torch.Tensor, epilogue: int, bias=None, res=None, c
     return out
 
 
+def gemm_t(a: torch.Tensor, b: torch.Tensor, trans_a: bool, trans_b: bool, epilogue: int = L.EPI_BIAS,
+           bias=None, res=None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``siglip2_gemm_t``: ``epilogue(op(a) @ op(b).T)`` with ``op(a) = a`` ([M, K])
+    or ``a.T`` (``trans_a``: ``a`` is [K, M]) and ``op(b) = b`` ([N, K]) or
+    ``b.T`` (``trans_b``: ``b`` is [K, N]).  Row-major operands with unit
+    column stride; the transposed ones are read as MN-major tiles, no copy."""
+    _need_cuda(a, b, bias, res, out)
+    assert a.dim() == 2 and b.dim() == 2 and a.stride(1) == 1 and b.stride(1) == 1
+    M, K = (a.shape[1], a.shape[0]) if trans_a else a.shape
+    N, Kb = (b.shape[1], b.shape[0]) if trans_b else b.shape
+    assert K == Kb, (a.shape, b.shape, trans_a, trans_b)
+    if out is None:
+        out = torch.empty((M, N), dtype=a.dtype, device=a.device)
+    L.call("siglip2_gemm_t", dtype_code(a.dtype), epilogue, int(trans_a), int(trans_b), a.data_ptr(), a.stride(0),
+           b.data_ptr(), b.stride(0), out.data_ptr(), out.stride(0), M, N, K, _ptr(bias), _ptr(res),
+           res.stride(0) if res is not None else 0, _stream(a.device))
+    return out
+
+
 def fold_layernorm(w: torch.Tensor, b: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, dtype):
     """LayerNorm(gamma, beta) followed by Linear(w, b) as a GEMM on the raw
     input: returns ``(w*gamma in dtype, c1, c2)`` with ``c1 = rowsum(w*gamma)``

@@ -16,9 +16,10 @@ Ops (``torch.ops.siglip2_b200.<name>``):
   token_image, patch_embed     -- patch Linear + resized position grid
   vision_tower                 -- the whole tower (``siglip2_forward``)
 
-Backward: ``gemm`` (bias, bias + GELU-tanh and bias + residual epilogues),
-``layernorm``, ``fmha_varlen`` and ``patch_embed`` have a stop-gap autograd
-formula (below); back-propagating through any other op raises.
+Backward: ``gemm`` (bias, bias + GELU-tanh and bias + residual epilogues;
+tensor-core dgrad / wgrad through ``gemm_t``), ``layernorm``, ``fmha_varlen``
+and ``patch_embed`` have an autograd formula (below); back-propagating through
+any other op raises.
 """
 from __future__ import annotations
 
@@ -52,11 +53,29 @@ def _(a, w, epilogue, bias, res, c1, c2, eps):
     return a.new_empty((a.shape[0], w.shape[0]))
 
 
-# Stop-gap backward of the plain epilogues (bias, bias + GELU-tanh, bias +
-# residual), so that the MLP can be trained through these kernels: dgrad and
-# wgrad run on the library's own GEMM (on transposed copies, the contracted
-# dimension zero-padded to a multiple of 8); the bias sums and the GELU-tanh
-# derivative (at the recomputed pre-activation) are fp32 torch arithmetic.
+@torch.library.custom_op("siglip2_b200::gemm_t", mutates_args=(), device_types="cuda")
+def gemm_t(a: Tensor, b: Tensor, trans_a: bool, trans_b: bool, epilogue: int, bias: Optional[Tensor],
+           res: Optional[Tensor]) -> Tensor:
+    """``siglip2_gemm_t``: ``epilogue(op(a) @ op(b).T)``, op = transpose when
+    the flag is set (the operand is read as MN-major tiles, not copied)."""
+    return ops.gemm_t(a, b, trans_a, trans_b, epilogue, bias, res)
+
+
+@gemm_t.register_fake
+def _(a, b, trans_a, trans_b, epilogue, bias, res):
+    M = a.shape[1] if trans_a else a.shape[0]
+    N = b.shape[1] if trans_b else b.shape[0]
+    return a.new_empty((M, N))
+
+
+# Backward of the plain epilogues (bias, bias + GELU-tanh, bias + residual).
+# bf16/f16: dgrad dA = dY W and wgrad dW = dY^T A run on the tensor cores with
+# the transposed operands read in place (siglip2_gemm_t); for bias + GELU the
+# pre-activation is recomputed by a GEMM whose epilogue multiplies the incoming
+# gradient by GELU-tanh' (SIGLIP2_EPI_BIAS_GELU_GRAD), so the GELU backward is
+# fused into that GEMM.  fp32 (and shapes the tensor-core path rejects): the
+# same products on the library GEMM over transposed copies, the contracted
+# dimension zero-padded to a multiple of 8.  Bias sums are fp32 torch.
 _GELU_K0 = math.sqrt(2.0 / math.pi)
 _GELU_K1 = 0.044715
 
@@ -89,17 +108,42 @@ def _gemm_setup(ctx, inputs, output):
     ctx.save_for_backward(a, w, bias)
 
 
+def _tensor_core_backward(a: Tensor, w: Tensor, grad: Tensor) -> bool:
+    """The transposed-operand GEMMs apply: half precision, row pitches and
+    the output widths multiples of 8 elements."""
+    return (a.dtype in (torch.bfloat16, torch.float16) and a.dtype == w.dtype == grad.dtype
+            and a.shape[1] % 8 == 0 and w.shape[0] % 8 == 0)
+
+
+def _dgrad(g: Tensor, w: Tensor) -> Tensor:
+    """dA = dY W: [M, N] x [N, K] with W read as the MN-major B operand."""
+    return gemm_t(g.contiguous(), w.contiguous(), False, True, L.EPI_BIAS, None, None)
+
+
+def _wgrad(g: Tensor, a: Tensor) -> Tensor:
+    """dW = dY^T A: [N, M] x [M, K] with both read as MN-major operands."""
+    return gemm_t(g.contiguous(), a.contiguous(), True, True, L.EPI_BIAS, None, None)
+
+
 def _gemm_backward(ctx, grad):
     a, w, bias = ctx.saved_tensors
     if ctx.epilogue not in (L.EPI_BIAS, L.EPI_BIAS_GELU, L.EPI_BIAS_RES):
         raise NotImplementedError("siglip2_b200::gemm: backward exists for the bias, bias+GELU and bias+residual "
                                   "epilogues only")
     g = grad
+    tc = _tensor_core_backward(a, w, grad)
     if ctx.epilogue == L.EPI_BIAS_GELU:
-        z = gemm(a.contiguous(), w.contiguous(), L.EPI_BIAS, bias, None, None, None, 0.0)
-        g = (grad.float() * _gelu_tanh_grad(z.float())).to(grad.dtype)
-    da = _matmul_nt(g, w.t()) if ctx.needs_input_grad[0] else None
-    dw = _matmul_nt(g.t(), a.t()) if ctx.needs_input_grad[1] else None
+        if tc:  # pre-activation recomputed, times GELU-tanh', in one GEMM epilogue
+            g = gemm(a.contiguous(), w.contiguous(), L.EPI_BIAS_GELU_GRAD, bias, grad.contiguous(), None, None, 0.0)
+        else:
+            z = gemm(a.contiguous(), w.contiguous(), L.EPI_BIAS, bias, None, None, None, 0.0)
+            g = (grad.float() * _gelu_tanh_grad(z.float())).to(grad.dtype)
+    if tc:
+        da = _dgrad(g, w) if ctx.needs_input_grad[0] else None
+        dw = _wgrad(g, a) if ctx.needs_input_grad[1] else None
+    else:
+        da = _matmul_nt(g, w.t()) if ctx.needs_input_grad[0] else None
+        dw = _matmul_nt(g.t(), a.t()) if ctx.needs_input_grad[1] else None
     db = g.float().sum(0) if ctx.needs_input_grad[3] else None
     dres = grad if ctx.needs_input_grad[4] else None
     return da, dw, None, db, dres, None, None, None
@@ -266,8 +310,12 @@ def _patch_embed_backward(ctx, grad):
     position table's gradient is the adjoint of the per-image antialiased
     bilinear resize, taken through torch's interpolate (one image at a time)."""
     patches, w, table = ctx.saved_tensors
-    d_patches = _matmul_nt(grad, w.t()) if ctx.needs_input_grad[0] else None
-    dw = _matmul_nt(grad.t(), patches.t()) if ctx.needs_input_grad[1] else None
+    if _tensor_core_backward(patches, w, grad):
+        d_patches = _dgrad(grad, w) if ctx.needs_input_grad[0] else None
+        dw = _wgrad(grad, patches) if ctx.needs_input_grad[1] else None
+    else:
+        d_patches = _matmul_nt(grad, w.t()) if ctx.needs_input_grad[0] else None
+        dw = _matmul_nt(grad.t(), patches.t()) if ctx.needs_input_grad[1] else None
     db = grad.float().sum(0) if ctx.needs_input_grad[2] else None
     dtable = None
     if ctx.needs_input_grad[3]:

@@ -229,3 +229,49 @@ def test_layernorm_fold_large_row_mean(dtype, source):
             ref = _gelu(ref)
         torch.cuda.synchronize()
         _close(out, ref, tol=1e-2)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M,N_out,K_in", [(1001, 1152, 4304), (4097, 4304, 1152), (39178, 3456, 1152),
+                                          (130, 768, 768), (7, 1152, 1152)])
+def test_gemm_transposed_operands_dgrad_wgrad(dtype, M, N_out, K_in):
+    """siglip2_gemm_t: dgrad dA = dY W (W read as the MN-major B operand) and
+    wgrad dW = dY^T A (both read MN-major) against fp32 torch on the same
+    inputs; token counts not multiples of the tile."""
+    g = torch.Generator(device="cuda").manual_seed(M + N_out)
+    dy = (torch.randn(M, N_out, device="cuda", generator=g) * 0.1).to(dtype)
+    w = (torch.randn(N_out, K_in, device="cuda", generator=g) * 0.03).to(dtype)
+    a = torch.randn(M, K_in, device="cuda", generator=g).to(dtype)
+    da = ops.gemm_t(dy, w, False, True)
+    dw = ops.gemm_t(dy, a, True, True)
+    torch.cuda.synchronize()
+    assert da.shape == (M, K_in) and dw.shape == (N_out, K_in)
+    _close(da, dy.float() @ w.float())
+    _close(dw, dy.float().T @ a.float())
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M,N,K", [(1000, 4304, 1152), (257, 3072, 768)])
+def test_gemm_gelu_gradient_epilogue(dtype, M, N, K):
+    """SIGLIP2_EPI_BIAS_GELU_GRAD: the pre-activation recomputed and the
+    incoming gradient multiplied by GELU-tanh' in the epilogue."""
+    g = torch.Generator(device="cuda").manual_seed(N + K)
+    a = torch.randn(M, K, device="cuda", generator=g).to(dtype)
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.03).to(dtype)
+    bias = torch.randn(N, device="cuda", generator=g) * 0.1
+    up = torch.randn(M, N, device="cuda", generator=g).to(dtype)
+    out = ops.gemm(a, w, L.EPI_BIAS_GELU_GRAD, bias=bias, res=up)
+    z = (a.float() @ w.float().T + bias).requires_grad_(True)
+    _gelu(z).backward(up.float())
+    torch.cuda.synchronize()
+    _close(out, z.grad, tol=2e-2)
+
+
+def test_gemm_transposed_rejects_bad_args():
+    a = torch.zeros(64, 100, dtype=torch.bfloat16, device="cuda")  # pitch 100: not a multiple of 8
+    w = torch.zeros(64, 128, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(L.Siglip2Error):
+        ops.gemm_t(a, w, True, True)
+    with pytest.raises(L.Siglip2Error):  # tensor-core only
+        ops.gemm_t(torch.zeros(64, 64, device="cuda"), torch.zeros(64, 128, device="cuda"), False, True)
+    L.check(L.load().siglip2_check_device(1))
