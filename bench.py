@@ -61,6 +61,9 @@ def parse():
     ap.add_argument("--workload", default="cfg2", choices=sorted(W.WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="bounded CPU-baseline sample length")
+    ap.add_argument("--mode", choices=["forward", "train"], default="forward",
+                    help="train: the reference benchmark.py's measurement (train(), forward and backward timed "
+                         "separately over 1024 full 16x16 images in mini-batches of 64)")
     return ap.parse_args()
 
 
@@ -172,9 +175,73 @@ def run_reference_arm(args, wl, rank, world):
     }), flush=True)
 
 
+# --------------------------------------------------------------------------- train mode
+def run_train_mode(args):
+    """The reference benchmark.py's measurement (benchmark.py:69-161,
+    report.md:4-6): So400m dims (Siglip2VisionConfig defaults), attention
+    dropout 0.1 in train(), 1024 images of full 16x16 grids in mini-batches
+    of 64, torch.randn patches in bf16; per mini-batch the forward
+    (``model((seq, grids))``) and the backward (``out.sum().backward()``) are
+    timed separately with CUDA events and scaled to the 1024 images; peak
+    memory from the caching allocator.  Prints one JSON line."""
+    from siglip2_b200 import Siglip2SequenceVisionTransformerOptimized, Siglip2VisionConfig
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = Siglip2VisionConfig()
+    cfg.vision_use_head = False  # the packed API returns last_hidden_state only
+    torch.manual_seed(0)
+    model = Siglip2SequenceVisionTransformerOptimized(cfg)
+    model.load_state_dict(W.init_state_dict(cfg, seed=1337, with_head=False))
+    model = model.to(device=dev, dtype=torch.bfloat16)
+    model.train()
+    bsz, max_patches, total = 64, 256, 1024
+    modifier = total // bsz
+    grids = torch.tensor([[16, 16]] * bsz, dtype=torch.int64)
+    batches = [torch.randn(bsz * max_patches, 768, generator=torch.Generator().manual_seed(i)).to(dev, torch.bfloat16)
+               for i in range(2)]
+    for i in range(args.warmup):
+        out = model((batches[i % 2], grids))
+        out.sum().backward()
+        model.zero_grad()
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats(dev)
+    fwd, bwd = [], []
+    with ClockSampler(0) as clk:
+        for i in range(args.steps):
+            e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            e[0].record()
+            out = model((batches[i % 2], grids))
+            e[1].record()
+            out.sum().backward()
+            e[2].record()
+            torch.cuda.synchronize()
+            fwd.append(e[0].elapsed_time(e[1]))
+            bwd.append(e[1].elapsed_time(e[2]))
+            model.zero_grad()
+    f_ms = sum(fwd) / len(fwd) * modifier
+    b_ms = sum(bwd) / len(bwd) * modifier
+    print(json.dumps({
+        "metric": "benchmark.py-shaped train step: So400m, 1024 full 16x16 images, mini-batch 64, bf16, "
+                  "train() with attention dropout 0.1",
+        "forward_ms_per_1024_images": round(f_ms, 2), "backward_ms_per_1024_images": round(b_ms, 2),
+        "forward_images_per_s": round(total / (f_ms / 1e3), 1),
+        "train_images_per_s": round(total / ((f_ms + b_ms) / 1e3), 1),
+        "peak_mem_mib": round(torch.cuda.max_memory_allocated(dev) / 2 ** 20, 1),
+        "steps": args.steps, "warmup": args.warmup, "clocks": clk.summary(),
+        "reference_report_md": {"original_model_py": {"forward_ms": 2099.66, "backward_ms": 2899.58,
+                                                      "peak_mem_mib": 19288.3},
+                                "optimized": {"forward_ms": 1273.94, "backward_ms": 2971.07, "peak_mem_mib": 12136.7},
+                                "hardware": "not stated in report.md"},
+    }), flush=True)
+
+
 # --------------------------------------------------------------------------- GPU arm
 def main():
     args = parse()
+    if args.mode == "train":
+        assert args.warmup >= 1
+        run_train_mode(args)
+        return
     wl = W.WORKLOADS[args.workload]
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))

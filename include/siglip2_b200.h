@@ -191,6 +191,18 @@ int siglip2_patch_embed(int dtype, const void* patches_dev, int patch_dim, const
 int siglip2_layernorm(int dtype, const void* x_dev, void* y_dev, const float* gamma_dev, const float* beta_dev,
                       int rows, int D, float eps, const int* cu_seqlens_dev, int max_patches, void* stream);
 
+/* Gradient of siglip2_layernorm (packed rows): dx [rows, D] (dtype), the
+ * row statistics stats_dev [rows] (mean, rstd) float pairs (scratch), and
+ * per-chunk partial sums dgamma_part / dbeta_part [ceil(rows / chunk_rows), D]
+ * fp32 (the caller sums them over chunks, in order):
+ *   dx = rstd (g - mean(g) - xh mean(g xh)), g = dy gamma, xh = (x - mean) rstd;
+ *   dgamma = sum_rows dy xh,  dbeta = sum_rows dy.
+ * Replaces the autograd backward of nn.LayerNorm (model.py:199,201,256) and
+ * of the reference's Triton LayerNorm (optimized_siglip2/ops/layer_norm.py:571-940). */
+int siglip2_layernorm_backward(int dtype, const void* x_dev, const void* dy_dev, const float* gamma_dev, int rows,
+                               int D, float eps, void* dx_dev, float* stats_dev, float* dgamma_part_dev,
+                               float* dbeta_part_dev, int chunk_rows, void* stream);
+
 /* Patch grid (grid_h, grid_w) of a height x width image under a budget of
  * max_patches patches of patch x patch pixels: the largest scale whose
  * patch-rounded size fits, found by the binary search of transformers'

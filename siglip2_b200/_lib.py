@@ -37,6 +37,8 @@ SIGNATURES = {
     "siglip2_patch_embed": (_c_int, [_c_int, _vp, _c_int, _vp, _vp, _vp, _c_int, _vp, _vp, _vp, _c_int, _c_int, _vp,
                                      _vp, _vp]),
     "siglip2_layernorm": (_c_int, [_c_int, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_float, _vp, _c_int, _vp]),
+    "siglip2_layernorm_backward": (_c_int, [_c_int, _vp, _vp, _vp, _c_int, _c_int, _c_float, _vp, _vp, _vp, _vp,
+                                            _c_int, _vp]),
     "siglip2_token_image": (_c_int, [_vp, _c_int, _c_int, _vp, _vp]),
     "siglip2_image_grid": (_c_int, [_c_int, _c_int, _c_int, _c_int, _vp, _vp]),
     "siglip2_l2_normalize": (_c_int, [_c_int, _vp, _c_int, _c_int, _c_int, _c_float, _vp, _c_int, _vp]),

@@ -328,3 +328,142 @@ __global__ void __launch_bounds__(256) rowsums_kernel(const T* __restrict__ x, i
 }
 
 }  // namespace sg
+
+namespace sg {
+
+// ---------------------------------------------------------------------------
+// LayerNorm backward (the gradient of layernorm_kernel / nn.LayerNorm,
+// model.py:199,201,256), two deterministic passes:
+//   rows:    one warp per row recomputes mean and rstd from x (two-pass, as
+//            the forward), then with g = dy * gamma and xh = (x - mean) rstd
+//              dx = rstd (g - mean(g) - xh mean(g xh))
+//            and writes dx and the row's (mean, rstd);
+//   columns: per chunk of rows, dgamma[c] = sum dy xh and dbeta[c] = sum dy,
+//            one partial row per chunk (summed over chunks in a fixed order
+//            by the caller), 64 columns per warp, warps of a CTA stepping
+//            through the chunk's rows and reduced in shared memory in order.
+// ---------------------------------------------------------------------------
+template <typename T, int MAXV>
+__global__ void __launch_bounds__(256) layernorm_bwd_rows_kernel(const T* __restrict__ x, const T* __restrict__ dy,
+                                                                 const float* __restrict__ gamma, int rows, int D,
+                                                                 float eps, T* __restrict__ dx,
+                                                                 float2* __restrict__ stats) {
+  constexpr int V = Vec16<T>::N;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int nvec = D / V;
+  const T* xr = x + static_cast<size_t>(row) * D;
+  const T* dr = dy + static_cast<size_t>(row) * D;
+  float f[MAXV][V];
+  float s = 0.f;
+#pragma unroll
+  for (int c = 0; c < MAXV; ++c) {
+    const int v = lane + c * 32;
+    if (v < nvec) {
+      load_vec(xr + v * V, f[c]);
+#pragma unroll
+      for (int k = 0; k < V; ++k) s += f[c][k];
+    }
+  }
+  const float mean = warp_sum(s) / static_cast<float>(D);
+  float q = 0.f;
+#pragma unroll
+  for (int c = 0; c < MAXV; ++c) {
+    const int v = lane + c * 32;
+    if (v < nvec) {
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        const float d = f[c][k] - mean;
+        q = fmaf(d, d, q);
+      }
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(q) / static_cast<float>(D) + eps);
+  // g = dy * gamma (kept in f: x is replaced by xh, g goes to a second array)
+  float gv[MAXV][V];
+  float sg = 0.f, sgx = 0.f;
+#pragma unroll
+  for (int c = 0; c < MAXV; ++c) {
+    const int v = lane + c * 32;
+    if (v < nvec) {
+      load_vec(dr + v * V, gv[c]);
+#pragma unroll
+      for (int k4 = 0; k4 < V / 4; ++k4) {
+        const float4 g4 = __ldg(reinterpret_cast<const float4*>(gamma + v * V) + k4);
+        gv[c][4 * k4] *= g4.x;
+        gv[c][4 * k4 + 1] *= g4.y;
+        gv[c][4 * k4 + 2] *= g4.z;
+        gv[c][4 * k4 + 3] *= g4.w;
+      }
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        f[c][k] = (f[c][k] - mean) * rstd;
+        sg += gv[c][k];
+        sgx = fmaf(gv[c][k], f[c][k], sgx);
+      }
+    }
+  }
+  const float inv_d = 1.f / static_cast<float>(D);
+  const float mg = warp_sum(sg) * inv_d, mgx = warp_sum(sgx) * inv_d;
+  T* o = dx + static_cast<size_t>(row) * D;
+#pragma unroll
+  for (int c = 0; c < MAXV; ++c) {
+    const int v = lane + c * 32;
+    if (v < nvec) {
+      float r[V];
+#pragma unroll
+      for (int k = 0; k < V; ++k) r[k] = rstd * (gv[c][k] - mg - f[c][k] * mgx);
+      store_vec(o + v * V, r);
+    }
+  }
+  if (lane == 0) stats[row] = make_float2(mean, rstd);
+}
+
+// grid (ceil(D / 64), chunks), 256 threads; chunk j covers rows [j * chunk_rows, ...)
+template <typename T>
+__global__ void __launch_bounds__(256) layernorm_bwd_cols_kernel(const T* __restrict__ x, const T* __restrict__ dy,
+                                                                 const float2* __restrict__ stats, int rows, int D,
+                                                                 int chunk_rows, float* __restrict__ dgamma_part,
+                                                                 float* __restrict__ dbeta_part) {
+  __shared__ float red[2][8][64];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.x * 64 + 2 * lane;  // this lane's two columns
+  const int r0 = blockIdx.y * chunk_rows;
+  const int r1 = min(rows, r0 + chunk_rows);
+  float g0 = 0.f, g1 = 0.f, b0 = 0.f, b1 = 0.f;
+  if (c < D) {
+    for (int r = r0 + warp; r < r1; r += 8) {
+      const float2 st = stats[r];
+      float xv[2], dv[2];
+      if constexpr (sizeof(T) == 4) {
+        const float2 a = *reinterpret_cast<const float2*>(x + static_cast<size_t>(r) * D + c);
+        const float2 d = *reinterpret_cast<const float2*>(dy + static_cast<size_t>(r) * D + c);
+        xv[0] = a.x; xv[1] = a.y; dv[0] = d.x; dv[1] = d.y;
+      } else {
+        const float2 a = Pack2<T>::unpack(*reinterpret_cast<const uint32_t*>(x + static_cast<size_t>(r) * D + c));
+        const float2 d = Pack2<T>::unpack(*reinterpret_cast<const uint32_t*>(dy + static_cast<size_t>(r) * D + c));
+        xv[0] = a.x; xv[1] = a.y; dv[0] = d.x; dv[1] = d.y;
+      }
+      g0 = fmaf(dv[0], (xv[0] - st.x) * st.y, g0);
+      g1 = fmaf(dv[1], (xv[1] - st.x) * st.y, g1);
+      b0 += dv[0];
+      b1 += dv[1];
+    }
+  }
+  red[0][warp][2 * lane] = g0;
+  red[0][warp][2 * lane + 1] = g1;
+  red[1][warp][2 * lane] = b0;
+  red[1][warp][2 * lane + 1] = b1;
+  __syncthreads();
+  if (threadIdx.x < 128) {
+    const int which = threadIdx.x >> 6, col = threadIdx.x & 63;
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += red[which][w][col];  // fixed order
+    const int cc = blockIdx.x * 64 + col;
+    if (cc < D) (which ? dbeta_part : dgamma_part)[static_cast<size_t>(blockIdx.y) * D + cc] = t;
+  }
+}
+
+}  // namespace sg

@@ -339,6 +339,46 @@ int sg_layernorm_impl(int dtype, const void* x, void* y, const float* g, const f
   }
 }
 
+template <typename T>
+int launch_layernorm_bwd(const void* x, const void* dy, const float* g, int rows, int D, float eps, void* dx,
+                         float2* stats, float* dg, float* db, int chunk_rows, cudaStream_t s) {
+  constexpr int V = Vec16<T>::N;
+  const int nvec = D / V;
+  const int grid = (rows + 7) / 8;
+  const T* xt = static_cast<const T*>(x);
+  const T* dyt = static_cast<const T*>(dy);
+  T* dxt = static_cast<T*>(dx);
+  if (nvec <= 32 * 2) layernorm_bwd_rows_kernel<T, 2><<<grid, 256, 0, s>>>(xt, dyt, g, rows, D, eps, dxt, stats);
+  else if (nvec <= 32 * 4) layernorm_bwd_rows_kernel<T, 4><<<grid, 256, 0, s>>>(xt, dyt, g, rows, D, eps, dxt, stats);
+  else if (nvec <= 32 * 8) layernorm_bwd_rows_kernel<T, 8><<<grid, 256, 0, s>>>(xt, dyt, g, rows, D, eps, dxt, stats);
+  else if (nvec <= 32 * 12) layernorm_bwd_rows_kernel<T, 12><<<grid, 256, 0, s>>>(xt, dyt, g, rows, D, eps, dxt, stats);
+  else return set_error(SIGLIP2_ERR_UNSUPPORTED, "LayerNorm width %d too large", D);
+  SG_LAUNCH_CHECK();
+  const dim3 cgrid((D + 63) / 64, (rows + chunk_rows - 1) / chunk_rows);
+  layernorm_bwd_cols_kernel<T><<<cgrid, 256, 0, s>>>(xt, dyt, stats, rows, D, chunk_rows, dg, db);
+  SG_LAUNCH_CHECK();
+  return SIGLIP2_OK;
+}
+
+int sg_layernorm_bwd_impl(int dtype, const void* x, const void* dy, const float* gamma, int rows, int D, float eps,
+                          void* dx, float* stats, float* dgamma_part, float* dbeta_part, int chunk_rows,
+                          cudaStream_t s) {
+  SG_CHECK_ARG(x && dy && gamma && dx && stats && dgamma_part && dbeta_part && rows >= 0 && D > 0 && chunk_rows > 0,
+               "bad LayerNorm backward arguments");
+  SG_CHECK_ARG(D % 8 == 0, "LayerNorm width %d must be a multiple of 8", D);
+  if (!aligned16(x) || !aligned16(dy) || !aligned16(dx) || !aligned16(gamma) ||
+      (reinterpret_cast<uintptr_t>(stats) & 7u))
+    return set_error(SIGLIP2_ERR_ALIGN, "LayerNorm backward: 16-byte aligned rows and gamma, 8-byte aligned stats");
+  if (rows == 0) return SIGLIP2_OK;
+  float2* st = reinterpret_cast<float2*>(stats);
+  switch (dtype) {
+    case SIGLIP2_BF16: return launch_layernorm_bwd<__nv_bfloat16>(x, dy, gamma, rows, D, eps, dx, st, dgamma_part, dbeta_part, chunk_rows, s);
+    case SIGLIP2_F16: return launch_layernorm_bwd<__half>(x, dy, gamma, rows, D, eps, dx, st, dgamma_part, dbeta_part, chunk_rows, s);
+    case SIGLIP2_F32: return launch_layernorm_bwd<float>(x, dy, gamma, rows, D, eps, dx, st, dgamma_part, dbeta_part, chunk_rows, s);
+    default: return set_error(SIGLIP2_ERR_ARG, "unknown dtype %d", dtype);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // position-embedding resize into packed token order
 // ---------------------------------------------------------------------------
@@ -984,6 +1024,13 @@ int siglip2_layernorm(int dtype, const void* x_dev, void* y_dev, const float* ga
                       int rows, int D, float eps, const int* cu_seqlens_dev, int max_patches, void* stream) {
   return sg_layernorm_impl(dtype, x_dev, y_dev, gamma_dev, beta_dev, rows, D, eps, cu_seqlens_dev, max_patches,
                            static_cast<cudaStream_t>(stream));
+}
+
+int siglip2_layernorm_backward(int dtype, const void* x_dev, const void* dy_dev, const float* gamma_dev, int rows,
+                               int D, float eps, void* dx_dev, float* stats_dev, float* dgamma_part_dev,
+                               float* dbeta_part_dev, int chunk_rows, void* stream) {
+  return sg_layernorm_bwd_impl(dtype, x_dev, dy_dev, gamma_dev, rows, D, eps, dx_dev, stats_dev, dgamma_part_dev,
+                               dbeta_part_dev, chunk_rows, static_cast<cudaStream_t>(stream));
 }
 
 int siglip2_image_grid(int height, int width, int patch, int max_patches, int* grid_h, int* grid_w) {

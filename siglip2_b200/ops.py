@@ -94,6 +94,24 @@ def layernorm(x: torch.Tensor, gamma, beta, eps: float, cu_seqlens=None, batch: 
     return y
 
 
+def layernorm_backward(x: torch.Tensor, dy: torch.Tensor, gamma: torch.Tensor, eps: float, chunk_rows: int = 1024):
+    """``siglip2_layernorm_backward``: ``(dx, dgamma, dbeta)`` of LayerNorm over
+    the last dimension (dgamma / dbeta fp32, summed over row chunks in order)."""
+    _need_cuda(x, dy, gamma)
+    D = x.shape[-1]
+    x2, dy2 = x.reshape(-1, D).contiguous(), dy.reshape(-1, D).contiguous().to(x.dtype)
+    rows = x2.shape[0]
+    chunks = max(1, -(-rows // chunk_rows))
+    dx = torch.empty_like(x2)
+    stats = torch.empty((rows, 2), dtype=torch.float32, device=x.device)
+    dg = torch.empty((chunks, D), dtype=torch.float32, device=x.device)
+    db = torch.empty((chunks, D), dtype=torch.float32, device=x.device)
+    L.call("siglip2_layernorm_backward", dtype_code(x.dtype), x2.data_ptr(), dy2.data_ptr(),
+           gamma.float().contiguous().data_ptr(), rows, D, float(eps), dx.data_ptr(), stats.data_ptr(),
+           dg.data_ptr(), db.data_ptr(), chunk_rows, _stream(x.device))
+    return dx.view(x.shape), dg.sum(0), db.sum(0)
+
+
 def token_image(cu_seqlens: torch.Tensor, n_tokens: int) -> torch.Tensor:
     out = torch.empty(n_tokens, dtype=torch.int32, device=cu_seqlens.device)
     L.call("siglip2_token_image", cu_seqlens.data_ptr(), cu_seqlens.numel() - 1, n_tokens, out.data_ptr(),

@@ -211,9 +211,10 @@ def _fmha_setup(ctx, inputs, output):
 def _fmha_backward(ctx, grad):
     """Stop-gap attention backward: the incoming gradient goes through the
     forward's dropout mask (regenerated from the seed by ``siglip2_dropout``),
-    then every sequence is recomputed with torch's
+    then the sequences are recomputed with torch's
     scaled_dot_product_attention and differentiated there (softmax(q k^T /
-    sqrt(hd)) v, the forward's definition), one sequence at a time."""
+    sqrt(hd)) v, the forward's definition), one batched call per distinct
+    sequence length."""
     (qkv,) = ctx.saved_tensors
     H, hd = ctx.heads, ctx.head_dim
     N = qkv.shape[0]
@@ -221,16 +222,23 @@ def _fmha_backward(ctx, grad):
     if ctx.dropout_p > 0:
         grad = ops.dropout(grad.contiguous(), ctx.dropout_p, ctx.seed)
     g = grad.reshape(N, H, hd)
-    parts = []
-    s = 0
-    for n in ctx.lengths:
+    # sequences of equal length go through one batched call (a batch of full
+    # 16x16 grids is one call per layer)
+    starts = np.concatenate([[0], np.cumsum(ctx.lengths)[:-1]]).astype(np.int64)
+    by_len: dict = {}
+    for i, n in enumerate(ctx.lengths):
+        by_len.setdefault(int(n), []).append(i)
+    dqkv = torch.empty((N, 3, H, hd), dtype=qkv.dtype, device=qkv.device)
+    for n, seqs in by_len.items():
+        rows = (torch.from_numpy(starts[seqs])[:, None] + torch.arange(n)[None, :]).reshape(-1).to(qkv.device)
+        xs = x.index_select(0, rows).view(len(seqs), n, 3, H, hd)
         with torch.enable_grad():
-            q, k, v = (x[s:s + n, i].transpose(0, 1)[None].requires_grad_(True) for i in range(3))
+            q, k, v = (xs[:, :, i].transpose(1, 2).requires_grad_(True) for i in range(3))  # [G, H, n, hd]
             o = torch.nn.functional.scaled_dot_product_attention(q, k, v, scale=hd ** -0.5)
-            dq, dk, dv = torch.autograd.grad(o, (q, k, v), g[s:s + n].transpose(0, 1)[None])
-        parts.append(torch.stack([t[0].transpose(0, 1) for t in (dq, dk, dv)], 1))
-        s += n
-    return torch.cat(parts, 0).reshape(N, 3 * H * hd), None, None, None, None, None, None, None
+            gs = g.index_select(0, rows).view(len(seqs), n, H, hd).transpose(1, 2)
+            dq, dk, dv = torch.autograd.grad(o, (q, k, v), gs)
+        dqkv.index_copy_(0, rows, torch.stack([t.transpose(1, 2) for t in (dq, dk, dv)], 2).reshape(-1, 3, H, hd))
+    return dqkv.reshape(N, 3 * H * hd), None, None, None, None, None, None, None
 
 
 fmha_varlen.register_autograd(_fmha_backward, setup_context=_fmha_setup)
@@ -254,10 +262,28 @@ def _layernorm_setup(ctx, inputs, output):
     ctx.save_for_backward(x, weight)
 
 
+@torch.library.custom_op("siglip2_b200::layernorm_backward", mutates_args=(), device_types="cuda")
+def layernorm_backward(x: Tensor, dy: Tensor, weight: Tensor, eps: float) -> tuple[Tensor, Tensor, Tensor]:
+    """``siglip2_layernorm_backward``: ``(dx, dweight, dbias)``."""
+    return ops.layernorm_backward(x, dy, weight, eps)
+
+
+@layernorm_backward.register_fake
+def _(x, dy, weight, eps):
+    D = x.shape[-1]
+    return (torch.empty_like(x, memory_format=torch.contiguous_format), weight.new_empty((D,), dtype=torch.float32),
+            weight.new_empty((D,), dtype=torch.float32))
+
+
 def _layernorm_backward(ctx, grad):
-    """Stop-gap LayerNorm backward in fp32 torch arithmetic (statistics
-    recomputed from x): dx = rstd (g - mean(g) - xh mean(g xh)), g = dy * w."""
+    """LayerNorm backward on the library's kernels (statistics recomputed
+    from x): dx = rstd (g - mean(g) - xh mean(g xh)), g = dy * w; dw = sum
+    dy xh, db = sum dy."""
     x, weight = ctx.saved_tensors
+    if x.shape[-1] % 8 == 0:
+        dx, dw, db = layernorm_backward(x, grad, weight, ctx.eps)
+        return (dx if ctx.needs_input_grad[0] else None, dw.to(weight.dtype) if ctx.needs_input_grad[1] else None,
+                db.to(weight.dtype) if ctx.needs_input_grad[2] else None, None)
     xf = x.float()
     mu = xf.mean(-1, keepdim=True)
     rstd = torch.rsqrt(((xf - mu) ** 2).mean(-1, keepdim=True) + ctx.eps)

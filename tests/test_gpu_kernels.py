@@ -186,3 +186,25 @@ def test_patch_embed_fused_position_resize(dtype, D):
     assert torch.allclose(mean, o.mean(1), rtol=1e-4, atol=1e-5)
     assert torch.allclose(var, o.var(1, unbiased=False), rtol=1e-3, atol=1e-6)
     assert torch.allclose(rs, ops.rowsums_reference(out), rtol=1e-3, atol=1e-5)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("rows,D", [(3000, 1152), (257, 768), (1, 1536), (2049, 1024)])
+def test_layernorm_backward_matches_autograd(dtype, rows, D):
+    """siglip2_layernorm_backward against torch autograd of F.layer_norm in
+    fp32 on the same (rounded) inputs: dx, dgamma, dbeta."""
+    g = torch.Generator(device="cuda").manual_seed(rows + D)
+    x = (torch.randn(rows, D, device="cuda", generator=g) * 2 + 0.5).to(dtype)
+    dy = torch.randn(rows, D, device="cuda", generator=g).to(dtype)
+    gamma = 1 + 0.1 * torch.randn(D, device="cuda", generator=g)
+    beta = 0.1 * torch.randn(D, device="cuda", generator=g)
+    dx, dg, db = ops.layernorm_backward(x, dy, gamma, 1e-6, chunk_rows=512)
+    xr = x.float().requires_grad_(True)
+    gr, br = gamma.clone().requires_grad_(True), beta.clone().requires_grad_(True)
+    F.layer_norm(xr, (D,), gr, br, 1e-6).backward(dy.float())
+    torch.cuda.synchronize()
+    tol = 1e-4 if dtype == torch.float32 else 2e-2
+    scale = xr.grad.abs().max().item()
+    assert (dx.float() - xr.grad).abs().max().item() <= tol * scale
+    assert torch.allclose(dg, gr.grad, rtol=1e-3, atol=1e-3 * max(1.0, rows ** 0.5))
+    assert torch.allclose(db, br.grad, rtol=1e-3, atol=1e-3 * max(1.0, rows ** 0.5))
