@@ -101,6 +101,24 @@ def bench_fmha(preset, images, max_patches, reps, dtype=torch.bfloat16, warmup=3
             **_clock()}
 
 
+def bench_backward_gemms(m, n, k, reps, warmup=3):
+    """dgrad dA = dY W and wgrad dW = dY^T A of y = A W^T (A [m, k], W [n, k])
+    on the transposed-operand tensor-core GEMM (siglip2_gemm_t), and the
+    GELU-gradient recompute GEMM; algorithmic 2 m n k FLOPs each."""
+    g = torch.Generator(device="cuda").manual_seed(0)
+    a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(n, k, device="cuda", generator=g) * 0.03).bfloat16()
+    dy = torch.randn(m, n, device="cuda", generator=g).bfloat16()
+    bias = torch.zeros(n, device="cuda")
+    out = []
+    for name, fn in (("dgrad", lambda: ops.gemm_t(dy, w, False, True)),
+                     ("wgrad", lambda: ops.gemm_t(dy, a, True, True)),
+                     ("gelu_grad_recompute", lambda: ops.gemm(a, w, L.EPI_BIAS_GELU_GRAD, bias=bias, res=dy))):
+        ms = _time(fn, reps, warmup)
+        out.append({"kernel": name, "m": m, "n": n, "k": k, "ms": ms, "tflops": 2 * m * n * k / ms / 1e9, **_clock()})
+    return out
+
+
 def bench_layer(preset, images, max_patches, reps):
     D, I, _, H = W.PRESETS[preset]
     N = int((lambda s: (s[:, 0] * s[:, 1]).sum())(_shapes(preset, images, max_patches)))
@@ -179,6 +197,12 @@ def main():
         sp.add_argument("--variant", type=int, default=0, help="GEMM kernel: 0 auto, 1 one SM, 2 SM pairs")
     f.add_argument("--fmha-variant", type=int, default=0,
                    help="attention kernel: 0 auto, 1 one query tile per CTA, 2 query-tile pairs")
+    bw = sub.add_parser("bwd")
+    bw.add_argument("--m", type=int, default=39178)
+    bw.add_argument("--n", type=int, default=4304)
+    bw.add_argument("--k", type=int, default=1152)
+    bw.add_argument("--reps", type=int, default=20)
+    bw.add_argument("--variant", type=int, default=0)
     pz = sub.add_parser("patchify")
     pz.add_argument("--images", type=int, default=64)
     pz.add_argument("--height", type=int, default=512)
@@ -198,6 +222,9 @@ def main():
     elif a.cmd == "patchify":
         print(json.dumps(bench_patchify(a.images, a.height, a.width, a.max_patches, a.reps, a.warmup,
                                         channels_last=not a.channels_first)))
+    elif a.cmd == "bwd":
+        for r in bench_backward_gemms(a.m, a.n, a.k, a.reps):
+            print(json.dumps(r))
     elif a.cmd == "fmha":
         L.check(L.load().siglip2_set_fmha_variant(a.fmha_variant))
         r = bench_fmha(a.preset, a.images, a.max_patches, a.reps, warmup=a.warmup)
