@@ -278,6 +278,34 @@ int siglip2_fmha_varlen_dropout(int dtype, const void* qkv_dev, int N, const int
                                 int n_tiles, int heads, int head_dim, void* out_dev, int ldo, float p,
                                 unsigned long long seed, unsigned long long offset, void* stream);
 
+/* The training forward: siglip2_fmha_varlen_dropout (p = 0: no dropout) that
+ * also writes lse_dev [N, heads] float32, the base-2 log-sum-exp of each
+ * query row's scaled logits (softmax_k = exp2(q.k * scale * log2(e) - lse)),
+ * which the backward needs.  bf16 / f16. */
+int siglip2_fmha_varlen_train(int dtype, const void* qkv_dev, int N, const int* cu_seqlens_dev, const int* tiles_dev,
+                              int n_tiles, int heads, int head_dim, void* out_dev, int ldo, float* lse_dev, float p,
+                              unsigned long long seed, unsigned long long offset, void* stream);
+
+/* dsum_dev[r * heads + h] = sum_d g[r, h*head_dim + d] * o[r, h*head_dim + d]
+ * (fp32): the row term D of the attention backward, from the incoming
+ * gradient g and the stored (possibly dropped-out) output o, both [N, ld]. */
+int siglip2_fmha_bwd_dsum(int dtype, const void* g_dev, const void* o_dev, int ld, int N, int heads, int head_dim,
+                          float* dsum_dev, void* stream);
+
+/* Attention backward on the tensor cores: dqkv_dev [N, 3*heads*head_dim]
+ * (dq | dk | dv, the layout of qkv_dev) from qkv_dev, dout_dev [N, ld_dout]
+ * (the gradient of the attention output, after the dropout mask), the
+ * forward's lse_dev and siglip2_fmha_bwd_dsum's dsum_dev [N, heads]:
+ *   dV = P^T dO, dK = scale dS^T Q, dQ = scale dS K, dS = P (dO V^T - D).
+ * Two passes of one kernel over the same (image, 128-row tile) list as the
+ * forward (tiles_dev): key tiles accumulate dK and dV, query tiles dQ, in
+ * TMEM; no atomics, deterministic.  bf16 / f16, head_dim 64, 72 or 96.
+ * Replaces the autograd backward of flex_attention (model.py:156-163). */
+int siglip2_fmha_varlen_backward(int dtype, const void* qkv_dev, const void* dout_dev, int ld_dout, int N,
+                                 const int* cu_seqlens_dev, const int* tiles_dev, int n_tiles, int heads,
+                                 int head_dim, const float* lse_dev, const float* dsum_dev, void* dqkv_dev,
+                                 void* stream);
+
 /* y[r, c] = x[r, c] * keep(r * width + c) / (1 - p) for r < rows, c < width,
  * with the mask of siglip2_fmha_varlen_dropout (x and y may be the same
  * buffer).  width a multiple of 8; rows 16-byte aligned with pitches

@@ -50,6 +50,11 @@ SIGNATURES = {
                                              _c_float, ctypes.c_ulonglong, ctypes.c_ulonglong, _vp]),
     "siglip2_dropout": (_c_int, [_c_int, _vp, _c_int, _c_int, _c_int, _c_float, ctypes.c_ulonglong,
                                  ctypes.c_ulonglong, _vp, _c_int, _vp]),
+    "siglip2_fmha_varlen_train": (_c_int, [_c_int, _vp, _c_int, _vp, _vp, _c_int, _c_int, _c_int, _vp, _c_int, _vp,
+                                           _c_float, ctypes.c_ulonglong, ctypes.c_ulonglong, _vp]),
+    "siglip2_fmha_bwd_dsum": (_c_int, [_c_int, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp]),
+    "siglip2_fmha_varlen_backward": (_c_int, [_c_int, _vp, _vp, _c_int, _c_int, _vp, _vp, _c_int, _c_int, _c_int,
+                                              _vp, _vp, _vp, _vp]),
     "siglip2_padded_head_dim": (_c_int, [_c_int]),
     "siglip2_head_pool": (_c_int, [_c_int, _vp, _c_int, _c_int, _vp, _c_int, _c_int, _vp, _vp, _vp, _vp]),
     "siglip2_head_pool_noalloc": (_c_int, [_c_int, _vp, _c_int, _c_int, _vp, _c_int, _c_int, _c_int, _vp, _vp,

@@ -50,6 +50,7 @@ struct FmhaParams {
   int ld_out;
   float scale_log2;   // head_dim^-0.5 * log2(e)
   DropoutParams drop; // attention-output dropout (p = 0: off)
+  float* lse;         // optional [N, heads]: base-2 log-sum-exp of each row's scaled logits (for the backward)
 };
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -405,6 +406,8 @@ __global__ void __launch_bounds__(192, 2)
       const int row = img_row0 + tile.y * 128 + r;
       const bool row_ok = (tile.y * 128 + r) < L;
       const float inv_l = 1.f / l;
+      // softmax_k = exp2(s_k * scale_log2 - lse2) with lse2 = m + log2(l)
+      if (p.lse != nullptr && row_ok) p.lse[static_cast<size_t>(row) * H + head] = m_use + log2f(l);
       T* orow = reinterpret_cast<T*>(p.out) + static_cast<size_t>(row) * p.ld_out + head * p.head_dim;
 #pragma unroll
       for (int c = 0; c < HDP / 16; ++c) {

@@ -471,6 +471,7 @@ __global__ void __launch_bounds__(384, 1)
       const int row = img_row0 + trow;
       const bool row_ok = trow < L;
       const float inv_l = 1.f / l;
+      if (p.lse != nullptr && row_ok) p.lse[static_cast<size_t>(row) * H + head] = m_use + log2f(l);
       T* orow = reinterpret_cast<T*>(p.out) + static_cast<size_t>(row) * p.ld_out + head * p.head_dim;
 #pragma unroll
       for (int c = 0; c < HDP / 16; ++c) {

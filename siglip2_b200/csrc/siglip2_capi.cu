@@ -12,6 +12,7 @@
 #include "rowops.cuh"
 #include "fmha.cuh"
 #include "fmha_pair.cuh"
+#include "fmha_bwd.cuh"
 #include "forward.cuh"
 #include "simt_f32.cuh"
 #include "patchify.cuh"
@@ -569,7 +570,7 @@ int sg_token_image_impl(const int* cu, int B, int N, int* tok_img, cudaStream_t 
 // ---------------------------------------------------------------------------
 template <typename T, int HDP>
 int launch_fmha(const void* qkv, int N, const int* cu, const int2* tiles, int n_tiles, int H, int hd, void* out, int ldo,
-                const DropoutParams& drop, cudaStream_t s) {
+                const DropoutParams& drop, float* lse, cudaStream_t s) {
   using C = FmhaCfg<HDP>;
   CUtensorMap tq, tqr, tk, tkr;
   // 3-D view [N][3H][hd] of the packed q | k | v columns: the remainder box
@@ -595,6 +596,7 @@ int launch_fmha(const void* qkv, int N, const int* cu, const int2* tiles, int n_
   p.ld_out = ldo;
   p.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(hd));
   p.drop = drop;
+  p.lse = lse;
   const bool pair = g_fmha_variant.load() == 2;
   auto kern = pair ? fmha_pair_kernel<T, HDP> : fmha_varlen_kernel<T, HDP>;
   const int smem = pair ? FmhaPairCfg<HDP>::kSmem : FmhaCfg<HDP>::kSmem;
@@ -618,14 +620,54 @@ int launch_fmha(const void* qkv, int N, const int* cu, const int2* tiles, int n_
 
 template <typename T>
 int dispatch_fmha(const void* qkv, int N, const int* cu, const int2* tiles, int n_tiles, int H, int hd, void* out,
-                  int ldo, const DropoutParams& d, cudaStream_t s) {
+                  int ldo, const DropoutParams& d, float* lse, cudaStream_t s) {
   switch (hd) {
-    case 64: return launch_fmha<T, 64>(qkv, N, cu, tiles, n_tiles, H, hd, out, ldo, d, s);
-    case 72: return launch_fmha<T, 80>(qkv, N, cu, tiles, n_tiles, H, hd, out, ldo, d, s);
-    case 80: return launch_fmha<T, 80>(qkv, N, cu, tiles, n_tiles, H, hd, out, ldo, d, s);
-    case 96: return launch_fmha<T, 96>(qkv, N, cu, tiles, n_tiles, H, hd, out, ldo, d, s);
+    case 64: return launch_fmha<T, 64>(qkv, N, cu, tiles, n_tiles, H, hd, out, ldo, d, lse, s);
+    case 72: return launch_fmha<T, 80>(qkv, N, cu, tiles, n_tiles, H, hd, out, ldo, d, lse, s);
+    case 80: return launch_fmha<T, 80>(qkv, N, cu, tiles, n_tiles, H, hd, out, ldo, d, lse, s);
+    case 96: return launch_fmha<T, 96>(qkv, N, cu, tiles, n_tiles, H, hd, out, ldo, d, lse, s);
     default: return set_error(SIGLIP2_ERR_UNSUPPORTED, "head_dim %d not supported (64, 72, 80, 96)", hd);
   }
+}
+
+// attention backward: the dK/dV pass (key tiles) and the dQ pass (query tiles)
+template <typename T, int HDP>
+int launch_fmha_bwd(const void* qkv, const void* dout, int ld_dout, int N, const int* cu, const int2* tiles,
+                    int n_tiles, int H, int hd, const float* lse, const float* dsum, void* dqkv, cudaStream_t s) {
+  CUtensorMap tq, tqr, td, tdr;
+  const int64_t row_bytes = 3ll * H * hd * 2;
+  SG_TRY(make_tmap_3d(&tq, qkv, 2, hd, 3 * H, N, hd * 2, row_bytes, 64, 1, 128));
+  SG_TRY(make_tmap_3d(&td, dout, 2, hd, H, N, hd * 2, static_cast<int64_t>(ld_dout) * 2, 64, 1, 128));
+  if (HDP > 64) {
+    SG_TRY(make_tmap_3d(&tqr, qkv, 2, hd, 3 * H, N, hd * 2, row_bytes, HDP - 64, 1, 128));
+    SG_TRY(make_tmap_3d(&tdr, dout, 2, hd, H, N, hd * 2, static_cast<int64_t>(ld_dout) * 2, HDP - 64, 1, 128));
+  } else {
+    tqr = tq;
+    tdr = td;
+  }
+  FmhaBwdParams p{};
+  p.cu = cu;
+  p.tiles = tiles;
+  p.n_items = n_tiles * H;
+  p.heads = H;
+  p.head_dim = hd;
+  p.scale = 1.f / sqrtf(static_cast<float>(hd));
+  p.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(hd));
+  p.lse = lse;
+  p.dsum = dsum;
+  p.dqkv = dqkv;
+  p.ld_dqkv = 3 * H * hd;
+  constexpr int smem = FmhaBwdCfg<HDP>::kSmem;
+  const int grid = std::min(p.n_items, sm_count());
+  auto kkv = fmha_bwd_kernel<T, HDP, false>;
+  auto kq = fmha_bwd_kernel<T, HDP, true>;
+  SG_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(kkv), smem));
+  SG_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(kq), smem));
+  kkv<<<grid, 192, smem, s>>>(tq, tqr, td, tdr, p);
+  SG_LAUNCH_CHECK();
+  kq<<<grid, 192, smem, s>>>(tq, tqr, td, tdr, p);
+  SG_LAUNCH_CHECK();
+  return SIGLIP2_OK;
 }
 
 // Dropout parameters from the entry-point arguments (p in [0, 1)).
@@ -662,9 +704,11 @@ int sg_dropout_impl(int dtype, const void* x, int ldx, int rows, int width, cons
 }
 
 int sg_fmha_impl(int dtype, const void* qkv, int N, const int* cu, const int* tiles, int n_tiles, int H, int hd,
-                 void* out, int ldo, cudaStream_t s, const DropoutParams* drop = nullptr) {
+                 void* out, int ldo, cudaStream_t s, const DropoutParams* drop = nullptr, float* lse = nullptr) {
   DropoutParams d{};
   if (drop) d = *drop;
+  if (lse && dtype == SIGLIP2_F32)
+    return set_error(SIGLIP2_ERR_UNSUPPORTED, "attention: the log-sum-exp output is tensor-core (bf16/f16) only");
   SG_CHECK_ARG(qkv && cu && tiles && out && N >= 0 && n_tiles >= 0 && H > 0 && hd > 0, "bad attention arguments");
   SG_CHECK_ARG(hd % 8 == 0 && ldo % 8 == 0 && ldo >= H * hd, "head_dim and ldo must be multiples of 8");
   if (N == 0 || n_tiles == 0) return SIGLIP2_OK;
@@ -674,8 +718,8 @@ int sg_fmha_impl(int dtype, const void* qkv, int N, const int* cu, const int* ti
   if (reinterpret_cast<uintptr_t>(tiles) & 7u)
     return set_error(SIGLIP2_ERR_ALIGN, "attention tile list must be 8-byte aligned (read as int32 pairs)");
   const int2* t2 = reinterpret_cast<const int2*>(tiles);
-  if (dtype == SIGLIP2_BF16) return dispatch_fmha<__nv_bfloat16>(qkv, N, cu, t2, n_tiles, H, hd, out, ldo, d, s);
-  if (dtype == SIGLIP2_F16) return dispatch_fmha<__half>(qkv, N, cu, t2, n_tiles, H, hd, out, ldo, d, s);
+  if (dtype == SIGLIP2_BF16) return dispatch_fmha<__nv_bfloat16>(qkv, N, cu, t2, n_tiles, H, hd, out, ldo, d, lse, s);
+  if (dtype == SIGLIP2_F16) return dispatch_fmha<__half>(qkv, N, cu, t2, n_tiles, H, hd, out, ldo, d, lse, s);
   if (dtype == SIGLIP2_F32) {
     // fp32: q | k | v with head_dim columns per head (no padding)
     dim3 grid(n_tiles, H);
@@ -1075,6 +1119,67 @@ int siglip2_fmha_varlen_dropout(int dtype, const void* qkv_dev, int N, const int
   SG_TRY(make_dropout(p, seed, offset, &d));
   return sg_fmha_impl(dtype, qkv_dev, N, cu_seqlens_dev, tiles_dev, n_tiles, heads, head_dim, out_dev, ldo,
                       static_cast<cudaStream_t>(stream), &d);
+}
+
+int siglip2_fmha_varlen_train(int dtype, const void* qkv_dev, int N, const int* cu_seqlens_dev, const int* tiles_dev,
+                              int n_tiles, int heads, int head_dim, void* out_dev, int ldo, float* lse_dev, float p,
+                              unsigned long long seed, unsigned long long offset, void* stream) {
+  SG_CHECK_ARG(lse_dev != nullptr, "the training forward needs the log-sum-exp output");
+  if (reinterpret_cast<uintptr_t>(lse_dev) & 3u) return set_error(SIGLIP2_ERR_ALIGN, "lse must be 4-byte aligned");
+  DropoutParams d{};
+  SG_TRY(make_dropout(p, seed, offset, &d));
+  return sg_fmha_impl(dtype, qkv_dev, N, cu_seqlens_dev, tiles_dev, n_tiles, heads, head_dim, out_dev, ldo,
+                      static_cast<cudaStream_t>(stream), &d, lse_dev);
+}
+
+int siglip2_fmha_bwd_dsum(int dtype, const void* g_dev, const void* o_dev, int ld, int N, int heads, int head_dim,
+                          float* dsum_dev, void* stream) {
+  SG_CHECK_ARG(g_dev && o_dev && dsum_dev && N >= 0 && heads > 0 && head_dim > 0 && ld >= heads * head_dim,
+               "bad attention-backward row-dot arguments");
+  const int v = dtype == SIGLIP2_F32 ? 4 : 8;
+  if (head_dim % 8 || ld % v || !aligned16(g_dev) || !aligned16(o_dev))
+    return set_error(SIGLIP2_ERR_ALIGN, "row-dot: head_dim a multiple of 8, 16-byte aligned rows");
+  const long long n = static_cast<long long>(N) * heads;
+  if (n == 0) return SIGLIP2_OK;
+  const unsigned blocks = static_cast<unsigned>((n + 255) / 256);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case SIGLIP2_BF16: fmha_bwd_dsum_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(g_dev), static_cast<const __nv_bfloat16*>(o_dev), ld, N, heads, head_dim, dsum_dev); break;
+    case SIGLIP2_F16: fmha_bwd_dsum_kernel<__half><<<blocks, 256, 0, s>>>(static_cast<const __half*>(g_dev), static_cast<const __half*>(o_dev), ld, N, heads, head_dim, dsum_dev); break;
+    case SIGLIP2_F32: fmha_bwd_dsum_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(g_dev), static_cast<const float*>(o_dev), ld, N, heads, head_dim, dsum_dev); break;
+    default: return set_error(SIGLIP2_ERR_ARG, "unknown dtype %d", dtype);
+  }
+  SG_LAUNCH_CHECK();
+  return SIGLIP2_OK;
+}
+
+int siglip2_fmha_varlen_backward(int dtype, const void* qkv_dev, const void* dout_dev, int ld_dout, int N,
+                                 const int* cu_seqlens_dev, const int* tiles_dev, int n_tiles, int heads,
+                                 int head_dim, const float* lse_dev, const float* dsum_dev, void* dqkv_dev,
+                                 void* stream) {
+  SG_CHECK_ARG(qkv_dev && dout_dev && cu_seqlens_dev && tiles_dev && lse_dev && dsum_dev && dqkv_dev && N >= 0 &&
+                   n_tiles >= 0 && heads > 0,
+               "bad attention backward arguments");
+  if (dtype != SIGLIP2_BF16 && dtype != SIGLIP2_F16)
+    return set_error(SIGLIP2_ERR_UNSUPPORTED, "attention backward: bf16 / f16 only");
+  if (ld_dout % 8 || ld_dout < heads * head_dim || !aligned16(dout_dev) || !aligned16(dqkv_dev) ||
+      (reinterpret_cast<uintptr_t>(tiles_dev) & 7u))
+    return set_error(SIGLIP2_ERR_ALIGN, "attention backward: 16-byte aligned rows and pitches, 8-byte aligned tiles");
+  if (N == 0 || n_tiles == 0) return SIGLIP2_OK;
+  if (heads > 65535 || static_cast<long long>(n_tiles) * heads > (1ll << 30))
+    return set_error(SIGLIP2_ERR_UNSUPPORTED, "too many heads or attention tiles");
+  const int2* t2 = reinterpret_cast<const int2*>(tiles_dev);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool bf = dtype == SIGLIP2_BF16;
+  switch (head_dim) {
+    case 64: return bf ? launch_fmha_bwd<__nv_bfloat16, 64>(qkv_dev, dout_dev, ld_dout, N, cu_seqlens_dev, t2, n_tiles, heads, head_dim, lse_dev, dsum_dev, dqkv_dev, s)
+                       : launch_fmha_bwd<__half, 64>(qkv_dev, dout_dev, ld_dout, N, cu_seqlens_dev, t2, n_tiles, heads, head_dim, lse_dev, dsum_dev, dqkv_dev, s);
+    case 72: return bf ? launch_fmha_bwd<__nv_bfloat16, 80>(qkv_dev, dout_dev, ld_dout, N, cu_seqlens_dev, t2, n_tiles, heads, head_dim, lse_dev, dsum_dev, dqkv_dev, s)
+                       : launch_fmha_bwd<__half, 80>(qkv_dev, dout_dev, ld_dout, N, cu_seqlens_dev, t2, n_tiles, heads, head_dim, lse_dev, dsum_dev, dqkv_dev, s);
+    case 96: return bf ? launch_fmha_bwd<__nv_bfloat16, 96>(qkv_dev, dout_dev, ld_dout, N, cu_seqlens_dev, t2, n_tiles, heads, head_dim, lse_dev, dsum_dev, dqkv_dev, s)
+                       : launch_fmha_bwd<__half, 96>(qkv_dev, dout_dev, ld_dout, N, cu_seqlens_dev, t2, n_tiles, heads, head_dim, lse_dev, dsum_dev, dqkv_dev, s);
+    default: return set_error(SIGLIP2_ERR_UNSUPPORTED, "attention backward: head_dim %d not supported (64, 72, 96)", head_dim);
+  }
 }
 
 int siglip2_dropout(int dtype, const void* x_dev, int ldx, int rows, int width, float p, unsigned long long seed,

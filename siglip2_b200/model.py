@@ -38,7 +38,7 @@ import torch.nn.functional as F
 
 from . import _lib as L
 from . import ops
-from . import torch_ops  # noqa: F401  (registers torch.ops.siglip2_b200)
+from . import torch_ops  # registers torch.ops.siglip2_b200
 from .ops import dtype_code, fold_layernorm
 
 _OPS = torch.ops.siglip2_b200
@@ -345,8 +345,8 @@ def _attention(m: nn.Module, x: torch.Tensor, seqs: Sequences) -> torch.Tensor:
     if x2.shape[0] != seqs.n_tokens:
         raise ValueError(f"{x2.shape[0]} rows but the sequences cover {seqs.n_tokens}")
     qkv = _OPS.gemm(x2, qkv_w, L.EPI_BIAS, qkv_b.float(), None, None, None, 0.0)
-    a = _OPS.fmha_varlen(qkv, seqs.cu_seqlens, seqs.tiles, m.num_heads, m.head_dim, seqs.lengths,
-                         *_dropout_args(m, m.dropout))
+    attn = torch_ops.attention_for_training if _needs_grad(m, x) else _OPS.fmha_varlen
+    a = attn(qkv, seqs.cu_seqlens, seqs.tiles, m.num_heads, m.head_dim, seqs.lengths, *_dropout_args(m, m.dropout))
     return _OPS.gemm(a, out_w, L.EPI_BIAS, out_b.float(), None, None, None, 0.0).view(*x.shape[:-1], -1)
 
 
@@ -503,8 +503,8 @@ def _encoder_layer_unfused(layer: nn.Module, x: torch.Tensor, seqs: Sequences) -
     h = _OPS.layernorm(x2, ln1.weight.float(), ln1.bias.float(), float(ln1.eps))
     wq, bq = at.qkv_params()
     qkv = _OPS.gemm(h, wq, L.EPI_BIAS, bq.float(), None, None, None, 0.0)
-    a = _OPS.fmha_varlen(qkv, seqs.cu_seqlens, seqs.tiles, at.num_heads, at.head_dim, seqs.lengths,
-                         *_dropout_args(at, at.dropout))
+    a = torch_ops.attention_for_training(qkv, seqs.cu_seqlens, seqs.tiles, at.num_heads, at.head_dim, seqs.lengths,
+                                         *_dropout_args(at, at.dropout))
     r = _OPS.gemm(a, at.out_proj.weight, L.EPI_BIAS_RES, at.out_proj.bias.float(), x2, None, None, 0.0)
     h = _OPS.layernorm(r, ln2.weight.float(), ln2.bias.float(), float(ln2.eps))
     m = _OPS.gemm(h, mlp.fc1.weight, L.EPI_BIAS_GELU, mlp.fc1.bias.float(), None, None, None, 0.0)

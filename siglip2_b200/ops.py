@@ -161,6 +161,41 @@ def fmha_varlen(qkv: torch.Tensor, cu_seqlens: torch.Tensor, tiles: torch.Tensor
     return out
 
 
+def fmha_varlen_train(qkv: torch.Tensor, cu_seqlens: torch.Tensor, tiles: torch.Tensor, heads: int, head_dim: int,
+                      dropout_p: float = 0.0, seed: int = 0, offset: int = 0):
+    """``siglip2_fmha_varlen_train``: ``(out [N, heads*head_dim], lse [N, heads])``,
+    the attention output (train-mode dropout when ``dropout_p > 0``) and the
+    base-2 log-sum-exp of each row the backward recomputes P from."""
+    _need_cuda(qkv, cu_seqlens, tiles)
+    N = qkv.shape[0]
+    out = torch.empty((N, heads * head_dim), dtype=qkv.dtype, device=qkv.device)
+    lse = torch.empty((N, heads), dtype=torch.float32, device=qkv.device)
+    L.call("siglip2_fmha_varlen_train", dtype_code(qkv.dtype), qkv.data_ptr(), N, cu_seqlens.data_ptr(),
+           tiles.data_ptr(), tiles.shape[0], heads, head_dim, out.data_ptr(), out.stride(0), lse.data_ptr(),
+           float(dropout_p), int(seed) & (2 ** 64 - 1), int(offset) & (2 ** 64 - 1), _stream(qkv.device))
+    return out, lse
+
+
+def fmha_varlen_backward(qkv: torch.Tensor, out: torch.Tensor, grad: torch.Tensor, lse: torch.Tensor,
+                         cu_seqlens: torch.Tensor, tiles: torch.Tensor, heads: int, head_dim: int,
+                         dropout_p: float = 0.0, seed: int = 0, offset: int = 0) -> torch.Tensor:
+    """Gradient of ``fmha_varlen_train`` w.r.t. ``qkv``: the row term
+    D = rowsum(grad . out) (``siglip2_fmha_bwd_dsum``), the incoming gradient
+    through the forward's dropout mask, then ``siglip2_fmha_varlen_backward``."""
+    _need_cuda(qkv, out, grad, lse)
+    N = qkv.shape[0]
+    grad = grad.contiguous()
+    dsum = torch.empty((N, heads), dtype=torch.float32, device=qkv.device)
+    L.call("siglip2_fmha_bwd_dsum", dtype_code(grad.dtype), grad.data_ptr(), out.data_ptr(), grad.stride(0), N,
+           heads, head_dim, dsum.data_ptr(), _stream(qkv.device))
+    g = dropout(grad, dropout_p, seed, offset) if dropout_p > 0 else grad
+    dqkv = torch.empty_like(qkv)
+    L.call("siglip2_fmha_varlen_backward", dtype_code(qkv.dtype), qkv.data_ptr(), g.data_ptr(), g.stride(0), N,
+           cu_seqlens.data_ptr(), tiles.data_ptr(), tiles.shape[0], heads, head_dim, lse.data_ptr(),
+           dsum.data_ptr(), dqkv.data_ptr(), _stream(qkv.device))
+    return dqkv
+
+
 def dropout(x: torch.Tensor, p: float, seed: int, offset: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
     """``siglip2_dropout``: ``x * keep / (1 - p)`` with the counter-based mask of
     the attention kernel's train mode (same ``seed``/``offset``, element index

@@ -220,7 +220,7 @@ def _fmha_backward(ctx, grad):
     N = qkv.shape[0]
     x = qkv.detach().view(N, 3, H, hd)
     if ctx.dropout_p > 0:
-        grad = ops.dropout(grad.contiguous(), ctx.dropout_p, ctx.seed)
+        grad = dropout(grad, ctx.dropout_p, ctx.seed)
     g = grad.reshape(N, H, hd)
     # sequences of equal length go through one batched call (a batch of full
     # 16x16 grids is one call per layer)
@@ -242,6 +242,74 @@ def _fmha_backward(ctx, grad):
 
 
 fmha_varlen.register_autograd(_fmha_backward, setup_context=_fmha_setup)
+
+
+@torch.library.custom_op("siglip2_b200::fmha_varlen_train", mutates_args=(), device_types="cuda")
+def fmha_varlen_train(qkv: Tensor, cu_seqlens: Tensor, tiles: Tensor, heads: int, head_dim: int,
+                      dropout_p: float = 0.0, seed: int = 0) -> tuple[Tensor, Tensor]:
+    """``siglip2_fmha_varlen_train``: ``(out, lse)``, the attention output
+    (train-mode output dropout when ``dropout_p > 0``) and the base-2
+    log-sum-exp of every row, kept for the tensor-core backward."""
+    return ops.fmha_varlen_train(qkv, cu_seqlens, tiles, heads, head_dim, dropout_p, seed)
+
+
+@fmha_varlen_train.register_fake
+def _(qkv, cu_seqlens, tiles, heads, head_dim, dropout_p=0.0, seed=0):
+    N = qkv.shape[0]
+    return qkv.new_empty((N, heads * head_dim)), qkv.new_empty((N, heads), dtype=torch.float32)
+
+
+def _fmha_train_setup(ctx, inputs, output):
+    qkv, cu_seqlens, tiles, heads, head_dim, dropout_p, seed = inputs
+    out, lse = output
+    ctx.heads, ctx.head_dim, ctx.dropout_p, ctx.seed = heads, head_dim, dropout_p, seed
+    ctx.save_for_backward(qkv, cu_seqlens, tiles, out, lse)
+
+
+@torch.library.custom_op("siglip2_b200::fmha_varlen_backward", mutates_args=(), device_types="cuda")
+def fmha_varlen_backward(qkv: Tensor, out: Tensor, grad: Tensor, lse: Tensor, cu_seqlens: Tensor, tiles: Tensor,
+                         heads: int, head_dim: int, dropout_p: float, seed: int) -> Tensor:
+    """``siglip2_fmha_bwd_dsum`` + ``siglip2_fmha_varlen_backward``: dqkv of the
+    training attention (the gradient through the forward's dropout mask)."""
+    return ops.fmha_varlen_backward(qkv, out, grad, lse, cu_seqlens, tiles, heads, head_dim, dropout_p, seed)
+
+
+@fmha_varlen_backward.register_fake
+def _(qkv, out, grad, lse, cu_seqlens, tiles, heads, head_dim, dropout_p, seed):
+    return torch.empty_like(qkv)
+
+
+@torch.library.custom_op("siglip2_b200::dropout", mutates_args=(), device_types="cuda")
+def dropout(x: Tensor, p: float, seed: int) -> Tensor:
+    """``siglip2_dropout``: the train-mode mask of ``seed`` applied to ``x``."""
+    return ops.dropout(x.contiguous(), p, seed)
+
+
+@dropout.register_fake
+def _(x, p, seed):
+    return torch.empty_like(x, memory_format=torch.contiguous_format)
+
+
+def _fmha_train_backward(ctx, grad_out, grad_lse):
+    """The attention backward on the tensor cores (the log-sum-exp output
+    carries no gradient)."""
+    qkv, cu_seqlens, tiles, out, lse = ctx.saved_tensors
+    dqkv = fmha_varlen_backward(qkv, out, grad_out, lse, cu_seqlens, tiles, ctx.heads, ctx.head_dim,
+                                ctx.dropout_p, ctx.seed)
+    return dqkv, None, None, None, None, None, None
+
+
+fmha_varlen_train.register_autograd(_fmha_train_backward, setup_context=_fmha_train_setup)
+
+
+def attention_for_training(qkv: Tensor, cu_seqlens: Tensor, tiles: Tensor, heads: int, head_dim: int,
+                           lengths: list[int], dropout_p: float = 0.0, seed: int = 0) -> Tensor:
+    """Attention with a backward: the tensor-core forward + backward pair
+    (bf16 / f16, head_dim 64, 72 or 96), else ``fmha_varlen`` with the
+    recompute-in-torch backward."""
+    if qkv.dtype in (torch.bfloat16, torch.float16) and head_dim in (64, 72, 96):
+        return fmha_varlen_train(qkv, cu_seqlens, tiles, heads, head_dim, dropout_p, seed)[0]
+    return fmha_varlen(qkv, cu_seqlens, tiles, heads, head_dim, lengths, dropout_p, seed)
 
 
 # --------------------------------------------------------------------------- row ops

@@ -119,6 +119,23 @@ def test_fake_shapes_of_the_registered_ops():
     assert pe.shape == (300, 1152)
 
 
+def test_fake_shapes_of_the_training_ops():
+    """The ops a train step adds: transposed-operand GEMMs, the attention with
+    its log-sum-exp and backward, the dropout mask and the LayerNorm backward."""
+    dy, x = _meta(300, 4304), _meta(300, 1152)
+    assert O.gemm_t(dy, _meta(4304, 1152), False, True, L.EPI_BIAS, None, None).shape == (300, 1152)
+    assert O.gemm_t(dy, x, True, True, L.EPI_BIAS, None, None).shape == (4304, 1152)
+    cu, tiles = _meta(3, dtype=torch.int32), _meta(4, 2, dtype=torch.int32)
+    qkv = _meta(300, 3456)
+    out, lse = O.fmha_varlen_train(qkv, cu, tiles, 16, 72, 0.1, 7)
+    assert out.shape == (300, 1152) and lse.shape == (300, 16) and lse.dtype == torch.float32
+    dqkv = O.fmha_varlen_backward(qkv, out, _meta(300, 1152), lse, cu, tiles, 16, 72, 0.1, 7)
+    assert dqkv.shape == qkv.shape and dqkv.dtype == qkv.dtype
+    assert O.dropout(x, 0.1, 3).shape == x.shape
+    dx, dw, db = O.layernorm_backward(x, _meta(300, 1152), _meta(1152, dtype=torch.float32), 1e-6)
+    assert dx.shape == x.shape and dw.shape == db.shape == (1152,) and dw.dtype == torch.float32
+
+
 @pytest.mark.parametrize("max_patches,pooled", [(0, False), (0, True), (256, True)])
 def test_fake_shapes_of_the_tower_op(max_patches, pooled):
     dims = [768, 3072, 1, 12, 64, 768, 16, L.DTYPE_BF16, 1]
