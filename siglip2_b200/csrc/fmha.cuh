@@ -59,6 +59,33 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// max of three floats in one instruction (sm_100)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float y;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(y) : "f"(a), "f"(b), "f"(c));
+  return y;
+}
+
+// packed fp32 pair arithmetic (sm_100): two lanes of FFMA / FADD per issue
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
 template <int HDP>
 struct FmhaCfg {
   static constexpr int R = HDP - 64;                  // remainder slab width (0, 16, 32)
@@ -346,13 +373,14 @@ __global__ void __launch_bounds__(192, 2)
           for (int k = 0; k < KT; ++k)
             if (k >= valid) s[k] = -INFINITY;
         }
-        float mx[8];
+        // tile maximum (3-input max), lazy rescale, then P = exp2(s * scale - m)
+        // with the scale-and-subtract and the row sums in packed f32x2 issues
+        float mx[4];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) mx[i] = s[i];
+        for (int i = 0; i < 4; ++i) mx[i] = fmaxf(s[2 * i], s[2 * i + 1]);
 #pragma unroll
-        for (int k = 8; k < KT; ++k) mx[k & 7] = fmaxf(mx[k & 7], s[k]);
-        float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-        mt *= sc;
+        for (int k = 4; k < KT / 2; ++k) mx[k & 3] = fmax3(mx[k & 3], s[2 * k], s[2 * k + 1]);
+        const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sc;
         float alpha = 1.f;
         if (j == 0) {
           m_use = mt;
@@ -360,18 +388,19 @@ __global__ void __launch_bounds__(192, 2)
           alpha = ex2_approx(m_use - mt);
           m_use = mt;
         }
-        float ps[8];
+        float2 ps2[4];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) ps[i] = 0.f;
+        for (int i = 0; i < 4; ++i) ps2[i] = make_float2(0.f, 0.f);
         uint32_t wv[KT / 2];
 #pragma unroll
         for (int k = 0; k < KT / 2; ++k) {
-          const float p0 = ex2_approx(fmaf(s[2 * k], sc, -m_use));
-          const float p1 = ex2_approx(fmaf(s[2 * k + 1], sc, -m_use));
-          ps[k & 7] += p0 + p1;
-          wv[k] = Pack2<T>::pack(p0, p1);
+          const float2 x = ffma2(make_float2(s[2 * k], s[2 * k + 1]), make_float2(sc, sc), make_float2(-m_use, -m_use));
+          const float2 pr = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+          ps2[k & 3] = fadd2(ps2[k & 3], pr);
+          wv[k] = Pack2<T>::pack(pr.x, pr.y);
         }
-        l = l * alpha + (((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7])));
+        const float2 pt = fadd2(fadd2(ps2[0], ps2[1]), fadd2(ps2[2], ps2[3]));
+        l = l * alpha + (pt.x + pt.y);
         if (j > 0) {
           // the previous PV must be done: P's columns are rewritten and O may be rescaled
           // (at j == 0 the previous item's last PV was waited for before its O was read)
