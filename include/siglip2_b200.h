@@ -97,7 +97,7 @@ int siglip2_set_gemm_variant(int variant);
 int siglip2_get_gemm_variant(void);
 
 /* Attention kernel selection for every later attention launch of the
- * process: 0 = automatic (default: paired query tiles), 1 = one 128-row
+ * process: 0 = automatic (one query tile per CTA), 1 = one 128-row
  * query tile per CTA (two CTAs per SM), 2 = two query tiles of the same
  * image and head per CTA sharing each K/V tile (one CTA per SM). */
 int siglip2_set_fmha_variant(int variant);
@@ -135,6 +135,30 @@ int siglip2_gemm(int dtype, int epilogue, const void* a_dev, int lda, const void
 int siglip2_gemm_t(int dtype, int epilogue, int trans_a, int trans_b, const void* a_dev, int lda, const void* b_dev,
                    int ldb, void* out_dev, int ldo, int M, int N, int K, const float* bias_dev, const void* res_dev,
                    int ldr, void* stream);
+
+/* 8-bit (e4m3) GEMM operands, the fp8 variant of the projections (the
+ * reference's nn.Linear layers, model.py:138-141, 183-184, run at bf16 there;
+ * the reference has no 8-bit path).
+ *
+ * siglip2_quantize_e4m3: per-row quantisation of x [rows, cols] (dtype
+ * F32/BF16/F16, row stride ldx elements) into e4m3 codes q [rows, cols]
+ * (row stride ldq bytes) and scale [rows]:
+ *   scale[r] = max_c |x[r,c]| / 448,  q[r,c] = e4m3_rne_satfinite(x[r,c] * (448 / max_c |x[r,c]|))
+ * (an all-zero row: scale 0, zero codes).  Per-token scales for activations,
+ * per-output-channel scales for a weight [N_out, K].  cols, ldx and ldq
+ * multiples of 8 (ldq of 16 for a GEMM operand), x and q 16-byte aligned.
+ *
+ * siglip2_gemm_e4m3: out[M,N] = epilogue(a_scale[m] * b_scale[n] *
+ * (A[M,K] . B[N,K]^T)) with A and B e4m3 codes (row strides lda / ldb in
+ * bytes), fp32 accumulation (tcgen05.mma kind::f8f6f4 on SM pairs), out in
+ * out_dtype (BF16 or F16).  Epilogues SIGLIP2_EPI_BIAS, SIGLIP2_EPI_BIAS_RES,
+ * SIGLIP2_EPI_BIAS_GELU; bias [N] required.  K, lda, ldb multiples of 16; N,
+ * ldo, ldr multiples of 8; pointers 16-byte aligned. */
+int siglip2_quantize_e4m3(int dtype, const void* x_dev, int ldx, int rows, int cols, void* q_dev, int ldq,
+                          float* scale_dev, void* stream);
+int siglip2_gemm_e4m3(int out_dtype, int epilogue, const void* a_dev, int lda, const float* a_scale_dev,
+                      const void* b_dev, int ldb, const float* b_scale_dev, void* out_dev, int ldo, int M, int N, int K,
+                      const float* bias_dev, const void* res_dev, int ldr, void* stream);
 
 /* LayerNorm statistics for the LayerNorm-folded GEMMs are kept per column
  * block ("slots"): a [rows][S] array of float pairs (mean, centred sum of

@@ -2,6 +2,7 @@
 command the ncu summaries under ``profiles/`` were captured with.
 
     python kernel_bench.py gemm --epi ln_gelu --m 39178 --n 4304 --k 1152
+    python kernel_bench.py gemm_e4m3 --m 39178 --n 4304 --k 1152 --epi bias_gelu
     python kernel_bench.py fmha --preset so400m --images 64 --max-patches 1024
     python kernel_bench.py layer --preset so400m --images 64 --max-patches 1024
     python kernel_bench.py patchify --images 64 --height 768 --width 1024 --max-patches 1024
@@ -101,6 +102,41 @@ def bench_fmha(preset, images, max_patches, reps, dtype=torch.bfloat16, warmup=3
             **_clock()}
 
 
+def bench_gemm_e4m3(m, n, k, epi, reps, warmup=3, cublas=False):
+    """The e4m3 GEMM (siglip2_gemm_e4m3, kind::f8f6f4 on SM pairs) against the
+    bf16 GEMM of the same shape and epilogue; 2 m n k FLOPs each.  The
+    per-row quantisation of A (siglip2_quantize_e4m3) is timed on its own:
+    bytes = m k (2 read + 1 written) + 4 m."""
+    g = torch.Generator(device="cuda").manual_seed(0)
+    a = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(n, k, device="cuda", generator=g) * 0.03).bfloat16()
+    bias = torch.randn(n, device="cuda", generator=g) * 0.1
+    qa, sa = ops.quantize_e4m3(a)
+    qw, sw = ops.quantize_e4m3(w)
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    r_in = torch.randn(m, n, device="cuda", generator=g).bfloat16() if epi == "bias_res" else None
+    code = EPIS[epi]
+    fl = 2 * m * n * k
+    res = []
+    ms = _time(lambda: ops.gemm_e4m3(qa, sa, qw, sw, code, bias, res=r_in, out=out), reps, warmup)
+    res.append({"kernel": "gemm_e4m3", "epi": epi, "M": m, "N": n, "K": k, "ms": ms, "tflops": fl / ms / 1e9, **_clock()})
+    ms = _time(lambda: ops.gemm(a, w, code, bias=bias, res=r_in, out=out), reps, warmup)
+    res.append({"kernel": "gemm_bf16", "epi": epi, "M": m, "N": n, "K": k, "ms": ms, "tflops": fl / ms / 1e9, **_clock()})
+    qo = torch.empty(m, k, device="cuda", dtype=torch.float8_e4m3fn)
+    so = torch.empty(m, device="cuda")
+    ms = _time(lambda: L.call("siglip2_quantize_e4m3", L.DTYPE_BF16, a.data_ptr(), k, m, k, qo.data_ptr(), k,
+                              so.data_ptr(), torch.cuda.current_stream().cuda_stream), reps, warmup)
+    res.append({"kernel": "quantize_e4m3", "rows": m, "cols": k, "ms": ms, "gbs": (3 * m * k + 4 * m) / ms / 1e6,
+                **_clock()})
+    if cublas:
+        one = torch.ones((), device="cuda")
+        ms = _time(lambda: torch._scaled_mm(qa, qw.t(), scale_a=one, scale_b=one, out_dtype=torch.bfloat16), reps,
+                   warmup)
+        res.append({"kernel": "torch._scaled_mm (cuBLAS, tensor-wise scales, no epilogue)", "M": m, "N": n, "K": k,
+                    "ms": ms, "tflops": fl / ms / 1e9, **_clock()})
+    return res
+
+
 def bench_backward_gemms(m, n, k, reps, warmup=3):
     """dgrad dA = dY W and wgrad dW = dY^T A of y = A W^T (A [m, k], W [n, k])
     on the transposed-operand tensor-core GEMM (siglip2_gemm_t), and the
@@ -182,6 +218,15 @@ def main():
     g.add_argument("--cublas", action="store_true", help="also time torch.matmul (cuBLAS) on the same operands")
     g.add_argument("--reps", type=int, default=20)
     g.add_argument("--warmup", type=int, default=3)
+    e8 = sub.add_parser("gemm_e4m3")
+    e8.add_argument("--m", type=int, default=39178)
+    e8.add_argument("--n", type=int, default=4304)
+    e8.add_argument("--k", type=int, default=1152)
+    e8.add_argument("--epi", default="bias_gelu", help="bias, bias_res or bias_gelu")
+    e8.add_argument("--cublas", action="store_true", help="also time torch._scaled_mm on the same codes")
+    e8.add_argument("--reps", type=int, default=20)
+    e8.add_argument("--warmup", type=int, default=3)
+    e8.add_argument("--variant", type=int, default=0)
     f = sub.add_parser("fmha")
     f.add_argument("--preset", default="so400m")
     f.add_argument("--images", type=int, default=64)
@@ -219,6 +264,9 @@ def main():
             if epi not in EPIS:
                 raise SystemExit(f"unknown epilogue {epi!r}")
             print(json.dumps(bench_gemm(a.m, a.n, a.k, epi, a.reps, warmup=a.warmup, cublas=a.cublas)))
+    elif a.cmd == "gemm_e4m3":
+        for r in bench_gemm_e4m3(a.m, a.n, a.k, a.epi, a.reps, a.warmup, a.cublas):
+            print(json.dumps(r))
     elif a.cmd == "patchify":
         print(json.dumps(bench_patchify(a.images, a.height, a.width, a.max_patches, a.reps, a.warmup,
                                         channels_last=not a.channels_first)))

@@ -55,6 +55,9 @@ SIGNATURES = {
     "siglip2_fmha_bwd_dsum": (_c_int, [_c_int, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp]),
     "siglip2_fmha_varlen_backward": (_c_int, [_c_int, _vp, _vp, _c_int, _c_int, _vp, _vp, _c_int, _c_int, _c_int,
                                               _vp, _vp, _vp, _vp]),
+    "siglip2_quantize_e4m3": (_c_int, [_c_int, _vp, _c_int, _c_int, _c_int, _vp, _c_int, _vp, _vp]),
+    "siglip2_gemm_e4m3": (_c_int, [_c_int, _c_int, _vp, _c_int, _vp, _vp, _c_int, _vp, _vp, _c_int, _c_int, _c_int,
+                                   _c_int, _vp, _vp, _c_int, _vp]),
     "siglip2_padded_head_dim": (_c_int, [_c_int]),
     "siglip2_head_pool": (_c_int, [_c_int, _vp, _c_int, _c_int, _vp, _c_int, _c_int, _vp, _vp, _vp, _vp]),
     "siglip2_head_pool_noalloc": (_c_int, [_c_int, _vp, _c_int, _c_int, _vp, _c_int, _c_int, _c_int, _vp, _vp,

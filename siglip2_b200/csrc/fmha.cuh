@@ -351,18 +351,15 @@ __global__ void __launch_bounds__(192, 2)
           break;
         }
         tc_fence_after();
+        // the whole S tile in one round trip
         float s[KT];
+        {
+          uint32_t su[KT];
 #pragma unroll
-        for (int c = 0; c < KT / 16; c += 2) {
-          uint32_t u[16], u2[16];
-          SG_TMEM_LD_16(tmem + c * 16 + lane_off, u);
-          SG_TMEM_LD_16(tmem + (c + 1) * 16 + lane_off, u2);
+          for (int c = 0; c < KT / 32; ++c) SG_TMEM_LD_32(tmem + c * 32 + lane_off, (su + c * 32));
           tmem_ld_wait();
 #pragma unroll
-          for (int k = 0; k < 16; ++k) {
-            s[c * 16 + k] = __uint_as_float(u[k]);
-            s[(c + 1) * 16 + k] = __uint_as_float(u2[k]);
-          }
+          for (int k = 0; k < KT; ++k) s[k] = __uint_as_float(su[k]);
         }
         // S is in registers: let the MMA warp compute the next S
         tc_fence_before();

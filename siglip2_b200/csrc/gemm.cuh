@@ -76,6 +76,11 @@ struct GemmParams {
   const int* tok_img;
   const int* pos_hw;
   const int* cu;
+  // 8-bit operands (gemm_tc2_kernel<..., kF8>): the accumulator of row m,
+  // column n is a_scale[m] * b_scale[n] times the product of the stored
+  // e4m3 values (per-row scales of A, per-output-channel scales of B)
+  const float* a_scale;
+  const float* b_scale;
 };
 
 constexpr int kGemmBM = 128;
@@ -162,7 +167,7 @@ __device__ __forceinline__ void load_param32(const float* __restrict__ p, int co
 // into L2.  `row_offset` is the first output row of this CTA's 128-row half
 // of the tile; `tempty_addr*` are the shared::cluster addresses of the
 // barriers that hand each accumulator back to the MMA issuer.
-template <typename T, int BN, int EPI, bool kCluster>
+template <typename T, int BN, int EPI, bool kCluster, bool kScale = false>
 __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtensorMap* tmO, const CUtensorMap* tmR,
                                               uint32_t tmem_base, uint32_t acc_stride, uint8_t* staging,
                                               uint64_t* resbar, uint64_t* tfull, uint32_t tempty_addr0,
@@ -230,6 +235,10 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
     const int my_row = row0 + lane;
     prefetch_tile(tile + tile_step);
     float mu = 0.f, rstd = 1.f;
+    float a_s = 1.f;  // kScale: this row's scale of A
+    if constexpr (kScale) {
+      if (my_row < p.M) a_s = __ldg(p.a_scale + my_row);
+    }
     if constexpr (kRsIn) {
       // LayerNorm statistics of the raw A row (the previous GEMM's rounded
       // output) merged from its column-block slots in a fixed order
@@ -301,6 +310,11 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
           }
         } else {
           float a[32];
+          if constexpr (kScale) {
+            load_param32(p.b_scale, col0, p.N, a);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] *= a_s * a[j];
+          }
           if (p.bias) {
             load_param32(p.bias, col0, p.N, a);
           } else {
@@ -719,17 +733,23 @@ struct Gemm2Cfg {
   static_assert(kStages >= 2 && kSmemBytes <= kSmemLimit, "GEMM shared-memory budget");
 };
 
-template <typename T, int BN, int EPI, int SUB>
+// kF8: A and B hold e4m3 values, read as pairs through the same 16-bit tensor
+// maps and 128-byte rows (a 64-wide slab of pairs is 128 K-elements); the
+// MMAs run kind::f8f6f4 (32 K-elements each) and the epilogue applies
+// a_scale / b_scale; T is the output type.  p.K counts pairs.
+template <typename T, int BN, int EPI, int SUB, bool kF8 = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
                     const GemmParams p) {
   constexpr bool kLN = epi_has_stat_warps(EPI);  // statistics warps in this kernel
   constexpr bool kRes = epi_has_res(EPI);
+  static_assert(!(kF8 && (kLN || epi_is_ln(EPI))), "8-bit operands: bias epilogues only");
   using Cfg = Gemm2Cfg<BN, SUB, EPI>;
   constexpr int EW = epi_warps(EPI);
   constexpr int STAGES = Cfg::kStages;
-  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  // instruction-descriptor format bits: bf16 (1) or f16 (0) for kind::f16, e4m3 (0) for kind::f8f6f4
+  constexpr bool kBF16 = !kF8 && std::is_same<T, __nv_bfloat16>::value;
   // the last column tile may be narrower (N - (n_tiles - 1) * BN, rounded up
   // to 16): its MMAs run at that width and the pair splits B at half of it
   const auto tile_width = [&](int n_tile) { return min(BN, (p.N - n_tile * BN + 15) & ~15); };
@@ -876,8 +896,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int sub = 0; sub < SUB; ++sub) {
 #pragma unroll
             for (int k = 0; k < kGemmBK / 16; ++k) {
-              umma_ss_pair(d_tmem, kmajor_desc(a_base + sub * Cfg::kSlabA + k * 32, 128),
-                           kmajor_desc(b_base + sub * Cfg::kSlabB + k * 32, 128), idesc, (kb | sub | k) != 0);
+              if constexpr (kF8)
+                umma_ss_pair_f8(d_tmem, kmajor_desc(a_base + sub * Cfg::kSlabA + k * 32, 128),
+                                kmajor_desc(b_base + sub * Cfg::kSlabB + k * 32, 128), idesc, (kb | sub | k) != 0);
+              else
+                umma_ss_pair(d_tmem, kmajor_desc(a_base + sub * Cfg::kSlabA + k * 32, 128),
+                             kmajor_desc(b_base + sub * Cfg::kSlabB + k * 32, 128), idesc, (kb | sub | k) != 0);
             }
           }
           umma_commit_pair_mc(&empty[stage], 0x3);
@@ -895,9 +919,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp < 2 + EW) {
     // ------------------------------------------------------------ epilogue (both CTAs)
     const uint32_t te0 = mapa_shared(smem_u32(&tempty[0]), 0), te1 = mapa_shared(smem_u32(&tempty[1]), 0);
-    gemm_epilogue<T, BN, EPI, true>(p, &tmO, &tmR, tmem_base, Cfg::kAccStride, staging, resbar, tfull, te0, te1,
-                                    sfull, sempty, st_mean, st_rstd, abort_flag, warp, lane, pair, num_pairs,
-                                    num_tiles, n_tiles, kTileRows, static_cast<int>(rank) * kGemmBM);
+    gemm_epilogue<T, BN, EPI, true, kF8>(p, &tmO, &tmR, tmem_base, Cfg::kAccStride, staging, resbar, tfull, te0,
+                                         te1, sfull, sempty, st_mean, st_rstd, abort_flag, warp, lane, pair,
+                                         num_pairs, num_tiles, n_tiles, kTileRows, static_cast<int>(rank) * kGemmBM);
   } else {
     // ------------------------------------------------------------ LayerNorm row statistics (both CTAs)
     if constexpr (kLN) {

@@ -12,6 +12,7 @@
 #include "rowops.cuh"
 #include "fmha.cuh"
 #include "fmha_pair.cuh"
+#include "fp8.cuh"
 #include "fmha_bwd.cuh"
 #include "forward.cuh"
 #include "simt_f32.cuh"
@@ -72,7 +73,7 @@ int launch_gemm_tc(const GemmIO& io, const GemmParams& p, cudaStream_t stream) {
 }
 
 // 2-SM variant: clusters of 2 CTAs, one pair per 2 SMs, 256 x BN tiles.
-template <typename T, int BN, int EPI, int SUB>
+template <typename T, int BN, int EPI, int SUB, bool kF8 = false>
 int launch_gemm_tc2(const GemmIO& io, const GemmParams& p, cudaStream_t stream) {
   CUtensorMap ta, tb, to, tr;
   SG_TRY(make_tmap_2d(&ta, io.a, 2, p.M, p.K, io.lda, kGemmBM, kGemmBK));
@@ -82,7 +83,7 @@ int launch_gemm_tc2(const GemmIO& io, const GemmParams& p, cudaStream_t stream) 
   else tr = to;
   constexpr int threads = kGemmThreads;
   constexpr int smem = Gemm2Cfg<BN, SUB, EPI>::kSmemBytes;
-  auto kern = gemm_tc2_kernel<T, BN, EPI, SUB>;
+  auto kern = gemm_tc2_kernel<T, BN, EPI, SUB, kF8>;
   SG_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem));
   const int tiles = ((p.M + 2 * kGemmBM - 1) / (2 * kGemmBM)) * ((p.N + BN - 1) / BN);
   const int pairs = std::min(tiles, sm_count() / 2);
@@ -418,6 +419,60 @@ int sg_rowsums_impl(int dtype, const void* x, int ldx, int M, int K, float2* rs,
   }
   SG_LAUNCH_CHECK();
   return SIGLIP2_OK;
+}
+
+// ---------------------------------------------------------------------------
+// 8-bit (e4m3) operands
+// ---------------------------------------------------------------------------
+int sg_quantize_e4m3_impl(int dtype, const void* x, int ldx, int rows, int cols, void* q, int ldq, float* scale,
+                          cudaStream_t s) {
+  SG_CHECK_ARG(x && q && scale && rows >= 0 && cols > 0 && ldx >= cols && ldq >= cols, "bad quantize arguments");
+  if (!aligned16(x) || !aligned16(q) || cols % 8 || ldx % 8 || ldq % 8)
+    return set_error(SIGLIP2_ERR_ALIGN, "quantize: 16-byte aligned x and q, cols, ldx and ldq multiples of 8");
+  if (rows == 0) return SIGLIP2_OK;
+  const int grid = std::min((rows + 7) / 8, 8 * sm_count());
+  uint8_t* qb = static_cast<uint8_t*>(q);
+  switch (dtype) {
+    case SIGLIP2_BF16: quantize_e4m3_rows_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), ldx, rows, cols, qb, ldq, scale); break;
+    case SIGLIP2_F16: quantize_e4m3_rows_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(x), ldx, rows, cols, qb, ldq, scale); break;
+    case SIGLIP2_F32: quantize_e4m3_rows_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(x), ldx, rows, cols, qb, ldq, scale); break;
+    default: return set_error(SIGLIP2_ERR_ARG, "unknown dtype %d", dtype);
+  }
+  SG_LAUNCH_CHECK();
+  return SIGLIP2_OK;
+}
+
+template <typename T>
+int dispatch_gemm_e4m3(int epi, const GemmIO& io, const GemmParams& p, cudaStream_t s) {
+  switch (epi) {
+    case kEpiBias: return launch_gemm_tc2<T, 256, kEpiBias, 2, true>(io, p, s);
+    case kEpiBiasRes: return launch_gemm_tc2<T, 256, kEpiBiasRes, 2, true>(io, p, s);
+    case kEpiBiasGelu: return launch_gemm_tc2<T, 256, kEpiBiasGelu, 2, true>(io, p, s);
+    default: return set_error(SIGLIP2_ERR_UNSUPPORTED, "e4m3 GEMM: epilogue %d not supported (0, 1, 4)", epi);
+  }
+}
+
+// out[M, N] = epilogue(a_scale[m] * b_scale[n] * (A[M, K] . B[N, K]^T)) with
+// A, B e4m3 codes (row strides lda / ldb in bytes), on the CTA-pair kernel.
+int sg_gemm_e4m3_impl(int out_dtype, int epi, const void* a, int lda, const float* a_scale, const void* b, int ldb,
+                      const float* b_scale, void* out, int ldo, int M, int N, int K, const float* bias,
+                      const void* res, int ldr, cudaStream_t stream) {
+  SG_CHECK_ARG(M >= 0 && N > 0 && K > 0, "bad GEMM shape M=%d N=%d K=%d", M, N, K);
+  if (M == 0) return SIGLIP2_OK;
+  SG_CHECK_ARG(a && b && out && a_scale && b_scale && bias, "null operand, scale or bias");
+  SG_CHECK_ARG(!epi_has_res(epi) || res, "residual epilogue needs res");
+  if (out_dtype != SIGLIP2_BF16 && out_dtype != SIGLIP2_F16)
+    return set_error(SIGLIP2_ERR_UNSUPPORTED, "e4m3 GEMM writes bf16 or f16 (dtype=%d)", out_dtype);
+  if (K % 16 || lda % 16 || ldb % 16 || N % 8 || ldo % 8 || (epi_has_res(epi) && ldr % 8))
+    return set_error(SIGLIP2_ERR_ALIGN, "e4m3 GEMM: K, lda, ldb multiples of 16; N, ldo, ldr multiples of 8");
+  if (lda < K || ldb < K || ldo < N || (epi_has_res(epi) && ldr < N))
+    return set_error(SIGLIP2_ERR_SHAPE, "leading dimension smaller than the row");
+  GemmParams p{};
+  p.M = M; p.N = N; p.K = K / 2;  // the kernel counts K in 16-bit pairs
+  p.bias = bias; p.a_scale = a_scale; p.b_scale = b_scale;
+  const GemmIO io{a, lda / 2, b, ldb / 2, out, ldo, res, ldr};
+  return out_dtype == SIGLIP2_BF16 ? dispatch_gemm_e4m3<__nv_bfloat16>(epi, io, p, stream)
+                                   : dispatch_gemm_e4m3<__half>(epi, io, p, stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -1027,6 +1082,18 @@ int siglip2_gemm_t(int dtype, int epilogue, int trans_a, int trans_b, const void
                    int ldr, void* stream) {
   return sg_gemm_t_impl(dtype, epilogue, trans_a, trans_b, a_dev, lda, b_dev, ldb, out_dev, ldo, M, N, K, bias_dev,
                         res_dev, ldr, static_cast<cudaStream_t>(stream));
+}
+
+int siglip2_quantize_e4m3(int dtype, const void* x_dev, int ldx, int rows, int cols, void* q_dev, int ldq,
+                          float* scale_dev, void* stream) {
+  return sg_quantize_e4m3_impl(dtype, x_dev, ldx, rows, cols, q_dev, ldq, scale_dev, static_cast<cudaStream_t>(stream));
+}
+
+int siglip2_gemm_e4m3(int out_dtype, int epilogue, const void* a_dev, int lda, const float* a_scale_dev,
+                      const void* b_dev, int ldb, const float* b_scale_dev, void* out_dev, int ldo, int M, int N, int K,
+                      const float* bias_dev, const void* res_dev, int ldr, void* stream) {
+  return sg_gemm_e4m3_impl(out_dtype, epilogue, a_dev, lda, a_scale_dev, b_dev, ldb, b_scale_dev, out_dev, ldo, M, N,
+                           K, bias_dev, res_dev, ldr, static_cast<cudaStream_t>(stream));
 }
 
 int siglip2_rowsum_slots(int dtype, int n) {

@@ -68,6 +68,38 @@ def gemm_t(a: torch.Tensor, b: torch.Tensor, trans_a: bool, trans_b: bool, epilo
     return out
 
 
+def quantize_e4m3(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """``siglip2_quantize_e4m3``: per-row e4m3 codes of ``x`` [rows, cols]
+    (fp32 / bf16 / f16) as a ``torch.float8_e4m3fn`` tensor and the fp32
+    per-row scales (``x ~ codes * scale[:, None]``)."""
+    _need_cuda(x)
+    assert x.dim() == 2 and x.stride(1) == 1
+    rows, cols = x.shape
+    q = torch.empty((rows, cols), dtype=torch.float8_e4m3fn, device=x.device)
+    scale = torch.empty(rows, dtype=torch.float32, device=x.device)
+    L.call("siglip2_quantize_e4m3", dtype_code(x.dtype), x.data_ptr(), x.stride(0), rows, cols, q.data_ptr(),
+           q.stride(0), scale.data_ptr(), _stream(x.device))
+    return q, scale
+
+
+def gemm_e4m3(a: torch.Tensor, a_scale: torch.Tensor, w: torch.Tensor, w_scale: torch.Tensor, epilogue: int,
+              bias: torch.Tensor, res=None, out_dtype=torch.bfloat16, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``siglip2_gemm_e4m3``: ``epilogue(a_scale[:, None] * w_scale[None, :] *
+    (a @ w.T))`` with ``a`` [M, K] and ``w`` [N, K] e4m3 codes (from
+    ``quantize_e4m3``), fp32 accumulation, ``out_dtype`` output."""
+    _need_cuda(a, a_scale, w, w_scale, bias, res, out)
+    assert a.dtype == torch.float8_e4m3fn and w.dtype == torch.float8_e4m3fn
+    assert a.dim() == 2 and w.dim() == 2 and a.shape[1] == w.shape[1] and a.stride(1) == 1 and w.stride(1) == 1
+    M, K = a.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    L.call("siglip2_gemm_e4m3", dtype_code(out.dtype), epilogue, a.data_ptr(), a.stride(0), a_scale.data_ptr(),
+           w.data_ptr(), w.stride(0), w_scale.data_ptr(), out.data_ptr(), out.stride(0), M, N, K, bias.data_ptr(),
+           _ptr(res), res.stride(0) if res is not None else 0, _stream(a.device))
+    return out
+
+
 def fold_layernorm(w: torch.Tensor, b: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, dtype):
     """LayerNorm(gamma, beta) followed by Linear(w, b) as a GEMM on the raw
     input: returns ``(w*gamma in dtype, c1, c2)`` with ``c1 = rowsum(w*gamma)``
