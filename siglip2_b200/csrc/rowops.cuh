@@ -334,14 +334,17 @@ namespace sg {
 // ---------------------------------------------------------------------------
 // LayerNorm backward (the gradient of layernorm_kernel / nn.LayerNorm,
 // model.py:199,201,256), two deterministic passes:
-//   rows:    one warp per row recomputes mean and rstd from x (two-pass, as
+//   rows:    one warp per row loads its x and dy vectors together (both in
+//            flight at once), recomputes mean and rstd from x (two-pass, as
 //            the forward), then with g = dy * gamma and xh = (x - mean) rstd
 //              dx = rstd (g - mean(g) - xh mean(g xh))
 //            and writes dx and the row's (mean, rstd);
 //   columns: per chunk of rows, dgamma[c] = sum dy xh and dbeta[c] = sum dy,
 //            one partial row per chunk (summed over chunks in a fixed order
-//            by the caller), 64 columns per warp, warps of a CTA stepping
-//            through the chunk's rows and reduced in shared memory in order.
+//            by the caller); each lane owns 8 columns (one 16-byte vector),
+//            a warp 256 columns of a row, the 8 warps of a CTA step through
+//            the chunk's rows four at a time (four rows' loads in flight)
+//            and are reduced in shared memory in warp order.
 // ---------------------------------------------------------------------------
 template <typename T, int MAXV>
 __global__ void __launch_bounds__(256) layernorm_bwd_rows_kernel(const T* __restrict__ x, const T* __restrict__ dy,
@@ -355,23 +358,27 @@ __global__ void __launch_bounds__(256) layernorm_bwd_rows_kernel(const T* __rest
   const int nvec = D / V;
   const T* xr = x + static_cast<size_t>(row) * D;
   const T* dr = dy + static_cast<size_t>(row) * D;
-  float f[MAXV][V];
-  float s = 0.f;
+  float f[MAXV][V], gv[MAXV][V];
 #pragma unroll
   for (int c = 0; c < MAXV; ++c) {
     const int v = lane + c * 32;
     if (v < nvec) {
       load_vec(xr + v * V, f[c]);
+      load_vec(dr + v * V, gv[c]);
+    }
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int c = 0; c < MAXV; ++c)
+    if (lane + c * 32 < nvec) {
 #pragma unroll
       for (int k = 0; k < V; ++k) s += f[c][k];
     }
-  }
   const float mean = warp_sum(s) / static_cast<float>(D);
   float q = 0.f;
 #pragma unroll
   for (int c = 0; c < MAXV; ++c) {
-    const int v = lane + c * 32;
-    if (v < nvec) {
+    if (lane + c * 32 < nvec) {
 #pragma unroll
       for (int k = 0; k < V; ++k) {
         const float d = f[c][k] - mean;
@@ -380,14 +387,12 @@ __global__ void __launch_bounds__(256) layernorm_bwd_rows_kernel(const T* __rest
     }
   }
   const float rstd = rsqrtf(warp_sum(q) / static_cast<float>(D) + eps);
-  // g = dy * gamma (kept in f: x is replaced by xh, g goes to a second array)
-  float gv[MAXV][V];
+  // g = dy * gamma in gv, xh in f
   float sg = 0.f, sgx = 0.f;
 #pragma unroll
   for (int c = 0; c < MAXV; ++c) {
     const int v = lane + c * 32;
     if (v < nvec) {
-      load_vec(dr + v * V, gv[c]);
 #pragma unroll
       for (int k4 = 0; k4 < V / 4; ++k4) {
         const float4 g4 = __ldg(reinterpret_cast<const float4*>(gamma + v * V) + k4);
@@ -420,48 +425,76 @@ __global__ void __launch_bounds__(256) layernorm_bwd_rows_kernel(const T* __rest
   if (lane == 0) stats[row] = make_float2(mean, rstd);
 }
 
-// grid (ceil(D / 64), chunks), 256 threads; chunk j covers rows [j * chunk_rows, ...)
+// 8 consecutive values of a row as floats (one or two 16-byte loads)
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float* f) {
+  if constexpr (sizeof(T) == 4) {
+    load_vec(p, f);
+    load_vec(p + 4, f + 4);
+  } else {
+    load_vec(p, f);
+  }
+}
+
+// grid (ceil(D / 256), chunks), 256 threads; chunk j covers rows [j * chunk_rows, ...)
 template <typename T>
 __global__ void __launch_bounds__(256) layernorm_bwd_cols_kernel(const T* __restrict__ x, const T* __restrict__ dy,
                                                                  const float2* __restrict__ stats, int rows, int D,
                                                                  int chunk_rows, float* __restrict__ dgamma_part,
                                                                  float* __restrict__ dbeta_part) {
-  __shared__ float red[2][8][64];
+  __shared__ float red[2][8][256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int c = blockIdx.x * 64 + 2 * lane;  // this lane's two columns
+  const int c = blockIdx.x * 256 + 8 * lane;  // this lane's 8 columns
   const int r0 = blockIdx.y * chunk_rows;
   const int r1 = min(rows, r0 + chunk_rows);
-  float g0 = 0.f, g1 = 0.f, b0 = 0.f, b1 = 0.f;
+  float g[8], b[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) g[k] = b[k] = 0.f;
   if (c < D) {
-    for (int r = r0 + warp; r < r1; r += 8) {
-      const float2 st = stats[r];
-      float xv[2], dv[2];
-      if constexpr (sizeof(T) == 4) {
-        const float2 a = *reinterpret_cast<const float2*>(x + static_cast<size_t>(r) * D + c);
-        const float2 d = *reinterpret_cast<const float2*>(dy + static_cast<size_t>(r) * D + c);
-        xv[0] = a.x; xv[1] = a.y; dv[0] = d.x; dv[1] = d.y;
-      } else {
-        const float2 a = Pack2<T>::unpack(*reinterpret_cast<const uint32_t*>(x + static_cast<size_t>(r) * D + c));
-        const float2 d = Pack2<T>::unpack(*reinterpret_cast<const uint32_t*>(dy + static_cast<size_t>(r) * D + c));
-        xv[0] = a.x; xv[1] = a.y; dv[0] = d.x; dv[1] = d.y;
+    int r = r0 + warp;
+    for (; r + 24 < r1; r += 32) {  // four rows (8 apart) per step, loads first
+      float xv[4][8], dv[4][8];
+      float2 st[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const size_t off = static_cast<size_t>(r + 8 * u) * D + c;
+        load8(x + off, xv[u]);
+        load8(dy + off, dv[u]);
+        st[u] = stats[r + 8 * u];
       }
-      g0 = fmaf(dv[0], (xv[0] - st.x) * st.y, g0);
-      g1 = fmaf(dv[1], (xv[1] - st.x) * st.y, g1);
-      b0 += dv[0];
-      b1 += dv[1];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          g[k] = fmaf(dv[u][k], (xv[u][k] - st[u].x) * st[u].y, g[k]);
+          b[k] += dv[u][k];
+        }
+    }
+    for (; r < r1; r += 8) {
+      float xv[8], dv[8];
+      const size_t off = static_cast<size_t>(r) * D + c;
+      load8(x + off, xv);
+      load8(dy + off, dv);
+      const float2 st = stats[r];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        g[k] = fmaf(dv[k], (xv[k] - st.x) * st.y, g[k]);
+        b[k] += dv[k];
+      }
     }
   }
-  red[0][warp][2 * lane] = g0;
-  red[0][warp][2 * lane + 1] = g1;
-  red[1][warp][2 * lane] = b0;
-  red[1][warp][2 * lane + 1] = b1;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    red[0][warp][8 * lane + k] = g[k];
+    red[1][warp][8 * lane + k] = b[k];
+  }
   __syncthreads();
-  if (threadIdx.x < 128) {
-    const int which = threadIdx.x >> 6, col = threadIdx.x & 63;
+  for (int i = threadIdx.x; i < 512; i += 256) {
+    const int which = i >> 8, col = i & 255;
     float t = 0.f;
 #pragma unroll
     for (int w = 0; w < 8; ++w) t += red[which][w][col];  // fixed order
-    const int cc = blockIdx.x * 64 + col;
+    const int cc = blockIdx.x * 256 + col;
     if (cc < D) (which ? dbeta_part : dgamma_part)[static_cast<size_t>(blockIdx.y) * D + cc] = t;
   }
 }

@@ -350,13 +350,17 @@ int launch_layernorm_bwd(const void* x, const void* dy, const float* g, int rows
   const T* xt = static_cast<const T*>(x);
   const T* dyt = static_cast<const T*>(dy);
   T* dxt = static_cast<T*>(dx);
+  // vectors per lane: exactly as many as the width needs (registers hold x and dy)
   if (nvec <= 32 * 2) layernorm_bwd_rows_kernel<T, 2><<<grid, 256, 0, s>>>(xt, dyt, g, rows, D, eps, dxt, stats);
+  else if (nvec <= 32 * 3) layernorm_bwd_rows_kernel<T, 3><<<grid, 256, 0, s>>>(xt, dyt, g, rows, D, eps, dxt, stats);
   else if (nvec <= 32 * 4) layernorm_bwd_rows_kernel<T, 4><<<grid, 256, 0, s>>>(xt, dyt, g, rows, D, eps, dxt, stats);
+  else if (nvec <= 32 * 5) layernorm_bwd_rows_kernel<T, 5><<<grid, 256, 0, s>>>(xt, dyt, g, rows, D, eps, dxt, stats);
+  else if (nvec <= 32 * 6) layernorm_bwd_rows_kernel<T, 6><<<grid, 256, 0, s>>>(xt, dyt, g, rows, D, eps, dxt, stats);
   else if (nvec <= 32 * 8) layernorm_bwd_rows_kernel<T, 8><<<grid, 256, 0, s>>>(xt, dyt, g, rows, D, eps, dxt, stats);
   else if (nvec <= 32 * 12) layernorm_bwd_rows_kernel<T, 12><<<grid, 256, 0, s>>>(xt, dyt, g, rows, D, eps, dxt, stats);
   else return set_error(SIGLIP2_ERR_UNSUPPORTED, "LayerNorm width %d too large", D);
   SG_LAUNCH_CHECK();
-  const dim3 cgrid((D + 63) / 64, (rows + chunk_rows - 1) / chunk_rows);
+  const dim3 cgrid((D + 255) / 256, (rows + chunk_rows - 1) / chunk_rows);
   layernorm_bwd_cols_kernel<T><<<cgrid, 256, 0, s>>>(xt, dyt, stats, rows, D, chunk_rows, dg, db);
   SG_LAUNCH_CHECK();
   return SIGLIP2_OK;

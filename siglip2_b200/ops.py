@@ -126,7 +126,7 @@ def layernorm(x: torch.Tensor, gamma, beta, eps: float, cu_seqlens=None, batch: 
     return y
 
 
-def layernorm_backward(x: torch.Tensor, dy: torch.Tensor, gamma: torch.Tensor, eps: float, chunk_rows: int = 1024):
+def layernorm_backward(x: torch.Tensor, dy: torch.Tensor, gamma: torch.Tensor, eps: float, chunk_rows: int = 128):
     """``siglip2_layernorm_backward``: ``(dx, dgamma, dbeta)`` of LayerNorm over
     the last dimension (dgamma / dbeta fp32, summed over row chunks in order)."""
     _need_cuda(x, dy, gamma)

@@ -144,7 +144,7 @@ def _gemm_backward(ctx, grad):
     else:
         da = _matmul_nt(g, w.t()) if ctx.needs_input_grad[0] else None
         dw = _matmul_nt(g.t(), a.t()) if ctx.needs_input_grad[1] else None
-    db = g.float().sum(0) if ctx.needs_input_grad[3] else None
+    db = g.sum(0, dtype=torch.float32) if ctx.needs_input_grad[3] else None
     dres = grad if ctx.needs_input_grad[4] else None
     return da, dw, None, db, dres, None, None, None
 
@@ -410,7 +410,7 @@ def _patch_embed_backward(ctx, grad):
     else:
         d_patches = _matmul_nt(grad, w.t()) if ctx.needs_input_grad[0] else None
         dw = _matmul_nt(grad.t(), patches.t()) if ctx.needs_input_grad[1] else None
-    db = grad.float().sum(0) if ctx.needs_input_grad[2] else None
+    db = grad.sum(0, dtype=torch.float32) if ctx.needs_input_grad[2] else None
     dtable = None
     if ctx.needs_input_grad[3]:
         G2, D = table.shape
