@@ -136,6 +136,30 @@ int siglip2_gemm_t(int dtype, int epilogue, int trans_a, int trans_b, const void
                    int ldb, void* out_dev, int ldo, int M, int N, int K, const float* bias_dev, const void* res_dev,
                    int ldr, void* stream);
 
+/* siglip2_gemm_t (SIGLIP2_EPI_BIAS, trans_b = 1) with a caller-provided
+ * fp32 workspace for splitting K: when the M x N output has too few
+ * 128 x 256 tiles to fill the SMs (weight gradients: dW [N_out, K_in] over
+ * K = tokens), K is cut into slices of at least 1024 elements, each slice's
+ * partial product goes to the workspace and a second kernel sums the slices
+ * in order (+ bias), so the result is deterministic.
+ * siglip2_gemm_t_workspace_size returns the bytes the split needs (0: no
+ * split for this shape; then siglip2_gemm_t_ws runs as siglip2_gemm_t and
+ * the workspace may be NULL).  Replaces the weight-gradient matmuls of the
+ * autograd backward of the reference's Linear layers (model.py:138-141,
+ * 183-184). */
+size_t siglip2_gemm_t_workspace_size(int epilogue, int trans_a, int trans_b, int M, int N, int K);
+
+/* Column sums of x [rows, cols] (row stride ld) in fp32, as per-chunk
+ * partials part [ceil(rows / chunk_rows), cols] that the caller sums over
+ * chunks in order (deterministic): the bias gradient of a Linear layer
+ * (db = sum over tokens of dy; the autograd backward of model.py:138-141,
+ * 183-184).  cols and ld multiples of 8, x 16-byte aligned. */
+int siglip2_colsum_partial(int dtype, const void* x_dev, int ld, int rows, int cols, int chunk_rows, float* part_dev,
+                           void* stream);
+int siglip2_gemm_t_ws(int dtype, int epilogue, int trans_a, int trans_b, const void* a_dev, int lda, const void* b_dev,
+                      int ldb, void* out_dev, int ldo, int M, int N, int K, const float* bias_dev, void* workspace_dev,
+                      size_t workspace_bytes, void* stream);
+
 /* 8-bit (e4m3) GEMM operands, the fp8 variant of the projections (the
  * reference's nn.Linear layers, model.py:138-141, 183-184, run at bf16 there;
  * the reference has no 8-bit path).

@@ -149,6 +149,7 @@ def bench_backward_gemms(m, n, k, reps, warmup=3):
     out = []
     for name, fn in (("dgrad", lambda: ops.gemm_t(dy, w, False, True)),
                      ("wgrad", lambda: ops.gemm_t(dy, a, True, True)),
+                     ("wgrad_splitk", lambda: ops.gemm_t_splitk(dy, a, True)),
                      ("gelu_grad_recompute", lambda: ops.gemm(a, w, L.EPI_BIAS_GELU_GRAD, bias=bias, res=dy))):
         ms = _time(fn, reps, warmup)
         out.append({"kernel": name, "m": m, "n": n, "k": k, "ms": ms, "tflops": 2 * m * n * k / ms / 1e9, **_clock()})

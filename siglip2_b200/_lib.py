@@ -55,6 +55,10 @@ SIGNATURES = {
     "siglip2_fmha_bwd_dsum": (_c_int, [_c_int, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp]),
     "siglip2_fmha_varlen_backward": (_c_int, [_c_int, _vp, _vp, _c_int, _c_int, _vp, _vp, _c_int, _c_int, _c_int,
                                               _vp, _vp, _vp, _vp]),
+    "siglip2_colsum_partial": (_c_int, [_c_int, _vp, _c_int, _c_int, _c_int, _c_int, _vp, _vp]),
+    "siglip2_gemm_t_workspace_size": (ctypes.c_size_t, [_c_int, _c_int, _c_int, _c_int, _c_int, _c_int]),
+    "siglip2_gemm_t_ws": (_c_int, [_c_int, _c_int, _c_int, _c_int, _vp, _c_int, _vp, _c_int, _vp, _c_int, _c_int,
+                                   _c_int, _c_int, _vp, _vp, ctypes.c_size_t, _vp]),
     "siglip2_quantize_e4m3": (_c_int, [_c_int, _vp, _c_int, _c_int, _c_int, _vp, _c_int, _vp, _vp]),
     "siglip2_gemm_e4m3": (_c_int, [_c_int, _c_int, _vp, _c_int, _vp, _vp, _c_int, _vp, _vp, _c_int, _c_int, _c_int,
                                    _c_int, _vp, _vp, _c_int, _vp]),

@@ -81,6 +81,13 @@ struct GemmParams {
   // e4m3 values (per-row scales of A, per-output-channel scales of B)
   const float* a_scale;
   const float* b_scale;
+  // split K (gemm_tc_kernel<..., kSplitK>): k_splits slices of k_per_split
+  // (a multiple of 128) K-elements each, slice s writes its fp32 partial
+  // product to part + s * M * ld_part; splitk_reduce_kernel sums them
+  int k_splits;
+  int k_per_split;
+  float* part;
+  int ld_part;
 };
 
 constexpr int kGemmBM = 128;
@@ -426,6 +433,88 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
 
 // LayerNorm row statistics of the A tiles (warps 6-9; thread r = row r of
 // this CTA's 128-row A half).  `ready[s]` signals that stage s has landed.
+// Split-K epilogue: the fp32 accumulator of one K slice straight to its
+// partial buffer (each thread one row, 128 contiguous bytes per 32-column
+// chunk), then the accumulator goes back to the MMA issuer.
+template <int BN>
+__device__ __forceinline__ void gemm_epilogue_part(const GemmParams& p, uint32_t tmem_base, uint32_t acc_stride,
+                                                   uint64_t* tfull, uint32_t tempty_addr0, uint32_t tempty_addr1,
+                                                   volatile int* abort_flag, int warp, int lane, int first_tile,
+                                                   int tile_step, int num_tiles, int mn_tiles, int n_tiles) {
+  constexpr int kPartCols = BN / 2;  // 8 warps: two per TMEM lane quarter, half the columns each
+  const int ew = warp - 2;
+  const int q = warp & 3;
+  const int part = ew / 4;
+  int t = 0;
+  for (int tile = first_tile; tile < num_tiles; tile += tile_step, ++t) {
+    const int buf = t & 1;
+    const uint32_t tph = (t >> 1) & 1;
+    const int split = tile / mn_tiles;
+    const int rem = tile - split * mn_tiles;
+    const int row = (rem / n_tiles) * kGemmBM + q * 32 + lane;
+    const int c0 = (rem % n_tiles) * BN + part * kPartCols;
+    if (*abort_flag || !mbar_wait(&tfull[buf], tph, 124)) {
+      *abort_flag = 1;
+      break;
+    }
+    tc_fence_after();
+    const uint32_t tbase = tmem_base + buf * acc_stride + part * kPartCols + (static_cast<uint32_t>(q * 32) << 16);
+    float* dst = p.part + (static_cast<size_t>(split) * p.M + row) * p.ld_part;
+#pragma unroll
+    for (int c = 0; c < kPartCols / 32; ++c) {
+      uint32_t r[32];
+      SG_TMEM_LD_32(tbase + c * 32, r);
+      tmem_ld_wait();
+      SG_REG_FENCE_32(r);
+      if (row < p.M) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int col = c0 + c * 32 + 4 * j;
+          if (col < p.N)  // N % 8 == 0
+            *reinterpret_cast<float4*>(dst + col) = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                                                __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+        }
+      }
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive_cluster(buf ? tempty_addr1 : tempty_addr0);
+  }
+}
+
+// out[m, n] = sum_s part[s][m][n] (+ bias[n]), the slices added in order;
+// 8 columns per thread
+template <typename T>
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ part, int splits, int M, int N,
+                                                            int ld_part, const float* __restrict__ bias,
+                                                            T* __restrict__ out, int ldo) {
+  const int nv = N / 8;
+  const size_t total = static_cast<size_t>(M) * nv;
+  const size_t slice = static_cast<size_t>(M) * ld_part;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int m = static_cast<int>(i / nv);
+    const int c = static_cast<int>(i - static_cast<size_t>(m) * nv) * 8;
+    const float* src = part + static_cast<size_t>(m) * ld_part + c;
+    float v[8];
+    if (bias) {
+      const float4 b0 = __ldg(reinterpret_cast<const float4*>(bias + c));
+      const float4 b1 = __ldg(reinterpret_cast<const float4*>(bias + c) + 1);
+      v[0] = b0.x; v[1] = b0.y; v[2] = b0.z; v[3] = b0.w; v[4] = b1.x; v[5] = b1.y; v[6] = b1.z; v[7] = b1.w;
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = 0.f;
+    }
+    for (int sp = 0; sp < splits; ++sp) {
+      const float4 a0 = __ldg(reinterpret_cast<const float4*>(src + sp * slice));
+      const float4 a1 = __ldg(reinterpret_cast<const float4*>(src + sp * slice) + 1);
+      v[0] += a0.x; v[1] += a0.y; v[2] += a0.z; v[3] += a0.w;
+      v[4] += a1.x; v[5] += a1.y; v[6] += a1.z; v[7] += a1.w;
+    }
+    store_vec(out + static_cast<size_t>(m) * ldo + c, v);
+  }
+}
+
 template <typename T, int STAGES, int SUB, bool kCluster>
 __device__ __forceinline__ void gemm_row_stats(const GemmParams& p, const uint8_t* smA, int stage_a_bytes,
                                                uint64_t* ready, uint64_t* empty, uint64_t* sfull, uint64_t* sempty,
@@ -495,7 +584,9 @@ __device__ __forceinline__ void gemm_row_stats(const GemmParams& p, const uint8_
 // Such a tile arrives as 64-column TMA boxes of 64 K-rows (128B swizzle),
 // one 8 KB chunk per 64 M (N) columns, and the UMMA reads it through an
 // MN-major descriptor (chunk stride 8 KB, 8-row groups 1 KB apart).
-template <typename T, int BN, int EPI, int SUB, bool kAT = false, bool kBT = false>
+// kSplitK: the tiles are (K slice, row tile, column tile); each writes its
+// fp32 partial product (gemm_epilogue_part) for splitk_reduce_kernel.
+template <typename T, int BN, int EPI, int SUB, bool kAT = false, bool kBT = false, bool kSplitK = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
@@ -503,6 +594,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   constexpr bool kLN = epi_has_stat_warps(EPI);  // statistics warps in this kernel
   constexpr bool kRes = epi_has_res(EPI);
   static_assert(!(kAT && kLN), "the statistics warps read K-major A tiles");
+  static_assert(!kSplitK || (EPI == kEpiBias && epi_warps(EPI) == 8), "split K: plain products only");
   using Cfg = GemmCfg<BN, SUB, EPI>;
   constexpr int EW = epi_warps(EPI);
   constexpr int STAGES = Cfg::kStages;
@@ -533,8 +625,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int lane = threadIdx.x & 31;
   const int m_tiles = (p.M + kGemmBM - 1) / kGemmBM;
   const int n_tiles = (p.N + BN - 1) / BN;
-  const int num_tiles = m_tiles * n_tiles;
-  const int nk = (p.K + kGemmBK * SUB - 1) / (kGemmBK * SUB);  // pipeline stages per tile
+  const int mn_tiles = m_tiles * n_tiles;
+  const int num_tiles = mn_tiles * (kSplitK ? p.k_splits : 1);
+  // first K element and pipeline stages of a tile (its K slice when split)
+  const auto tile_k0 = [&](int tile) { return kSplitK ? (tile / mn_tiles) * p.k_per_split : 0; };
+  const auto tile_nk = [&](int tile) {
+    const int k0 = tile_k0(tile);
+    const int klen = kSplitK ? min(p.K - k0, p.k_per_split) : p.K;
+    return (klen + kGemmBK * SUB - 1) / (kGemmBK * SUB);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -577,8 +676,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int issued = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile / n_tiles) * kGemmBM;
-        const int n0 = (tile % n_tiles) * BN;
+        const int rem = tile % mn_tiles;
+        const int m0 = (rem / n_tiles) * kGemmBM;
+        const int n0 = (rem % n_tiles) * BN;
+        const int k0 = tile_k0(tile), nk = tile_nk(tile);
         for (int kb = 0; kb < nk; ++kb) {
           if (*abort_flag || !mbar_wait(&empty[stage], phase ^ 1, 101)) {
             ok = false;
@@ -588,7 +689,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
 #pragma unroll
           for (int sub = 0; sub < SUB; ++sub) {
-            const int kx = (kb * SUB + sub) * kGemmBK;
+            const int kx = k0 + (kb * SUB + sub) * kGemmBK;
             uint8_t* sa = smA + stage * Cfg::kStageA + sub * Cfg::kSlabA;
             uint8_t* sb = smB + stage * Cfg::kStageB + sub * Cfg::kSlabB;
             if constexpr (kAT) {
@@ -641,6 +742,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * Cfg::kAccStride;
+        const int nk = tile_nk(tile);
         for (int kb = 0; kb < nk; ++kb) {
           if (*abort_flag || !mbar_wait(&full[stage], phase, 112)) {
             ok = false;
@@ -683,15 +785,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // TMEM -> registers -> fused math -> 64B-swizzled staging -> TMA store
     // (the residual, if any, arrives in the same staging buffer by TMA).
     const uint32_t te0 = mapa_shared(smem_u32(&tempty[0]), 0), te1 = mapa_shared(smem_u32(&tempty[1]), 0);
-    gemm_epilogue<T, BN, EPI, false>(p, &tmO, &tmR, tmem_base, Cfg::kAccStride, staging, resbar, tfull, te0, te1,
-                                     sfull, sempty, st_mean, st_rstd, abort_flag, warp, lane, blockIdx.x, gridDim.x,
-                                     num_tiles, n_tiles, kGemmBM, 0);
+    if constexpr (kSplitK)
+      gemm_epilogue_part<BN>(p, tmem_base, Cfg::kAccStride, tfull, te0, te1, abort_flag, warp, lane, blockIdx.x,
+                             gridDim.x, num_tiles, mn_tiles, n_tiles);
+    else
+      gemm_epilogue<T, BN, EPI, false>(p, &tmO, &tmR, tmem_base, Cfg::kAccStride, staging, resbar, tfull, te0, te1,
+                                       sfull, sempty, st_mean, st_rstd, abort_flag, warp, lane, blockIdx.x, gridDim.x,
+                                       num_tiles, n_tiles, kGemmBM, 0);
   } else {
     // ------------------------------------------------------------ LayerNorm row statistics
     if constexpr (kLN) {
       gemm_row_stats<T, STAGES, SUB, false>(p, smA, Cfg::kStageA, full, empty, sfull, sempty, st_mean, st_rstd,
                                        abort_flag, threadIdx.x - (2 + EW) * 32, lane, blockIdx.x, gridDim.x,
-                                       num_tiles, nk);
+                                       num_tiles, tile_nk(0));
     }
   }
 

@@ -499,4 +499,52 @@ __global__ void __launch_bounds__(256) layernorm_bwd_cols_kernel(const T* __rest
   }
 }
 
+// Column sums of x [rows, cols] in fp32 (the bias gradient of a Linear
+// layer: db = sum over tokens of dy), deterministic: grid (ceil(cols / 256),
+// chunks), chunk j writes part[j][c] = sum of its chunk_rows rows; each lane
+// owns 8 columns, the 8 warps of a CTA step through the chunk four rows at a
+// time and are reduced in shared memory in warp order; the caller sums the
+// chunks in order.
+template <typename T>
+__global__ void __launch_bounds__(256) colsum_part_kernel(const T* __restrict__ x, int ld, int rows, int cols,
+                                                          int chunk_rows, float* __restrict__ part) {
+  __shared__ float red[8][256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.x * 256 + 8 * lane;
+  const int r0 = blockIdx.y * chunk_rows;
+  const int r1 = min(rows, r0 + chunk_rows);
+  float b[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) b[k] = 0.f;
+  if (c < cols) {
+    int r = r0 + warp;
+    for (; r + 24 < r1; r += 32) {
+      float v[4][8];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) load8(x + static_cast<size_t>(r + 8 * u) * ld + c, v[u]);
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) b[k] += v[u][k];
+    }
+    for (; r < r1; r += 8) {
+      float v[8];
+      load8(x + static_cast<size_t>(r) * ld + c, v);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) b[k] += v[k];
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) red[warp][8 * lane + k] = b[k];
+  __syncthreads();
+  {
+    const int col = threadIdx.x;
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += red[w][col];  // fixed order
+    const int cc = blockIdx.x * 256 + col;
+    if (cc < cols) part[static_cast<size_t>(blockIdx.y) * cols + cc] = t;
+  }
+}
+
 }  // namespace sg

@@ -41,7 +41,7 @@ inline void set_pdl_attr(cudaLaunchAttribute* a) {
   a->val.programmaticStreamSerializationAllowed = 1;
 }
 
-template <typename T, int BN, int EPI, int SUB, bool kAT = false, bool kBT = false>
+template <typename T, int BN, int EPI, int SUB, bool kAT = false, bool kBT = false, bool kSplitK = false>
 int launch_gemm_tc(const GemmIO& io, const GemmParams& p, cudaStream_t stream) {
   CUtensorMap ta, tb, to, tr;
   // transposed operands are [K][M] / [K][N] in memory: 64 x 64 boxes
@@ -54,9 +54,9 @@ int launch_gemm_tc(const GemmIO& io, const GemmParams& p, cudaStream_t stream) {
   else tr = to;
   constexpr int threads = kGemmThreads;
   constexpr int smem = GemmCfg<BN, SUB, EPI>::kSmemBytes;
-  auto kern = gemm_tc_kernel<T, BN, EPI, SUB, kAT, kBT>;
+  auto kern = gemm_tc_kernel<T, BN, EPI, SUB, kAT, kBT, kSplitK>;
   SG_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem));
-  const int tiles = ((p.M + kGemmBM - 1) / kGemmBM) * ((p.N + BN - 1) / BN);
+  const int tiles = ((p.M + kGemmBM - 1) / kGemmBM) * ((p.N + BN - 1) / BN) * (kSplitK ? p.k_splits : 1);
   const int grid = tiles < sm_count() ? tiles : sm_count();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
@@ -144,6 +144,17 @@ int dispatch_epi(int epi, const GemmIO& io, const GemmParams& p, cudaStream_t s)
 // Transposed-operand GEMMs of the backward (one SM per 128 x 256 tile).
 template <typename T, bool kAT, bool kBT>
 int dispatch_epi_t(int epi, const GemmIO& io, const GemmParams& p, cudaStream_t s) {
+  if (p.k_splits > 1) {
+    // K sliced over more tiles than SMs would otherwise get; the partial
+    // products are summed (+ bias) in slice order by splitk_reduce_kernel
+    SG_TRY((launch_gemm_tc<T, 256, kEpiBias, 2, kAT, kBT, true>(io, p, s)));
+    const size_t total = static_cast<size_t>(p.M) * (p.N / 8);
+    const int grid = static_cast<int>(std::min<size_t>((total + 255) / 256, 8 * static_cast<size_t>(sm_count())));
+    splitk_reduce_kernel<T><<<grid, 256, 0, s>>>(p.part, p.k_splits, p.M, p.N, p.ld_part, p.bias,
+                                                 static_cast<T*>(io.out), io.ldo);
+    SG_LAUNCH_CHECK();
+    return SIGLIP2_OK;
+  }
   switch (epi) {
     case kEpiBias: return launch_gemm_tc<T, 256, kEpiBias, 2, kAT, kBT>(io, p, s);
     case kEpiBiasGeluGrad: return launch_gemm_tc<T, 256, kEpiBiasGeluGrad, 2, kAT, kBT>(io, p, s);
@@ -263,9 +274,40 @@ int sg_gemm_impl(int dtype, int epi, const void* a, int lda, const void* b, int 
 
 // out[M, N] = epi(op(A) . op(B)^T) with op(A) = A [M][K] or, trans_a, A
 // stored [K][M]; op(B) = B [N][K] or, trans_b, B stored [K][N].
+// K slices for a transposed-operand GEMM whose 128 x 256 tiles would leave
+// SMs idle (the weight gradients: few output tiles, long K = tokens).  In
+// units of the GEMM's time at full occupancy, S slices cost 1 / (tile waves
+// filled) for the products plus, for S > 1, the fp32 partials written and
+// read back: 8 S M N bytes against 2 M N K FLOPs, i.e. about 880 S / K at
+// the measured ~1.1 PFLOP/s per-tile rate and ~5 TB/s.  The cheapest S
+// (slices of at least 1024 K-elements, S <= 8) is taken.
+struct KSplit {
+  int splits;
+  int k_per_split;
+};
+KSplit choose_k_splits(int M, int N, int K) {
+  const int tiles = ((M + kGemmBM - 1) / kGemmBM) * ((N + 255) / 256);
+  const int sms = sm_count();
+  KSplit best{1, K};
+  double best_cost = 1e30;
+  for (int s = 1; s <= 8; ++s) {
+    const int kps = ((K + s - 1) / s + 127) / 128 * 128;
+    const int splits = (K + kps - 1) / kps;
+    if (splits != s || (s > 1 && kps < 1024)) continue;
+    const long long work = static_cast<long long>(tiles) * s;
+    const long long waves = (work + sms - 1) / sms;
+    const double cost = static_cast<double>(waves * sms) / static_cast<double>(work) + (s > 1 ? 880.0 * s / K : 0.0);
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = {s, kps};
+    }
+  }
+  return best;
+}
+
 int sg_gemm_t_impl(int dtype, int epi, int trans_a, int trans_b, const void* a, int lda, const void* b, int ldb,
                    void* out, int ldo, int M, int N, int K, const float* bias, const void* res, int ldr,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, void* workspace = nullptr, size_t workspace_bytes = 0) {
   SG_CHECK_ARG(M >= 0 && N > 0 && K > 0, "bad GEMM shape M=%d N=%d K=%d", M, N, K);
   if (M == 0) return SIGLIP2_OK;
   SG_CHECK_ARG(a && b && out, "null operand");
@@ -287,6 +329,20 @@ int sg_gemm_t_impl(int dtype, int epi, int trans_a, int trans_b, const void* a, 
   p.N = N;
   p.K = K;
   p.bias = bias;
+  p.k_splits = 1;
+  if (workspace != nullptr && epi == kEpiBias && trans_b) {
+    const KSplit ks = choose_k_splits(M, N, K);
+    if (ks.splits > 1) {
+      const size_t need = static_cast<size_t>(ks.splits) * M * N * sizeof(float);
+      if (workspace_bytes < need)
+        return set_error(SIGLIP2_ERR_ARG, "split-K GEMM needs %zu workspace bytes, got %zu", need, workspace_bytes);
+      if (!aligned16(workspace)) return set_error(SIGLIP2_ERR_ALIGN, "workspace must be 16-byte aligned");
+      p.k_splits = ks.splits;
+      p.k_per_split = ks.k_per_split;
+      p.part = static_cast<float*>(workspace);
+      p.ld_part = N;
+    }
+  }
   GemmIO io{a, lda, b, ldb, out, ldo, res, ldr};
   const bool bf = dtype == SIGLIP2_BF16;
   if (!trans_a && !trans_b)
@@ -1086,6 +1142,38 @@ int siglip2_gemm_t(int dtype, int epilogue, int trans_a, int trans_b, const void
                    int ldr, void* stream) {
   return sg_gemm_t_impl(dtype, epilogue, trans_a, trans_b, a_dev, lda, b_dev, ldb, out_dev, ldo, M, N, K, bias_dev,
                         res_dev, ldr, static_cast<cudaStream_t>(stream));
+}
+
+int siglip2_colsum_partial(int dtype, const void* x_dev, int ld, int rows, int cols, int chunk_rows, float* part_dev,
+                           void* stream) {
+  SG_CHECK_ARG(x_dev && part_dev && rows >= 0 && cols > 0 && ld >= cols && chunk_rows > 0, "bad colsum arguments");
+  if (!aligned16(x_dev) || cols % 8 || ld % 8)
+    return set_error(SIGLIP2_ERR_ALIGN, "colsum: x 16-byte aligned, cols and ld multiples of 8");
+  if (rows == 0) return SIGLIP2_OK;
+  const dim3 grid((cols + 255) / 256, (rows + chunk_rows - 1) / chunk_rows);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case SIGLIP2_BF16: colsum_part_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x_dev), ld, rows, cols, chunk_rows, part_dev); break;
+    case SIGLIP2_F16: colsum_part_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(x_dev), ld, rows, cols, chunk_rows, part_dev); break;
+    case SIGLIP2_F32: colsum_part_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(x_dev), ld, rows, cols, chunk_rows, part_dev); break;
+    default: return set_error(SIGLIP2_ERR_ARG, "unknown dtype %d", dtype);
+  }
+  SG_LAUNCH_CHECK();
+  return SIGLIP2_OK;
+}
+
+size_t siglip2_gemm_t_workspace_size(int epilogue, int trans_a, int trans_b, int M, int N, int K) {
+  if (M <= 0 || N <= 0 || K <= 0 || epilogue != kEpiBias || !trans_b) return 0;
+  (void)trans_a;
+  const KSplit ks = choose_k_splits(M, N, K);
+  return ks.splits > 1 ? static_cast<size_t>(ks.splits) * M * N * sizeof(float) : 0;
+}
+
+int siglip2_gemm_t_ws(int dtype, int epilogue, int trans_a, int trans_b, const void* a_dev, int lda, const void* b_dev,
+                      int ldb, void* out_dev, int ldo, int M, int N, int K, const float* bias_dev, void* workspace_dev,
+                      size_t workspace_bytes, void* stream) {
+  return sg_gemm_t_impl(dtype, epilogue, trans_a, trans_b, a_dev, lda, b_dev, ldb, out_dev, ldo, M, N, K, bias_dev,
+                        nullptr, 0, static_cast<cudaStream_t>(stream), workspace_dev, workspace_bytes);
 }
 
 int siglip2_quantize_e4m3(int dtype, const void* x_dev, int ldx, int rows, int cols, void* q_dev, int ldq,

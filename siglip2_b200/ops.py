@@ -68,6 +68,42 @@ def gemm_t(a: torch.Tensor, b: torch.Tensor, trans_a: bool, trans_b: bool, epilo
     return out
 
 
+def gemm_t_splitk(a: torch.Tensor, b: torch.Tensor, trans_a: bool, bias=None,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """``siglip2_gemm_t_ws``: ``op(a) @ b`` (+ bias) as ``gemm_t`` with
+    ``trans_b`` (``b`` is [K, N]), K split over a workspace from the caching
+    allocator when the output has too few tiles to fill the SMs (the weight
+    gradients)."""
+    _need_cuda(a, b, bias, out)
+    assert a.dim() == 2 and b.dim() == 2 and a.stride(1) == 1 and b.stride(1) == 1
+    M, K = (a.shape[1], a.shape[0]) if trans_a else a.shape
+    Kb, N = b.shape
+    assert K == Kb, (a.shape, b.shape, trans_a)
+    if out is None:
+        out = torch.empty((M, N), dtype=a.dtype, device=a.device)
+    nbytes = L.load().siglip2_gemm_t_workspace_size(L.EPI_BIAS, int(trans_a), 1, M, N, K)
+    ws = torch.empty(max(nbytes, 16) // 4, dtype=torch.float32, device=a.device) if nbytes else None
+    L.call("siglip2_gemm_t_ws", dtype_code(a.dtype), L.EPI_BIAS, int(trans_a), 1, a.data_ptr(), a.stride(0),
+           b.data_ptr(), b.stride(0), out.data_ptr(), out.stride(0), M, N, K, _ptr(bias), _ptr(ws), nbytes,
+           _stream(a.device))
+    return out
+
+
+def colsum(x: torch.Tensor, chunk_rows: int = 256) -> torch.Tensor:
+    """``siglip2_colsum_partial`` + an in-order sum of the chunk partials:
+    the fp32 column sums of ``x`` [rows, cols] (a bias gradient)."""
+    _need_cuda(x)
+    assert x.dim() == 2 and x.stride(1) == 1
+    rows, cols = x.shape
+    chunks = max(1, -(-rows // chunk_rows))
+    part = torch.empty((chunks, cols), dtype=torch.float32, device=x.device)
+    if rows == 0:
+        return torch.zeros(cols, dtype=torch.float32, device=x.device)
+    L.call("siglip2_colsum_partial", dtype_code(x.dtype), x.data_ptr(), x.stride(0), rows, cols, chunk_rows,
+           part.data_ptr(), _stream(x.device))
+    return part.sum(0)
+
+
 def quantize_e4m3(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """``siglip2_quantize_e4m3``: per-row e4m3 codes of ``x`` [rows, cols]
     (fp32 / bf16 / f16) as a ``torch.float8_e4m3fn`` tensor and the fp32

@@ -57,7 +57,11 @@ def _(a, w, epilogue, bias, res, c1, c2, eps):
 def gemm_t(a: Tensor, b: Tensor, trans_a: bool, trans_b: bool, epilogue: int, bias: Optional[Tensor],
            res: Optional[Tensor]) -> Tensor:
     """``siglip2_gemm_t``: ``epilogue(op(a) @ op(b).T)``, op = transpose when
-    the flag is set (the operand is read as MN-major tiles, not copied)."""
+    the flag is set (the operand is read as MN-major tiles, not copied).
+    Plain products with a transposed ``b`` (dgrad, wgrad) go through
+    ``siglip2_gemm_t_ws``, which splits K when the output has few tiles."""
+    if trans_b and epilogue == L.EPI_BIAS and res is None:
+        return ops.gemm_t_splitk(a, b, trans_a, bias)
     return ops.gemm_t(a, b, trans_a, trans_b, epilogue, bias, res)
 
 
@@ -102,6 +106,24 @@ def _matmul_nt(a: Tensor, b: Tensor) -> Tensor:
     return gemm(a, b, L.EPI_BIAS, zero, None, None, None, 0.0)[:, :N]
 
 
+@torch.library.custom_op("siglip2_b200::colsum", mutates_args=(), device_types="cuda")
+def colsum(x: Tensor) -> Tensor:
+    """``siglip2_colsum_partial``: fp32 column sums of ``x`` [rows, cols] (a
+    bias gradient), deterministic."""
+    return ops.colsum(x.contiguous())
+
+
+@colsum.register_fake
+def _(x):
+    return x.new_empty((x.shape[1],), dtype=torch.float32)
+
+
+def _bias_grad(g: Tensor) -> Tensor:
+    if g.dim() == 2 and g.shape[1] % 8 == 0 and g.dtype in (torch.bfloat16, torch.float16, torch.float32):
+        return colsum(g)
+    return g.sum(0, dtype=torch.float32)
+
+
 def _gemm_setup(ctx, inputs, output):
     a, w, epilogue, bias, res, c1, c2, eps = inputs
     ctx.epilogue = epilogue
@@ -144,7 +166,7 @@ def _gemm_backward(ctx, grad):
     else:
         da = _matmul_nt(g, w.t()) if ctx.needs_input_grad[0] else None
         dw = _matmul_nt(g.t(), a.t()) if ctx.needs_input_grad[1] else None
-    db = g.sum(0, dtype=torch.float32) if ctx.needs_input_grad[3] else None
+    db = _bias_grad(g) if ctx.needs_input_grad[3] else None
     dres = grad if ctx.needs_input_grad[4] else None
     return da, dw, None, db, dres, None, None, None
 
@@ -410,7 +432,7 @@ def _patch_embed_backward(ctx, grad):
     else:
         d_patches = _matmul_nt(grad, w.t()) if ctx.needs_input_grad[0] else None
         dw = _matmul_nt(grad.t(), patches.t()) if ctx.needs_input_grad[1] else None
-    db = grad.sum(0, dtype=torch.float32) if ctx.needs_input_grad[2] else None
+    db = _bias_grad(grad) if ctx.needs_input_grad[2] else None
     dtable = None
     if ctx.needs_input_grad[3]:
         G2, D = table.shape

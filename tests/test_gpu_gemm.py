@@ -275,3 +275,32 @@ def test_gemm_transposed_rejects_bad_args():
     with pytest.raises(L.Siglip2Error):  # tensor-core only
         ops.gemm_t(torch.zeros(64, 64, device="cuda"), torch.zeros(64, 128, device="cuda"), False, True)
     L.check(L.load().siglip2_check_device(1))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("tokens,N_out,K_in", [(16384, 4304, 1152), (16384, 1152, 1152), (39178, 1152, 4304),
+                                               (4097, 1152, 1152), (9000, 768, 768)])
+def test_gemm_splitk_weight_gradient(dtype, tokens, N_out, K_in):
+    """siglip2_gemm_t_ws: the weight gradient dW = dY^T A with K (= tokens)
+    split over an fp32 workspace when the [N_out, K_in] output has few tiles,
+    the slices summed in order (+ bias): against fp32 torch, against the
+    unsplit siglip2_gemm_t, and bit-identical across two calls."""
+    lib = L.load()
+    nbytes = lib.siglip2_gemm_t_workspace_size(L.EPI_BIAS, 1, 1, N_out, K_in, tokens)
+    assert nbytes > 0, "these shapes leave SMs idle without a split"
+    g = torch.Generator(device="cuda").manual_seed(tokens + N_out)
+    dy = (torch.randn(tokens, N_out, device="cuda", generator=g) * 0.1).to(dtype)
+    a = torch.randn(tokens, K_in, device="cuda", generator=g).to(dtype)
+    bias = torch.randn(K_in, device="cuda", generator=g)
+    dw = ops.gemm_t_splitk(dy, a, True)
+    dw2 = ops.gemm_t_splitk(dy, a, True)
+    dwb = ops.gemm_t_splitk(dy, a, True, bias=bias)
+    plain = ops.gemm_t(dy, a, True, True)
+    torch.cuda.synchronize()
+    ref = dy.float().T @ a.float()
+    _close(dw, ref)
+    _close(dwb, ref + bias)
+    assert torch.equal(dw, dw2)
+    # the same fp32 sums in another order, one rounding to 8 significant bits
+    # (bf16): at most a couple of ulps of the largest magnitude apart
+    assert (dw.float() - plain.float()).abs().max().item() <= 2 ** -6 * ref.abs().max().item()

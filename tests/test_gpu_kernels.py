@@ -208,3 +208,18 @@ def test_layernorm_backward_matches_autograd(dtype, rows, D):
     assert (dx.float() - xr.grad).abs().max().item() <= tol * scale
     assert torch.allclose(dg, gr.grad, rtol=1e-3, atol=1e-3 * max(1.0, rows ** 0.5))
     assert torch.allclose(db, br.grad, rtol=1e-3, atol=1e-3 * max(1.0, rows ** 0.5))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("rows,cols", [(16384, 4304), (1, 8), (1000, 1152), (257, 3456)])
+def test_colsum_bias_gradient(dtype, rows, cols):
+    """siglip2_colsum_partial (+ the in-order chunk sum): fp32 column sums
+    against torch's fp32 sum of the same values, identical on a second call."""
+    g = torch.Generator(device="cuda").manual_seed(rows + cols)
+    x = torch.randn(rows, cols, device="cuda", generator=g).to(dtype)
+    s1 = ops.colsum(x)
+    s2 = ops.colsum(x)
+    ref = x.double().sum(0)
+    torch.cuda.synchronize()
+    assert s1.dtype == torch.float32 and torch.equal(s1, s2)
+    assert (s1.double() - ref).abs().max().item() < 1e-5 * rows ** 0.5 * x.float().abs().max().item() + 1e-6
