@@ -843,7 +843,10 @@ struct Gemm2Cfg {
 // maps and 128-byte rows (a 64-wide slab of pairs is 128 K-elements); the
 // MMAs run kind::f8f6f4 (32 K-elements each) and the epilogue applies
 // a_scale / b_scale; T is the output type.  p.K counts pairs.
-template <typename T, int BN, int EPI, int SUB, bool kF8 = false>
+// kBT: B stored transposed, [K][N] (N contiguous), as the backward's dgrad
+// reads the forward weight: each CTA's half of B arrives as 64-column x
+// 64-K-row boxes (8 KB chunks) and the MMA reads it as an MN-major operand.
+template <typename T, int BN, int EPI, int SUB, bool kF8 = false, bool kBT = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR,
@@ -851,7 +854,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   constexpr bool kLN = epi_has_stat_warps(EPI);  // statistics warps in this kernel
   constexpr bool kRes = epi_has_res(EPI);
   static_assert(!(kF8 && (kLN || epi_is_ln(EPI))), "8-bit operands: bias epilogues only");
+  static_assert(!(kBT && (kF8 || kLN)), "MN-major B: 16-bit operands, no statistics warps");
   using Cfg = Gemm2Cfg<BN, SUB, EPI>;
+  constexpr int kChunk = 64 * kGemmBK * 2;  // one MN-major chunk of B: 64 columns x 64 K-rows
   constexpr int EW = epi_warps(EPI);
   constexpr int STAGES = Cfg::kStages;
   // instruction-descriptor format bits: bf16 (1) or f16 (0) for kind::f16, e4m3 (0) for kind::f8f6f4
@@ -948,7 +953,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int sub = 0; sub < SUB; ++sub) {
             const int kx = (kb * SUB + sub) * kGemmBK;
             tma_load_2d_pair(smA + stage * Cfg::kStageA + sub * Cfg::kSlabA, &tmA, fbar, kx, m0);
-            tma_load_2d_pair(smB + stage * Cfg::kStageB + sub * Cfg::kSlabB, &tmB, fbar, kx, n0);
+            if constexpr (kBT) {
+#pragma unroll
+              for (int c = 0; c < BN / 2 / 64; ++c)
+                tma_load_2d_pair(smB + stage * Cfg::kStageB + sub * Cfg::kSlabB + c * kChunk, &tmB, fbar, n0 + 64 * c,
+                                 kx);
+            } else {
+              tma_load_2d_pair(smB + stage * Cfg::kStageB + sub * Cfg::kSlabB, &tmB, fbar, kx, n0);
+            }
           }
           ++issued;
           if (++stage == STAGES) {
@@ -983,7 +995,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * Cfg::kAccStride;
-        const uint32_t idesc = make_idesc(2 * kGemmBM, tile_width(tile % n_tiles), kBF16, false, false);
+        const uint32_t idesc = make_idesc(2 * kGemmBM, tile_width(tile % n_tiles), kBF16, false, kBT);
         for (int kb = 0; kb < nk; ++kb) {
           if (*abort_flag || !mbar_wait<true>(&full[stage], phase, 152)) {
             ok = false;
@@ -1002,12 +1014,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int sub = 0; sub < SUB; ++sub) {
 #pragma unroll
             for (int k = 0; k < kGemmBK / 16; ++k) {
+              // K-major: 16 K-elements = 32 bytes along the row; MN-major: 16 K-rows = 2 KB
+              const uint64_t bd = kBT ? smem_desc(b_base + sub * Cfg::kSlabB + k * 2048, kChunk, 1024, kSw128)
+                                      : kmajor_desc(b_base + sub * Cfg::kSlabB + k * 32, 128);
               if constexpr (kF8)
-                umma_ss_pair_f8(d_tmem, kmajor_desc(a_base + sub * Cfg::kSlabA + k * 32, 128),
-                                kmajor_desc(b_base + sub * Cfg::kSlabB + k * 32, 128), idesc, (kb | sub | k) != 0);
+                umma_ss_pair_f8(d_tmem, kmajor_desc(a_base + sub * Cfg::kSlabA + k * 32, 128), bd, idesc,
+                                (kb | sub | k) != 0);
               else
-                umma_ss_pair(d_tmem, kmajor_desc(a_base + sub * Cfg::kSlabA + k * 32, 128),
-                             kmajor_desc(b_base + sub * Cfg::kSlabB + k * 32, 128), idesc, (kb | sub | k) != 0);
+                umma_ss_pair(d_tmem, kmajor_desc(a_base + sub * Cfg::kSlabA + k * 32, 128), bd, idesc,
+                             (kb | sub | k) != 0);
             }
           }
           umma_commit_pair_mc(&empty[stage], 0x3);

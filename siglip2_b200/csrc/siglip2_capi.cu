@@ -73,17 +73,19 @@ int launch_gemm_tc(const GemmIO& io, const GemmParams& p, cudaStream_t stream) {
 }
 
 // 2-SM variant: clusters of 2 CTAs, one pair per 2 SMs, 256 x BN tiles.
-template <typename T, int BN, int EPI, int SUB, bool kF8 = false>
+template <typename T, int BN, int EPI, int SUB, bool kF8 = false, bool kBT = false>
 int launch_gemm_tc2(const GemmIO& io, const GemmParams& p, cudaStream_t stream) {
   CUtensorMap ta, tb, to, tr;
   SG_TRY(make_tmap_2d(&ta, io.a, 2, p.M, p.K, io.lda, kGemmBM, kGemmBK));
-  SG_TRY(make_tmap_2d(&tb, io.b, 2, p.N, p.K, io.ldb, BN / 2, kGemmBK));
+  // transposed B is [K][N] in memory: 64 x 64 boxes
+  if (kBT) SG_TRY(make_tmap_2d(&tb, io.b, 2, p.K, p.N, io.ldb, kGemmBK, 64));
+  else SG_TRY(make_tmap_2d(&tb, io.b, 2, p.N, p.K, io.ldb, BN / 2, kGemmBK));
   SG_TRY(make_tmap_2d(&to, io.out, 2, p.M, p.N, io.ldo, 32, kEpiCols));
   if (epi_has_res(EPI)) SG_TRY(make_tmap_2d(&tr, io.res, 2, p.M, p.N, io.ldr, 32, kEpiCols));
   else tr = to;
   constexpr int threads = kGemmThreads;
   constexpr int smem = Gemm2Cfg<BN, SUB, EPI>::kSmemBytes;
-  auto kern = gemm_tc2_kernel<T, BN, EPI, SUB, kF8>;
+  auto kern = gemm_tc2_kernel<T, BN, EPI, SUB, kF8, kBT>;
   SG_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem));
   const int tiles = ((p.M + 2 * kGemmBM - 1) / (2 * kGemmBM)) * ((p.N + BN - 1) / BN);
   const int pairs = std::min(tiles, sm_count() / 2);
@@ -155,6 +157,9 @@ int dispatch_epi_t(int epi, const GemmIO& io, const GemmParams& p, cudaStream_t 
     SG_LAUNCH_CHECK();
     return SIGLIP2_OK;
   }
+  // dgrad (K-major A, MN-major B): on CTA pairs like the forward's GEMMs
+  if (!kAT && kBT && epi == kEpiBias && g_gemm_variant.load() != 1)
+    return launch_gemm_tc2<T, 256, kEpiBias, 2, false, true>(io, p, s);
   switch (epi) {
     case kEpiBias: return launch_gemm_tc<T, 256, kEpiBias, 2, kAT, kBT>(io, p, s);
     case kEpiBiasGeluGrad: return launch_gemm_tc<T, 256, kEpiBiasGeluGrad, 2, kAT, kBT>(io, p, s);
