@@ -66,25 +66,13 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return y;
 }
 
-// packed fp32 pair arithmetic (sm_100): two lanes of FFMA / FADD per issue
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
-  float2 d;
-  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
-      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-  return d;
-}
-__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
-  float2 d;
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "add.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return d;
-}
+// keeps the compiler from using tcgen05.ld destination registers before the
+// tcgen05.wait::ld that makes them valid
+#define SG_REG_FENCE_16(r)                                                                               \
+  asm volatile(""                                                                                        \
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),       \
+                 "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),   \
+                 "+r"(r[14]), "+r"(r[15]))
 
 template <int HDP>
 struct FmhaCfg {
@@ -435,11 +423,19 @@ __global__ void __launch_bounds__(192, 2)
       // softmax_k = exp2(s_k * scale_log2 - lse2) with lse2 = m + log2(l)
       if (p.lse != nullptr && row_ok) p.lse[static_cast<size_t>(row) * H + head] = m_use + log2f(l);
       T* orow = reinterpret_cast<T*>(p.out) + static_cast<size_t>(row) * p.ld_out + head * p.head_dim;
+      // the whole O row in one TMEM round trip, then O is free for the next
+      // item's first PV while this row is scaled and stored
+      uint32_t ou[HDP];
+#pragma unroll
+      for (int c = 0; c < HDP / 16; ++c) SG_TMEM_LD_16(tmem + C::kColO + c * 16 + lane_off, (ou + c * 16));
+      tmem_ld_wait();
+#pragma unroll
+      for (int c = 0; c < HDP / 16; ++c) SG_REG_FENCE_16((ou + c * 16));
+      tc_fence_before();
+      mbar_arrive(o_free);
 #pragma unroll
       for (int c = 0; c < HDP / 16; ++c) {
-        uint32_t u[16];
-        SG_TMEM_LD_16(tmem + C::kColO + c * 16 + lane_off, u);
-        tmem_ld_wait();
+        const uint32_t* u = ou + c * 16;
         if (row_ok) {
 #pragma unroll
           for (int gg = 0; gg < 2; ++gg) {
@@ -466,9 +462,6 @@ __global__ void __launch_bounds__(192, 2)
           }
         }
       }
-      // O is in registers: the next item's first PV may overwrite it
-      tc_fence_before();
-      mbar_arrive(o_free);
     }
     if (!ok) *abort_flag = 1;
   }

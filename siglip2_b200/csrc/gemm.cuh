@@ -269,7 +269,8 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
     // sums over this warp's columns of the rounded outputs minus the first of
     // them (kRsOut): shifted sums keep the slot variance exact when the row's
     // mean is large against its spread
-    float rs1 = 0.f, rs2 = 0.f, rs_shift = 0.f;
+    float rs_shift = 0.f;
+    float2 rs1v = make_float2(0.f, 0.f), rs2v = make_float2(0.f, 0.f);
     AxisTaps ay{0, 0, 0.f, 1.f, 0.f}, ax{0, 0, 0.f, 1.f, 0.f};  // position-embedding taps of this row (kPos)
     if constexpr (kPos) {
       if (my_row < p.M) {
@@ -310,17 +311,27 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
           float a[32], b[32];
           load_param32(p.c1, col0, p.N, a);
           load_param32(p.c2, col0, p.N, b);
+          // column pairs in packed f32x2 issues (lane-wise the same roundings)
+          const float2 nmu2 = make_float2(-mu, -mu), rstd2 = make_float2(rstd, rstd);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            v[j] = fmaf(rstd, fmaf(-mu, a[j], v[j]), b[j]);
-            if constexpr (kGelu) v[j] = gelu_tanh(v[j]);
+          for (int j = 0; j < 32; j += 2) {
+            float2 t = ffma2(rstd2, ffma2(nmu2, make_float2(a[j], a[j + 1]), make_float2(v[j], v[j + 1])),
+                             make_float2(b[j], b[j + 1]));
+            if constexpr (kGelu) t = gelu_tanh2(t);
+            v[j] = t.x;
+            v[j + 1] = t.y;
           }
         } else {
           float a[32];
           if constexpr (kScale) {
             load_param32(p.b_scale, col0, p.N, a);
+            const float2 as2 = make_float2(a_s, a_s);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] *= a_s * a[j];
+            for (int j = 0; j < 32; j += 2) {
+              const float2 t = fmul2(make_float2(v[j], v[j + 1]), fmul2(as2, make_float2(a[j], a[j + 1])));
+              v[j] = t.x;
+              v[j + 1] = t.y;
+            }
           }
           if (p.bias) {
             load_param32(p.bias, col0, p.N, a);
@@ -329,9 +340,11 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
             for (int j = 0; j < 32; ++j) a[j] = 0.f;
           }
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            v[j] += a[j];
-            if constexpr (kGelu) v[j] = gelu_tanh(v[j]);
+          for (int j = 0; j < 32; j += 2) {
+            float2 t = fadd2(make_float2(v[j], v[j + 1]), make_float2(a[j], a[j + 1]));
+            if constexpr (kGelu) t = gelu_tanh2(t);
+            v[j] = t.x;
+            v[j + 1] = t.y;
           }
         }
         if constexpr (kPos) {
@@ -374,8 +387,9 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
               v[g * 8 + 2 * h] = f.x * gelu_tanh_grad(v[g * 8 + 2 * h]);
               v[g * 8 + 2 * h + 1] = f.y * gelu_tanh_grad(v[g * 8 + 2 * h + 1]);
             } else {
-              v[g * 8 + 2 * h] += f.x;
-              v[g * 8 + 2 * h + 1] += f.y;
+              const float2 t = fadd2(make_float2(v[g * 8 + 2 * h], v[g * 8 + 2 * h + 1]), f);
+              v[g * 8 + 2 * h] = t.x;
+              v[g * 8 + 2 * h + 1] = t.y;
             }
           }
         }
@@ -396,9 +410,10 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
             for (int h2 = 0; h2 < 4; ++h2) {
               const float2 f = Pack2<T>::unpack(ow[h2]);
               if (c == 0 && g == 0 && h2 == 0) rs_shift = f.x;
-              const float a0 = f.x - rs_shift, a1 = f.y - rs_shift;
-              rs1 += a0 + a1;
-              rs2 = fmaf(a0, a0, fmaf(a1, a1, rs2));
+              // even and odd columns in the two lanes of packed issues
+              const float2 d = fadd2(f, make_float2(-rs_shift, -rs_shift));
+              rs1v = fadd2(rs1v, d);
+              rs2v = ffma2(d, d, rs2v);
             }
           }
         }
@@ -424,7 +439,7 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
       // this warp's column block is one slot (block width kPartCols = BN / 2)
       if (my_row < p.M && c0 < p.N)
         p.rs_acc[static_cast<size_t>(my_row) * p.rs_ld + c0 / kPartCols] =
-            slot_stats_from_shifted(rs1, rs2, rs_shift, min(kPartCols, p.N - c0));
+            slot_stats_from_shifted(rs1v.x + rs1v.y, rs2v.x + rs2v.y, rs_shift, min(kPartCols, p.N - c0));
     }
   }
   if (lane == 0) tma_store_wait_all<0>();

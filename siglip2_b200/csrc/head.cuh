@@ -137,143 +137,272 @@ __global__ void head_pool_kernel(const T* __restrict__ x, int D, int H, const in
 }
 
 // ---------------------------------------------------------------------------
-// Parallel form of the pooling (used by siglip2_head_pool / the forward):
-//   head_scores_kernel: scores[t][h] = x_t . u_h for every packed token t,
-//     one warp per token, u staged in shared memory; grid over all tokens.
-//   head_pool_rows_kernel: one CTA per (image, 64-column chunk): per-head max
-//     and normaliser of the image's scores, then rows of x and their softmax
-//     weights staged through shared memory 32 rows at a time; thread
-//     (head, 4 columns) accumulates sum_j p_jh x_j.
+// Parallel form of the pooling (used by the forward):
+//   head_scores_kernel: scores[t][h] = x_t . u_h for every packed token t.
+//     Each warp takes 4 tokens at a time and lane l owns the 4-column groups
+//     l, l + 32, ... of D (loads two groups ahead of the FMAs), so every
+//     float4 of u read from shared memory feeds 16 FMAs (4 tokens x 4
+//     columns).  The 64 partial sums of a lane (4 tokens x 16 heads) are then
+//     reduce-scattered across the warp (62 shuffles): lane l ends with the
+//     totals of entries 2l and 2l + 1, i.e. token l / 8, heads 2 (l % 8) and
+//     2 (l % 8) + 1.
+//   head_pool_rows_kernel: one CTA per (image, 128-column chunk): per-head
+//     max and normaliser of the image's scores (one online pass over
+//     coalesced score rows, 16 loads in flight per thread), then the softmax
+//     weights of 64 rows at a time in shared memory (double-buffered: the
+//     next block's scores load while this block runs).  Warp w takes rows
+//     w, w + 4, ... of each block (16 row loads in flight per lane) for all
+//     16 heads and lane c columns 4c..4c+3 of the chunk, 64 FMAs per 8-byte
+//     load; the four warps' partial sums are added in a fixed order at the
+//     end, so the result is deterministic.
 // ---------------------------------------------------------------------------
+// 4 consecutive elements: one 8-byte load (16-bit types) or one 16-byte load
+// (fp32), kept raw until used
 template <typename T>
-__global__ void head_scores_kernel(const T* __restrict__ x, int D, int H, const int* __restrict__ cu, int B,
-                                   int pad_P, const int* __restrict__ tok_img, int N, const float* __restrict__ u,
-                                   float* __restrict__ scores) {
-  extern __shared__ float su[];  // [H][D]
-  for (int i = threadIdx.x; i < H * D; i += blockDim.x) su[i] = u[i];
+struct Raw4 {
+  using type = uint2;
+};
+template <>
+struct Raw4<float> {
+  using type = float4;
+};
+template <typename T>
+__device__ __forceinline__ T from_float(float v) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    return __float2bfloat16_rn(v);
+  } else if constexpr (std::is_same<T, __half>::value) {
+    return __float2half_rn(v);
+  } else {
+    return v;
+  }
+}
+template <typename T>
+__device__ __forceinline__ typename Raw4<T>::type load_raw4(const T* p) {
+  return *reinterpret_cast<const typename Raw4<T>::type*>(p);
+}
+template <typename T>
+__device__ __forceinline__ void unpack_raw4(const typename Raw4<T>::type& r, float* f) {
+  if constexpr (sizeof(T) == 4) {
+    f[0] = r.x;
+    f[1] = r.y;
+    f[2] = r.z;
+    f[3] = r.w;
+  } else {
+    const float2 a = Pack2<T>::unpack(r.x), b = Pack2<T>::unpack(r.y);
+    f[0] = a.x;
+    f[1] = a.y;
+    f[2] = b.x;
+    f[3] = b.y;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) head_scores_kernel(const T* __restrict__ x, int D, int H,
+                                                          const int* __restrict__ cu, int pad_P,
+                                                          const int* __restrict__ tok_img, int N,
+                                                          const float* __restrict__ u, float* __restrict__ scores) {
+  extern __shared__ float su[];  // [16][D]; heads past H are zero
+  for (int i = threadIdx.x; i < 16 * D; i += blockDim.x) su[i] = i < H * D ? u[i] : 0.f;
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-  const int nvec = D / 8;
-  for (int t = blockIdx.x * nwarps + warp; t < N; t += gridDim.x * nwarps) {
-    size_t row = static_cast<size_t>(t);
-    if (pad_P > 0) {
-      const int b = tok_img[t];
-      row = static_cast<size_t>(b) * pad_P + (t - cu[b]);
-    }
-    const T* xr = x + row * D;
-    float acc[16];
+  const int ngroups = D >> 2;
+  using R = typename Raw4<T>::type;
+  for (int t0 = (blockIdx.x * nwarps + warp) * 4; t0 < N; t0 += gridDim.x * nwarps * 4) {
+    const T* xr[4];
+    bool ok[4];
 #pragma unroll
-    for (int h = 0; h < 16; ++h) acc[h] = 0.f;
-    for (int v = lane; v < nvec; v += 32) {
-      float f[8];
-      if constexpr (sizeof(T) == 4) {
-        load_vec(xr + v * 8, f);
-        load_vec(xr + v * 8 + 4, f + 4);
-      } else {
-        load_vec(xr + v * 8, f);
+    for (int k = 0; k < 4; ++k) {
+      const int t = t0 + k;
+      ok[k] = t < N;
+      size_t row = ok[k] ? static_cast<size_t>(t) : 0;
+      if (pad_P > 0 && ok[k]) {
+        const int b = tok_img[t];
+        row = static_cast<size_t>(b) * pad_P + (t - cu[b]);
       }
+      xr[k] = x + row * D;
+    }
+    float acc[64];
+#pragma unroll
+    for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+    // raw loads two column groups ahead of the FMAs (8 loads in flight per lane)
+    R r0[4], r1[4], r2[4];
+    auto load_group = [&](int g, R (&dst)[4]) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) dst[k] = (ok[k] && g < ngroups) ? load_raw4(xr[k] + 4 * g) : R{};
+    };
+    load_group(lane, r0);
+    load_group(lane + 32, r1);
+    for (int g = lane; g < ngroups; g += 32) {
+      load_group(g + 64, r2);
+      float f[4][4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) unpack_raw4<T>(r0[k], f[k]);
 #pragma unroll
       for (int h = 0; h < 16; ++h) {
-        if (h < H) {
-          const float4* uh = reinterpret_cast<const float4*>(su + h * D + v * 8);
-          const float4 a = uh[0], b = uh[1];
-          acc[h] = fmaf(f[0], a.x, fmaf(f[1], a.y, fmaf(f[2], a.z, fmaf(f[3], a.w, acc[h]))));
-          acc[h] = fmaf(f[4], b.x, fmaf(f[5], b.y, fmaf(f[6], b.z, fmaf(f[7], b.w, acc[h]))));
-        }
+        const float4 w = *reinterpret_cast<const float4*>(su + h * D + 4 * g);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          acc[k * 16 + h] = fmaf(f[k][0], w.x, fmaf(f[k][1], w.y, fmaf(f[k][2], w.z, fmaf(f[k][3], w.w, acc[k * 16 + h]))));
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        r0[k] = r1[k];
+        r1[k] = r2[k];
       }
     }
+    // reduce-scatter over the warp: after step s a lane keeps 32 >> s entries
+    // (the upper or lower half of what it held, by bit 4 - s of its index)
 #pragma unroll
-    for (int h = 0; h < 16; ++h) {
-      if (h < H) {
-        const float sv = warp_sum(acc[h]);
-        if (lane == h) scores[static_cast<size_t>(t) * H + h] = sv;
+    for (int s = 0; s < 5; ++s) {
+      const int half = 32 >> s;
+      const bool up = (lane >> (4 - s)) & 1;
+#pragma unroll
+      for (int i = 0; i < half; ++i) {
+        const float send = up ? acc[i] : acc[i + half];
+        const float keep = up ? acc[i + half] : acc[i];
+        acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16 >> s);
       }
+    }
+    const int k = lane >> 3, h0 = 2 * (lane & 7);
+    bool okk = false;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) okk = kk == k ? ok[kk] : okk;
+    if (okk) {
+      float* dst = scores + static_cast<size_t>(t0 + k) * H;
+      if (h0 < H) dst[h0] = acc[0];
+      if (h0 + 1 < H) dst[h0 + 1] = acc[1];
     }
   }
 }
 
-// block = 256 threads: thread (h = tid / 16, q = tid % 16) owns columns
-// [c0 + 4q, c0 + 4q + 4) of head h (H <= 16, 64 columns per CTA)
 template <typename T>
-__global__ void __launch_bounds__(256) head_pool_rows_kernel(const T* __restrict__ x, int D, int H,
+__global__ void __launch_bounds__(128) head_pool_rows_kernel(const T* __restrict__ x, int D, int H,
                                                              const int* __restrict__ cu, int pad_P,
                                                              const float* __restrict__ scores,
                                                              T* __restrict__ pooled) {
-  constexpr int RB = 32;                  // rows per staging block
-  __shared__ float sx[RB][64];            // x rows, this CTA's 64 columns
-  __shared__ float sp[RB][16];            // softmax weights of those rows
+  constexpr int RB = 64;  // rows per block of softmax weights (16 per warp)
+  __shared__ __align__(16) float sp[2][RB][16];
+  __shared__ __align__(16) float red[4][16][128];  // per-warp partial sums, merged in warp order
+  __shared__ float red_m[8][16], red_s[8][16];
   __shared__ float smx[16], sinv[16];
   const int b = blockIdx.x;
-  const int c0 = blockIdx.y * 64;
+  const int c0 = blockIdx.y * 128;
   const int t0 = cu[b];
   const int L = cu[b + 1] - t0;
   const size_t base = pad_P > 0 ? static_cast<size_t>(b) * pad_P : static_cast<size_t>(t0);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // per-head max and normaliser over the image (warp h handles heads h, h+8)
-  for (int h = warp; h < H; h += 8) {
-    float m = -INFINITY;
-    for (int j = lane; j < L; j += 32) m = fmaxf(m, scores[static_cast<size_t>(t0 + j) * H + h]);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int rg = tid >> 4, hh = tid & 15;  // score loads: row group, head (16 heads = one 64-byte row)
+  // per-head max and normaliser over the image: thread (rg, hh) keeps an
+  // online (max, sum) over rows rg, rg + 8, ..., and the 8 partials of each
+  // head are merged in shared memory
+  {
+    float m = -INFINITY, sum = 0.f;
+    if (hh < H) {
+      for (int j0 = rg; j0 < L; j0 += 8 * 16) {
+        float v[16];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float sum = 0.f;
-    for (int j = lane; j < L; j += 32) sum += exp2f(scores[static_cast<size_t>(t0 + j) * H + h] - m);
-    sum = warp_sum(sum);
-    if (lane == 0) {
-      smx[h] = m;
-      sinv[h] = 1.f / sum;
-    }
-  }
-  __syncthreads();
-  const int h = threadIdx.x >> 4, q = threadIdx.x & 15;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int j0 = 0; j0 < L; j0 += RB) {
-    const int nr = min(RB, L - j0);
-    // stage rows (64 columns = 8 vectors of 8 per row) and weights
-    for (int i = threadIdx.x; i < RB * 8; i += 256) {
-      const int r = i >> 3, v = i & 7;
-      float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      const int col = c0 + v * 8;
-      if (r < nr && col < D) {
-        const T* src = x + (base + j0 + r) * D + col;
-        if constexpr (sizeof(T) == 4) {
-          load_vec(src, f);
-          load_vec(src + 4, f + 4);
-        } else {
-          load_vec(src, f);
+        for (int i = 0; i < 16; ++i) {
+          const int j = j0 + 8 * i;
+          v[i] = j < L ? scores[static_cast<size_t>(t0 + j) * H + hh] : -INFINITY;
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          if (v[i] > m) {
+            sum = sum * exp2f(m - v[i]) + 1.f;
+            m = v[i];
+          } else if (v[i] > -INFINITY) {
+            sum += exp2f(v[i] - m);
+          }
         }
       }
-#pragma unroll
-      for (int k = 0; k < 8; ++k) sx[r][v * 8 + k] = f[k];
     }
-    for (int i = threadIdx.x; i < RB * 16; i += 256) {
-      const int r = i >> 4, hh = i & 15;
-      sp[r][hh] = (r < nr && hh < H) ? exp2f(scores[static_cast<size_t>(t0 + j0 + r) * H + hh] - smx[hh]) * sinv[hh]
-                                     : 0.f;
-    }
+    red_m[rg][hh] = m;
+    red_s[rg][hh] = sum;
     __syncthreads();
-    if (h < H) {
-#pragma unroll 8
-      for (int r = 0; r < RB; ++r) {
-        const float pw = sp[r][h];
-        const float4 xv = *reinterpret_cast<const float4*>(&sx[r][4 * q]);
-        acc[0] = fmaf(pw, xv.x, acc[0]);
-        acc[1] = fmaf(pw, xv.y, acc[1]);
-        acc[2] = fmaf(pw, xv.z, acc[2]);
-        acc[3] = fmaf(pw, xv.w, acc[3]);
-      }
+    if (tid < 16) {
+      float M = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) M = fmaxf(M, red_m[r][tid]);
+      float S = 0.f;
+#pragma unroll
+      for (int r = 0; r < 8; ++r)
+        if (red_m[r][tid] > -INFINITY) S += red_s[r][tid] * exp2f(red_m[r][tid] - M);
+      smx[tid] = M;
+      sinv[tid] = 1.f / S;
     }
     __syncthreads();
   }
-  const int col = c0 + 4 * q;
-  if (h < H && col < D) {
-    T* o = pooled + (static_cast<size_t>(b) * H + h) * D + col;
-    if constexpr (sizeof(T) == 4) {
-      *reinterpret_cast<float4*>(o) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-    } else {
-      uint2 w;
-      w.x = Pack2<T>::pack(acc[0], acc[1]);
-      w.y = Pack2<T>::pack(acc[2], acc[3]);
-      *reinterpret_cast<uint2*>(o) = w;
+  // softmax weights of a 64-row block: thread (rg, hh) owns rows rg + 8i
+  float pv[8];
+  auto load_p = [&](int j0) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int j = j0 + rg + 8 * i;
+      pv[i] = (j < L && hh < H) ? scores[static_cast<size_t>(t0 + j) * H + hh] : 0.f;
+    }
+  };
+  auto store_p = [&](int j0, int buf) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = rg + 8 * i;
+      sp[buf][r][hh] = (j0 + r < L && hh < H) ? exp2f(pv[i] - smx[hh]) * sinv[hh] : 0.f;
+    }
+  };
+  // thread (warp w, lane c): rows w, w + 4, ... of each block, all 16 heads,
+  // columns c0 + 4c .. + 3
+  const int col = c0 + 4 * lane;
+  const bool col_ok = col < D;  // D % 8 == 0
+  using R = typename Raw4<T>::type;
+  float acc[16][4];
+#pragma unroll
+  for (int a = 0; a < 16; ++a)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[a][e] = 0.f;
+  load_p(0);
+  store_p(0, 0);
+  __syncthreads();
+  int buf = 0;
+  for (int j0 = 0; j0 < L; j0 += RB, buf ^= 1) {
+    const bool more = j0 + RB < L;
+    if (more) load_p(j0 + RB);  // the next block's scores are in flight during this block
+    if (col_ok) {
+      const T* xr = x + (base + j0) * D + col;
+      R raw[16];  // this warp's 16 rows of the block, all loads in flight at once
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int rr = warp + 4 * i;
+        raw[i] = j0 + rr < L ? load_raw4(xr + static_cast<size_t>(rr) * D) : R{};
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int rr = warp + 4 * i;
+        float f[4];
+        unpack_raw4<T>(raw[i], f);
+        const float4* pr = reinterpret_cast<const float4*>(&sp[buf][rr][0]);
+#pragma unroll
+        for (int hq = 0; hq < 4; ++hq) {
+          const float4 pw = pr[hq];
+          const float w4[4] = {pw.x, pw.y, pw.z, pw.w};
+#pragma unroll
+          for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[4 * hq + a][e] = fmaf(w4[a], f[e], acc[4 * hq + a][e]);
+        }
+      }
+    }
+    if (more) store_p(j0 + RB, buf ^ 1);
+    __syncthreads();
+  }
+  // merge the four warps' partial sums in a fixed order (deterministic)
+#pragma unroll
+  for (int a = 0; a < 16; ++a)
+    *reinterpret_cast<float4*>(&red[warp][a][4 * lane]) = make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+  __syncthreads();
+  const int oc = c0 + tid;  // one output column per thread
+  if (oc < D) {
+    for (int h = 0; h < H; ++h) {
+      const float v = ((red[0][h][tid] + red[1][h][tid]) + red[2][h][tid]) + red[3][h][tid];
+      pooled[(static_cast<size_t>(b) * H + h) * D + oc] = from_float<T>(v);
     }
   }
 }

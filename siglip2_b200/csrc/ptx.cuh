@@ -462,12 +462,51 @@ __device__ __forceinline__ float tanh_approx(float x) {
 }
 
 // GELU with the tanh approximation: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
+// packed fp32 pair arithmetic (sm_100): two lanes of FFMA / FADD / FMUL per
+// issue, each lane rounded exactly as the scalar instruction
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
 __device__ __forceinline__ float gelu_tanh(float x) {
   const float k0 = 0.7978845608028654f;   // sqrt(2/pi)
   const float k01 = 0.0356774081363001f;  // sqrt(2/pi) * 0.044715
   const float h = 0.5f * x;
   const float z = x * fmaf(k01, x * x, k0);  // sqrt(2/pi) (x + 0.044715 x^3)
   return fmaf(h, tanh_approx(z), h);
+}
+
+// gelu_tanh on a pair with packed issues (the same roundings per lane)
+__device__ __forceinline__ float2 gelu_tanh2(float2 x) {
+  const float k0 = 0.7978845608028654f;
+  const float k01 = 0.0356774081363001f;
+  const float2 h = fmul2(make_float2(0.5f, 0.5f), x);
+  const float2 z = fmul2(x, ffma2(make_float2(k01, k01), fmul2(x, x), make_float2(k0, k0)));
+  return ffma2(h, make_float2(tanh_approx(z.x), tanh_approx(z.y)), h);
 }
 
 // d/dx of gelu_tanh: 0.5 (1 + t) + 0.5 x (1 - t^2) sqrt(2/pi) (1 + 3 * 0.044715 x^2), t = tanh(...)

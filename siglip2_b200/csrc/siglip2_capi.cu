@@ -866,18 +866,18 @@ int sg_fmha_impl(int dtype, const void* qkv, int N, const int* cu, const int* ti
 template <typename T>
 int launch_head_pool_parallel(const void* x, int D, int H, const int* cu, int B, int pad_P, const int* tok_img, int N,
                               const float* u, float* scores, void* pooled, cudaStream_t s) {
-  const int smem = H * D * 4;
+  const int smem = 16 * D * 4;  // u for 16 heads (zero past H)
   auto ks = head_scores_kernel<T>;
   SG_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(ks), smem));
-  const int warps = 16;
-  int blocks = (N + warps - 1) / warps;
-  blocks = std::min(blocks, 4 * sm_count());
+  // 8 warps of 4 tokens per CTA and sweep; two CTAs per SM
+  int blocks = (N + 31) / 32;
+  blocks = std::min(blocks, 2 * sm_count());
   if (N > 0) {
-    ks<<<blocks, warps * 32, smem, s>>>(static_cast<const T*>(x), D, H, cu, B, pad_P, tok_img, N, u, scores);
+    ks<<<blocks, 256, smem, s>>>(static_cast<const T*>(x), D, H, cu, pad_P, tok_img, N, u, scores);
     SG_LAUNCH_CHECK();
   }
-  dim3 grid(B, (D + 63) / 64);
-  head_pool_rows_kernel<T><<<grid, 256, 0, s>>>(static_cast<const T*>(x), D, H, cu, pad_P, scores,
+  dim3 grid(B, (D + 127) / 128);
+  head_pool_rows_kernel<T><<<grid, 128, 0, s>>>(static_cast<const T*>(x), D, H, cu, pad_P, scores,
                                                 static_cast<T*>(pooled));
   SG_LAUNCH_CHECK();
   return SIGLIP2_OK;
