@@ -332,10 +332,6 @@ __global__ void __launch_bounds__(192, 2)
       const int img_row0 = __ldg(p.cu + tile.x);
       const int L = __ldg(p.cu + tile.x + 1) - img_row0;
       const int n_kv = (L + KT - 1) / KT;
-      // every row of this warp lies past the image end (the last query tile
-      // of an image): its S, P and O lanes are never used, so the warp only
-      // keeps its barrier arrivals in phase
-      const bool dead = tile.y * 128 + q * 32 >= L;
       float m_use = 0.f, l = 0.f;
       for (int j = 0; j < n_kv; ++j, ++g) {
         if (*abort_flag || !mbar_wait(s_full, g & 1, 221)) {
@@ -343,18 +339,6 @@ __global__ void __launch_bounds__(192, 2)
           break;
         }
         tc_fence_after();
-        if (dead) {
-          // s_full(g) completes only after p_full(g - 1) did; for j > 0 the
-          // pv_done wait orders this p_full arrival after the previous phase
-          tc_fence_before();
-          mbar_arrive(s_free);
-          if (j > 0 && !mbar_wait(pv_done, (g - 1) & 1, 224)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive(p_full);
-          continue;
-        }
         // the whole S tile in one round trip
         float s[KT];
         {
