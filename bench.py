@@ -424,6 +424,8 @@ def main():
 
     if rank == 0:
         tok_all = int((shapes_all[:, 0] * shapes_all[:, 1]).sum())
+        in_mb = pv.numel() * pv.element_size() / 1e6
+        w_gb = sum(t.numel() * t.element_size() for t in model.parameters()) / 1e9
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
@@ -434,7 +436,7 @@ def main():
                        "padding_frac": round(1 - tok_all / (B_all * wl.max_patches), 4),
                        "parallelism": f"dp{world} (global batch sharded by image cost, NCCL all-gather of "
                                       f"pooled embeddings)",
-                       "l2": "working set (inputs 100 MB + weights 0.86 GB per step) larger than L2"},
+                       "l2": f"working set (inputs {in_mb:.0f} MB + weights {w_gb:.2f} GB per step) larger than L2"},
             "value_per_gpu": value / world,
             "tflops_algorithmic": round(tflops, 1), "pct_of_peak": round(100 * tflops / (world * peak_tf), 2),
             "tflops_note": "whole job; pct_of_peak against n_gpus x the per-GPU peak",
