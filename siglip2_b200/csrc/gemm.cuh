@@ -88,53 +88,6 @@ struct GemmParams {
   int k_per_split;
   float* part;
   int ld_part;
-  // CTA-pair kernel: split the full-width tiles of the last, partial wave
-  // into two half-width tiles (GemmTileMap); chosen per shape on the host
-  int split_tail;
-};
-
-// Tile order of the persistent GEMMs.  Tiles are numbered row block by row
-// block (the column tiles of a row block adjacent, so the CTAs working on one
-// row block at the same time share its A rows in L2) and worker q takes tiles
-// q, q + workers, ...  With split, the full-width tiles of the last, partial
-// wave are each cut into two half-width tiles, which spreads that wave's work
-// over twice as many workers.  decode(t) gives tile t's row block, first
-// column and width (the last column tile may be narrower: N - n0 rounded up
-// to 16).
-struct GemmTileMap {
-  int n_tiles, N, BN, main, count;
-  __device__ __forceinline__ int width(int col) const { return min(BN, (N - col * BN + 15) & ~15); }
-  __device__ __forceinline__ void init(int m_tiles, int nt, int n, int bn, int workers, bool split) {
-    n_tiles = nt;
-    N = n;
-    BN = bn;
-    const int total = m_tiles * nt;
-    main = split ? (total / workers) * workers : total;
-    count = main;
-    for (int j = main; j < total; ++j) count += width(j % nt) == bn ? 2 : 1;
-  }
-  __device__ __forceinline__ void decode(int t, int& rb, int& n0, int& w) const {
-    if (t < main) {
-      rb = t / n_tiles;
-      const int col = t - rb * n_tiles;
-      n0 = col * BN;
-      w = width(col);
-      return;
-    }
-    int i = t - main;
-    for (int j = main;; ++j) {  // at most `workers` tiles past main
-      const int col = j % n_tiles;
-      const int wj = width(col);
-      const int cnt = wj == BN ? 2 : 1;
-      if (i < cnt) {
-        rb = j / n_tiles;
-        n0 = col * BN + i * (BN / 2);
-        w = cnt == 2 ? BN / 2 : wj;
-        return;
-      }
-      i -= cnt;
-    }
-  }
 };
 
 constexpr int kGemmBM = 128;
@@ -227,8 +180,8 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
                                               uint64_t* resbar, uint64_t* tfull, uint32_t tempty_addr0,
                                               uint32_t tempty_addr1, uint64_t* sfull, uint64_t* sempty,
                                               const float* st_mean, const float* st_rstd, volatile int* abort_flag,
-                                              int warp, int lane, int first_tile, int tile_step,
-                                              const GemmTileMap& tmap, int rows_per_tile, int row_offset) {
+                                              int warp, int lane, int first_tile, int tile_step, int num_tiles,
+                                              int n_tiles, int rows_per_tile, int row_offset) {
   constexpr bool kStat = epi_has_stat_warps(EPI);  // mu/rstd from this kernel's statistics warps
   constexpr bool kRsIn = (EPI == kEpiLnRs || EPI == kEpiLnRsGelu);  // mu/rstd from row sums
   constexpr bool kLnMath = epi_is_ln(EPI);
@@ -251,20 +204,13 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
   uint32_t rph = 0;  // bit b: parity of the next completion of rbar[b]
   int sb = 0;        // staging buffer of the current chunk
 
-  // first row, this warp's first column and the tile's column end
-  auto tile_pos = [&](int tile, int& m0, int& c0, int& cend) {
-    int rb, n0, w;
-    tmap.decode(tile, rb, n0, w);
-    m0 = rb * rows_per_tile + row_offset;
-    c0 = n0 + part * kPartCols;
-    cend = min(p.N, n0 + w);
-  };
+  auto tile_m0 = [&](int tile) { return (tile / n_tiles) * rows_per_tile + row_offset; };
+  auto tile_c0 = [&](int tile) { return (tile % n_tiles) * BN + part * kPartCols; };  // this warp's first column
   // L1/L2 prefetch of what the epilogue of `tile` reads besides TMEM
   auto prefetch_tile = [&](int tile) {
-    if (tile >= tmap.count) return;
-    int pm0, pc0, pcend;
-    tile_pos(tile, pm0, pc0, pcend);
-    if (q == 0 && lane < NCH && pc0 + lane * 32 < pcend) {  // 32 floats = one 128-byte line per lane
+    if (tile >= num_tiles) return;
+    const int pm0 = tile_m0(tile), pc0 = tile_c0(tile);
+    if (q == 0 && lane < NCH && pc0 + lane * 32 < p.N) {  // 32 floats = one 128-byte line per lane
       if constexpr (kLnMath) {
         prefetch_l1(p.c1 + pc0 + lane * 32);
         prefetch_l1(p.c2 + pc0 + lane * 32);
@@ -280,18 +226,18 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
       }
     }
     if constexpr (kRes) {
-      if (lane < NCH && pm0 + q * 32 < p.M && pc0 + lane * kEpiCols < pcend)
+      if (lane < NCH && pm0 + q * 32 < p.M && pc0 + lane * kEpiCols < p.N)
         tma_prefetch_l2_2d(tmR, pc0 + lane * kEpiCols, pm0 + q * 32);
     }
   };
 
   prefetch_tile(first_tile);
   int t = 0;
-  for (int tile = first_tile; tile < tmap.count; tile += tile_step, ++t) {
+  for (int tile = first_tile; tile < num_tiles; tile += tile_step, ++t) {
     const int buf = t & 1;
     const uint32_t tph = (t >> 1) & 1;
-    int m0, c0, cend;
-    tile_pos(tile, m0, c0, cend);
+    const int m0 = tile_m0(tile);
+    const int c0 = tile_c0(tile);
     const int row0 = m0 + q * 32;
     const int my_row = row0 + lane;
     prefetch_tile(tile + tile_step);
@@ -360,7 +306,7 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
       float v[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(cur[j]);
-      if (col0 < cend) {
+      if (col0 < p.N) {
         if constexpr (kLnMath) {
           float a[32], b[32];
           load_param32(p.c1, col0, p.N, a);
@@ -458,7 +404,7 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
         *reinterpret_cast<uint4*>(srow + ((g ^ sw) << 4)) = o;
         if constexpr (kRsOut) {
           // statistics of exactly what the next GEMM will read (the rounded values)
-          if (col0 + g * 8 < cend) {
+          if (col0 + g * 8 < p.N) {
             const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
 #pragma unroll
             for (int h2 = 0; h2 < 4; ++h2) {
@@ -474,7 +420,7 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
       }
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0 && col0 < cend && row0 < p.M) {
+      if (lane == 0 && col0 < p.N && row0 < p.M) {
         tma_store_2d(tmO, sbuf, col0, row0);
       }
       if (lane == 0) tma_store_commit();
@@ -491,9 +437,9 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
     }
     if constexpr (kRsOut) {
       // this warp's column block is one slot (block width kPartCols = BN / 2)
-      if (my_row < p.M && c0 < cend)
+      if (my_row < p.M && c0 < p.N)
         p.rs_acc[static_cast<size_t>(my_row) * p.rs_ld + c0 / kPartCols] =
-            slot_stats_from_shifted(rs1v.x + rs1v.y, rs2v.x + rs2v.y, rs_shift, min(kPartCols, cend - c0));
+            slot_stats_from_shifted(rs1v.x + rs1v.y, rs2v.x + rs2v.y, rs_shift, min(kPartCols, p.N - c0));
     }
   }
   if (lane == 0) tma_store_wait_all<0>();
@@ -857,13 +803,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if constexpr (kSplitK)
       gemm_epilogue_part<BN>(p, tmem_base, Cfg::kAccStride, tfull, te0, te1, abort_flag, warp, lane, blockIdx.x,
                              gridDim.x, num_tiles, mn_tiles, n_tiles);
-    else {
-      GemmTileMap tmap;
-      tmap.init(m_tiles, n_tiles, p.N, BN, gridDim.x, false);  // plain order: tiles t = row block * n_tiles + column
+    else
       gemm_epilogue<T, BN, EPI, false>(p, &tmO, &tmR, tmem_base, Cfg::kAccStride, staging, resbar, tfull, te0, te1,
                                        sfull, sempty, st_mean, st_rstd, abort_flag, warp, lane, blockIdx.x, gridDim.x,
-                                       tmap, kGemmBM, 0);
-    }
+                                       num_tiles, n_tiles, kGemmBM, 0);
   } else {
     // ------------------------------------------------------------ LayerNorm row statistics
     if constexpr (kLN) {
@@ -933,9 +876,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   constexpr int STAGES = Cfg::kStages;
   // instruction-descriptor format bits: bf16 (1) or f16 (0) for kind::f16, e4m3 (0) for kind::f8f6f4
   constexpr bool kBF16 = !kF8 && std::is_same<T, __nv_bfloat16>::value;
-  // a tile's MMAs run at its width (GemmTileMap: the last column tile may be
-  // narrower, tiles of a split tail half as wide) and the pair splits B at
-  // half of it
+  // the last column tile may be narrower (N - (n_tiles - 1) * BN, rounded up
+  // to 16): its MMAs run at that width and the pair splits B at half of it
+  const auto tile_width = [&](int n_tile) { return min(BN, (p.N - n_tile * BN + 15) & ~15); };
   constexpr int kTileRows = 2 * kGemmBM;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -966,9 +909,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int num_pairs = gridDim.x >> 1;
   const int m_tiles = (p.M + kTileRows - 1) / kTileRows;
   const int n_tiles = (p.N + BN - 1) / BN;
-  GemmTileMap tmap;
-  tmap.init(m_tiles, n_tiles, p.N, BN, num_pairs, p.split_tail != 0);
-  const int num_tiles = tmap.count;
+  const int num_tiles = m_tiles * n_tiles;
   const int nk = (p.K + kGemmBK * SUB - 1) / (kGemmBK * SUB);  // pipeline stages per tile
 
   if (threadIdx.x == 0) {
@@ -1013,10 +954,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int issued = 0;
       bool ok = true;
       for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
-        int rb, tn0, tw;
-        tmap.decode(tile, rb, tn0, tw);
-        const int m0 = rb * kTileRows + static_cast<int>(rank) * kGemmBM;
-        const int n0 = tn0 + static_cast<int>(rank) * (tw / 2);
+        const int m0 = (tile / n_tiles) * kTileRows + static_cast<int>(rank) * kGemmBM;
+        const int n0 = (tile % n_tiles) * BN + static_cast<int>(rank) * (tile_width(tile % n_tiles) / 2);
         for (int kb = 0; kb < nk; ++kb) {
           if (*abort_flag || !mbar_wait<true>(&empty[stage], phase ^ 1, 141)) {
             ok = false;
@@ -1071,9 +1010,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * Cfg::kAccStride;
-        int rb, tn0, tw;
-        tmap.decode(tile, rb, tn0, tw);
-        const uint32_t idesc = make_idesc(2 * kGemmBM, tw, kBF16, false, kBT);
+        const uint32_t idesc = make_idesc(2 * kGemmBM, tile_width(tile % n_tiles), kBF16, false, kBT);
         for (int kb = 0; kb < nk; ++kb) {
           if (*abort_flag || !mbar_wait<true>(&full[stage], phase, 152)) {
             ok = false;
@@ -1120,7 +1057,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint32_t te0 = mapa_shared(smem_u32(&tempty[0]), 0), te1 = mapa_shared(smem_u32(&tempty[1]), 0);
     gemm_epilogue<T, BN, EPI, true, kF8>(p, &tmO, &tmR, tmem_base, Cfg::kAccStride, staging, resbar, tfull, te0,
                                          te1, sfull, sempty, st_mean, st_rstd, abort_flag, warp, lane, pair,
-                                         num_pairs, tmap, kTileRows, static_cast<int>(rank) * kGemmBM);
+                                         num_pairs, num_tiles, n_tiles, kTileRows, static_cast<int>(rank) * kGemmBM);
   } else {
     // ------------------------------------------------------------ LayerNorm row statistics (both CTAs)
     if constexpr (kLN) {

@@ -3,7 +3,6 @@
 // for sm_100a only.
 #include <algorithm>
 #include <climits>
-#include <tuple>
 #include <cmath>
 #include <type_traits>
 #include <vector>
@@ -73,48 +72,9 @@ int launch_gemm_tc(const GemmIO& io, const GemmParams& p, cudaStream_t stream) {
   return SIGLIP2_OK;
 }
 
-// Whether the CTA-pair GEMM splits the full-width tiles of its last, partial
-// wave into half-width tiles (GemmTileMap): the columns each pair computes
-// are counted for both orders and the one with the smaller maximum wins
-// (e.g. M = 39,178, N = 1,152 on 74 pairs: 10 -> 9.5 full tiles' worth).
-// Memoised per shape.
-int gemm_split_tail(int M, int N, int BN, int pairs) {
-  static std::mutex mu;
-  static std::map<std::tuple<int, int, int, int>, int> memo;
-  const auto key = std::make_tuple(M, N, BN, pairs);
-  {
-    std::lock_guard<std::mutex> g(mu);
-    const auto it = memo.find(key);
-    if (it != memo.end()) return it->second;
-  }
-  const int mt = (M + 2 * kGemmBM - 1) / (2 * kGemmBM), nt = (N + BN - 1) / BN;
-  const int total = mt * nt, main_tiles = (total / pairs) * pairs;
-  int split = 0;
-  if (main_tiles < total) {
-    auto width = [&](int col) { return std::min(BN, (N - col * BN + 15) & ~15); };
-    std::vector<long long> plain(pairs, 0), cut(pairs, 0);
-    for (int j = 0; j < total; ++j) plain[j % pairs] += width(j % nt);
-    long long t = 0;
-    for (int j = 0; j < total; ++j) {
-      const int w = width(j % nt);
-      if (j >= main_tiles && w == BN) {
-        cut[t++ % pairs] += BN / 2;
-        cut[t++ % pairs] += BN / 2;
-      } else {
-        cut[t++ % pairs] += w;
-      }
-    }
-    split = *std::max_element(cut.begin(), cut.end()) < *std::max_element(plain.begin(), plain.end()) ? 1 : 0;
-  }
-  std::lock_guard<std::mutex> g(mu);
-  memo[key] = split;
-  return split;
-}
-
 // 2-SM variant: clusters of 2 CTAs, one pair per 2 SMs, 256 x BN tiles.
 template <typename T, int BN, int EPI, int SUB, bool kF8 = false, bool kBT = false>
-int launch_gemm_tc2(const GemmIO& io, const GemmParams& p_in, cudaStream_t stream) {
-  GemmParams p = p_in;
+int launch_gemm_tc2(const GemmIO& io, const GemmParams& p, cudaStream_t stream) {
   CUtensorMap ta, tb, to, tr;
   SG_TRY(make_tmap_2d(&ta, io.a, 2, p.M, p.K, io.lda, kGemmBM, kGemmBK));
   // transposed B is [K][N] in memory: 64 x 64 boxes
@@ -129,7 +89,6 @@ int launch_gemm_tc2(const GemmIO& io, const GemmParams& p_in, cudaStream_t strea
   SG_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem));
   const int tiles = ((p.M + 2 * kGemmBM - 1) / (2 * kGemmBM)) * ((p.N + BN - 1) / BN);
   const int pairs = std::min(tiles, sm_count() / 2);
-  p.split_tail = gemm_split_tail(p.M, p.N, BN, pairs);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.blockDim = dim3(threads, 1, 1);
