@@ -153,6 +153,17 @@ struct GemmCfg {
                  "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31]))
 
 __device__ __forceinline__ void load_param32(const float* __restrict__ p, int col0, int N, float* v) {
+  if (col0 + 32 <= N) {  // the whole chunk inside N: no per-vector checks
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 f = __ldg(reinterpret_cast<const float4*>(p + col0) + q);
+      v[4 * q] = f.x;
+      v[4 * q + 1] = f.y;
+      v[4 * q + 2] = f.z;
+      v[4 * q + 3] = f.w;
+    }
+    return;
+  }
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
     float4 f = make_float4(0.f, 0.f, 0.f, 0.f);

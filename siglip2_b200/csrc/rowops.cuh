@@ -77,6 +77,28 @@ __device__ __forceinline__ float2 slot_stats_from_shifted(float s1, float s2, fl
 // (mu, rstd) of a K-column row from its `slots` slot statistics (blocks of kRowSumBlock)
 __device__ __forceinline__ void slot_stats_merge(const float2* __restrict__ r, int slots, int K, float eps, float& mu,
                                                  float& rstd) {
+  constexpr int kMaxSlots = 16;  // K <= 2048: every slot loaded once, all loads in flight together
+  if (slots <= kMaxSlots) {
+    float2 v[kMaxSlots];
+#pragma unroll
+    for (int j = 0; j < kMaxSlots; ++j) v[j] = j < slots ? r[j] : make_float2(0.f, 0.f);
+    float sm = 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxSlots; ++j)
+      if (j < slots) sm = fmaf(static_cast<float>(min(kRowSumBlock, K - j * kRowSumBlock)), v[j].x, sm);
+    const float m = sm / static_cast<float>(K);
+    float m2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxSlots; ++j) {
+      if (j < slots) {
+        const float dm = v[j].x - m;
+        m2 += fmaf(static_cast<float>(min(kRowSumBlock, K - j * kRowSumBlock)) * dm, dm, v[j].y);
+      }
+    }
+    mu = m;
+    rstd = rsqrtf(m2 / static_cast<float>(K) + eps);
+    return;
+  }
   float sm = 0.f;
   for (int j = 0; j < slots; ++j) sm = fmaf(static_cast<float>(min(kRowSumBlock, K - j * kRowSumBlock)), r[j].x, sm);
   const float m = sm / static_cast<float>(K);
