@@ -5,6 +5,7 @@ command the ncu summaries under ``profiles/`` were captured with.
     python kernel_bench.py gemm_e4m3 --m 39178 --n 4304 --k 1152 --epi bias_gelu
     python kernel_bench.py fmha --preset so400m --images 64 --max-patches 1024
     python kernel_bench.py layer --preset so400m --images 64 --max-patches 1024
+    python kernel_bench.py patch_embed --preset so400m --images 64 --max-patches 1024
     python kernel_bench.py patchify --images 64 --height 768 --width 1024 --max-patches 1024
 
 Prints one JSON line per measurement: milliseconds per launch, the
@@ -170,6 +171,28 @@ def bench_layer(preset, images, max_patches, reps):
     return out
 
 
+def bench_patch_embed(preset, images, max_patches, reps, warmup=3):
+    """``siglip2_patch_embed`` (patch Linear + antialiased resize of the 16x16
+    position table in the epilogue + slot statistics) on the seeded NaFlex
+    grids; 2 N 768 D FLOPs per launch (the resize is not counted)."""
+    D = W.PRESETS[preset][0]
+    shapes = _shapes(preset, images, max_patches)
+    lens = (shapes[:, 0] * shapes[:, 1]).tolist()
+    N = sum(lens)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0).tolist()), dtype=torch.int32, device="cuda")
+    hw = shapes.to(torch.int32).flatten().cuda()
+    tok = ops.token_image(cu, N)
+    patches = (torch.rand(N, 768, device="cuda", generator=g) * 2 - 1).bfloat16()
+    w = (torch.randn(D, 768, device="cuda", generator=g) * 0.02).bfloat16()
+    bias = torch.randn(D, device="cuda", generator=g) * 0.02
+    table = torch.randn(256, D, device="cuda", generator=g) * 0.02
+    rs = torch.empty((N, ops.rowsum_slots(torch.bfloat16, D), 2), device="cuda")
+    ms = _time(lambda: ops.patch_embed(patches, w, bias, table, hw, cu, tok, rs), reps, warmup)
+    return {"kernel": "patch_embed", "preset": preset, "images": images, "tokens": N, "ms": ms,
+            "tflops": 2 * N * 768 * D / ms / 1e9, **_clock()}
+
+
 def bench_patchify(images: int, height: int, width: int, max_patches: int, reps: int, warmup: int = 3,
                    channels_last: bool = True) -> dict:
     """``siglip2_patchify`` on ``images`` random uint8 images of one size
@@ -249,6 +272,13 @@ def main():
     bw.add_argument("--k", type=int, default=1152)
     bw.add_argument("--reps", type=int, default=20)
     bw.add_argument("--variant", type=int, default=0)
+    pe = sub.add_parser("patch_embed")
+    pe.add_argument("--preset", default="so400m")
+    pe.add_argument("--images", type=int, default=64)
+    pe.add_argument("--max-patches", type=int, default=1024)
+    pe.add_argument("--reps", type=int, default=20)
+    pe.add_argument("--warmup", type=int, default=3)
+    pe.add_argument("--variant", type=int, default=0)
     pz = sub.add_parser("patchify")
     pz.add_argument("--images", type=int, default=64)
     pz.add_argument("--height", type=int, default=512)
@@ -268,6 +298,8 @@ def main():
     elif a.cmd == "gemm_e4m3":
         for r in bench_gemm_e4m3(a.m, a.n, a.k, a.epi, a.reps, a.warmup, a.cublas):
             print(json.dumps(r))
+    elif a.cmd == "patch_embed":
+        print(json.dumps(bench_patch_embed(a.preset, a.images, a.max_patches, a.reps, a.warmup)))
     elif a.cmd == "patchify":
         print(json.dumps(bench_patchify(a.images, a.height, a.width, a.max_patches, a.reps, a.warmup,
                                         channels_last=not a.channels_first)))
