@@ -283,7 +283,6 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
     float rs_shift = 0.f;
     float2 rs1v = make_float2(0.f, 0.f), rs2v = make_float2(0.f, 0.f);
     AxisTaps ay{0, 0, 0.f, 1.f, 0.f}, ax{0, 0, 0.f, 1.f, 0.f};  // position-embedding taps of this row (kPos)
-    int pny = 0, pnx = 0;  // the warp's largest tap counts per axis (kPos)
     if constexpr (kPos) {
       if (my_row < p.M) {
         const int b = p.tok_img[my_row];
@@ -292,8 +291,6 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
         ay = axis_taps(i / w, p.pos_hw[2 * b], p.pos_grid);
         ax = axis_taps(i - (i / w) * w, w, p.pos_grid);
       }
-      pny = __reduce_max_sync(0xffffffffu, static_cast<unsigned>(ay.hi - ay.lo));
-      pnx = __reduce_max_sync(0xffffffffu, static_cast<unsigned>(ax.hi - ax.lo));
     }
     const uint32_t tbase =
         tmem_base + buf * acc_stride + part * kPartCols + (static_cast<uint32_t>(q * 32) << 16);
@@ -363,38 +360,24 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
         }
         if constexpr (kPos) {
           // separable triangle-filter taps over the fp32 table (L2-resident):
-          // 2 x 2 taps when upsampling, more when the image side is < grid.
-          // Every lane runs the warp's largest tap counts (taps past a lane's
-          // own window get weight 0 and a clamped index, so its sum is
-          // unchanged): the loop does not diverge, and the common 2 x 2 case
-          // is unrolled with its loads in flight together.
-          const bool inside = col0 + 32 <= p.N;
-          auto tap = [&](int ty, int tx) {
-            const int ya = min(ay.lo + ty, p.pos_grid - 1), xa = min(ax.lo + tx, p.pos_grid - 1);
-            const float wgt = (ty < ay.hi - ay.lo && tx < ax.hi - ax.lo)
-                                  ? axis_w(ay, ay.lo + ty) * axis_w(ax, ax.lo + tx)
-                                  : 0.f;
-            const float4* src =
-                reinterpret_cast<const float4*>(p.pos_table + static_cast<size_t>(ya * p.pos_grid + xa) * p.N + col0);
+          // 2 x 2 taps when upsampling, more when the image side is < grid
+          for (int ya = ay.lo; ya < ay.hi; ++ya) {
+            const float wy = axis_w(ay, ya);
+            for (int xa = ax.lo; xa < ax.hi; ++xa) {
+              const float wgt = wy * axis_w(ax, xa);
+              const float4* src =
+                  reinterpret_cast<const float4*>(p.pos_table + static_cast<size_t>(ya * p.pos_grid + xa) * p.N + col0);
 #pragma unroll
-            for (int q4 = 0; q4 < 8; ++q4) {
-              if (inside || col0 + 4 * q4 < p.N) {
-                const float4 f = __ldg(src + q4);
-                v[4 * q4] = fmaf(wgt, f.x, v[4 * q4]);
-                v[4 * q4 + 1] = fmaf(wgt, f.y, v[4 * q4 + 1]);
-                v[4 * q4 + 2] = fmaf(wgt, f.z, v[4 * q4 + 2]);
-                v[4 * q4 + 3] = fmaf(wgt, f.w, v[4 * q4 + 3]);
+              for (int q4 = 0; q4 < 8; ++q4) {
+                if (col0 + 4 * q4 < p.N) {
+                  const float4 f = __ldg(src + q4);
+                  v[4 * q4] = fmaf(wgt, f.x, v[4 * q4]);
+                  v[4 * q4 + 1] = fmaf(wgt, f.y, v[4 * q4 + 1]);
+                  v[4 * q4 + 2] = fmaf(wgt, f.z, v[4 * q4 + 2]);
+                  v[4 * q4 + 3] = fmaf(wgt, f.w, v[4 * q4 + 3]);
+                }
               }
             }
-          };
-          if (pny == 2 && pnx == 2) {
-            tap(0, 0);
-            tap(0, 1);
-            tap(1, 0);
-            tap(1, 1);
-          } else {
-            for (int ty = 0; ty < pny; ++ty)
-              for (int tx = 0; tx < pnx; ++tx) tap(ty, tx);
           }
         }
       }
