@@ -215,12 +215,22 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
   uint32_t rph = 0;  // bit b: parity of the next completion of rbar[b]
   int sb = 0;        // staging buffer of the current chunk
 
-  auto tile_m0 = [&](int tile) { return (tile / n_tiles) * rows_per_tile + row_offset; };
-  auto tile_c0 = [&](int tile) { return (tile % n_tiles) * BN + part * kPartCols; };  // this warp's first column
-  // L1/L2 prefetch of what the epilogue of `tile` reads besides TMEM
-  auto prefetch_tile = [&](int tile) {
+  // tile coordinates (row block, column tile), advanced by tile_step without
+  // a division per tile
+  const int step_rb = tile_step / n_tiles, step_col = tile_step - step_rb * n_tiles;
+  int cur_rb = first_tile / n_tiles, cur_col = first_tile - cur_rb * n_tiles;
+  auto advance = [&](int& rb, int& col) {
+    col += step_col;
+    rb += step_rb;
+    if (col >= n_tiles) {
+      col -= n_tiles;
+      ++rb;
+    }
+  };
+  // L1/L2 prefetch of what the epilogue of `tile` (row block rb, column tile col) reads besides TMEM
+  auto prefetch_tile = [&](int tile, int rb, int col) {
     if (tile >= num_tiles) return;
-    const int pm0 = tile_m0(tile), pc0 = tile_c0(tile);
+    const int pm0 = rb * rows_per_tile + row_offset, pc0 = col * BN + part * kPartCols;  // this warp's first column
     if (q == 0 && lane < NCH && pc0 + lane * 32 < p.N) {  // 32 floats = one 128-byte line per lane
       if constexpr (kLnMath) {
         prefetch_l1(p.c1 + pc0 + lane * 32);
@@ -242,16 +252,17 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
     }
   };
 
-  prefetch_tile(first_tile);
+  prefetch_tile(first_tile, cur_rb, cur_col);
   int t = 0;
   for (int tile = first_tile; tile < num_tiles; tile += tile_step, ++t) {
     const int buf = t & 1;
     const uint32_t tph = (t >> 1) & 1;
-    const int m0 = tile_m0(tile);
-    const int c0 = tile_c0(tile);
+    const int m0 = cur_rb * rows_per_tile + row_offset;
+    const int c0 = cur_col * BN + part * kPartCols;  // this warp's first column
     const int row0 = m0 + q * 32;
     const int my_row = row0 + lane;
-    prefetch_tile(tile + tile_step);
+    advance(cur_rb, cur_col);  // from here on: the next tile's coordinates
+    prefetch_tile(tile + tile_step, cur_rb, cur_col);
     float mu = 0.f, rstd = 1.f;
     float a_s = 1.f;  // kScale: this row's scale of A
     if constexpr (kScale) {
