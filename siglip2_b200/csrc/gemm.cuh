@@ -88,11 +88,6 @@ struct GemmParams {
   int k_per_split;
   float* part;
   int ld_part;
-  // residual / incoming-gradient operand of the kRes epilogues, [M][ldr] of
-  // the output type: each epilogue thread loads its own row's next chunk
-  // into registers while the current chunk is processed
-  const void* res;
-  int ldr;
 };
 
 constexpr int kGemmBM = 128;
@@ -216,7 +211,8 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
   const int part = ew / 4;
   const int row_in_tile = q * 32 + lane;
   uint8_t* stg = staging + ew * (kEpiBufs * kEpiBufBytes);
-  (void)resbar;  // residual chunks now arrive by plain loads (see load_res)
+  uint64_t* rbar = resbar + kEpiBufs * ew;
+  uint32_t rph = 0;  // bit b: parity of the next completion of rbar[b]
   int sb = 0;        // staging buffer of the current chunk
 
   // tile coordinates (row block, column tile), advanced by tile_step without
@@ -267,17 +263,6 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
     const int my_row = row0 + lane;
     advance(cur_rb, cur_col);  // from here on: the next tile's coordinates
     prefetch_tile(tile + tile_step, cur_rb, cur_col);
-    // kRes: this row's residual for the first chunk, in flight while the
-    // accumulator is still being computed; later chunks one chunk ahead
-    uint4 rcur[4], rnxt[4];
-    auto load_res = [&](int col, uint4 (&dst)[4]) {
-      const T* src = reinterpret_cast<const T*>(p.res) + static_cast<size_t>(my_row) * p.ldr + col;
-#pragma unroll
-      for (int g = 0; g < 4; ++g)  // N % 8 == 0: a 16-byte vector is all inside N or all outside
-        dst[g] = (my_row < p.M && col + 8 * g < p.N) ? *reinterpret_cast<const uint4*>(src + 8 * g)
-                                                     : make_uint4(0u, 0u, 0u, 0u);
-    };
-    if constexpr (kRes) load_res(c0, rcur);
     float mu = 0.f, rstd = 1.f;
     float a_s = 1.f;  // kScale: this row's scale of A
     if constexpr (kScale) {
@@ -334,7 +319,10 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
       // the store issued from this buffer two chunks ago must have read it
       if (lane == 0) tma_store_wait_read<1>();
       if constexpr (kRes) {
-        if (c + 1 < NCH) load_res(col0 + kEpiCols, rnxt);
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&rbar[sb], kEpiBufBytes);
+          tma_load_2d(sbuf, tmR, &rbar[sb], col0, row0);
+        }
       }
       __syncwarp();
       float v[32];
@@ -408,9 +396,11 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
       const int sw = (lane >> 1) & 3;
       uint8_t* srow = sbuf + lane * (kEpiCols * 2);
       if constexpr (kRes) {
+        if (!mbar_wait(&rbar[sb], (rph >> sb) & 1, 123)) *abort_flag = 1;
+        rph ^= 1u << sb;
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
-          const uint4 rv = rcur[g];
+          const uint4 rv = *reinterpret_cast<const uint4*>(srow + ((g ^ sw) << 4));
           const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
           for (int h = 0; h < 4; ++h) {
@@ -457,10 +447,6 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, const CUtenso
       }
       if (lane == 0) tma_store_commit();
       sb ^= 1;
-      if constexpr (kRes) {
-#pragma unroll
-        for (int g = 0; g < 4; ++g) rcur[g] = rnxt[g];
-      }
       if (c + 1 < NCH) {
         tmem_ld_wait();
         SG_REG_FENCE_32(nxt);

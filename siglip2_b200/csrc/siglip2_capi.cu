@@ -42,10 +42,7 @@ inline void set_pdl_attr(cudaLaunchAttribute* a) {
 }
 
 template <typename T, int BN, int EPI, int SUB, bool kAT = false, bool kBT = false, bool kSplitK = false>
-int launch_gemm_tc(const GemmIO& io, const GemmParams& p_in, cudaStream_t stream) {
-  GemmParams p = p_in;
-  p.res = io.res;
-  p.ldr = io.ldr;
+int launch_gemm_tc(const GemmIO& io, const GemmParams& p, cudaStream_t stream) {
   CUtensorMap ta, tb, to, tr;
   // transposed operands are [K][M] / [K][N] in memory: 64 x 64 boxes
   if (kAT) SG_TRY(make_tmap_2d(&ta, io.a, 2, p.K, p.M, io.lda, kGemmBK, 64));
@@ -77,10 +74,7 @@ int launch_gemm_tc(const GemmIO& io, const GemmParams& p_in, cudaStream_t stream
 
 // 2-SM variant: clusters of 2 CTAs, one pair per 2 SMs, 256 x BN tiles.
 template <typename T, int BN, int EPI, int SUB, bool kF8 = false, bool kBT = false>
-int launch_gemm_tc2(const GemmIO& io, const GemmParams& p_in, cudaStream_t stream) {
-  GemmParams p = p_in;
-  p.res = io.res;
-  p.ldr = io.ldr;
+int launch_gemm_tc2(const GemmIO& io, const GemmParams& p, cudaStream_t stream) {
   CUtensorMap ta, tb, to, tr;
   SG_TRY(make_tmap_2d(&ta, io.a, 2, p.M, p.K, io.lda, kGemmBM, kGemmBK));
   // transposed B is [K][N] in memory: 64 x 64 boxes
